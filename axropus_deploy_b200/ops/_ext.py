@@ -1,0 +1,32 @@
+"""Loader of the sm_100a kernel extension ``_C``.
+
+CUDA tensors always run through the extension; if it is missing on a machine with a
+GPU the call raises instead of silently falling back to PyTorch, so a GPU run can
+never pass on a fallback path. CPU tensors use the plain PyTorch oracles next to
+each op (the references the kernel tests compare against)."""
+from __future__ import annotations
+
+import importlib
+import os
+
+_C = None
+_ERR = None
+
+
+def cuda_ext():
+    global _C, _ERR
+    if _C is not None:
+        return _C
+    try:
+        _C = importlib.import_module("axropus_deploy_b200._C")
+    except ImportError as e:  # pragma: no cover - exercised on GPU boxes only
+        _ERR = e
+        raise RuntimeError(
+            "axropus_deploy_b200._C (the sm_100a kernels) is not built; run "
+            "`python setup.py build_ext --inplace` (or __graft_entry__.build()). "
+            f"Import error: {e}") from e
+    return _C
+
+
+def ext_path() -> str:
+    return os.path.abspath(cuda_ext().__file__)

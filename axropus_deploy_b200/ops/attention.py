@@ -1,0 +1,121 @@
+"""Paged attention ops: split-KV decode and causal varlen prefill.
+
+CUDA tensors run the sm_100a kernels; CPU tensors run the fp32 PyTorch oracle
+(gather the sequence's pages, dequantise, softmax attention)."""
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+
+from ._ext import cuda_ext
+from .kvcache import KVCache
+
+_SMS = {}
+
+
+def _num_sms(device: torch.device) -> int:
+    idx = device.index or 0
+    if idx not in _SMS:
+        _SMS[idx] = torch.cuda.get_device_properties(idx).multi_processor_count
+    return _SMS[idx]
+
+
+def gather_seq_kv(cache: KVCache, layer: int, block_row: torch.Tensor, seq_len: int):
+    """fp32 K, V of one sequence: [seq_len, H, D] each (oracle helper)."""
+    n_pages = (seq_len + 15) // 16
+    ids = block_row[:n_pages].long()
+    u = cache.read_units(ids)[:, layer]  # [n, 2, H, P, D]
+    k = u[:, 0].permute(0, 2, 1, 3).reshape(n_pages * 16, cache.num_kv_heads, cache.head_dim)[:seq_len]
+    v = u[:, 1].permute(0, 2, 1, 3).reshape(n_pages * 16, cache.num_kv_heads, cache.head_dim)[:seq_len]
+    return k, v
+
+
+def _ref_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_pos0: int, scale: float) -> torch.Tensor:
+    """q [n, Hq, D], k/v [S, Hkv, D] fp32; causal with query i at absolute q_pos0 + i."""
+    hq, hkv = q.shape[1], k.shape[1]
+    g = hq // hkv
+    k = k.repeat_interleave(g, dim=1)
+    v = v.repeat_interleave(g, dim=1)
+    s = torch.einsum("nhd,shd->hns", q.float(), k) * scale
+    n, S = q.shape[0], k.shape[0]
+    qpos = torch.arange(n, device=q.device)[:, None] + q_pos0
+    kpos = torch.arange(S, device=q.device)[None, :]
+    s = s.masked_fill(kpos > qpos, float("-inf"))
+    p = torch.softmax(s, dim=-1)
+    return torch.einsum("hns,shd->nhd", p, v)
+
+
+class DecodeWorkspace:
+    """Scratch for split-KV decode: partial outputs and log-sum-exps."""
+
+    def __init__(self):
+        self.o = None
+        self.lse = None
+
+    def get(self, B: int, Hq: int, S: int, D: int, device) -> tuple:
+        need = B * Hq * S
+        if self.o is None or self.lse.numel() < need or self.o.device != device:
+            self.o = torch.empty(need * D, dtype=torch.float32, device=device)
+            self.lse = torch.empty(need, dtype=torch.float32, device=device)
+        return self.o, self.lse
+
+
+_WS = DecodeWorkspace()
+
+
+def decode_num_splits(batch: int, kv_heads: int, max_pages: int, device: torch.device) -> int:
+    return int(cuda_ext().decode_num_splits(batch, kv_heads, max_pages, _num_sms(device)))
+
+
+def decode_attention(q: torch.Tensor, cache: KVCache, layer: int, block_table: torch.Tensor, seq_lens: torch.Tensor,
+                     scale: Optional[float] = None, max_seq_len: Optional[int] = None,
+                     num_splits: Optional[int] = None, out: Optional[torch.Tensor] = None,
+                     workspace: Optional[DecodeWorkspace] = None) -> torch.Tensor:
+    """q [B, Hq, D] (rotated) -> out [B, Hq, D]; attends to seq_lens[b] cached tokens."""
+    B, Hq, D = q.shape
+    scale = scale if scale is not None else 1.0 / math.sqrt(D)
+    if out is None:
+        out = torch.empty_like(q)
+    if q.is_cuda:
+        if max_seq_len is None:
+            max_seq_len = int(seq_lens.max().item()) if B else 0
+        max_pages = (max_seq_len + 15) // 16
+        S = num_splits if num_splits is not None else decode_num_splits(B, cache.num_kv_heads, max_pages, q.device)
+        ws = workspace or _WS
+        po, pl = ws.get(B, Hq, S, D, q.device) if S > 1 else (out, out)
+        k, v, km, vm, bs, hs, mbs, mhs = cache.layer_args(layer)
+        cuda_ext().decode_attention(q, k, v, km, vm, bs, hs, mbs, mhs, cache.fmt, block_table, seq_lens,
+                                    cache.num_kv_heads, scale, S, max_pages, out, po, pl)
+        return out
+    for b in range(B):
+        n = int(seq_lens[b])
+        k, v = gather_seq_kv(cache, layer, block_table[b], n)
+        out[b] = _ref_attn(q[b:b + 1].float(), k, v, n - 1, scale)[0].to(out.dtype)
+    return out
+
+
+def prefill_attention(q: torch.Tensor, cache: KVCache, layer: int, block_table: torch.Tensor, cu_q: torch.Tensor,
+                      seq_lens: torch.Tensor, max_q: int, scale: Optional[float] = None,
+                      out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """q [T, Hq, D] packed new tokens of B sequences (cu_q offsets); seq_lens = total
+    cached length per sequence including the new tokens."""
+    T, Hq, D = q.shape
+    scale = scale if scale is not None else 1.0 / math.sqrt(D)
+    if out is None:
+        out = torch.empty_like(q)
+    if q.is_cuda:
+        k, v, km, vm, bs, hs, mbs, mhs = cache.layer_args(layer)
+        cuda_ext().prefill_attention(q, k, v, km, vm, bs, hs, mbs, mhs, cache.fmt, block_table, cu_q, seq_lens,
+                                     cache.num_kv_heads, scale, max_q, out)
+        return out
+    cu = cu_q.tolist()
+    for b in range(len(cu) - 1):
+        s0, s1 = cu[b], cu[b + 1]
+        if s1 == s0:
+            continue
+        n = int(seq_lens[b])
+        k, v = gather_seq_kv(cache, layer, block_table[b], n)
+        out[s0:s1] = _ref_attn(q[s0:s1].float(), k, v, n - (s1 - s0), scale).to(out.dtype)
+    return out

@@ -1,0 +1,41 @@
+// Torch bindings of the sm_100a kernels (module axropus_deploy_b200._C).
+#include <torch/extension.h>
+
+namespace axr {
+void page_transfer(int64_t src_data, int64_t src_meta, std::vector<int64_t> src_strides, int64_t src_fmt,
+                   int64_t dst_data, int64_t dst_meta, std::vector<int64_t> dst_strides, int64_t dst_fmt,
+                   torch::Tensor src_ids, torch::Tensor dst_ids, int64_t n_lk, int64_t H, int64_t D,
+                   int64_t max_ctas);
+int64_t decode_num_splits(int64_t batch, int64_t kv_heads, int64_t max_pages, int64_t sms);
+void decode_attention(torch::Tensor q, int64_t k, int64_t v, int64_t km, int64_t vm, int64_t blk_stride,
+                      int64_t head_stride, int64_t mblk_stride, int64_t mhead_stride, int64_t fmt,
+                      torch::Tensor block_table, torch::Tensor seq_lens, int64_t Hkv, double scale,
+                      int64_t num_splits, int64_t max_pages, torch::Tensor out, torch::Tensor part_o,
+                      torch::Tensor part_lse);
+void prefill_attention(torch::Tensor q, int64_t k, int64_t v, int64_t km, int64_t vm, int64_t blk_stride,
+                       int64_t head_stride, int64_t mblk_stride, int64_t mhead_stride, int64_t fmt,
+                       torch::Tensor block_table, torch::Tensor cu_q, torch::Tensor seq_lens, int64_t Hkv,
+                       double scale, int64_t max_q, torch::Tensor out);
+void rmsnorm(torch::Tensor x, c10::optional<torch::Tensor> residual, torch::Tensor w, double eps,
+             torch::Tensor out);
+void rope_kv_write(torch::Tensor qkv, torch::Tensor pos, torch::Tensor slots, torch::Tensor cos_sin,
+                   torch::Tensor q_out, int64_t k, int64_t v, int64_t km, int64_t vm, int64_t blk_stride,
+                   int64_t head_stride, int64_t mblk_stride, int64_t mhead_stride, int64_t fmt, int64_t Hq,
+                   int64_t Hkv);
+void silu_mul(torch::Tensor gate_up, torch::Tensor out);
+void argmax_rows(torch::Tensor logits, torch::Tensor out);
+void spec_verify(torch::Tensor logits, torch::Tensor draft, torch::Tensor out);
+}  // namespace axr
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "sm_100a kernels of axropus_deploy_b200";
+  m.def("page_transfer", &axr::page_transfer);
+  m.def("decode_num_splits", &axr::decode_num_splits);
+  m.def("decode_attention", &axr::decode_attention);
+  m.def("prefill_attention", &axr::prefill_attention);
+  m.def("rmsnorm", &axr::rmsnorm);
+  m.def("rope_kv_write", &axr::rope_kv_write);
+  m.def("silu_mul", &axr::silu_mul);
+  m.def("argmax_rows", &axr::argmax_rows);
+  m.def("spec_verify", &axr::spec_verify);
+}
