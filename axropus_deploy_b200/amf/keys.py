@@ -122,7 +122,7 @@ class AmfContext:
     rope_base_bits: int = 0
     rope_scale_bits: int = 0
     sampling_hash: int = 0
-    rng_hash: int = RNG_HASH_CONST
+    rng_hash: int = 0
 
     def as_dict(self) -> dict:
         return dict(self.__dict__)

@@ -1,0 +1,351 @@
+"""Serving engine: continuous batching over a paged KV cache with AMF restore.
+
+One engine per GPU. Each :meth:`LLMEngine.step`:
+
+1. **Admission.** Waiting requests are admitted while blocks and the prefill token
+   budget allow. For each: the live prefix cache (G2) is matched block by block;
+   the rest of the page-aligned prefix is looked up in the AMF tiers; a hit is
+   restored straight into freshly allocated blocks by the page-transfer kernel
+   (pull + dequantise + scatter, over NVLink when the owning shard is another GPU)
+   and the restored blocks are registered in the prefix cache as computed.
+2. **Prefill** of every admitted request's uncomputed tokens (restored or cached
+   pages are skipped), one varlen batch; cold prefixes are then captured into the G1
+   tier (quantise + push to the owner shard).
+3. **Decode** of all running requests, one token each (split-KV attention over the
+   pages, bf16/FP8/INT4). Optional CUDA graphs replay the decode step.
+
+Reference: the AMF state machine of the native engine (core/engine.cpp:2607-3120)
+and the vLLM connector path (korith_vllm_ext/amf_kv_connector.py), where restore
+and save are per-layer PyTorch index-puts synchronous with the forward pass.
+"""
+from __future__ import annotations
+
+import itertools
+import logging
+import time
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional, Sequence
+
+import numpy as np
+import torch
+
+from .. import ops
+from ..amf.manager import AmfHit, AmfManager
+from ..models.llama import AttnMeta, LlamaModel
+from ..ops.kvcache import PAGE, KVCache
+from .block_manager import BlockManager, block_hashes
+
+log = logging.getLogger(__name__)
+
+
+@dataclass
+class SamplingParams:
+    max_tokens: int = 16
+    temperature: float = 0.0
+    stop_token_ids: Sequence[int] = ()
+    seed: Optional[int] = None
+
+
+@dataclass
+class Request:
+    req_id: str
+    prompt: List[int]
+    params: SamplingParams
+    amf_prefix_len: Optional[int] = None
+    blocks: List[int] = field(default_factory=list)
+    num_computed: int = 0
+    output: List[int] = field(default_factory=list)
+    state: str = "waiting"
+    t_arrival: float = 0.0
+    t_admit: float = 0.0
+    t_first_token: float = 0.0
+    t_finish: float = 0.0
+    amf_tier: str = "cold"
+    local_cached_tokens: int = 0
+    restored_tokens: int = 0
+    restore_ms: float = 0.0
+    row: int = -1
+
+    @property
+    def ttft_ms(self) -> float:
+        return (self.t_first_token - self.t_arrival) * 1e3
+
+    @property
+    def seq_len(self) -> int:
+        return len(self.prompt) + len(self.output)
+
+
+@dataclass
+class EngineConfig:
+    num_blocks: int = 1024
+    kv_fmt: str = "bf16"
+    max_batch: int = 64
+    max_prefill_tokens: int = 16384
+    max_model_len: int = 32768
+    enable_prefix_cache: bool = True
+    capture_on_miss: bool = True
+    amf_min_tokens: int = 64
+    cuda_graphs: bool = False
+
+
+class LLMEngine:
+    def __init__(self, model: LlamaModel, cfg: EngineConfig, amf: Optional[AmfManager] = None):
+        self.model = model
+        self.cfg = cfg
+        self.amf = amf
+        mc = model.cfg
+        self.device = model.device
+        self.cache = KVCache(model.num_layers, cfg.num_blocks, mc.num_kv_heads, mc.head_dim, cfg.kv_fmt, self.device)
+        self.bm = BlockManager(cfg.num_blocks, cfg.enable_prefix_cache)
+        self.max_blocks_per_seq = (cfg.max_model_len + PAGE - 1) // PAGE
+        self.block_table = torch.zeros(cfg.max_batch, self.max_blocks_per_seq, dtype=torch.int32, device=self.device)
+        self.free_rows = list(range(cfg.max_batch - 1, -1, -1))
+        self.waiting: List[Request] = []
+        self.running: List[Request] = []
+        self.finished: List[Request] = []
+        self._ids = itertools.count()
+        self._graphs = None
+        if cfg.cuda_graphs and self.device.type == "cuda" and not model.cfg.is_moe:
+            from .cuda_graph import DecodeGraphRunner
+
+            self._graphs = DecodeGraphRunner(self)
+        self.stat = {"steps": 0, "prefill_tokens": 0, "decode_tokens": 0, "restored_tokens": 0,
+                     "local_cached_tokens": 0, "cold_prefill_tokens": 0}
+
+    # ------------------------------------------------------------------ API
+    def add_request(self, prompt: Sequence[int], params: Optional[SamplingParams] = None, req_id: Optional[str] = None,
+                    amf_prefix_len: Optional[int] = None, arrival: Optional[float] = None) -> Request:
+        params = params or SamplingParams()
+        if len(prompt) + params.max_tokens > self.cfg.max_model_len:
+            raise ValueError("prompt + max_tokens exceeds max_model_len")
+        r = Request(req_id or f"req-{next(self._ids)}", [int(t) for t in prompt], params, amf_prefix_len)
+        r.t_arrival = arrival if arrival is not None else time.perf_counter()
+        self.waiting.append(r)
+        return r
+
+    def has_unfinished(self) -> bool:
+        return bool(self.waiting or self.running)
+
+    def generate(self, prompts: Sequence[Sequence[int]], params: Optional[SamplingParams] = None) -> List[List[int]]:
+        reqs = [self.add_request(p, params) for p in prompts]
+        while self.has_unfinished():
+            self.step()
+        return [r.output for r in reqs]
+
+    def generate_requests(self, prompts: Sequence[Sequence[int]], params: Optional[SamplingParams] = None,
+                          amf_prefix_len: Optional[int] = None) -> List[List[int]]:
+        """Public batch API: run the prompts to completion and return their tokens."""
+        reqs = [self.add_request(p, params, amf_prefix_len=amf_prefix_len) for p in prompts]
+        while self.has_unfinished():
+            self.step()
+        return [r.output for r in reqs]
+
+    def close(self) -> None:
+        """Release CUDA graphs (they hold device memory and must go before the
+        process group is destroyed)."""
+        if self._graphs is not None:
+            self._graphs.close()
+            self._graphs = None
+
+    def evict_live_cache(self, fraction: float = 1.0) -> int:
+        """Drop cached (unreferenced) KV blocks -- forces later requests to restore from AMF."""
+        return self.bm.evict_cached(fraction)
+
+    # ------------------------------------------------------------------ step
+    def step(self) -> List[Request]:
+        self.stat["steps"] += 1
+        done: List[Request] = []
+        admitted = self._admit()
+        if admitted:
+            done += self._prefill(admitted)
+        decoding = [r for r in self.running if r.state == "running" and r not in admitted]
+        if decoding:
+            done += self._decode(decoding)
+        return done
+
+    # ------------------------------------------------------------------ admission
+    def _amf_limit(self, r: Request) -> int:
+        lim = (len(r.prompt) - 1) // PAGE * PAGE  # keep >= 1 token to prefill
+        if r.amf_prefix_len is not None:
+            lim = min(lim, r.amf_prefix_len // PAGE * PAGE)
+        return max(0, lim)
+
+    def _admit(self) -> List[Request]:
+        admitted: List[Request] = []
+        budget = self.cfg.max_prefill_tokens
+        while self.waiting and self.free_rows:
+            r = self.waiting[0]
+            limit = self._amf_limit(r)
+            full_pages = (len(r.prompt) - 1) // PAGE
+            hashes = block_hashes(r.prompt, full_pages)
+            matched = self.bm.match_prefix(hashes)
+            n_local = len(matched)
+            hit: Optional[AmfHit] = None
+            if self.amf is not None and n_local * PAGE < limit:
+                hit = self.amf.lookup(r.prompt, limit)
+                if hit is not None and hit.n_pages <= n_local:
+                    hit.release()
+                    hit = None
+            computed_pages = max(n_local, hit.n_pages if hit else 0)
+            new_tokens = len(r.prompt) - computed_pages * PAGE
+            if admitted and new_tokens > budget:
+                self.bm.release(matched)
+                if hit:
+                    hit.release()
+                break
+            need = (len(r.prompt) + r.params.max_tokens + PAGE - 1) // PAGE - n_local
+            if not self.bm.can_allocate(need):
+                self.bm.release(matched)
+                if hit:
+                    hit.release()
+                if not self.running and not admitted:
+                    raise MemoryError("request does not fit in the KV cache")
+                break
+            self.waiting.pop(0)
+            r.blocks = matched + self.bm.allocate(need)
+            r.t_admit = time.perf_counter()
+            r.local_cached_tokens = n_local * PAGE
+            if hit is not None:
+                t0 = time.perf_counter()
+                blk = torch.tensor(r.blocks[n_local:hit.n_pages], dtype=torch.int32)
+                try:
+                    hit.restore(self.cache, blk, first_page=n_local)
+                    if self.device.type == "cuda":
+                        torch.cuda.current_stream().synchronize()
+                finally:
+                    hit.release()
+                r.restore_ms = (time.perf_counter() - t0) * 1e3
+                r.restored_tokens = (hit.n_pages - n_local) * PAGE
+                r.amf_tier = hit.tier
+                self.bm.register_computed(r.blocks[n_local:hit.n_pages], hashes[n_local:hit.n_pages])
+                if hit.tier in ("lmcache", "disk") and self.amf.promote_lmcache_hits:
+                    self.amf.capture(r.prompt[:hit.n_tokens], self.cache,
+                                     torch.tensor(r.blocks[:hit.n_pages], dtype=torch.int32),
+                                     promote_from=hit.tier)
+                self.amf.note_restored(hit, r.restore_ms, 0.0)
+                self.stat["restored_tokens"] += r.restored_tokens
+            elif n_local:
+                r.amf_tier = "apc"
+            r.num_computed = computed_pages * PAGE
+            self.stat["local_cached_tokens"] += n_local * PAGE
+            r.row = self.free_rows.pop()
+            r.state = "running"
+            self.running.append(r)
+            admitted.append(r)
+            budget -= new_tokens
+        return admitted
+
+    # ------------------------------------------------------------------ forward helpers
+    def _sample(self, logits: torch.Tensor, reqs: List[Request]) -> List[int]:
+        if all(r.params.temperature <= 0 for r in reqs):
+            return ops.argmax(logits).tolist()
+        out = ops.argmax(logits).tolist()
+        for i, r in enumerate(reqs):
+            if r.params.temperature > 0:
+                p = torch.softmax(logits[i] / r.params.temperature, dim=-1)
+                g = torch.Generator(device=p.device)
+                g.manual_seed((r.params.seed or 0) + len(r.output))
+                out[i] = int(torch.multinomial(p, 1, generator=g))
+        return out
+
+    def _append(self, r: Request, tok: int, done: List[Request]) -> None:
+        now = time.perf_counter()
+        if not r.output:
+            r.t_first_token = now
+        r.output.append(tok)
+        if len(r.output) >= r.params.max_tokens or tok in r.params.stop_token_ids:
+            r.state = "finished"
+            r.t_finish = now
+            self.running.remove(r)
+            self.bm.release(r.blocks)
+            self.free_rows.append(r.row)
+            r.row = -1
+            self.finished.append(r)
+            done.append(r)
+
+    def _set_rows(self, reqs: List[Request]) -> None:
+        for r in reqs:
+            row = torch.tensor(r.blocks, dtype=torch.int32)
+            self.block_table[r.row, : len(r.blocks)] = row.to(self.device, non_blocking=True)
+
+    def _prefill(self, reqs: List[Request]) -> List[Request]:
+        toks, pos, slots, cu, lens = [], [], [], [0], []
+        for r in reqs:
+            s = r.num_computed
+            n = len(r.prompt) - s
+            toks.extend(r.prompt[s:])
+            p = np.arange(s, len(r.prompt))
+            pos.extend(p.tolist())
+            b = np.asarray(r.blocks, dtype=np.int64)
+            slots.extend((b[p // PAGE] * PAGE + p % PAGE).tolist())
+            cu.append(cu[-1] + n)
+            lens.append(len(r.prompt))
+            self.stat["prefill_tokens"] += n
+            if r.amf_tier == "cold":
+                self.stat["cold_prefill_tokens"] += n
+        self._set_rows(reqs)
+        dev = self.device
+        rows = torch.tensor([r.row for r in reqs], dtype=torch.long, device=dev)
+        meta = AttnMeta(
+            mode="prefill",
+            positions=torch.tensor(pos, dtype=torch.int32).to(dev, non_blocking=True),
+            slots=torch.tensor(slots, dtype=torch.int32).to(dev, non_blocking=True),
+            block_table=self.block_table.index_select(0, rows),
+            seq_lens=torch.tensor(lens, dtype=torch.int32).to(dev, non_blocking=True),
+            cu_q=torch.tensor(cu, dtype=torch.int32).to(dev, non_blocking=True),
+            max_q=max(cu[i + 1] - cu[i] for i in range(len(reqs))),
+            max_seq_len=max(lens),
+            logits_idx=torch.tensor([c - 1 for c in cu[1:]], dtype=torch.int32).to(dev, non_blocking=True),
+        )
+        logits = self.model.forward(torch.tensor(toks, dtype=torch.int32).to(dev, non_blocking=True), meta,
+                                    self.cache)
+        new = self._sample(logits, reqs)
+        done: List[Request] = []
+        for r, t in zip(reqs, new):
+            full = len(r.prompt) // PAGE
+            self.bm.register_computed(r.blocks[:full], block_hashes(r.prompt, full))
+            if self.amf is not None and self.cfg.capture_on_miss and r.amf_tier == "cold":
+                lim = self._amf_limit(r)
+                if lim >= self.cfg.amf_min_tokens:
+                    self.amf.capture(r.prompt[:lim], self.cache, torch.tensor(r.blocks[: lim // PAGE],
+                                                                              dtype=torch.int32))
+            r.num_computed = len(r.prompt)
+            self._append(r, t, done)
+        return done
+
+    def decode_meta(self, reqs: List[Request]) -> tuple:
+        toks, pos, slots, lens = [], [], [], []
+        for r in reqs:
+            p = r.seq_len - 1
+            toks.append(r.output[-1])
+            pos.append(p)
+            slots.append(r.blocks[p // PAGE] * PAGE + p % PAGE)
+            lens.append(p + 1)
+        return toks, pos, slots, lens
+
+    def _decode(self, reqs: List[Request]) -> List[Request]:
+        toks, pos, slots, lens = self.decode_meta(reqs)
+        self.stat["decode_tokens"] += len(reqs)
+        if self._graphs is not None:
+            logits = self._graphs.run(reqs, toks, pos, slots, lens)
+        else:
+            dev = self.device
+            rows = torch.tensor([r.row for r in reqs], dtype=torch.long, device=dev)
+            host = torch.tensor([toks, pos, slots, lens], dtype=torch.int32)
+            d = host.to(dev, non_blocking=True)
+            meta = AttnMeta(mode="decode", positions=d[1], slots=d[2], block_table=self.block_table.index_select(0, rows),
+                            seq_lens=d[3], max_seq_len=max(lens))
+            logits = self.model.forward(d[0], meta, self.cache)
+        new = self._sample(logits, reqs)
+        done: List[Request] = []
+        for r, t in zip(reqs, new):
+            self._append(r, t, done)
+        return done
+
+    # ------------------------------------------------------------------ telemetry
+    def stats(self) -> Dict:
+        out = dict(self.stat)
+        out["blocks"] = self.bm.stats()
+        if self.amf is not None:
+            out["amf"] = self.amf.stats()
+        return out

@@ -1,0 +1,154 @@
+"""Llama-3 / Mixtral decoder with a paged KV cache.
+
+Weights are random-initialised at the real shapes (no checkpoints on these boxes).
+Projections are fused (QKV, gate/up) and stored ``[in, out]``; the dense GEMMs are
+library GEMMs (cuBLAS through torch.matmul), everything around them runs the
+framework's kernels: fused residual RMSNorm, RoPE + paged KV write, paged prefill /
+split-KV decode attention reading bf16/FP8/INT4 pages, SwiGLU, greedy argmax.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import List, Optional
+
+import torch
+
+from .. import ops
+from ..ops.kvcache import KVCache
+from .config import ModelConfig
+
+
+@dataclass
+class LayerWeights:
+    attn_norm: torch.Tensor
+    wqkv: torch.Tensor
+    wo: torch.Tensor
+    mlp_norm: torch.Tensor
+    w_gate_up: Optional[torch.Tensor] = None  # dense MLP [H, 2F]
+    w_down: Optional[torch.Tensor] = None     # [F, H]
+    w_router: Optional[torch.Tensor] = None   # MoE [H, E]
+    e_gate_up: Optional[torch.Tensor] = None  # [E, H, 2F]
+    e_down: Optional[torch.Tensor] = None     # [E, F, H]
+
+
+@dataclass
+class AttnMeta:
+    """Per-step attention metadata (all CUDA/CPU tensors on the model device)."""
+
+    mode: str                  # "prefill" or "decode"
+    positions: torch.Tensor    # [T] int32
+    slots: torch.Tensor        # [T] int32 (block*16+offset)
+    block_table: torch.Tensor  # [B, max_blocks] int32
+    seq_lens: torch.Tensor     # [B] int32 total kv length after this step
+    cu_q: Optional[torch.Tensor] = None  # [B+1] int32 (prefill)
+    max_q: int = 1
+    max_seq_len: int = 0
+    logits_idx: Optional[torch.Tensor] = None  # [B] rows of the hidden state to sample
+    num_splits: Optional[int] = None
+
+
+class LlamaModel:
+    def __init__(self, cfg: ModelConfig, device="cpu", dtype=torch.bfloat16, seed: int = 0,
+                 init_std: float = 0.02, layers: Optional[int] = None):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.dtype = dtype
+        g = torch.Generator(device=self.device).manual_seed(seed)
+        H, F = cfg.hidden, cfg.ffn
+        n_layers = layers if layers is not None else cfg.num_layers
+
+        def rnd(*shape, std=init_std):
+            t = torch.empty(*shape, dtype=dtype, device=self.device)
+            t.normal_(0.0, std, generator=g)
+            return t
+
+        def ones(n):
+            return torch.ones(n, dtype=dtype, device=self.device)
+
+        self.embed = rnd(cfg.vocab, H, std=1.0)
+        self.layers: List[LayerWeights] = []
+        for _ in range(n_layers):
+            lw = LayerWeights(ones(H), rnd(H, cfg.q_size + 2 * cfg.kv_size), rnd(cfg.q_size, H), ones(H))
+            if cfg.is_moe:
+                lw.w_router = rnd(H, cfg.num_experts)
+                lw.e_gate_up = rnd(cfg.num_experts, H, 2 * F)
+                lw.e_down = rnd(cfg.num_experts, F, H)
+            else:
+                lw.w_gate_up = rnd(H, 2 * F)
+                lw.w_down = rnd(F, H)
+            self.layers.append(lw)
+        self.final_norm = ones(H)
+        self.lm_head = rnd(H, cfg.vocab)
+        self.cos_sin = ops.rope_cos_sin(min(cfg.max_position, 1 << 17), cfg.head_dim, cfg.rope_theta,
+                                        cfg.rope_scaling, self.device)
+        self.scale = 1.0 / math.sqrt(cfg.head_dim)
+
+    @property
+    def num_layers(self) -> int:
+        return len(self.layers)
+
+    def weight_bytes(self) -> int:
+        n = self.embed.numel() + self.lm_head.numel() + self.final_norm.numel()
+        for lw in self.layers:
+            for t in (lw.attn_norm, lw.wqkv, lw.wo, lw.mlp_norm, lw.w_gate_up, lw.w_down, lw.w_router,
+                      lw.e_gate_up, lw.e_down):
+                if t is not None:
+                    n += t.numel()
+        return n * 2
+
+    # ------------------------------------------------------------------ MLPs
+    def _mlp(self, lw: LayerWeights, x: torch.Tensor) -> torch.Tensor:
+        if lw.w_gate_up is not None:
+            return ops.silu_mul(x @ lw.w_gate_up) @ lw.w_down
+        return self._moe(lw, x)
+
+    def _moe(self, lw: LayerWeights, x: torch.Tensor) -> torch.Tensor:
+        cfg = self.cfg
+        logits = (x @ lw.w_router).float()
+        w, idx = torch.topk(logits, cfg.top_k, dim=-1)
+        w = torch.softmax(w, dim=-1)  # Mixtral renormalises over the selected experts
+        out = torch.zeros(x.shape[0], cfg.hidden, dtype=torch.float32, device=x.device)
+        flat = idx.flatten()
+        order = torch.argsort(flat)
+        counts = torch.bincount(flat, minlength=cfg.num_experts).tolist()
+        tok = order // cfg.top_k
+        start = 0
+        for e, c in enumerate(counts):
+            if c == 0:
+                continue
+            sel = order[start:start + c]
+            t = tok[start:start + c]
+            h = ops.silu_mul(x[t] @ lw.e_gate_up[e]) @ lw.e_down[e]
+            out.index_add_(0, t, h.float() * w.flatten()[sel, None])
+            start += c
+        return out.to(x.dtype)
+
+    # ------------------------------------------------------------------ forward
+    def forward(self, tokens: torch.Tensor, meta: AttnMeta, cache: KVCache) -> torch.Tensor:
+        """tokens [T] -> logits of the rows in ``meta.logits_idx`` ([B, vocab], fp32 on GPU)."""
+        cfg = self.cfg
+        T = tokens.shape[0]
+        h = self.embed[tokens.long()]
+        residual = h.clone()
+        x = ops.rmsnorm(h, self.layers[0].attn_norm if self.layers else self.final_norm, cfg.rms_eps)
+        for li, lw in enumerate(self.layers):
+            if li > 0:
+                x = ops.rmsnorm(h, lw.attn_norm, cfg.rms_eps, residual=residual)
+            qkv = x @ lw.wqkv
+            q = ops.rope_kv_write(qkv, meta.positions, meta.slots, self.cos_sin, cache, li, cfg.num_heads,
+                                  cfg.num_kv_heads)
+            if meta.mode == "decode":
+                a = ops.decode_attention(q, cache, li, meta.block_table, meta.seq_lens, self.scale,
+                                         max_seq_len=meta.max_seq_len, num_splits=meta.num_splits)
+            else:
+                a = ops.prefill_attention(q, cache, li, meta.block_table, meta.cu_q, meta.seq_lens, meta.max_q,
+                                          self.scale)
+            h = a.view(T, cfg.q_size) @ lw.wo
+            x = ops.rmsnorm(h, lw.mlp_norm, cfg.rms_eps, residual=residual)
+            h = self._mlp(lw, x)
+        idx = meta.logits_idx if meta.logits_idx is not None else torch.arange(T, device=tokens.device)
+        hs = h[idx.long()]
+        rs = residual[idx.long()].clone()
+        x = ops.rmsnorm(hs, self.final_norm, cfg.rms_eps, residual=rs)
+        return (x @ self.lm_head).float()

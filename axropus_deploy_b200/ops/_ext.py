@@ -11,6 +11,32 @@ import os
 
 _C = None
 _ERR = None
+# Kernels of this framework launched so far (per process). Each wrapper call adds the
+# number of kernels it launches; CUDA-graph replays add what their capture recorded.
+LAUNCHES = [0]
+_KERNELS_PER_CALL = {"decode_attention": lambda a: 2 if a[14] > 1 else 1}
+
+
+class _Counted:
+    def __init__(self, mod):
+        self._mod = mod
+        self.__file__ = mod.__file__
+
+    def __getattr__(self, name):
+        fn = getattr(self._mod, name)
+        if not callable(fn) or name in ("decode_num_splits",):
+            return fn
+        per = _KERNELS_PER_CALL.get(name)
+
+        def call(*a):
+            LAUNCHES[0] += per(a) if per else 1
+            return fn(*a)
+
+        return call
+
+
+def launches() -> int:
+    return LAUNCHES[0]
 
 
 def cuda_ext():
@@ -18,7 +44,7 @@ def cuda_ext():
     if _C is not None:
         return _C
     try:
-        _C = importlib.import_module("axropus_deploy_b200._C")
+        _C = _Counted(importlib.import_module("axropus_deploy_b200._C"))
     except ImportError as e:  # pragma: no cover - exercised on GPU boxes only
         _ERR = e
         raise RuntimeError(

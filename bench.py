@@ -1,0 +1,376 @@
+"""Headline benchmark: AMF-backed serving of Llama-3-8B, data parallel over N GPUs.
+
+Workload: 64 distinct 8192-token prefixes of seeded uniform
+random token ids; requests reuse a Zipf(1.1)-chosen prefix with probability 0.9
+(else a fresh random prefix), append a 128-token random suffix and generate 128
+tokens greedily. The G1 pool (raw bf16 by default) is sharded over the N GPUs by
+prefix hash; a request whose prefix lives on another GPU's shard is restored over
+NVLink by the fused pull + scatter kernel. Random-init weights of the real
+architecture; synthetic token data.
+
+Phases (every rank runs its own engine, one process per GPU):
+  1. populate: each rank prefills its share of the 64 prefixes cold and captures them
+     into their owner shards (untimed);
+  2. latency probe: one request at a time, TTFT of AMF hits vs cold prefills and the
+     restore bandwidth, timed with CUDA events;
+  3. throughput: W warm-up waves then exactly K timed waves of B requests per rank
+     (admission + restore/prefill + 128 decode steps each), bracketed by barrier +
+     synchronize, CUDA-event timed, max over ranks. ``value`` = output tokens/s of
+     the whole job;
+  4. e2e: the same waves through the public API (LLMEngine.generate_requests) timed
+     on the host clock, inputs staged from pinned host memory and the generated
+     tokens read back every step.
+
+``--impl reference`` runs the reference's own vLLM + AMFKVConnector build from
+baseline/_ref on the same workload shape, or prints why it cannot.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+BASELINE_DECODE_TOKS = 286.83  # warm decode throughput (Korith_AMF_Benchmarks.txt:12)
+METRIC = "p50/p99 TTFT on AMF hit vs cold prefill; restore GB/s; decode tok/s at 1/2/4/8 B200"
+
+
+def parse_args(argv=None):
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=5)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--model", default="llama3-8b")
+    p.add_argument("--batch", type=int, default=32, help="requests per wave per GPU")
+    p.add_argument("--prefixes", type=int, default=64)
+    p.add_argument("--prefix-len", type=int, default=8192)
+    p.add_argument("--suffix-len", type=int, default=128)
+    p.add_argument("--out-tokens", type=int, default=128)
+    p.add_argument("--reuse", type=float, default=0.9)
+    p.add_argument("--zipf", type=float, default=1.1)
+    p.add_argument("--pool", default="raw", choices=["raw", "fp8", "int4"])
+    p.add_argument("--kv-fmt", default="bf16", choices=["bf16", "fp8", "int4"])
+    p.add_argument("--ttft-samples", type=int, default=12)
+    p.add_argument("--e2e-waves", type=int, default=2)
+    p.add_argument("--graphs", type=int, default=1)
+    p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--layers", type=int, default=None, help="debug only: fewer layers (invalidates the number)")
+    return p.parse_args(argv)
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.idx)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except FileNotFoundError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = max(mx, float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() in ("active", "1", "yes"):
+                    reasons.add(n)
+        loaded = [s for s in sm if s > 0.5 * mx] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- workload
+class Workload:
+    def __init__(self, args, vocab: int, rank: int):
+        self.args = args
+        self.vocab = vocab
+        g = np.random.default_rng(args.seed)
+        self.prefixes = [g.integers(0, vocab, args.prefix_len, dtype=np.int64).tolist() for _ in range(args.prefixes)]
+        ranks = np.arange(1, args.prefixes + 1, dtype=np.float64)
+        p = ranks ** (-args.zipf)
+        self.zipf_p = p / p.sum()
+        self.rng = np.random.default_rng(args.seed * 1000 + 17 + rank)
+
+    def request(self, force: str = ""):
+        a = self.args
+        reuse = force == "hit" or (force != "cold" and self.rng.random() < a.reuse)
+        if reuse:
+            i = int(self.rng.choice(a.prefixes, p=self.zipf_p))
+            prefix = self.prefixes[i]
+        else:
+            prefix = self.rng.integers(0, self.vocab, a.prefix_len, dtype=np.int64).tolist()
+        suffix = self.rng.integers(0, self.vocab, a.suffix_len, dtype=np.int64).tolist()
+        return prefix + suffix, reuse
+
+
+def pct(xs, q):
+    if not xs:
+        return None
+    return float(np.percentile(np.asarray(xs), q))
+
+
+# ----------------------------------------------------------------------------- ours
+def run_ours(args) -> None:
+    import torch
+
+    from axropus_deploy_b200.amf.manager import AmfManager
+    from axropus_deploy_b200.engine import EngineConfig, LLMEngine, SamplingParams
+    from axropus_deploy_b200.models.config import get_config
+    from axropus_deploy_b200.models.llama import LlamaModel
+    from axropus_deploy_b200.ops._ext import cuda_ext
+    from axropus_deploy_b200.ops.kvcache import PAGE
+    from axropus_deploy_b200.parallel.dist import (all_gather_object, all_reduce_max, barrier, init_distributed,
+                                                   job_tag, shutdown)
+    from axropus_deploy_b200.parallel.sharded_pool import build_pool
+
+    info = init_distributed(timeout_s=600.0)
+    dev = info.device
+    assert dev.type == "cuda", "bench.py needs a GPU"
+    cuda_ext()
+    cfg = get_config(args.model)
+    torch.manual_seed(args.seed)
+    model = LlamaModel(cfg, dev, seed=args.seed, layers=args.layers)
+    L = model.num_layers
+
+    tok_per_req = args.prefix_len + args.suffix_len + args.out_tokens
+    blocks_per_req = math.ceil(tok_per_req / PAGE)
+    num_blocks = int(args.batch * blocks_per_req * 1.15) + 64
+    pages_per_prefix = args.prefix_len // PAGE
+    slots_per_shard = int(math.ceil(1.25 * args.prefixes * pages_per_prefix / info.world)) + 64
+    tag = job_tag()
+    pool = build_pool(info, L, cfg.num_kv_heads, cfg.head_dim, args.pool, slots_per_shard, tag)
+    amf = AmfManager(raw_pool=pool if args.pool == "raw" else None, comp_pool=pool if args.pool != "raw" else None,
+                     min_tokens=64)
+    ecfg = EngineConfig(num_blocks=num_blocks, kv_fmt=args.kv_fmt, max_batch=args.batch,
+                        max_prefill_tokens=2 * (args.prefix_len + args.suffix_len),
+                        max_model_len=tok_per_req + PAGE, cuda_graphs=bool(args.graphs))
+    eng = LLMEngine(model, ecfg, amf)
+    wl = Workload(args, cfg.vocab, info.rank)
+    sp = SamplingParams(max_tokens=args.out_tokens)
+
+    def run_requests(prompts):
+        reqs = [eng.add_request(p, sp, amf_prefix_len=args.prefix_len) for p in prompts]
+        while eng.has_unfinished():
+            eng.step()
+        return reqs
+
+    # ---- 1. populate the pool (each rank its share), untimed
+    mine = [i for i in range(args.prefixes) if i % info.world == info.rank]
+    for j in range(0, len(mine), 4):
+        prompts = [wl.prefixes[i] + [1] * 16 for i in mine[j:j + 4]]
+        reqs = [eng.add_request(p, SamplingParams(max_tokens=1), amf_prefix_len=args.prefix_len) for p in prompts]
+        while eng.has_unfinished():
+            eng.step()
+    eng.evict_live_cache()
+    torch.cuda.synchronize()
+    barrier(info)
+
+    # ---- 2. latency probe: one request at a time
+    def single(prompt):
+        eng.evict_live_cache()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        r = eng.add_request(prompt, SamplingParams(max_tokens=1), amf_prefix_len=args.prefix_len)
+        e0.record()
+        eng.step()
+        e1.record()
+        e1.synchronize()
+        while eng.has_unfinished():
+            eng.step()
+        return r, e0.elapsed_time(e1)
+
+    ttft_hit, ttft_cold, restore_ms, restore_bytes, remote_hits = [], [], [], 0, 0
+    for _ in range(2):  # warm the paths
+        single(wl.request("hit")[0])
+        single(wl.request("cold")[0])
+    for _ in range(args.ttft_samples):
+        r, ms = single(wl.request("hit")[0])
+        if r.amf_tier.startswith("g1"):
+            ttft_hit.append(ms)
+            restore_ms.append(r.restore_ms)
+            restore_bytes += r.restored_tokens * cfg.kv_bytes_per_token() * L / cfg.num_layers
+        r, ms = single(wl.request("cold")[0])
+        ttft_cold.append(ms)
+    # restore bandwidth with device timing: restore the same hit repeatedly into fresh blocks
+    from axropus_deploy_b200.amf.keys import pool_key
+    probe = wl.prefixes[0]
+    hit = amf.lookup(probe + [0] * 16, args.prefix_len)
+    rest_gbps = None
+    if hit is not None:
+        blocks = torch.tensor(eng.bm.allocate(hit.n_pages), dtype=torch.int32)
+        times = []
+        for _ in range(6):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            hit.restore(eng.cache, blocks)
+            e1.record()
+            e1.synchronize()
+            times.append(e0.elapsed_time(e1))
+        hit.release()
+        eng.bm.release(blocks.tolist())
+        kv_bytes = hit.n_tokens * cfg.kv_bytes_per_token() * L / cfg.num_layers
+        rest_gbps = kv_bytes / (min(times[1:]) * 1e-3) / 1e9
+    barrier(info)
+
+    # ---- 3. throughput waves
+    for _ in range(args.warmup):
+        run_requests([wl.request()[0] for _ in range(args.batch)])
+    waves = [[wl.request()[0] for _ in range(args.batch)] for _ in range(args.steps)]
+    sampler = ClockSampler(dev.index)
+    torch.cuda.synchronize()
+    barrier(info)
+    sampler.start()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    st0 = dict(eng.stat)
+    amf0 = dict(amf.stat)
+    from axropus_deploy_b200.ops._ext import launches as n_launches
+
+    t_start.record()
+    launches_before = n_launches()
+    for w in waves:
+        run_requests(w)
+    t_end.record()
+    torch.cuda.synchronize()
+    launches_timed = n_launches() - launches_before
+    barrier(info)
+    clocks = sampler.stop()
+    ms = t_start.elapsed_time(t_end)
+    ms_max = all_reduce_max(ms, info)
+    out_tokens = args.steps * args.batch * args.out_tokens * info.world
+    value = out_tokens / (ms_max / 1e3)
+    wave_stats = {k: eng.stat[k] - st0.get(k, 0) for k in ("restored_tokens", "cold_prefill_tokens",
+                                                          "local_cached_tokens", "decode_tokens")}
+    hits = {k: amf.stat[k] - amf0.get(k, 0) for k in ("hits_g1_raw", "hits_g1_pool", "misses")}
+
+    # ---- 4. e2e through the public API on the host clock
+    e2e_waves = [[wl.request()[0] for _ in range(args.batch)] for _ in range(args.e2e_waves)]
+    torch.cuda.synchronize()
+    barrier(info)
+    h0 = time.perf_counter()
+    h2d = d2h = 0
+    for w in e2e_waves:
+        outs = eng.generate_requests(w, sp, amf_prefix_len=args.prefix_len)
+        h2d += sum(len(p) for p in w) * 4 + args.batch * args.out_tokens * 4 * 4
+        d2h += sum(len(o) for o in outs) * 4
+    torch.cuda.synchronize()
+    e2e_s = time.perf_counter() - h0
+    e2e_s = all_reduce_max(e2e_s, info)
+    e2e_val = args.e2e_waves * args.batch * args.out_tokens * info.world / e2e_s
+
+    gathered = all_gather_object({"ttft_hit": ttft_hit, "ttft_cold": ttft_cold, "restore_ms": restore_ms,
+                                  "rest_gbps": rest_gbps, "clocks": clocks, "ms": ms, "waves": wave_stats,
+                                  "hits": hits}, info)
+    if info.rank == 0:
+        all_hit = [x for g in gathered for x in g["ttft_hit"]]
+        all_cold = [x for g in gathered for x in g["ttft_cold"]]
+        gbps = [g["rest_gbps"] for g in gathered if g["rest_gbps"]]
+        ck = gathered[0]["clocks"]
+        reasons = sorted({r for g in gathered for r in (g["clocks"].get("reasons") or [])})
+        res = {
+            "metric": METRIC,
+            "value": round(value, 2),
+            "unit": "output tokens/s (whole job)",
+            "n_gpus": info.world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_max / args.steps, 3),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": round(value / BASELINE_DECODE_TOKS, 3),
+            "dtype": "bf16",
+            "data": "synthetic (seeded uniform random token ids; random-init weights)",
+            "config": {"model": cfg.name + ("" if args.layers is None else f"-{args.layers}L-INVALID"),
+                       "global_batch": args.batch * info.world, "seq_len": args.prefix_len + args.suffix_len,
+                       "parallelism": f"dp{info.world}", "output_tokens": args.out_tokens,
+                       "prefixes": args.prefixes, "reuse": args.reuse, "zipf": args.zipf,
+                       "pool": args.pool, "kv_cache": args.kv_fmt, "pool_sharding": f"{info.world} shards by prefix hash",
+                       "l2": "inputs larger than L2 (every decode step reads >30 GB of KV and weights)",
+                       "step": "one wave of batch requests per GPU: restore/prefill + 128 decode steps"},
+            "ttft_ms": {"hit_p50": pct(all_hit, 50), "hit_p99": pct(all_hit, 99), "cold_p50": pct(all_cold, 50),
+                        "cold_p99": pct(all_cold, 99), "samples_hit": len(all_hit), "samples_cold": len(all_cold)},
+            "restore_gbps": round(statistics.median(gbps), 1) if gbps else None,
+            "restore_gbps_note": "bf16 KV bytes written into the live cache per second, device-timed",
+            "wave_mix": gathered[0]["waves"], "amf_hits_rank0": gathered[0]["hits"],
+            "clocks": {"sm_mhz": ck.get("sm_mhz"), "sm_max_mhz": ck.get("sm_max_mhz"), "reasons": reasons},
+            "e2e": {"value": round(e2e_val, 2), "unit": "output tokens/s (whole job)",
+                    "h2d_bytes_per_step": int(h2d / max(1, args.e2e_waves)),
+                    "d2h_bytes_per_step": int(d2h / max(1, args.e2e_waves))},
+            "gpu_launches": int(launches_timed),
+            "baseline_note": "vs_baseline divides by the reference's published warm decode rate "
+                             "(286.83 tok/s, llama.cpp 1B q4, batch 1, GPU not stated)",
+        }
+        print(json.dumps(res), flush=True)
+    eng.close()
+    shutdown(info)
+
+
+# ----------------------------------------------------------------------------- reference
+def run_reference(args) -> None:
+    from baseline_reference import run as ref_run  # noqa: E402
+
+    ref_run(args)
+
+
+def main(argv=None):
+    args = parse_args(argv)
+    if args.impl == "reference":
+        sys.path.insert(0, os.path.join(ROOT, "baseline"))
+        try:
+            run_reference(args)
+        except Exception as exc:  # one line, never a traceback as the result
+            if int(os.environ.get("RANK", "0")) == 0:
+                print(json.dumps({"impl": "reference", "unavailable": f"{type(exc).__name__}: {exc}"[:400]}),
+                      flush=True)
+        return
+    run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -416,6 +416,7 @@ PYBIND11_MODULE(_native, m) {
       .def("release_rank", &ShardDirectory::release_rank)
       .def("reclaim_stale", &ShardDirectory::reclaim_stale)
       .def("note_savings", &ShardDirectory::note_savings)
+      .def("lengths", &ShardDirectory::lengths)
       .def("info", [](ShardDirectory& d, int shard) {
         const ShardInfo i = d.info(shard);
         py::dict o;

@@ -8,7 +8,9 @@
 #include <time.h>
 #include <unistd.h>
 
+#include <algorithm>
 #include <atomic>
+#include <functional>
 #include <chrono>
 #include <cmath>
 #include <cstring>
@@ -33,6 +35,8 @@ std::uint64_t mix64(std::uint64_t x) {
   return x;
 }
 
+constexpr int kMaxLens = 256;
+
 struct GlobalHdr {
   std::uint64_t magic;
   std::uint32_t version;
@@ -41,6 +45,12 @@ struct GlobalHdr {
   std::uint32_t ready;
   std::uint64_t total_bytes;
   std::uint64_t shard_off[kMaxRanks];
+  // Distinct prefix lengths (tokens) of READY entries over all shards, with counts:
+  // lookups probe only these lengths when searching the longest cached prefix.
+  pthread_mutex_t len_mu;
+  std::uint32_t n_lens;
+  std::uint32_t len_val[kMaxLens];
+  std::uint32_t len_cnt[kMaxLens];
 };
 
 struct ShardHdr {
@@ -196,8 +206,55 @@ ShardDirectory::ShardDirectory(const std::string& name, int world,
         lay_->free_stack[s][i] = static_cast<std::int32_t>(n_slots[s] - 1 - i);
       for (std::uint32_t i = 0; i < n_slots[s]; ++i) lay_->next_slot[s][i] = -1;
     }
+    {
+      pthread_mutexattr_t a;
+      pthread_mutexattr_init(&a);
+      pthread_mutexattr_setpshared(&a, PTHREAD_PROCESS_SHARED);
+      pthread_mutexattr_setrobust(&a, PTHREAD_MUTEX_ROBUST);
+      pthread_mutex_init(&lay_->g->len_mu, &a);
+      pthread_mutexattr_destroy(&a);
+    }
     __atomic_store_n(&lay_->g->ready, 1u, __ATOMIC_RELEASE);
   }
+}
+
+void ShardDirectory::note_len(std::uint32_t n_tokens, int delta) {
+  GlobalHdr* g = lay_->g;
+  int rc = pthread_mutex_lock(&g->len_mu);
+  if (rc == EOWNERDEAD) pthread_mutex_consistent(&g->len_mu);
+  else if (rc != 0) return;
+  int idx = -1;
+  for (std::uint32_t i = 0; i < g->n_lens; ++i)
+    if (g->len_val[i] == n_tokens) { idx = static_cast<int>(i); break; }
+  if (delta > 0) {
+    if (idx < 0 && g->n_lens < static_cast<std::uint32_t>(kMaxLens)) {
+      idx = static_cast<int>(g->n_lens++);
+      g->len_val[idx] = n_tokens;
+      g->len_cnt[idx] = 0;
+    }
+    if (idx >= 0) g->len_cnt[idx] += 1;
+  } else if (idx >= 0) {
+    if (g->len_cnt[idx] > 0) g->len_cnt[idx] -= 1;
+    if (g->len_cnt[idx] == 0) {  // swap-remove
+      const std::uint32_t last = g->n_lens - 1;
+      g->len_val[idx] = g->len_val[last];
+      g->len_cnt[idx] = g->len_cnt[last];
+      g->n_lens = last;
+    }
+  }
+  pthread_mutex_unlock(&g->len_mu);
+}
+
+std::vector<std::uint32_t> ShardDirectory::lengths() {
+  GlobalHdr* g = lay_->g;
+  std::vector<std::uint32_t> out;
+  int rc = pthread_mutex_lock(&g->len_mu);
+  if (rc == EOWNERDEAD) pthread_mutex_consistent(&g->len_mu);
+  else if (rc != 0) return out;
+  out.assign(g->len_val, g->len_val + g->n_lens);
+  pthread_mutex_unlock(&g->len_mu);
+  std::sort(out.begin(), out.end(), std::greater<std::uint32_t>());
+  return out;
 }
 
 ShardDirectory::~ShardDirectory() {
@@ -279,6 +336,7 @@ DirEntry* ShardDirectory::slot_for_insert_locked(int s, std::uint64_t key) {
 
 void ShardDirectory::free_chain_locked(int s, DirEntry* e) {
   ShardHdr* h = lay_->hdr[s];
+  if (e->phase == static_cast<std::uint32_t>(EntryPhase::kReady)) note_len(e->n_tokens, -1);
   std::int32_t slot = e->first_slot;
   std::uint32_t n = 0;
   while (slot >= 0 && n < e->n_chunks) {
@@ -427,6 +485,7 @@ bool ShardDirectory::commit(int s, std::uint64_t key) {
   if (!e || e->phase != static_cast<std::uint32_t>(EntryPhase::kWriting)) return false;
   e->phase = static_cast<std::uint32_t>(EntryPhase::kReady);
   e->phase_ns = mono_ns();
+  note_len(e->n_tokens, +1);
   ShardHdr* h = lay_->hdr[s];
   h->stats.inserts += 1;
   h->stats.bytes_stored += e->nbytes;

@@ -104,6 +104,8 @@ class ShardDirectory {
   ShardInfo info(int shard);
   std::vector<DirEntry> entries(int shard);
   void note_savings(int shard, std::uint64_t key, double savings_ms);
+  // Distinct token lengths of READY entries (all shards), longest first.
+  std::vector<std::uint32_t> lengths();
 
  private:
   struct Layout;
@@ -114,6 +116,7 @@ class ShardDirectory {
   DirEntry* slot_for_insert_locked(int shard, std::uint64_t key);
   void free_chain_locked(int shard, DirEntry* e);
   bool evict_one_locked(int shard, std::vector<std::uint64_t>* evicted);
+  void note_len(std::uint32_t n_tokens, int delta);
   double score_locked(const DirEntry& e, std::uint64_t now_ns, std::uint64_t chunk_bytes) const;
 
   std::string name_;
