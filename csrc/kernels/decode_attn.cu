@@ -6,6 +6,8 @@
 // and int4_decode_attention.cu:39-177 (contiguous caches, one CTA per (batch, head),
 // never wired in) and the SDPA fallback kernels/dispatch.py:117-152.
 //
+// Two kernels: decode_tc_kernel (tensor cores, head_dim 128, described below) and
+// decode_attn_kernel (CUDA cores, head_dim 64). For the latter:
 // Grid (splits, kv_heads, batch); 4 warps per CTA. A CTA owns one KV head of one
 // sequence and a contiguous range of pages; the G query heads of that KV head
 // (GQA group) are processed together so each KV byte is read once. Warps take pages
@@ -290,6 +292,408 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(DecodeParams p) {
   }
 }
 
+
+// ======================================================================================
+// Tensor-core split-KV decode (head_dim 128): the kernel every D=128 call uses.
+//
+// A warp owns a stream of pages (pages pg0+warp, pg0+warp+4, ...) and pipelines them
+// through a private STAGES-deep ring of shared-memory buffers filled by cp.async, so
+// the loads of the next pages are in flight while the current page is computed.
+// Per page (16 tokens) the warp runs two warp-level MMAs (m16n8k16, f32 accumulate):
+//   S^T[16 tok x 8 heads]  = K[16 x 128] . Q^T[128 x 8]     (GQA heads padded to 8)
+//   O^T[128 x 8 heads]    += V^T[128 x 16] . P^T[16 x 8]
+// The head_dim axis of the first MMA is permuted (any permutation applied to both K
+// and Q leaves QK^T unchanged) so each lane's K fragment is 16 consecutive dims of one
+// 64-dim group, read with 128-bit shared loads, and each MMA k-step stays inside one
+// group -- which lets INT4 apply its per-group scale/zero to partial accumulators.
+// bf16 pages run bf16 MMAs; FP8 and INT4 pages run f16 MMAs on the exact codes (e4m3
+// and 0..15 are exact in f16) with the per-token scales applied to the scores, and
+// their V page is dequantised into an f16 tile for the ldmatrix.trans PV operand.
+// ======================================================================================
+template <int FMT>
+struct TcCfg {
+  static constexpr int KB = FMT == kBF16 ? 4096 : (FMT == kFP8Token ? 2048 : 1024);  // K (=V) unit bytes
+  static constexpr int MB = FMT == kBF16 ? 0 : (FMT == kFP8Token ? 64 : 128);        // meta bytes per unit
+  static constexpr int STAGE = 2 * KB + 2 * MB;
+  static constexpr int STAGES = FMT == kBF16 ? 3 : 4;
+  static constexpr int VT = FMT == kBF16 ? 0 : 4096;  // f16 V tile (dequantised)
+  static constexpr int WARP = STAGES * STAGE + VT + 256;
+  static constexpr int SMEM = 4 * WARP;
+};
+
+// byte offset of 16B chunk `c` of K row `r` in the LDS-friendly swizzle
+template <int FMT>
+__device__ __forceinline__ int ksw(int r, int c) {
+  if constexpr (FMT == kBF16) return r * 256 + ((c ^ (r & 1)) << 4);
+  else if constexpr (FMT == kFP8Token) return r * 128 + ((c ^ ((r & 1) << 2)) << 4);
+  else return r * 64 + ((c ^ (((r >> 1) & 1) << 1)) << 4);
+}
+// ldmatrix-friendly swizzle of a [16 tok][128 dims] 16-bit tile
+__device__ __forceinline__ int vsw(int r, int c) { return r * 256 + ((c ^ (r & 7)) << 4); }
+
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1, bool f16) {
+  if (f16) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                 : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  } else {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                 : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  }
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ uint32_t fp8x2_h2(uint32_t two_codes) {
+  __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(two_codes & 0xffff), __NV_E4M3);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+// one byte of two nibbles -> f16x2 (lo, hi) holding the integers 0..15
+__device__ __forceinline__ uint32_t nib2_h2(uint32_t byte) {
+  const uint32_t x = (byte & 0x0Fu) | ((byte & 0xF0u) << 12) | 0x64006400u;  // 1024 + n
+  __half2 h = *reinterpret_cast<const __half2*>(&x);
+  h = __hsub2(h, __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400)));
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+template <int FMT>
+__device__ __forceinline__ void tc_issue_page(const DecodeParams& p, int blk, int kvh, char* st, int lane) {
+  using C = TcCfg<FMT>;
+  const char* ku = p.k + blk * p.blk_stride + kvh * p.head_stride;
+  const char* vu = p.v + blk * p.blk_stride + kvh * p.head_stride;
+  char* sk = st;
+  char* sv = st + C::KB;
+#pragma unroll
+  for (int i = 0; i < C::KB / 16 / 32; ++i) {
+    const int c = lane + i * 32;
+    if constexpr (FMT == kBF16) {
+      const int r = c >> 4, cc = c & 15;
+      cp_async16(sk + ksw<FMT>(r, cc), ku + c * 16);
+      cp_async16(sv + vsw(r, cc), vu + c * 16);
+    } else if constexpr (FMT == kFP8Token) {
+      const int r = c >> 3, cc = c & 7;
+      cp_async16(sk + ksw<FMT>(r, cc), ku + c * 16);
+      cp_async16(sv + c * 16, vu + c * 16);
+    } else {
+      const int r = c >> 2, cc = c & 3;
+      cp_async16(sk + ksw<FMT>(r, cc), ku + c * 16);
+      cp_async16(sv + c * 16, vu + c * 16);
+    }
+  }
+  if constexpr (FMT != kBF16) {
+    const char* km = p.km + blk * p.mblk_stride + kvh * p.mhead_stride;
+    const char* vm = p.vm + blk * p.mblk_stride + kvh * p.mhead_stride;
+    constexpr int MC = C::MB / 16;  // 4 (fp8) or 8 (int4) chunks per meta unit
+    if (lane < MC) cp_async16(st + 2 * C::KB + lane * 16, km + lane * 16);
+    else if (lane < 2 * MC) cp_async16(st + 2 * C::KB + C::MB + (lane - MC) * 16, vm + (lane - MC) * 16);
+  }
+}
+
+template <int FMT, int G>
+__global__ void __launch_bounds__(128) decode_tc_kernel(DecodeParams p) {
+  using C = TcCfg<FMT>;
+  constexpr bool F16 = FMT != kBF16;
+  extern __shared__ __align__(128) char smem[];
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z, S = gridDim.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  char* wbase = smem + warp * C::WARP;
+  char* vtile = wbase + C::STAGES * C::STAGE;
+  uint16_t* pt = reinterpret_cast<uint16_t*>(vtile + C::VT);  // P^T [8 heads][16 tok]
+
+  const int seq_len = p.seq_lens[b];
+  const int n_pages = (seq_len + kPage - 1) / kPage;
+  const int pg0 = split * p.pages_per_split;
+  const int pg1 = min(n_pages, pg0 + p.pages_per_split);
+  const int my_n = pg1 > pg0 + warp ? (pg1 - pg0 - warp + 3) / 4 : 0;
+  const int* bt = p.block_table + (long long)b * p.bt_stride;
+
+  // Q^T fragments (B operand), dims permuted: k-step kk, lane t -> dims base..base+3
+  uint32_t qb[8][2];
+  float qsum[2] = {0.f, 0.f};  // INT4: sum of this lane's q dims per group, head g
+  {
+    const __nv_bfloat16* qrow = p.q + ((long long)b * p.Hq + kvh * G + (g < G ? g : 0)) * 128;
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      const int base = (kk >> 2) * 64 + t * 16 + (kk & 3) * 4;
+      float f[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) f[e] = g < G ? __bfloat162float(qrow[base + e]) * p.scale_log2 : 0.f;
+      if constexpr (F16) {
+        qb[kk][0] = pack_h2(f[0], f[1]);
+        qb[kk][1] = pack_h2(f[2], f[3]);
+        const __half2 h0 = *reinterpret_cast<__half2*>(&qb[kk][0]);
+        const __half2 h1 = *reinterpret_cast<__half2*>(&qb[kk][1]);
+        qsum[kk >> 2] += __low2float(h0) + __high2float(h0) + __low2float(h1) + __high2float(h1);
+      } else {
+        qb[kk][0] = pack_bf16x2(f[0], f[1]);
+        qb[kk][1] = pack_bf16x2(f[2], f[3]);
+      }
+    }
+  }
+  float qs_col[2][2];  // [group][j]: q-sum of head 2t+j (INT4 zero-point term)
+  if constexpr (FMT == kINT4G64) {
+#pragma unroll
+    for (int gr = 0; gr < 2; ++gr) {
+      qsum[gr] += __shfl_xor_sync(0xffffffffu, qsum[gr], 1);
+      qsum[gr] += __shfl_xor_sync(0xffffffffu, qsum[gr], 2);
+#pragma unroll
+      for (int j = 0; j < 2; ++j) qs_col[gr][j] = __shfl_sync(0xffffffffu, qsum[gr], 4 * (2 * t + j));
+    }
+  }
+
+  float o[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m[2] = {-FLT_MAX, -FLT_MAX}, l[2] = {0.f, 0.f};
+
+  // prologue
+#pragma unroll
+  for (int s = 0; s < C::STAGES - 1; ++s) {
+    if (s < my_n) tc_issue_page<FMT>(p, bt[pg0 + warp + 4 * s], kvh, wbase + s * C::STAGE, lane);
+    cp_async_commit();
+  }
+  for (int i = 0; i < my_n; ++i) {
+    {
+      const int ni = i + C::STAGES - 1;
+      if (ni < my_n) tc_issue_page<FMT>(p, bt[pg0 + warp + 4 * ni], kvh, wbase + (ni % C::STAGES) * C::STAGE, lane);
+      cp_async_commit();
+    }
+    cp_async_wait<C::STAGES - 1>();
+    __syncwarp();
+    const char* st = wbase + (i % C::STAGES) * C::STAGE;
+    const char* sk = st;
+    const int pg = pg0 + warp + 4 * i;
+
+    // ---- S^T = K . Q^T
+    float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int gr = 0; gr < 2; ++gr) {
+      uint32_t ka[2][8];  // [row g | g+8][4 k-steps x (a-lo, a-hi)]
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int r = g + 8 * h;
+        if constexpr (FMT == kBF16) {
+          const uint4 x = *reinterpret_cast<const uint4*>(sk + ksw<FMT>(r, gr * 8 + t * 2));
+          const uint4 y = *reinterpret_cast<const uint4*>(sk + ksw<FMT>(r, gr * 8 + t * 2 + 1));
+          ka[h][0] = x.x; ka[h][1] = x.y; ka[h][2] = x.z; ka[h][3] = x.w;
+          ka[h][4] = y.x; ka[h][5] = y.y; ka[h][6] = y.z; ka[h][7] = y.w;
+        } else if constexpr (FMT == kFP8Token) {
+          const uint4 x = *reinterpret_cast<const uint4*>(sk + ksw<FMT>(r, gr * 4 + t));
+          const uint32_t w[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            ka[h][2 * q] = fp8x2_h2(w[q]);
+            ka[h][2 * q + 1] = fp8x2_h2(w[q] >> 16);
+          }
+        } else {
+          const uint2 x = *reinterpret_cast<const uint2*>(sk + ksw<FMT>(r, gr * 2 + (t >> 1)) + (t & 1) * 8);
+          const uint32_t w[2] = {x.x, x.y};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t word = w[q >> 1] >> ((q & 1) * 16);
+            ka[h][2 * q] = nib2_h2(word & 0xff);
+            ka[h][2 * q + 1] = nib2_h2((word >> 8) & 0xff);
+          }
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int kk = gr * 4 + q;
+        if constexpr (FMT == kINT4G64) {
+          if (gr == 0) mma16816(s0, ka[0][2 * q], ka[1][2 * q], ka[0][2 * q + 1], ka[1][2 * q + 1], qb[kk][0], qb[kk][1], true);
+          else mma16816(s1, ka[0][2 * q], ka[1][2 * q], ka[0][2 * q + 1], ka[1][2 * q + 1], qb[kk][0], qb[kk][1], true);
+        } else {
+          mma16816(s0, ka[0][2 * q], ka[1][2 * q], ka[0][2 * q + 1], ka[1][2 * q + 1], qb[kk][0], qb[kk][1], F16);
+        }
+      }
+    }
+    // ---- per-token scales, masking
+    const int tok0 = pg * kPage + g, tok1 = tok0 + 8;
+    float sc[4];
+    if constexpr (FMT == kBF16) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sc[e] = s0[e];
+    } else if constexpr (FMT == kFP8Token) {
+      const float* ks = reinterpret_cast<const float*>(st + 2 * C::KB);
+      const float k0 = ks[g], k1 = ks[g + 8];
+      sc[0] = s0[0] * k0; sc[1] = s0[1] * k0; sc[2] = s0[2] * k1; sc[3] = s0[3] * k1;
+    } else {
+      const uint32_t* km = reinterpret_cast<const uint32_t*>(st + 2 * C::KB);  // [tok][group] (scale, zero)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t m0 = km[(g + 8 * h) * 2 + 0], m1 = km[(g + 8 * h) * 2 + 1];
+        const float a0 = half_bits_to_float(m0 & 0xffff), z0 = half_bits_to_float(m0 >> 16);
+        const float a1 = half_bits_to_float(m1 & 0xffff), z1 = half_bits_to_float(m1 >> 16);
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+          sc[2 * h + j] = s0[2 * h + j] * a0 + qs_col[0][j] * z0 + s1[2 * h + j] * a1 + qs_col[1][j] * z1;
+      }
+    }
+    if (tok0 >= seq_len) { sc[0] = -FLT_MAX; sc[1] = -FLT_MAX; }
+    if (tok1 >= seq_len) { sc[2] = -FLT_MAX; sc[3] = -FLT_MAX; }
+    // ---- online softmax (columns = heads 2t, 2t+1)
+    float pv[4];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      float mx = fmaxf(sc[j], sc[2 + j]);
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+      const float mn = fmaxf(m[j], mx);
+      const float alpha = exp2f(m[j] - mn);
+      m[j] = mn;
+      pv[j] = sc[j] == -FLT_MAX ? 0.f : exp2f(sc[j] - mn);
+      pv[2 + j] = sc[2 + j] == -FLT_MAX ? 0.f : exp2f(sc[2 + j] - mn);
+      l[j] = l[j] * alpha + pv[j] + pv[2 + j];
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        o[mt][j] *= alpha;
+        o[mt][2 + j] *= alpha;
+      }
+    }
+    // ---- P^T to shared (for the B operand)
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int hcol = 2 * t + j;
+      uint16_t a, c;
+      if constexpr (F16) {
+        a = __half_as_ushort(__float2half_rn(pv[j]));
+        c = __half_as_ushort(__float2half_rn(pv[2 + j]));
+      } else {
+        a = __bfloat16_as_ushort(__float2bfloat16(pv[j]));
+        c = __bfloat16_as_ushort(__float2bfloat16(pv[2 + j]));
+      }
+      pt[hcol * 16 + g] = a;
+      pt[hcol * 16 + g + 8] = c;
+    }
+    // ---- V tile (FP8 / INT4: dequantise into the f16 ldmatrix tile)
+    const char* vt;
+    if constexpr (FMT == kBF16) {
+      vt = st + C::KB;
+    } else {
+      const char* sv = st + C::KB;
+      const char* vm = st + 2 * C::KB + C::MB;
+      const int cc = lane & 15;
+#pragma unroll
+      for (int i2 = 0; i2 < 8; ++i2) {
+        const int r = (lane >> 4) + 2 * i2;
+        uint32_t h4[4];
+        if constexpr (FMT == kFP8Token) {
+          const uint2 x = *reinterpret_cast<const uint2*>(sv + r * 128 + cc * 8);
+          const float vs = reinterpret_cast<const float*>(vm)[r];
+          const uint32_t w[2] = {x.x, x.y};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float2 f = e4m3x2_to_float2((w[q >> 1] >> ((q & 1) * 16)) & 0xffff);
+            h4[q] = pack_h2(f.x * vs, f.y * vs);
+          }
+        } else {
+          const uint32_t x = *reinterpret_cast<const uint32_t*>(sv + r * 64 + cc * 4);
+          const uint32_t mm = reinterpret_cast<const uint32_t*>(vm)[r * 2 + (cc >> 3)];
+          const float a = half_bits_to_float(mm & 0xffff), z = half_bits_to_float(mm >> 16);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t byte = (x >> (8 * q)) & 0xff;
+            h4[q] = pack_h2(float(byte & 0xf) * a + z, float(byte >> 4) * a + z);
+          }
+        }
+        *reinterpret_cast<uint4*>(vtile + vsw(r, cc)) = make_uint4(h4[0], h4[1], h4[2], h4[3]);
+      }
+      vt = vtile;
+    }
+    __syncwarp();
+    const uint32_t b0 = *reinterpret_cast<const uint32_t*>(pt + g * 16 + 2 * t);
+    const uint32_t b1 = *reinterpret_cast<const uint32_t*>(pt + g * 16 + 2 * t + 8);
+    // ---- O^T += V^T . P^T
+    {
+      const uint32_t vbase = static_cast<uint32_t>(__cvta_generic_to_shared(vt));
+      const int mi = lane >> 3, r = (mi >> 1) * 8 + (lane & 7);
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        uint32_t a0, a1, a2, a3;
+        asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(a0), "=r"(a1), "=r"(a2), "=r"(a3)
+                     : "r"(vbase + vsw(r, 2 * mt + (mi & 1))));
+        mma16816(o[mt], a0, a1, a2, a3, b0, b1, F16);
+      }
+    }
+    __syncwarp();
+  }
+  cp_async_wait<0>();
+
+  // ---- merge warps (reuses the stage buffers)
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    l[j] += __shfl_xor_sync(0xffffffffu, l[j], 4);
+    l[j] += __shfl_xor_sync(0xffffffffu, l[j], 8);
+    l[j] += __shfl_xor_sync(0xffffffffu, l[j], 16);
+  }
+  __syncthreads();
+  float* wm = reinterpret_cast<float*>(smem);          // [4][8]
+  float* wl = wm + 32;                                 // [4][8]
+  float* wacc = wl + 32;                               // [4][8][128]
+  if (g == 0) {
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      wm[warp * 8 + 2 * t + j] = m[j];
+      wl[warp * 8 + 2 * t + j] = l[j];
+    }
+  }
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int head = 2 * t + (e & 1), dim = mt * 16 + g + (e >> 1) * 8;
+      wacc[(warp * 8 + head) * 128 + dim] = o[mt][e];
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < G * 128; i += blockDim.x) {
+    const int hh = i / 128, d = i % 128;
+    float M = -FLT_MAX;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, wm[w * 8 + hh]);
+    float L = 0.f, O = 0.f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const float mw = wm[w * 8 + hh];
+      const float f = mw == -FLT_MAX ? 0.f : exp2f(mw - M);
+      L += wl[w * 8 + hh] * f;
+      O += wacc[(w * 8 + hh) * 128 + d] * f;
+    }
+    const int hq = kvh * G + hh;
+    const float ov = L > 0.f ? O / L : 0.f;
+    if (S == 1) {
+      p.out[((long long)b * p.Hq + hq) * 128 + d] = __float2bfloat16(ov);
+    } else {
+      const long long base = ((long long)b * p.Hq + hq) * S + split;
+      p.part_o[base * 128 + d] = ov;
+      if (d == 0) p.part_lse[base] = L > 0.f ? M + log2f(L) : -FLT_MAX;
+    }
+  }
+}
+
+template <int FMT>
+static void launch_tc(int G, dim3 grid, const DecodeParams& p, cudaStream_t st) {
+  constexpr int smem = TcCfg<FMT>::SMEM;
+  auto go = [&](auto kern) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    kern<<<grid, 128, smem, st>>>(p);
+  };
+  switch (G) {
+    case 1: go(decode_tc_kernel<FMT, 1>); break;
+    case 2: go(decode_tc_kernel<FMT, 2>); break;
+    case 4: go(decode_tc_kernel<FMT, 4>); break;
+    case 8: go(decode_tc_kernel<FMT, 8>); break;
+    default: TORCH_CHECK(false, "decode_attention: GQA group ", G, " unsupported");
+  }
+}
+
 template <int D>
 __global__ void decode_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_lse,
                                       __nv_bfloat16* __restrict__ out, int S) {
@@ -374,9 +778,9 @@ void decode_attention(torch::Tensor q, int64_t k, int64_t v, int64_t km, int64_t
   dim3 grid(S, Hkv, B);
   auto st = at::cuda::getCurrentCUDAStream();
   if (D == 128) {
-    if (fmt == kBF16) launch_g<128, kBF16>(G, grid, p, st);
-    else if (fmt == kFP8Token) launch_g<128, kFP8Token>(G, grid, p, st);
-    else if (fmt == kINT4G64) launch_g<128, kINT4G64>(G, grid, p, st);
+    if (fmt == kBF16) launch_tc<kBF16>(G, grid, p, st);
+    else if (fmt == kFP8Token) launch_tc<kFP8Token>(G, grid, p, st);
+    else if (fmt == kINT4G64) launch_tc<kINT4G64>(G, grid, p, st);
     else TORCH_CHECK(false, "decode_attention: unsupported cache format ", fmt);
   } else if (D == 64) {
     if (fmt == kBF16) launch_g<64, kBF16>(G, grid, p, st);
