@@ -24,16 +24,16 @@ PAGE = 16
 
 
 def block_hashes(tokens: Sequence[int], n_blocks: Optional[int] = None) -> List[bytes]:
-    """Chained 16-byte hashes of the first ``n_blocks`` full blocks of ``tokens``."""
-    arr = np.asarray(tokens, dtype=np.int64).astype("<i4")
-    nb = len(arr) // PAGE if n_blocks is None else min(n_blocks, len(arr) // PAGE)
-    out: List[bytes] = []
-    parent = b"\x00" * 16
-    for i in range(nb):
-        h = hashlib.blake2b(parent + arr[i * PAGE:(i + 1) * PAGE].tobytes(), digest_size=16).digest()
-        out.append(h)
-        parent = h
-    return out
+    """Chained 16-byte hashes of the first ``n_blocks`` full blocks of ``tokens``
+    (computed natively; equal hashes mean equal whole prefixes)."""
+    from .._native_loader import native
+
+    arr = tokens if isinstance(tokens, np.ndarray) else np.asarray(tokens, dtype=np.int64)
+    if arr.dtype != np.int32:
+        arr = (arr.astype(np.int64) & 0xFFFFFFFF).astype(np.uint32).view(np.int32)
+    h = native().block_chain_hashes(arr, PAGE, -1 if n_blocks is None else n_blocks)
+    raw = h.tobytes()
+    return [raw[16 * i:16 * (i + 1)] for i in range(h.shape[0])]
 
 
 class BlockManager:

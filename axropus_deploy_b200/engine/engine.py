@@ -65,6 +65,8 @@ class Request:
     restored_tokens: int = 0
     restore_ms: float = 0.0
     row: int = -1
+    prompt_np: Optional[np.ndarray] = None
+    hashes: List[bytes] = field(default_factory=list)
 
     @property
     def ttft_ms(self) -> float:
@@ -118,7 +120,9 @@ class LLMEngine:
         params = params or SamplingParams()
         if len(prompt) + params.max_tokens > self.cfg.max_model_len:
             raise ValueError("prompt + max_tokens exceeds max_model_len")
-        r = Request(req_id or f"req-{next(self._ids)}", [int(t) for t in prompt], params, amf_prefix_len)
+        arr = np.asarray(prompt, dtype=np.int64)
+        r = Request(req_id or f"req-{next(self._ids)}", arr.tolist(), params, amf_prefix_len)
+        r.prompt_np = (arr & 0xFFFFFFFF).astype(np.uint32).view(np.int32)
         r.t_arrival = arrival if arrival is not None else time.perf_counter()
         self.waiting.append(r)
         return r
@@ -177,12 +181,13 @@ class LLMEngine:
             r = self.waiting[0]
             limit = self._amf_limit(r)
             full_pages = (len(r.prompt) - 1) // PAGE
-            hashes = block_hashes(r.prompt, full_pages)
+            hashes = block_hashes(r.prompt_np, full_pages)
+            r.hashes = hashes
             matched = self.bm.match_prefix(hashes)
             n_local = len(matched)
             hit: Optional[AmfHit] = None
             if self.amf is not None and n_local * PAGE < limit:
-                hit = self.amf.lookup(r.prompt, limit)
+                hit = self.amf.lookup(r.prompt_np, limit)
                 if hit is not None and hit.n_pages <= n_local:
                     hit.release()
                     hit = None
@@ -219,7 +224,7 @@ class LLMEngine:
                 r.amf_tier = hit.tier
                 self.bm.register_computed(r.blocks[n_local:hit.n_pages], hashes[n_local:hit.n_pages])
                 if hit.tier in ("lmcache", "disk") and self.amf.promote_lmcache_hits:
-                    self.amf.capture(r.prompt[:hit.n_tokens], self.cache,
+                    self.amf.capture(r.prompt_np[:hit.n_tokens], self.cache,
                                      torch.tensor(r.blocks[:hit.n_pages], dtype=torch.int32),
                                      promote_from=hit.tier)
                 self.amf.note_restored(hit, r.restore_ms, 0.0)
@@ -303,11 +308,12 @@ class LLMEngine:
         done: List[Request] = []
         for r, t in zip(reqs, new):
             full = len(r.prompt) // PAGE
-            self.bm.register_computed(r.blocks[:full], block_hashes(r.prompt, full))
+            hs = r.hashes if len(r.hashes) >= full else block_hashes(r.prompt_np, full)
+            self.bm.register_computed(r.blocks[:full], hs[:full])
             if self.amf is not None and self.cfg.capture_on_miss and r.amf_tier == "cold":
                 lim = self._amf_limit(r)
                 if lim >= self.cfg.amf_min_tokens:
-                    self.amf.capture(r.prompt[:lim], self.cache, torch.tensor(r.blocks[: lim // PAGE],
+                    self.amf.capture(r.prompt_np[:lim], self.cache, torch.tensor(r.blocks[: lim // PAGE],
                                                                               dtype=torch.int32))
             r.num_computed = len(r.prompt)
             self._append(r, t, done)

@@ -63,6 +63,14 @@ def all_reduce_max(x: float, info: DistInfo) -> float:
     return float(t.item())
 
 
+def all_reduce_min(x: float, info: DistInfo) -> float:
+    if not info.is_dist:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=info.device if info.device.type == "cuda" else "cpu")
+    dist.all_reduce(t, op=dist.ReduceOp.MIN)
+    return float(t.item())
+
+
 def all_reduce_sum(x: float, info: DistInfo) -> float:
     if not info.is_dist:
         return x

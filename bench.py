@@ -165,8 +165,8 @@ def run_ours(args) -> None:
     from axropus_deploy_b200.models.llama import LlamaModel
     from axropus_deploy_b200.ops._ext import cuda_ext
     from axropus_deploy_b200.ops.kvcache import PAGE
-    from axropus_deploy_b200.parallel.dist import (all_gather_object, all_reduce_max, barrier, init_distributed,
-                                                   job_tag, shutdown)
+    from axropus_deploy_b200.parallel.dist import (all_gather_object, all_reduce_max, all_reduce_min, barrier,
+                                                   init_distributed, job_tag, shutdown)
     from axropus_deploy_b200.parallel.sharded_pool import build_pool
 
     info = init_distributed(timeout_s=600.0)
@@ -182,15 +182,24 @@ def run_ours(args) -> None:
     blocks_per_req = math.ceil(tok_per_req / PAGE)
     num_blocks = int(args.batch * blocks_per_req * 1.15) + 64
     pages_per_prefix = args.prefix_len // PAGE
-    slots_per_shard = int(math.ceil(1.25 * args.prefixes * pages_per_prefix / info.world)) + 64
+    ecfg = EngineConfig(num_blocks=num_blocks, kv_fmt=args.kv_fmt, max_batch=args.batch,
+                        max_prefill_tokens=2 * (args.prefix_len + args.suffix_len),
+                        max_model_len=tok_per_req + PAGE, cuda_graphs=bool(args.graphs))
+    eng = LLMEngine(model, ecfg, None)
+    # G1 pool: at least 1.25x the prefix set over the node, grown into the HBM left after
+    # weights and the live cache (keeping 12 GB of headroom for activations and graphs)
+    from axropus_deploy_b200.amf.pool import PoolSlab
+    chunk = PoolSlab.chunk_bytes(L, cfg.num_kv_heads, cfg.head_dim, args.pool)
+    need = int(math.ceil(1.25 * args.prefixes * pages_per_prefix / info.world)) + 64
+    free, _ = torch.cuda.mem_get_info(dev)
+    room = max(0, int((free - (12 << 30)) // chunk))
+    slots_per_shard = max(need, min(room, 3 * need))
+    slots_per_shard = int(min(slots_per_shard, all_reduce_min(slots_per_shard, info)))
     tag = job_tag()
     pool = build_pool(info, L, cfg.num_kv_heads, cfg.head_dim, args.pool, slots_per_shard, tag)
     amf = AmfManager(raw_pool=pool if args.pool == "raw" else None, comp_pool=pool if args.pool != "raw" else None,
                      min_tokens=64)
-    ecfg = EngineConfig(num_blocks=num_blocks, kv_fmt=args.kv_fmt, max_batch=args.batch,
-                        max_prefill_tokens=2 * (args.prefix_len + args.suffix_len),
-                        max_model_len=tok_per_req + PAGE, cuda_graphs=bool(args.graphs))
-    eng = LLMEngine(model, ecfg, amf)
+    eng.amf = amf
     wl = Workload(args, cfg.vocab, info.rank)
     sp = SamplingParams(max_tokens=args.out_tokens)
 
@@ -237,25 +246,35 @@ def run_ours(args) -> None:
             restore_bytes += r.restored_tokens * cfg.kv_bytes_per_token() * L / cfg.num_layers
         r, ms = single(wl.request("cold")[0])
         ttft_cold.append(ms)
-    # restore bandwidth with device timing: restore the same hit repeatedly into fresh blocks
+    # restore bandwidth with device timing: restore one prefix owned by this GPU's shard
+    # and (N > 1) one owned by another GPU's shard (pulled over NVLink), 6 times each
     from axropus_deploy_b200.amf.keys import pool_key
-    probe = wl.prefixes[0]
-    hit = amf.lookup(probe + [0] * 16, args.prefix_len)
-    rest_gbps = None
-    if hit is not None:
-        blocks = torch.tensor(eng.bm.allocate(hit.n_pages), dtype=torch.int32)
-        times = []
-        for _ in range(6):
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            hit.restore(eng.cache, blocks)
-            e1.record()
-            e1.synchronize()
-            times.append(e0.elapsed_time(e1))
-        hit.release()
-        eng.bm.release(blocks.tolist())
-        kv_bytes = hit.n_tokens * cfg.kv_bytes_per_token() * L / cfg.num_layers
-        rest_gbps = kv_bytes / (min(times[1:]) * 1e-3) / 1e9
+
+    def restore_gbps(owner_local: bool):
+        for idx, pf in enumerate(wl.prefixes):
+            own = pool.owner(pool_key(pf[:args.prefix_len])) == info.rank
+            if own != owner_local:
+                continue
+            hit = amf.lookup(pf + [0] * 16, args.prefix_len)
+            if hit is None:
+                continue
+            blocks = torch.tensor(eng.bm.allocate(hit.n_pages), dtype=torch.int32)
+            times = []
+            for _ in range(6):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                hit.restore(eng.cache, blocks)
+                e1.record()
+                e1.synchronize()
+                times.append(e0.elapsed_time(e1))
+            hit.release()
+            eng.bm.release(blocks.tolist())
+            kv_bytes = hit.n_tokens * cfg.kv_bytes_per_token() * L / cfg.num_layers
+            return kv_bytes / (min(times[1:]) * 1e-3) / 1e9
+        return None
+
+    rest_gbps = restore_gbps(True)
+    rest_gbps_remote = restore_gbps(False) if info.world > 1 else None
     barrier(info)
 
     # ---- 3. throughput waves
@@ -305,12 +324,13 @@ def run_ours(args) -> None:
     e2e_val = args.e2e_waves * args.batch * args.out_tokens * info.world / e2e_s
 
     gathered = all_gather_object({"ttft_hit": ttft_hit, "ttft_cold": ttft_cold, "restore_ms": restore_ms,
-                                  "rest_gbps": rest_gbps, "clocks": clocks, "ms": ms, "waves": wave_stats,
+                                  "rest_gbps": rest_gbps, "rest_remote": rest_gbps_remote, "clocks": clocks, "ms": ms, "waves": wave_stats,
                                   "hits": hits}, info)
     if info.rank == 0:
         all_hit = [x for g in gathered for x in g["ttft_hit"]]
         all_cold = [x for g in gathered for x in g["ttft_cold"]]
         gbps = [g["rest_gbps"] for g in gathered if g["rest_gbps"]]
+        gbps_r = [g["rest_remote"] for g in gathered if g["rest_remote"]]
         ck = gathered[0]["clocks"]
         reasons = sorted({r for g in gathered for r in (g["clocks"].get("reasons") or [])})
         res = {
@@ -336,7 +356,11 @@ def run_ours(args) -> None:
             "ttft_ms": {"hit_p50": pct(all_hit, 50), "hit_p99": pct(all_hit, 99), "cold_p50": pct(all_cold, 50),
                         "cold_p99": pct(all_cold, 99), "samples_hit": len(all_hit), "samples_cold": len(all_cold)},
             "restore_gbps": round(statistics.median(gbps), 1) if gbps else None,
-            "restore_gbps_note": "bf16 KV bytes written into the live cache per second, device-timed",
+            "restore_gbps_nvlink": round(statistics.median(gbps_r), 1) if gbps_r else None,
+            "restore_gbps_note": "bf16 KV bytes written into the live cache per second, device-timed; "
+                                 "restore_gbps = prefix owned by this GPU's shard, restore_gbps_nvlink = owned by "
+                                 "another GPU's shard (fused pull over NVLink + scatter)",
+            "pool_slots_per_shard": slots_per_shard,
             "wave_mix": gathered[0]["waves"], "amf_hits_rank0": gathered[0]["hits"],
             "clocks": {"sm_mhz": ck.get("sm_mhz"), "sm_max_mhz": ck.get("sm_max_mhz"), "reasons": reasons},
             "e2e": {"value": round(e2e_val, 2), "unit": "output tokens/s (whole job)",

@@ -1,0 +1,79 @@
+"""CPU end-to-end: BASELINE config 1 plumbing, engine restore equivalence, prefix cache
+registration of restored blocks, worker save/restore API and the block manager."""
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+sys.path.insert(0, str(Path(__file__).resolve().parents[1] / "examples"))
+
+from axropus_deploy_b200.amf import AmfManager, G1Pool  # noqa: E402
+from axropus_deploy_b200.engine import BlockManager, EngineConfig, LLMEngine, SamplingParams, block_hashes  # noqa: E402
+from axropus_deploy_b200.models.config import get_config  # noqa: E402
+from axropus_deploy_b200.models.llama import LlamaModel  # noqa: E402
+
+
+def test_config1_plumbing():
+    import config1_cpu_plumbing as c1
+
+    r = c1.run()
+    assert r["raw_bit_exact"] and r["disk_reload_bit_exact"] and r["disk_lookup"] == "hit"
+    assert r["fp8_max_abs_err"] < 0.25 and r["fp8_rel_err"] < 0.05
+    assert r["int4_max_abs_err"] < 0.6 and r["int4_rel_err"] < 0.12
+    assert r["fp8_bytes"] < 0.6 * r["raw_bytes"] and r["int4_bytes"] < 0.35 * r["raw_bytes"]
+
+
+@pytest.fixture(scope="module")
+def model():
+    return LlamaModel(get_config("tiny"), "cpu", seed=0)
+
+
+@pytest.mark.parametrize("fmt", ["raw", "fp8", "int4"])
+def test_restore_then_decode_equals_cold(model, fmt):
+    cfg = model.cfg
+    pool = G1Pool(cfg.num_layers, cfg.num_kv_heads, cfg.head_dim, fmt, slots_per_shard=64)
+    amf = AmfManager(raw_pool=pool if fmt == "raw" else None, comp_pool=pool if fmt != "raw" else None)
+    eng = LLMEngine(model, EngineConfig(num_blocks=160, max_model_len=1024), amf)
+    g = torch.Generator().manual_seed(1)
+    prefix = torch.randint(0, 32000, (512,), generator=g).tolist()
+    p1 = prefix + torch.randint(0, 32000, (20,), generator=g).tolist()
+    p2 = prefix + torch.randint(0, 32000, (33,), generator=g).tolist()
+    cold = eng.add_request(p1, SamplingParams(max_tokens=6), amf_prefix_len=512)
+    while eng.has_unfinished():
+        eng.step()
+    eng.evict_live_cache()
+    warm = eng.add_request(p1, SamplingParams(max_tokens=6), amf_prefix_len=512)
+    other = eng.add_request(p2, SamplingParams(max_tokens=6), amf_prefix_len=512)
+    while eng.has_unfinished():
+        eng.step()
+    assert cold.amf_tier == "cold" and warm.amf_tier.startswith("g1") and warm.restored_tokens == 512
+    assert other.amf_tier == "apc"  # restored blocks were registered and reused by the second request
+    assert warm.output == cold.output
+    st = eng.stats()
+    assert st["amf"]["captures"] == 1 and st["restored_tokens"] == 512
+
+
+def test_block_manager_prefix_cache():
+    bm = BlockManager(8)
+    toks = list(range(64))
+    hs = block_hashes(toks)
+    b = bm.allocate(4)
+    bm.register_computed(b, hs)
+    bm.release(b)
+    assert bm.stats()["cached"] == 4
+    got = bm.match_prefix(block_hashes(toks[:48] + [99] * 16))
+    assert got == b[:3]
+    bm.release(got)
+    assert bm.evict_cached(0.5) == 2
+    x = bm.allocate(8)
+    assert len(set(x)) == 8 and bm.num_free() == 0
+    with pytest.raises(MemoryError):
+        bm.allocate(1)
+
+
+def test_hashes_are_chained():
+    a = block_hashes(list(range(48)))
+    b = block_hashes([7] + list(range(1, 48)))
+    assert all(x != y for x, y in zip(a, b))  # a change in block 0 changes every later hash
