@@ -77,7 +77,8 @@ def test_memory_field_cadence():
     first = n.memory_field_update(st, {"now_ms": 0})
     a = n.memory_field_update(st, {"now_ms": 10, "max_bytes": 100, "bytes": 99})  # too soon: unchanged
     assert a == first
-    b = n.memory_field_update(st, {"now_ms": 20, "max_bytes": 100, "bytes": 99})  # 2 requests: updates
+    n.memory_field_update(st, {"now_ms": 20, "max_bytes": 100, "bytes": 99})
+    b = n.memory_field_update(st, {"now_ms": 30, "max_bytes": 100, "bytes": 99})  # after 2 skipped requests
     assert b["eviction_pressure"] > first["eviction_pressure"]
 
 
