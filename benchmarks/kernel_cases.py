@@ -1,0 +1,109 @@
+"""Small, self-contained cases of each hot kernel, for profiling one kernel at a time
+(e.g. under ncu with -k/-c). Sizes are chosen so inputs exceed the 126 MB L2 while the
+whole run stays within a few GB of device memory.
+
+    python benchmarks/kernel_cases.py decode|decode_int4|decode_fp8|restore|restore_fp8|capture_int4|
+                                      prefill|gemm|rmsnorm|rope
+"""
+import os
+import sys
+
+import torch
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+from axropus_deploy_b200 import ops  # noqa: E402
+from axropus_deploy_b200.amf.pool import PoolSlab  # noqa: E402
+from axropus_deploy_b200.ops import KVCache  # noqa: E402
+from axropus_deploy_b200.ops.gemm import gemm  # noqa: E402
+
+
+def decode(fmt="bf16"):
+    # Llama-3-8B attention geometry: 32 q heads / 8 kv heads, batch 32, 4096-token context
+    B, T = 32, 4096
+    pages = T // 16
+    cache = KVCache(1, B * pages, 8, 128, fmt, "cuda")
+    if fmt == "bf16":
+        cache.data.normal_()
+    else:
+        cache.data.random_(0, 255)
+        cache.meta.fill_(0.01)
+    bt = torch.randperm(B * pages, device="cuda").to(torch.int32).view(B, pages)
+    sl = torch.full((B,), T, dtype=torch.int32, device="cuda")
+    q = torch.randn(B, 32, 128, device="cuda").to(torch.bfloat16)
+    for _ in range(3):
+        ops.decode_attention(q, cache, 0, bt, sl, max_seq_len=T)
+
+
+def restore(pool_fmt="raw", cache_fmt="bf16"):
+    # one 8192-token prefix of a 32-layer / 8-kv-head model (1 GiB bf16): pool -> live cache
+    slab = PoolSlab(512, 32, 8, 128, pool_fmt, "cuda")
+    slab.slab.random_(0, 255)
+    if pool_fmt == "fp8":
+        for s in range(512):  # keep the per-page scales finite
+            slab.slab[s * slab.chunk + slab.data_region: s * slab.chunk + slab.data_region + slab.n_units * 4].view(
+                torch.float32).fill_(0.01)
+    cache = KVCache(32, 600, 8, 128, cache_fmt, "cuda")
+    src = torch.arange(512, dtype=torch.int32, device="cuda")
+    dst = torch.randperm(600, device="cuda")[:512].to(torch.int32)
+    for _ in range(3):
+        ops.page_transfer(slab, src, cache, dst)
+
+
+def capture(pool_fmt="int4"):
+    cache = KVCache(32, 600, 8, 128, "bf16", "cuda")
+    cache.data.normal_()
+    slab = PoolSlab(512, 32, 8, 128, pool_fmt, "cuda")
+    src = torch.randperm(600, device="cuda")[:512].to(torch.int32)
+    dst = torch.arange(512, dtype=torch.int32, device="cuda")
+    for _ in range(3):
+        ops.page_transfer(cache, src, slab, dst)
+
+
+def prefill():
+    T = 4096
+    cache = KVCache(1, T // 16, 8, 128, "bf16", "cuda")
+    cache.data.normal_()
+    bt = torch.arange(T // 16, dtype=torch.int32, device="cuda").view(1, -1)
+    cu = torch.tensor([0, T], dtype=torch.int32, device="cuda")
+    sl = torch.tensor([T], dtype=torch.int32, device="cuda")
+    q = torch.randn(T, 32, 128, device="cuda").to(torch.bfloat16)
+    for _ in range(3):
+        ops.prefill_attention(q, cache, 0, bt, cu, sl, T)
+
+
+def gemm_case():
+    a = torch.randn(8192, 4096, device="cuda").to(torch.bfloat16)
+    w = torch.randn(6144, 4096, device="cuda").to(torch.bfloat16)
+    for _ in range(3):
+        gemm(a, w)
+
+
+def rmsnorm():
+    x = torch.randn(32768, 4096, device="cuda").to(torch.bfloat16)
+    r = torch.randn_like(x)
+    w = torch.ones(4096, device="cuda").to(torch.bfloat16)
+    for _ in range(3):
+        ops.rmsnorm(x, w, 1e-5, residual=r)
+
+
+def rope():
+    T = 32768
+    qkv = torch.randn(T, 6144, device="cuda").to(torch.bfloat16)
+    cache = KVCache(1, T // 16, 8, 128, "bf16", "cuda")
+    pos = torch.arange(T, dtype=torch.int32, device="cuda")
+    cs = ops.rope_cos_sin(T, 128, 500000.0, None, "cuda")
+    for _ in range(3):
+        ops.rope_kv_write(qkv, pos, pos.clone(), cs, cache, 0, 32, 8)
+
+
+CASES = {"decode": lambda: decode("bf16"), "decode_int4": lambda: decode("int4"),
+         "decode_fp8": lambda: decode("fp8"), "restore": lambda: restore("raw", "bf16"),
+         "restore_fp8": lambda: restore("fp8", "bf16"), "capture_int4": lambda: capture("int4"),
+         "prefill": prefill, "gemm": gemm_case, "rmsnorm": rmsnorm, "rope": rope}
+
+if __name__ == "__main__":
+    for name in sys.argv[1:] or ["decode"]:
+        CASES[name]()
+    torch.cuda.synchronize()
+    print("ok", *sys.argv[1:])

@@ -25,6 +25,8 @@ void rope_kv_write(torch::Tensor qkv, torch::Tensor pos, torch::Tensor slots, to
 void silu_mul(torch::Tensor gate_up, torch::Tensor out);
 void argmax_rows(torch::Tensor logits, torch::Tensor out);
 void spec_verify(torch::Tensor logits, torch::Tensor draft, torch::Tensor out);
+void gemm_tc(torch::Tensor a, torch::Tensor b, torch::Tensor out, c10::optional<torch::Tensor> residual, double alpha,
+             torch::Tensor err);
 }  // namespace axr
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -38,4 +40,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("silu_mul", &axr::silu_mul);
   m.def("argmax_rows", &axr::argmax_rows);
   m.def("spec_verify", &axr::spec_verify);
+  m.def("gemm_tc", &axr::gemm_tc);
 }
