@@ -1,0 +1,130 @@
+"""Tensor parallelism with the collectives fused into tcgen05 GEMMs.
+
+:class:`TpGemm` owns the symmetric-memory buffers of the fused kernels
+(``csrc/kernels/gemm_tp.cu``) and launches them:
+
+* :meth:`ag_gemm` -- column-parallel layer: ``Y = AllGather_rows(X_shard) x W_shard^T``.
+  Each GPU passes its ``[rows, K]`` shard and gets ``[world*rows, N_shard]``; the
+  all-gather happens inside the GEMM kernel (peer row blocks pulled over NVLink
+  while local tiles are multiplied).
+* :meth:`gemm_rs` -- row-parallel layer: ``Y_shard = ReduceScatter_rows(A x W_shard^T)``.
+  Each GPU passes ``[world*rows, K_shard]`` and gets its ``[rows, N]`` slice of the
+  sum; partial tiles are pushed to their owner GPU from the GEMM epilogue.
+* :meth:`gemm` -- the same persistent kernel without communication.
+
+The NCCL + cuBLAS composition of the same layers (``all_gather_into_tensor`` +
+``matmul``, ``matmul`` + ``reduce_scatter_tensor``) is kept as :func:`ag_gemm_nccl` /
+:func:`gemm_rs_nccl`: it is the baseline the fused kernels are measured against.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from ..ops._ext import cuda_ext
+from ..ops.gemm import error_flag
+from .dist import DistInfo
+
+MODE_PLAIN, MODE_AG, MODE_RS = 0, 1, 2
+TILE_M = 128
+
+
+def _symm(n: int, dtype: torch.dtype, info: DistInfo):
+    if info.world == 1:
+        t = torch.zeros(n, dtype=dtype, device=info.device)
+        return t, [t.data_ptr()]
+    import torch.distributed._symmetric_memory as symm
+
+    t = symm.empty(n, dtype=dtype, device=info.device)
+    t.zero_()
+    h = symm.rendezvous(t, dist.group.WORLD)
+    _KEEP.append((t, h))
+    return t, [int(p) for p in h.buffer_ptrs]
+
+
+_KEEP: list = []
+
+
+class TpGemm:
+    def __init__(self, info: DistInfo, max_rows_per_rank: int, k_ag: int, n_rs: int):
+        if max_rows_per_rank % TILE_M:
+            raise ValueError("rows per rank must be a multiple of 128")
+        self.info = info
+        self.world, self.rank = info.world, info.rank
+        self.max_rpr = max_rows_per_rank
+        self.k_ag, self.n_rs = k_ag, n_rs
+        dev = info.device
+        W, R = self.world, max_rows_per_rank
+        self.staging, self.staging_ptrs = [], []
+        for _ in range(2):
+            t, ptrs = _symm(W * R * k_ag, torch.bfloat16, info)
+            self.staging.append(t)
+            self.staging_ptrs.append(ptrs)
+        self.ready, ready_ptrs = _symm(W, torch.int32, info)
+        self.recv, recv_ptrs = _symm(2 * W * R * n_rs, torch.bfloat16, info)
+        self.cnt, cnt_ptrs = _symm(2 * (R // TILE_M), torch.int32, info)
+        self.block_flag = torch.zeros(W * R // TILE_M, dtype=torch.int32, device=dev)
+        i64 = dict(dtype=torch.int64, device=dev)
+        self.peer_ready = torch.tensor(ready_ptrs, **i64)
+        self.peer_recv = torch.tensor(recv_ptrs, **i64)
+        self.peer_cnt = torch.tensor(cnt_ptrs, **i64)
+        self._staging_ptr_t = [torch.tensor(p, **i64) for p in self.staging_ptrs]
+        self.ag_epoch = 0
+        self.rs_epoch = 0
+        self.err = error_flag(dev)
+
+    # ------------------------------------------------------------------ fused ops
+    def ag_gemm(self, x_shard: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        rows, K = x_shard.shape
+        if K != self.k_ag or rows > self.max_rpr or rows % TILE_M:
+            raise ValueError(f"ag_gemm: shard {tuple(x_shard.shape)} does not fit the communicator")
+        W = self.world
+        self.ag_epoch += 1
+        par = self.ag_epoch & 1
+        st = self.staging[par][: W * rows * K].view(W * rows, K)
+        st[self.rank * rows:(self.rank + 1) * rows].copy_(x_shard)
+        peer_a = self._staging_ptr_t[par] + torch.arange(W, device=st.device, dtype=torch.int64) * (rows * K * 2)
+        if out is None:
+            out = torch.empty(W * rows, w.shape[0], dtype=torch.bfloat16, device=st.device)
+        cuda_ext().gemm_tp(x_shard, w, out, MODE_AG, self.rank, W, rows, self.ag_epoch, peer_a, st,
+                           self.block_flag, self.ready, self.peer_ready, None, None, None, None, self.err)
+        return out
+
+    def gemm_rs(self, a: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        M, K = a.shape
+        N = w.shape[0]
+        W = self.world
+        rows = M // W
+        if M % W or rows > self.max_rpr or rows % TILE_M or N != self.n_rs:
+            raise ValueError(f"gemm_rs: input {tuple(a.shape)} x {tuple(w.shape)} does not fit the communicator")
+        self.rs_epoch += 1
+        if out is None:
+            out = torch.empty(rows, N, dtype=torch.bfloat16, device=a.device)
+        recv = self.recv[: 2 * W * rows * N]
+        cuda_ext().gemm_tp(a, w, out, MODE_RS, self.rank, W, rows, self.rs_epoch, None, None, None, None, None,
+                           self.peer_recv, self.peer_cnt, recv, self.cnt, self.err)
+        return out
+
+    @staticmethod
+    def gemm(a: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if out is None:
+            out = torch.empty(a.shape[0], w.shape[0], dtype=torch.bfloat16, device=a.device)
+        cuda_ext().gemm_tp(a, w, out, MODE_PLAIN, 0, 1, a.shape[0], 0, None, None, None, None, None, None, None,
+                           None, None, error_flag(a.device))
+        return out
+
+
+# ---------------------------------------------------------------------- NCCL baselines
+def ag_gemm_nccl(x_shard: torch.Tensor, w: torch.Tensor, world: int) -> torch.Tensor:
+    full = torch.empty(world * x_shard.shape[0], x_shard.shape[1], dtype=x_shard.dtype, device=x_shard.device)
+    dist.all_gather_into_tensor(full, x_shard)
+    return full @ w.t()
+
+
+def gemm_rs_nccl(a: torch.Tensor, w: torch.Tensor, world: int) -> torch.Tensor:
+    part = a @ w.t()
+    out = torch.empty(a.shape[0] // world, w.shape[0], dtype=part.dtype, device=a.device)
+    dist.reduce_scatter_tensor(out, part)
+    return out

@@ -27,6 +27,12 @@ void argmax_rows(torch::Tensor logits, torch::Tensor out);
 void spec_verify(torch::Tensor logits, torch::Tensor draft, torch::Tensor out);
 void gemm_tc(torch::Tensor a, torch::Tensor b, torch::Tensor out, c10::optional<torch::Tensor> residual, double alpha,
              torch::Tensor err);
+void gemm_tp(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t mode, int64_t rank, int64_t world,
+             int64_t rows_per_rank, int64_t epoch, c10::optional<torch::Tensor> peer_a,
+             c10::optional<torch::Tensor> staging, c10::optional<torch::Tensor> block_flag,
+             c10::optional<torch::Tensor> ready, c10::optional<torch::Tensor> peer_ready,
+             c10::optional<torch::Tensor> peer_recv, c10::optional<torch::Tensor> peer_cnt,
+             c10::optional<torch::Tensor> recv, c10::optional<torch::Tensor> cnt, torch::Tensor err);
 }  // namespace axr
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -41,4 +47,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("argmax_rows", &axr::argmax_rows);
   m.def("spec_verify", &axr::spec_verify);
   m.def("gemm_tc", &axr::gemm_tc);
+  m.def("gemm_tp", &axr::gemm_tp);
 }

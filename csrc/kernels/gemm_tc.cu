@@ -89,17 +89,19 @@ __global__ void __launch_bounds__(128, 1) gemm_tc_kernel(const __grid_constant__
       }
       __threadfence();
     }
+    int issued = 0;
     for (int kt = 0; ok && kt < num_k; ++kt) {
       const int s = kt % GSTAGES;
       if (kt >= GSTAGES && !tc::mbar_wait(&empty[s], ((kt / GSTAGES) + 1) & 1, g.err, 1)) { ok = false; break; }
       tc::mbar_arrive_expect_tx(&full[s], GA_BYTES + GB_BYTES);
       tc::tma_load_2d(sA + s * GA_BYTES, &tmA, kt * GBK, m0, &full[s]);
       tc::tma_load_2d(sB + s * GB_BYTES, &tmB, kt * GBK, n0, &full[s]);
+      issued = kt + 1;
     }
     if (!ok) {
-      // let the last issued loads land before the CTA can exit
-      for (int kt = max(0, num_k - GSTAGES); kt < num_k; ++kt)
-        tc::mbar_wait(&full[kt % GSTAGES], (kt / GSTAGES) & 1, g.err, 1);
+      // let the loads this thread issued land before the CTA can exit
+      for (int kt = max(0, issued - GSTAGES); kt < issued; ++kt)
+        tc::mbar_wait_quiet(&full[kt % GSTAGES], (kt / GSTAGES) & 1);
     }
   } else if (warp == 1 && lane == 0) {
     // ---------------- MMA issuer
@@ -118,8 +120,8 @@ __global__ void __launch_bounds__(128, 1) gemm_tc_kernel(const __grid_constant__
       }
       tc::mma_commit(&empty[s]);
     }
-    (void)ok;
     tc::mma_commit(acc_ready);  // arrives once every MMA above has completed
+    if (!ok) tc::mbar_wait_quiet(acc_ready, 0);  // the epilogue may have given up: drain before TMEM is freed
   }
   __syncwarp();
 

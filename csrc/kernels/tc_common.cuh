@@ -71,6 +71,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, volatil
   }
 }
 
+// Bounded wait that ignores the error flag: used on the way out of a failed kernel to
+// let this CTA's own TMA writes / MMAs land before shared memory and TMEM are released.
+__device__ __forceinline__ bool mbar_wait_quiet(uint64_t* bar, uint32_t phase) {
+  const unsigned long long t0 = globaltimer();
+  while (!mbar_try_wait(bar, phase)) {
+    if (globaltimer() - t0 > kWaitLimitNs) return false;
+  }
+  return true;
+}
+
 // 2D tiled TMA load into shared memory, completion signalled on `bar` (no multicast).
 __device__ __forceinline__ void tma_load_2d(void* smem, const CUtensorMap* map, int x, int y, uint64_t* bar) {
   asm volatile(
