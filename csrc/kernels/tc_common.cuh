@@ -4,7 +4,7 @@
 // on an mbarrier is bounded by %globaltimer: on timeout the waiter records an error
 // code in a caller-provided flag and the kernel winds down (waits for its own TMA
 // traffic with another bounded wait, frees its TMEM and returns) instead of spinning
-// forever. No TMA load in this framework uses .multicast::cluster.
+// forever. Every TMA load here is a plain per-CTA load into its own shared memory.
 #pragma once
 
 #include <cuda.h>
