@@ -52,7 +52,7 @@ class DecodeGraphRunner:
         # pre-size the split scratch for the largest bucket so every graph shares it
         from ..ops import attention as att
 
-        D, Hq = eng.model.cfg.head_dim, eng.model.cfg.num_heads
+        D, Hq = eng.model.cfg.head_dim, getattr(eng.model, "hq", eng.model.cfg.num_heads)
         self.ws.get(self.max_b, Hq, max(self.splits[b], 64), D, eng.device)
         prev = att._WS
         att._WS = self.ws

@@ -97,7 +97,9 @@ class LLMEngine:
         self.amf = amf
         mc = model.cfg
         self.device = model.device
-        self.cache = KVCache(model.num_layers, cfg.num_blocks, mc.num_kv_heads, mc.head_dim, cfg.kv_fmt, self.device)
+        kv_heads = getattr(model, "cache_kv_heads", mc.num_kv_heads)  # tensor parallel: this GPU's heads
+        self.cache = KVCache(model.num_layers, cfg.num_blocks, kv_heads, mc.head_dim, cfg.kv_fmt, self.device)
+        self._agree = getattr(model, "agree_min", None)
         self.bm = BlockManager(cfg.num_blocks, cfg.enable_prefix_cache)
         self.max_blocks_per_seq = (cfg.max_model_len + PAGE - 1) // PAGE
         self.block_table = torch.zeros(cfg.max_batch, self.max_blocks_per_seq, dtype=torch.int32, device=self.device)
@@ -188,6 +190,11 @@ class LLMEngine:
             hit: Optional[AmfHit] = None
             if self.amf is not None and n_local * PAGE < limit:
                 hit = self.amf.lookup(r.prompt_np, limit)
+                if self._agree is not None:
+                    # tensor parallel: every rank restores the same pages (the shortest hit)
+                    n = self._agree(hit.n_pages if hit is not None else 0)
+                    if hit is not None and n < hit.n_pages:
+                        hit.n_tokens = n * PAGE
                 if hit is not None and hit.n_pages <= n_local:
                     hit.release()
                     hit = None

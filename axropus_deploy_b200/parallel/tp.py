@@ -29,6 +29,7 @@ from .dist import DistInfo
 
 MODE_PLAIN, MODE_AG, MODE_RS = 0, 1, 2
 TILE_M = 128
+AG_CHUNKS = 8  # a remote 128-row block is pulled as 8 independently flagged chunks
 
 
 def _symm(n: int, dtype: torch.dtype, info: DistInfo):
@@ -55,6 +56,11 @@ class TpGemm:
         self.world, self.rank = info.world, info.rank
         self.max_rpr = max_rows_per_rank
         self.k_ag, self.n_rs = k_ag, n_rs
+        self.ag_epoch = 0
+        self.rs_epoch = 0
+        self.on_gpu = info.device.type == "cuda"
+        if not self.on_gpu:
+            return  # CPU ranks (gloo): the same layers composed from host collectives
         dev = info.device
         W, R = self.world, max_rows_per_rank
         self.staging, self.staging_ptrs = [], []
@@ -65,14 +71,14 @@ class TpGemm:
         self.ready, ready_ptrs = _symm(W, torch.int32, info)
         self.recv, recv_ptrs = _symm(2 * W * R * n_rs, torch.bfloat16, info)
         self.cnt, cnt_ptrs = _symm(2 * (R // TILE_M), torch.int32, info)
-        self.block_flag = torch.zeros(W * R // TILE_M, dtype=torch.int32, device=dev)
+        self.ag_flags = torch.zeros(W * R // TILE_M * AG_CHUNKS, dtype=torch.int32, device=dev)
+        self.rs_done = torch.zeros(2 * (R // TILE_M), dtype=torch.int32, device=dev)
         i64 = dict(dtype=torch.int64, device=dev)
         self.peer_ready = torch.tensor(ready_ptrs, **i64)
         self.peer_recv = torch.tensor(recv_ptrs, **i64)
         self.peer_cnt = torch.tensor(cnt_ptrs, **i64)
         self._staging_ptr_t = [torch.tensor(p, **i64) for p in self.staging_ptrs]
-        self.ag_epoch = 0
-        self.rs_epoch = 0
+        self._shard_offsets = torch.arange(W, dtype=torch.int64, device=dev)
         self.err = error_flag(dev)
 
     # ------------------------------------------------------------------ fused ops
@@ -81,15 +87,17 @@ class TpGemm:
         if K != self.k_ag or rows > self.max_rpr or rows % TILE_M:
             raise ValueError(f"ag_gemm: shard {tuple(x_shard.shape)} does not fit the communicator")
         W = self.world
+        if not self.on_gpu:
+            return _ag_gemm_host(x_shard, w, W, out)
         self.ag_epoch += 1
         par = self.ag_epoch & 1
         st = self.staging[par][: W * rows * K].view(W * rows, K)
         st[self.rank * rows:(self.rank + 1) * rows].copy_(x_shard)
-        peer_a = self._staging_ptr_t[par] + torch.arange(W, device=st.device, dtype=torch.int64) * (rows * K * 2)
+        peer_a = self._staging_ptr_t[par] + self._shard_offsets * (rows * K * 2)
         if out is None:
             out = torch.empty(W * rows, w.shape[0], dtype=torch.bfloat16, device=st.device)
         cuda_ext().gemm_tp(x_shard, w, out, MODE_AG, self.rank, W, rows, self.ag_epoch, peer_a, st,
-                           self.block_flag, self.ready, self.peer_ready, None, None, None, None, self.err)
+                           self.ag_flags, self.ready, self.peer_ready, None, None, None, None, self.err)
         return out
 
     def gemm_rs(self, a: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
@@ -99,12 +107,14 @@ class TpGemm:
         rows = M // W
         if M % W or rows > self.max_rpr or rows % TILE_M or N != self.n_rs:
             raise ValueError(f"gemm_rs: input {tuple(a.shape)} x {tuple(w.shape)} does not fit the communicator")
+        if not self.on_gpu:
+            return _gemm_rs_host(a, w, W, self.rank, out)
         self.rs_epoch += 1
         if out is None:
             out = torch.empty(rows, N, dtype=torch.bfloat16, device=a.device)
         recv = self.recv[: 2 * W * rows * N]
-        cuda_ext().gemm_tp(a, w, out, MODE_RS, self.rank, W, rows, self.rs_epoch, None, None, None, None, None,
-                           self.peer_recv, self.peer_cnt, recv, self.cnt, self.err)
+        cuda_ext().gemm_tp(a, w, out, MODE_RS, self.rank, W, rows, self.rs_epoch, None, None, self.rs_done, None,
+                           None, self.peer_recv, self.peer_cnt, recv, self.cnt, self.err)
         return out
 
     @staticmethod
@@ -114,6 +124,28 @@ class TpGemm:
         cuda_ext().gemm_tp(a, w, out, MODE_PLAIN, 0, 1, a.shape[0], 0, None, None, None, None, None, None, None,
                            None, None, error_flag(a.device))
         return out
+
+
+def _ag_gemm_host(x_shard, w, world, out=None):
+    parts = [torch.empty_like(x_shard) for _ in range(world)]
+    dist.all_gather(parts, x_shard.contiguous())
+    y = (torch.cat(parts).float() @ w.float().t()).to(x_shard.dtype)
+    if out is not None:
+        out.copy_(y)
+        return out
+    return y
+
+
+def _gemm_rs_host(a, w, world, rank, out=None):
+    part = (a.float() @ w.float().t()).to(a.dtype)  # each partial rounded like the fused kernel's
+    part = part.float()
+    dist.all_reduce(part)
+    rows = a.shape[0] // world
+    y = part[rank * rows:(rank + 1) * rows].to(a.dtype)
+    if out is not None:
+        out.copy_(y)
+        return out
+    return y
 
 
 # ---------------------------------------------------------------------- NCCL baselines

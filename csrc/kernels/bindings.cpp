@@ -29,7 +29,7 @@ void gemm_tc(torch::Tensor a, torch::Tensor b, torch::Tensor out, c10::optional<
              torch::Tensor err);
 void gemm_tp(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t mode, int64_t rank, int64_t world,
              int64_t rows_per_rank, int64_t epoch, c10::optional<torch::Tensor> peer_a,
-             c10::optional<torch::Tensor> staging, c10::optional<torch::Tensor> block_flag,
+             c10::optional<torch::Tensor> staging, c10::optional<torch::Tensor> flags,
              c10::optional<torch::Tensor> ready, c10::optional<torch::Tensor> peer_ready,
              c10::optional<torch::Tensor> peer_recv, c10::optional<torch::Tensor> peer_cnt,
              c10::optional<torch::Tensor> recv, c10::optional<torch::Tensor> cnt, torch::Tensor err);

@@ -36,7 +36,12 @@ namespace axr {
 
 constexpr int TBM = 128, TBN = 256, TBK = 64, TST = 4;
 constexpr int TA_BYTES = TBM * TBK * 2, TB_BYTES = TBN * TBK * 2;
-constexpr int TSMEM = 1024 + TST * (TA_BYTES + TB_BYTES) + 256;
+constexpr int EPI_COLS = 64;                      // epilogue staging width (columns per pass)
+constexpr int STG_BYTES = 4 * 32 * EPI_COLS * 2;  // one [32 x 64] bf16 tile per epilogue warp
+constexpr int TSMEM = 1024 + TST * (TA_BYTES + TB_BYTES) + STG_BYTES + 256;
+constexpr int TP_THREADS = 320;
+constexpr int AG_CH = 8;   // a remote 128-row block is pulled as 8 chunks of 16 rows
+constexpr int RS_CH = 16;  // an owned 128-row block is reduced as 16 chunks of 8 rows
 constexpr int MODE_PLAIN = 0, MODE_AG = 1, MODE_RS = 2;
 
 struct TpArgs {
@@ -49,7 +54,7 @@ struct TpArgs {
   // AG
   const int64_t* peer_a;  // [world] base addresses of the peers' A shards [rows_per_rank, K]
   __nv_bfloat16* staging;   // local [M, K]; the TMA map of A covers it
-  int* block_flag;          // local [M / 128]: epoch when the block is in staging
+  int* flags;               // AG: [M/128][AG_CH] epoch of each pulled chunk; RS: [rows/128][2] chunks reduced
   int* ready;               // local [world]: epoch when peer p's shard is ready
   const int64_t* peer_ready;  // [world] addresses of each peer's `ready` array
   // RS
@@ -81,7 +86,7 @@ __device__ __forceinline__ void red_add_release_sys(int* p, int v) {
   asm volatile("red.release.sys.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 __device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
-__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+__device__ __forceinline__ void comm_bar() { asm volatile("bar.sync 2, 128;" ::: "memory"); }
 
 // bounded wait until *p >= target
 template <bool SYS>
@@ -97,18 +102,61 @@ __device__ __forceinline__ bool wait_geq(const int* p, int target, volatile int*
   return true;
 }
 
-__global__ void __launch_bounds__(192, 1) gemm_tp_kernel(const __grid_constant__ CUtensorMap tmA,
-                                                         const __grid_constant__ CUtensorMap tmB, TpArgs g) {
+// Thread 0 of the comm warps waits; the outcome reaches all 128 comm threads through
+// shared memory and the barrier, so the four warps always take the same branch.
+__device__ __forceinline__ bool comm_wait(const int* p, int target, volatile int* err, int code, int ct,
+                                          volatile int* shared_ok) {
+  if (ct == 0) *shared_ok = wait_geq<true>(p, target, err, code) ? 1 : 0;
+  comm_bar();
+  const bool ok = *shared_ok != 0;
+  comm_bar();  // nobody overwrites shared_ok before everyone has read it
+  return ok;
+}
+
+// Tile t -> (m-block, n-block). Tiles run in groups of GROUP_M row blocks with the row
+// block varying fastest inside a group, so the CTAs in flight share both their A rows and
+// their B columns through L2 (B is streamed from HBM about M / (128 * GROUP_M) times).
+// The row-block ordinal o maps to a row block per mode. AG: this GPU's own row blocks
+// first, then the remote ones in the order they are pulled. RS: every GPU walks the row
+// blocks in the same interleaved order (block j of owner 0, of owner 1, ...), so block j
+// of every owner completes at about the same time and its reduction overlaps the GEMM of
+// the blocks after it.
+constexpr int GROUP_M = 16;
+__device__ __forceinline__ void tp_tile(const TpArgs& g, int t, int num_n, int num_m, int first_m, int& mt,
+                                        int& nt) {
+  const int group = GROUP_M * num_n;
+  const int first_o = (t / group) * GROUP_M;
+  const int gm = min(num_m - first_o, GROUP_M);
+  const int in = t - (t / group) * group;
+  const int o = first_o + in % gm;
+  nt = in / gm;
+  if (g.mode == MODE_AG) {
+    mt = (o + first_m) % num_m;
+  } else if (g.mode == MODE_RS) {
+    const int lblocks = g.rows_per_rank / TBM;
+    mt = (o % g.world) * lblocks + o / g.world;
+  } else {
+    mt = o;
+  }
+}
+
+// Roles (320 threads): warp 0 TMA producer, warp 1 MMA issuer (and TMEM owner: warp 2),
+// warps 2-5 epilogue (TMEM lane group = warp % 4), warps 6-9 communication (AG pulls of
+// peer rows, RS reduction of the partial tiles received).
+__global__ void __launch_bounds__(TP_THREADS, 1) gemm_tp_kernel(const __grid_constant__ CUtensorMap tmA,
+                                                                const __grid_constant__ CUtensorMap tmB, TpArgs g) {
   extern __shared__ __align__(1024) char tsm_raw[];
   char* base = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(tsm_raw) + 1023) & ~uintptr_t(1023));
   char* sA = base;
   char* sB = base + TST * TA_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + TST * TB_BYTES);
+  char* stg = sB + TST * TB_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(stg + STG_BYTES);
   uint64_t* empty = full + TST;
   uint64_t* accf = empty + TST;  // [2]
   uint64_t* acce = accf + 2;     // [2]
   uint64_t* drain = acce + 2;    // MMA completion on the way out
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* comm_ok = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_m = (g.M + TBM - 1) / TBM, num_n = (g.N + TBN - 1) / TBN;
@@ -144,21 +192,17 @@ __global__ void __launch_bounds__(192, 1) gemm_tp_kernel(const __grid_constant__
   tc::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  auto tile_mn = [&](int t, int& mt, int& nt) {
-    nt = t % num_n;
-    mt = (t / num_n + first_m) % num_m;
-  };
-
   if (warp == 0) {
     if (lane == 0) {  // ---------------- TMA producer
       int it = 0;
       bool ok = true;
       for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
         int mt, nt;
-        tile_mn(t, mt, nt);
+        tp_tile(g, t, num_n, num_m, first_m, mt, nt);
         if (g.mode == MODE_AG && (mt * TBM) / g.rows_per_rank != g.rank) {
-          if (!wait_geq<false>(g.block_flag + mt, g.epoch, g.err, 5)) { ok = false; break; }
-          fence_proxy_async_global();
+          for (int ch = 0; ok && ch < AG_CH; ++ch) ok = wait_geq<false>(g.flags + mt * AG_CH + ch, g.epoch, g.err, 5);
+          if (!ok) break;
+          fence_proxy_async_global();  // order the TMA reads after the pulled rows
         }
         for (int kt = 0; kt < num_k; ++kt, ++it) {
           const int s = it % TST;
@@ -198,109 +242,162 @@ __global__ void __launch_bounds__(192, 1) gemm_tp_kernel(const __grid_constant__
       tc::mma_commit(drain);
       tc::mbar_wait_quiet(drain, 0);  // every MMA of this CTA has completed
     }
-  } else {
-    // ---------------- epilogue warps 2..5 (128 threads)
-    const int et = threadIdx.x - 64;  // 0..127
-    const int lg = warp & 3;          // TMEM lane group this warp may access
-    if (g.mode == MODE_AG) {
-      // pull the remote row blocks assigned to this CTA
-      const int blocks = g.M / TBM;
-      for (int b = blockIdx.x; b < blocks; b += gridDim.x) {
-        const int p = (b * TBM) / g.rows_per_rank;
-        if (p == g.rank) continue;
-        if (!wait_geq<true>(g.ready + p, g.epoch, g.err, 7)) break;
-        const int r0 = b * TBM - p * g.rows_per_rank;
-        const char* src = reinterpret_cast<const char*>(g.peer_a[p]) + (long long)r0 * g.K * 2;
-        char* dst = reinterpret_cast<char*>(g.staging) + (long long)b * TBM * g.K * 2;
-        const long long vecs = (long long)TBM * g.K / 8;
-        for (long long v = et; v < vecs; v += 128) {
-          const uint4 x = ld_v4(src + v * 16);  // plain load from the peer over NVLink
-          *reinterpret_cast<uint4*>(dst + v * 16) = x;
-        }
-        fence_proxy_async_global();  // make the generic-proxy writes visible to TMA reads
-        __threadfence();
-        epi_bar();
-        if (et == 0) st_release_gpu(g.block_flag + b, g.epoch);
-      }
-    }
+  } else if (warp < 6) {
+    // ---------------- epilogue warps 2..5: TMEM -> registers -> bf16 -> shared staging -> coalesced stores
+    const int lg = warp & 3;  // TMEM lane group this warp may access
+    char* my_stg = stg + (warp - 2) * (32 * EPI_COLS * 2);
+    const bool vec_ok = g.mode == MODE_RS || (g.ldc & 7) == 0;
     int i = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
       int mt, nt;
-      tile_mn(t, mt, nt);
+      tp_tile(g, t, num_n, num_m, first_m, mt, nt);
       const int buf = i & 1;
       bool ok = tc::mbar_wait(&accf[buf], (i >> 1) & 1, g.err, 3);
       ok = __all_sync(0xffffffffu, ok) && __shfl_sync(0xffffffffu, *g.err, 0) == 0;
       tc::tc_fence_after();
       if (!ok) break;
-      const int row = mt * TBM + lg * 32 + lane;
-      __nv_bfloat16* dst_row = nullptr;
-      if (row < g.M) {
-        if (g.mode == MODE_RS) {
-          const int owner = row / g.rows_per_rank, lr = row % g.rows_per_rank;
-          __nv_bfloat16* recv = reinterpret_cast<__nv_bfloat16*>(g.peer_recv[owner]);
-          dst_row = recv + (((long long)parity * g.world + g.rank) * g.rows_per_rank + lr) * g.N;
-        } else {
-          dst_row = g.c + (long long)row * g.ldc;
-        }
-      }
 #pragma unroll 1
-      for (int c = 0; c < TBN / 16; ++c) {
-        uint32_t r[16];
-        tc::tmem_ld16(tmem + buf * TBN + (static_cast<uint32_t>(lg * 32) << 16) + c * 16, r);
+      for (int cg = 0; cg < TBN / EPI_COLS; ++cg) {
+        uint32_t r[4][16];
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          tc::tmem_ld16(tmem + buf * TBN + (static_cast<uint32_t>(lg * 32) << 16) + cg * EPI_COLS + c * 16, r[c]);
         tc::tmem_ld_wait();
-        const int col = nt * TBN + c * 16;
-        if (dst_row != nullptr && col < g.N) {
-          __nv_bfloat16* cp = dst_row + col;
-          if (col + 16 <= g.N) {
-            uint4 o0 = make_uint4(pack_bf16x2(__uint_as_float(r[0]), __uint_as_float(r[1])),
-                                  pack_bf16x2(__uint_as_float(r[2]), __uint_as_float(r[3])),
-                                  pack_bf16x2(__uint_as_float(r[4]), __uint_as_float(r[5])),
-                                  pack_bf16x2(__uint_as_float(r[6]), __uint_as_float(r[7])));
-            uint4 o1 = make_uint4(pack_bf16x2(__uint_as_float(r[8]), __uint_as_float(r[9])),
-                                  pack_bf16x2(__uint_as_float(r[10]), __uint_as_float(r[11])),
-                                  pack_bf16x2(__uint_as_float(r[12]), __uint_as_float(r[13])),
-                                  pack_bf16x2(__uint_as_float(r[14]), __uint_as_float(r[15])));
-            reinterpret_cast<uint4*>(cp)[0] = o0;  // local, or a peer's receive slot (NVLink)
-            reinterpret_cast<uint4*>(cp)[1] = o1;
-          } else {
-            for (int j = 0; j < 16 && col + j < g.N; ++j) cp[j] = __float2bfloat16(__uint_as_float(r[j]));
+        if (cg == TBN / EPI_COLS - 1) {  // accumulator buffer fully read: hand it back to the MMA warp
+          tc::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) tc::mbar_arrive(&acce[buf]);
+        }
+        // this lane's row -> staging, 16-byte granules XOR-swizzled by row to avoid bank conflicts
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const uint32_t* v = &r[c][h * 8];
+            const uint4 o = make_uint4(pack_bf16x2(__uint_as_float(v[0]), __uint_as_float(v[1])),
+                                       pack_bf16x2(__uint_as_float(v[2]), __uint_as_float(v[3])),
+                                       pack_bf16x2(__uint_as_float(v[4]), __uint_as_float(v[5])),
+                                       pack_bf16x2(__uint_as_float(v[6]), __uint_as_float(v[7])));
+            const int gidx = (c * 2 + h) ^ (lane & 7);
+            *reinterpret_cast<uint4*>(my_stg + lane * 128 + gidx * 16) = o;
           }
         }
+        __syncwarp();
+        // 32 rows x 128 bytes: 8 lanes write one row's 128 contiguous bytes
+#pragma unroll
+        for (int it2 = 0; it2 < 8; ++it2) {
+          const int rr = it2 * 4 + (lane >> 3), gq = lane & 7;
+          const uint4 v = *reinterpret_cast<const uint4*>(my_stg + rr * 128 + ((gq ^ (rr & 7)) * 16));
+          const int row = mt * TBM + lg * 32 + rr;
+          const int col = nt * TBN + cg * EPI_COLS + gq * 8;
+          if (row < g.M && col < g.N) {
+            __nv_bfloat16* dst;
+            if (g.mode == MODE_RS) {
+              const int owner = row / g.rows_per_rank, lr = row - owner * g.rows_per_rank;
+              dst = reinterpret_cast<__nv_bfloat16*>(g.peer_recv[owner]) +
+                    (((long long)parity * g.world + g.rank) * g.rows_per_rank + lr) * g.N + col;
+            } else {
+              dst = g.c + (long long)row * g.ldc + col;
+            }
+            if (vec_ok && col + 8 <= g.N) {
+              *reinterpret_cast<uint4*>(dst) = v;  // local, or a peer's receive slot (NVLink)
+            } else {
+              const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&v);
+              for (int j = 0; j < 8 && col + j < g.N; ++j) dst[j] = e[j];
+            }
+          }
+        }
+        __syncwarp();
       }
-      tc::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&acce[buf]);
       if (g.mode == MODE_RS) {
+        // this warp's 32 rows of the partial tile are out: count them at the owner
         __threadfence_system();
-        epi_bar();
-        if (et == 0) {
+        __syncwarp();
+        if (lane == 0) {
           const int owner = (mt * TBM) / g.rows_per_rank, lb = (mt * TBM - owner * g.rows_per_rank) / TBM;
           red_add_release_sys(reinterpret_cast<int*>(g.peer_cnt[owner]) + 2 * lb + parity, 1);
         }
       }
     }
-    if (g.mode == MODE_RS) {
-      // reduce this GPU's row blocks once all partial tiles have arrived
-      const int lblocks = g.rows_per_rank / TBM;
-      const int target = g.world * num_n;
-      for (int lb = blockIdx.x; lb < lblocks; lb += gridDim.x) {
-        if (!wait_geq<true>(g.cnt + 2 * lb + parity, target, g.err, 8)) break;
-        const long long vecs = (long long)TBM * g.N / 8;
-        for (long long v = et; v < vecs; v += 128) {
-          const long long e = (long long)lb * TBM * g.N + v * 8;
-          float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-          for (int p = 0; p < g.world; ++p) {
-            const uint4 x = *reinterpret_cast<const uint4*>(
-                g.recv + ((long long)parity * g.world + p) * g.rows_per_rank * g.N + e);
-            acc[0] += bf16_lo(x.x); acc[1] += bf16_hi(x.x); acc[2] += bf16_lo(x.y); acc[3] += bf16_hi(x.y);
-            acc[4] += bf16_lo(x.z); acc[5] += bf16_hi(x.z); acc[6] += bf16_lo(x.w); acc[7] += bf16_hi(x.w);
-          }
-          *reinterpret_cast<uint4*>(g.out_rs + e) =
-              make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]), pack_bf16x2(acc[4], acc[5]),
-                         pack_bf16x2(acc[6], acc[7]));
+  } else {
+    // ---------------- communication warps 6..9 (128 threads)
+    const int ct = threadIdx.x - 192;
+    if (g.mode == MODE_AG) {
+      // pull remote 16-row chunks, in the order the tiles consume them
+      const int nb = g.M / TBM, lbk = g.rows_per_rank / TBM;
+      const int items = (nb - lbk) * AG_CH;
+      const long long vecs = 16LL * g.K / 8;  // 16-byte vectors per chunk (16 rows x K)
+      for (int item = blockIdx.x; item < items; item += gridDim.x) {
+        const int b = (first_m + lbk + item / AG_CH) % nb, ch = item % AG_CH;
+        const int p = (b * TBM) / g.rows_per_rank;
+        if (!comm_wait(g.ready + p, g.epoch, g.err, 7, ct, comm_ok)) break;
+        const long long r0 = (long long)b * TBM - (long long)p * g.rows_per_rank + ch * 16;
+        const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(g.peer_a[p]) + r0 * g.K * 2);
+        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<char*>(g.staging) +
+                                              ((long long)b * TBM + ch * 16) * g.K * 2);
+        for (long long v = ct; v < vecs; v += 128 * 8) {
+          uint4 x[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            if (v + u * 128 < vecs) x[u] = src[v + u * 128];  // peer memory over NVLink, 8 loads in flight
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            if (v + u * 128 < vecs) dst[v + u * 128] = x[u];
         }
-        epi_bar();  // every thread is done with this block's receive slots
-        if (et == 0) red_add_release_sys(g.cnt + 2 * lb + parity, -target);
+        fence_proxy_async_global();  // the TMA (async proxy) reads these rows next
+        __threadfence();
+        comm_bar();
+        if (ct == 0) st_release_gpu(g.flags + b * AG_CH + ch, g.epoch);
+      }
+    } else if (g.mode == MODE_RS) {
+      // reduce this GPU's rows, 8-row chunks, as soon as all partial tiles of a block are in
+      const int lbk = g.rows_per_rank / TBM;
+      const int items = lbk * RS_CH;
+      const int target = g.world * num_n * 4;  // one arrival per epilogue warp per tile
+      const long long vecs = 8LL * g.N / 8;     // 16-byte vectors per chunk (8 rows x N)
+      const long long slot = (long long)g.rows_per_rank * g.N;
+      const __nv_bfloat16* rbase = g.recv + (long long)parity * g.world * slot;
+      for (int item = blockIdx.x; item < items; item += gridDim.x) {
+        const int lb = item / RS_CH, ch = item % RS_CH;
+        if (!comm_wait(g.cnt + 2 * lb + parity, target, g.err, 8, ct, comm_ok)) break;
+        const long long e0 = ((long long)lb * TBM + ch * 8) * g.N;
+        for (long long v = ct; v < vecs; v += 128 * 2) {
+          float acc[2][8];
+#pragma unroll
+          for (int u = 0; u < 2; ++u)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[u][j] = 0.f;
+          for (int p = 0; p < g.world; ++p) {
+            uint4 x[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u)
+              if (v + u * 128 < vecs)
+                x[u] = *reinterpret_cast<const uint4*>(rbase + p * slot + e0 + (v + u * 128) * 8);
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              if (v + u * 128 < vecs) {
+                acc[u][0] += bf16_lo(x[u].x); acc[u][1] += bf16_hi(x[u].x);
+                acc[u][2] += bf16_lo(x[u].y); acc[u][3] += bf16_hi(x[u].y);
+                acc[u][4] += bf16_lo(x[u].z); acc[u][5] += bf16_hi(x[u].z);
+                acc[u][6] += bf16_lo(x[u].w); acc[u][7] += bf16_hi(x[u].w);
+              }
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < 2; ++u)
+            if (v + u * 128 < vecs)
+              *reinterpret_cast<uint4*>(g.out_rs + e0 + (v + u * 128) * 8) =
+                  make_uint4(pack_bf16x2(acc[u][0], acc[u][1]), pack_bf16x2(acc[u][2], acc[u][3]),
+                             pack_bf16x2(acc[u][4], acc[u][5]), pack_bf16x2(acc[u][6], acc[u][7]));
+        }
+        comm_bar();  // every comm thread is done with this chunk's receive slots
+        if (ct == 0) {
+          // the last chunk of a block takes the block's arrivals back off its counter
+          if (atomicAdd(g.flags + 2 * lb + parity, 1) == RS_CH - 1) {
+            g.flags[2 * lb + parity] = 0;
+            red_add_release_sys(g.cnt + 2 * lb + parity, -target);
+          }
+        }
       }
     }
   }
@@ -324,24 +421,27 @@ void tp_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, int64
   TORCH_CHECK(rc == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", static_cast<int>(rc));
 }
 
-int tp_grid(int tiles, int dev) {
+int tp_grid(int work, int dev) {
   int sms = 0;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   int per_sm = 0;
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemm_tp_kernel, 192, TSMEM);
-  return std::max(1, std::min(tiles, sms * std::max(1, per_sm)));
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemm_tp_kernel, TP_THREADS, TSMEM);
+  return std::max(1, std::min(work, sms * std::max(1, per_sm)));
 }
 }  // namespace
 
 // mode 0/1: out [M, N]; mode 2: out [rows_per_rank, N]. For AG/RS every pointer array is
 // an int64 CUDA tensor of `world` addresses (this GPU's own buffers at index `rank`).
+// flags: AG int32 [M/128 * 8] chunk epochs (zero-initialised once); RS int32
+// [rows_per_rank/128 * 2] reduce-done counters (zero-initialised once).
 void gemm_tp(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t mode, int64_t rank, int64_t world,
              int64_t rows_per_rank, int64_t epoch, c10::optional<torch::Tensor> peer_a,
-             c10::optional<torch::Tensor> staging, c10::optional<torch::Tensor> block_flag,
+             c10::optional<torch::Tensor> staging, c10::optional<torch::Tensor> flags,
              c10::optional<torch::Tensor> ready, c10::optional<torch::Tensor> peer_ready,
              c10::optional<torch::Tensor> peer_recv, c10::optional<torch::Tensor> peer_cnt,
              c10::optional<torch::Tensor> recv, c10::optional<torch::Tensor> cnt, torch::Tensor err) {
   TORCH_CHECK(b.is_cuda() && b.scalar_type() == torch::kBFloat16 && b.stride(1) == 1, "b: bf16 [N, K] row-major");
+  TORCH_CHECK(err.is_cuda() && err.scalar_type() == torch::kInt32, "err: int32 CUDA tensor");
   const int N = b.size(0), K = b.size(1);
   TpArgs g{};
   g.N = N;
@@ -354,20 +454,24 @@ void gemm_tp(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t mode, 
   g.err = err.data_ptr<int>();
   const void* a_ptr;
   int64_t lda;
+  int comm_items = 0;
   if (mode == MODE_AG) {
-    TORCH_CHECK(staging.has_value() && peer_a.has_value() && block_flag.has_value() && ready.has_value() &&
+    TORCH_CHECK(staging.has_value() && peer_a.has_value() && flags.has_value() && ready.has_value() &&
                     peer_ready.has_value(),
-                "AG mode needs staging, peer_a, block_flag, ready, peer_ready");
-    TORCH_CHECK(rows_per_rank % TBM == 0, "rows per rank must be a multiple of 128");
+                "AG mode needs staging, peer_a, flags, ready, peer_ready");
+    TORCH_CHECK(rows_per_rank % TBM == 0 && K % 8 == 0, "AG: rows per rank must be a multiple of 128, K of 8");
     g.M = static_cast<int>(world * rows_per_rank);
+    TORCH_CHECK(staging->numel() >= static_cast<int64_t>(g.M) * K && flags->numel() >= (g.M / TBM) * AG_CH,
+                "AG buffers too small");
     // the local shard lives in staging already (rows rank*rows_per_rank ...)
     g.staging = reinterpret_cast<__nv_bfloat16*>(staging->data_ptr());
     g.peer_a = peer_a->data_ptr<int64_t>();
-    g.block_flag = block_flag->data_ptr<int>();
+    g.flags = flags->data_ptr<int>();
     g.ready = ready->data_ptr<int>();
     g.peer_ready = peer_ready->data_ptr<int64_t>();
     a_ptr = staging->data_ptr();
     lda = K;
+    comm_items = (g.M / TBM - static_cast<int>(rows_per_rank) / TBM) * AG_CH;
   } else {
     TORCH_CHECK(a.is_cuda() && a.scalar_type() == torch::kBFloat16 && a.stride(1) == 1 && a.size(1) == K,
                 "a: bf16 [M, K] row-major");
@@ -376,17 +480,21 @@ void gemm_tp(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t mode, 
     lda = a.stride(0);
   }
   if (mode == MODE_RS) {
-    TORCH_CHECK(peer_recv.has_value() && peer_cnt.has_value() && recv.has_value() && cnt.has_value(),
-                "RS mode needs peer_recv, peer_cnt, recv, cnt");
+    TORCH_CHECK(peer_recv.has_value() && peer_cnt.has_value() && recv.has_value() && cnt.has_value() &&
+                    flags.has_value(),
+                "RS mode needs peer_recv, peer_cnt, recv, cnt, flags");
     TORCH_CHECK(g.M == world * rows_per_rank && rows_per_rank % TBM == 0 && N % 8 == 0, "RS shape");
     TORCH_CHECK(out.is_contiguous() && out.size(0) == rows_per_rank && out.size(1) == N, "RS out: [rows_per_rank, N]");
-    TORCH_CHECK(recv->numel() >= 2 * world * rows_per_rank * N && cnt->numel() >= 2 * rows_per_rank / TBM,
-                "RS receive buffers too small");
+    TORCH_CHECK(recv->numel() >= 2 * world * rows_per_rank * N && cnt->numel() >= 2 * rows_per_rank / TBM &&
+                    flags->numel() >= 2 * rows_per_rank / TBM,
+                "RS buffers too small");
     g.peer_recv = peer_recv->data_ptr<int64_t>();
     g.peer_cnt = peer_cnt->data_ptr<int64_t>();
     g.recv = reinterpret_cast<__nv_bfloat16*>(recv->data_ptr());
     g.cnt = cnt->data_ptr<int>();
+    g.flags = flags->data_ptr<int>();
     g.out_rs = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+    comm_items = static_cast<int>(rows_per_rank / TBM) * RS_CH;
   } else {
     TORCH_CHECK(out.size(0) == g.M && out.size(1) == N && out.stride(1) == 1, "out shape");
     g.c = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
@@ -402,10 +510,10 @@ void gemm_tp(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t mode, 
     attr = true;
   }
   const int tiles = ((g.M + TBM - 1) / TBM) * ((N + TBN - 1) / TBN);
-  const int grid = tp_grid(tiles, b.device().index());
+  const int grid = tp_grid(std::max(tiles, comm_items), b.device().index());
   void* args[] = {&ta, &tb, &g};
-  AXR_CHECK_CUDA(cudaLaunchCooperativeKernel(reinterpret_cast<void*>(gemm_tp_kernel), dim3(grid), dim3(192), args,
-                                             TSMEM, at::cuda::getCurrentCUDAStream()));
+  AXR_CHECK_CUDA(cudaLaunchCooperativeKernel(reinterpret_cast<void*>(gemm_tp_kernel), dim3(grid), dim3(TP_THREADS),
+                                             args, TSMEM, at::cuda::getCurrentCUDAStream()));
 }
 
 }  // namespace axr
