@@ -52,12 +52,18 @@ def main():
     ap.add_argument("--out-tokens", type=int, default=256)
     ap.add_argument("--hit-samples", type=int, default=8)
     ap.add_argument("--decode-batch", type=int, default=16)
-    ap.add_argument("--pool", default="fp8_page")
+    ap.add_argument("--pool", default="fp8", choices=["raw", "fp8", "int4"])
     ap.add_argument("--pool-gb", type=float, default=40.0)
     ap.add_argument("--tp-impl", default="fused", choices=["fused", "nccl"])
     ap.add_argument("--graphs", type=int, default=1)
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--nccl-samples", type=int, default=2,
+                    help="cold prefills also timed with NCCL all-gather/reduce-scatter + cuBLAS")
+    ap.add_argument("--check", action="store_true",
+                    help="numerics only: TP model vs the dense model on every rank (tiny128)")
     args = ap.parse_args()
+    if args.check:
+        return check()
 
     info = init_distributed(timeout_s=600.0)
     dev = info.device
@@ -143,7 +149,28 @@ def main():
     if all_reduce_min(have, info) == 0:
         rest_gbps = None
 
-    # decode throughput: a batch of hit requests, all tokens generated
+    # the same cold prefill with the collectives done by NCCL (+ cuBLAS GEMMs)
+    ttft_cold_nccl = []
+    if args.tp_impl == "fused" and args.nccl_samples > 0:
+        model.fused = False
+        for i in range(args.nccl_samples):
+            eng.evict_live_cache()
+            eng.amf.disable_restore = True
+            r, ms = timed_first_token(prefixes[i % len(prefixes)] + suffix())
+            eng.amf.disable_restore = False
+            ttft_cold_nccl.append(ms)
+        model.fused = True
+
+    # decode throughput: a batch of hit requests, all tokens generated (one untimed
+    # batch first so the decode graphs of this batch size are captured)
+    for timed in (False, True):
+        eng.evict_live_cache()
+        n_out = args.out_tokens if timed else 4
+        reqs = [eng.add_request(prefixes[i % len(prefixes)] + suffix(), SamplingParams(max_tokens=n_out),
+                                amf_prefix_len=args.prefix_len) for i in range(args.decode_batch)]
+        if not timed:
+            while eng.has_unfinished():
+                eng.step()
     eng.evict_live_cache()
     reqs = [eng.add_request(prefixes[i % len(prefixes)] + suffix(), SamplingParams(max_tokens=args.out_tokens),
                             amf_prefix_len=args.prefix_len) for i in range(args.decode_batch)]
@@ -170,6 +197,7 @@ def main():
             "prefix_len": args.prefix_len, "prefixes": args.prefixes, "suffix_len": args.suffix_len,
             "pool": args.pool, "pool_gb_per_gpu": args.pool_gb,
             "ttft_cold_ms": {"p50": pct(ttft_cold, 50), "p99": pct(ttft_cold, 99), "n": len(ttft_cold)},
+            "ttft_cold_nccl_ms": {"p50": pct(ttft_cold_nccl, 50), "n": len(ttft_cold_nccl)},
             "ttft_hit_ms": {"p50": pct(ttft_hit, 50), "p99": pct(ttft_hit, 99), "n": len(ttft_hit)},
             "restore_ms_p50": pct(restore_ms, 50), "restore_gbps_per_gpu": rest_gbps, "hit_tiers": tiers,
             "decode_batch": args.decode_batch, "decode_tokens": dec_tokens,
@@ -178,6 +206,42 @@ def main():
             "data": "synthetic random tokens, random-init weights",
         }), flush=True)
     shutdown(info)
+
+
+def check():
+    """TP model (fused AG/RS prefill + replicated decode) vs the dense model, logits."""
+    from axropus_deploy_b200.models.llama import AttnMeta, LlamaModel
+    from axropus_deploy_b200.ops.kvcache import KVCache
+
+    info = init_distributed(timeout_s=120.0)
+    dev = info.device
+    cfg = get_config("tiny128")
+    dense = LlamaModel(cfg, dev, seed=3, init_std=0.05)
+    tp = TpLlamaModel(cfg, info, dense=dense, max_tokens=2048, sp_min_tokens=256)
+    T = 700
+    tokens = torch.randint(0, cfg.vocab, (T,), generator=torch.Generator().manual_seed(1)).to(dev, torch.int32)
+    errs = {}
+    for name, m, heads in (("dense", dense, cfg.num_kv_heads), ("tp", tp, tp.hkv)):
+        cache = KVCache(m.num_layers, 64, heads, cfg.head_dim, "bf16", dev)
+        bt = torch.arange(64, dtype=torch.int32, device=dev)[None]
+        pos = torch.arange(T, dtype=torch.int32, device=dev)
+        meta = AttnMeta("prefill", pos, pos, bt, torch.tensor([T], dtype=torch.int32, device=dev),
+                        cu_q=torch.tensor([0, T], dtype=torch.int32, device=dev), max_q=T, max_seq_len=T,
+                        logits_idx=torch.tensor([T - 1], dtype=torch.int32, device=dev))
+        lp = m.forward(tokens, meta, cache)
+        p1 = torch.tensor([T], dtype=torch.int32, device=dev)
+        dmeta = AttnMeta("decode", p1, p1, bt, torch.tensor([T + 1], dtype=torch.int32, device=dev), max_seq_len=T + 1)
+        ld = m.forward(tokens[:1], dmeta, cache)
+        errs[name] = (lp, ld)
+    rel = [float((errs["tp"][i] - errs["dense"][i]).norm() / errs["dense"][i].norm()) for i in range(2)]
+    ok = max(rel) < 3e-2
+    if info.rank == 0:
+        print(json.dumps({"check": "tp_vs_dense", "world": info.world, "rel_prefill": rel[0], "rel_decode": rel[1],
+                          "ok": ok}), flush=True)
+        print("TP_LLAMA_CHECK", "ok" if ok else "FAILED", flush=True)
+    shutdown(info)
+    if not ok:
+        sys.exit(1)
 
 
 if __name__ == "__main__":

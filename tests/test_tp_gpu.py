@@ -68,3 +68,16 @@ def test_gemm_tp_two_gpus():
     r = subprocess.run(cmd, capture_output=True, text=True, env=env, cwd=ROOT)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert "TP_CHECK ok" in r.stdout
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tp_llama_two_gpus():
+    """Tensor-parallel Llama (fused sequence-parallel prefill, replicated decode) vs the dense model."""
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "20", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr", "127.0.0.1", "--master-port", "29532",
+           os.path.join(ROOT, "benchmarks", "tp_llama.py"), "--check"]
+    r = subprocess.run(cmd, capture_output=True, text=True, env=env, cwd=ROOT)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert "TP_LLAMA_CHECK ok" in r.stdout
