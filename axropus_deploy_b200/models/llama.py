@@ -143,7 +143,7 @@ class LlamaModel:
                                          max_seq_len=meta.max_seq_len, num_splits=meta.num_splits)
             else:
                 a = ops.prefill_attention(q, cache, li, meta.block_table, meta.cu_q, meta.seq_lens, meta.max_q,
-                                          self.scale)
+                                          self.scale, max_seq_len=meta.max_seq_len)
             h = a.view(T, cfg.q_size) @ lw.wo
             x = ops.rmsnorm(h, lw.mlp_norm, cfg.rms_eps, residual=residual)
             h = self._mlp(lw, x)

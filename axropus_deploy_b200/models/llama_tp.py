@@ -164,7 +164,7 @@ class TpLlamaModel:
                                  max_seq_len=meta.max_seq_len, num_splits=meta.num_splits, out=out)
         else:
             ops.prefill_attention(q, cache, li, meta.block_table, meta.cu_q, meta.seq_lens, meta.max_q, self.scale,
-                                  out=out)
+                                  out=out, max_seq_len=meta.max_seq_len)
 
     # ------------------------------------------------------------------ forward
     def forward(self, tokens: torch.Tensor, meta: AttnMeta, cache: KVCache) -> torch.Tensor:

@@ -96,19 +96,40 @@ def decode_attention(q: torch.Tensor, cache: KVCache, layer: int, block_table: t
     return out
 
 
+def prefill_num_splits(batch: int, heads: int, max_q: int, max_seq_len: Optional[int], device) -> int:
+    """KV slices per query tile so that a short suffix over a long prefix still fills
+    the GPU (about two 80 KB CTAs per SM); 1 when the query tiles alone do."""
+    if not max_seq_len:
+        return 1
+    ctas = max(1, -(-max_q // 64)) * heads * max(1, batch)
+    target = 2 * _num_sms(device)
+    if ctas >= target:
+        return 1
+    kv_tiles = -(-max_seq_len // 64)
+    return int(max(1, min(-(-target // ctas), kv_tiles // 4, 32)))
+
+
+_PREFILL_WS = DecodeWorkspace()
+
+
 def prefill_attention(q: torch.Tensor, cache: KVCache, layer: int, block_table: torch.Tensor, cu_q: torch.Tensor,
                       seq_lens: torch.Tensor, max_q: int, scale: Optional[float] = None,
-                      out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                      out: Optional[torch.Tensor] = None, max_seq_len: Optional[int] = None,
+                      num_splits: Optional[int] = None) -> torch.Tensor:
     """q [T, Hq, D] packed new tokens of B sequences (cu_q offsets); seq_lens = total
-    cached length per sequence including the new tokens."""
+    cached length per sequence including the new tokens. With ``max_seq_len`` (the
+    longest seq_lens entry) the KV range is split when the query tiles are too few."""
     T, Hq, D = q.shape
     scale = scale if scale is not None else 1.0 / math.sqrt(D)
     if out is None:
         out = torch.empty_like(q)
     if q.is_cuda:
         k, v, km, vm, bs, hs, mbs, mhs = cache.layer_args(layer)
+        S = num_splits if num_splits is not None else prefill_num_splits(seq_lens.shape[0], Hq, max_q, max_seq_len,
+                                                                          q.device)
+        po, pl = _PREFILL_WS.get(T, Hq, S, D, q.device) if S > 1 else (None, None)
         cuda_ext().prefill_attention(q, k, v, km, vm, bs, hs, mbs, mhs, cache.fmt, block_table, cu_q, seq_lens,
-                                     cache.num_kv_heads, scale, max_q, out)
+                                     cache.num_kv_heads, scale, max_q, out, S, po, pl)
         return out
     cu = cu_q.tolist()
     for b in range(len(cu) - 1):

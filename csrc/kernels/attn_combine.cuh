@@ -1,0 +1,34 @@
+// Log-sum-exp combine of split-KV attention partials (shared by split-KV decode and
+// split-KV prefill).
+//
+// part_o [R, S, D] fp32 holds each split's normalised output for row r (a (token, head)
+// pair), part_lse [R, S] its log2-domain log-sum-exp (max + log2(sum)), -FLT_MAX when
+// the split saw no key for that row; out [R, D] bf16.
+#pragma once
+
+#include <cuda_bf16.h>
+
+#include <cfloat>
+
+namespace axr {
+
+template <int D>
+__global__ void decode_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_lse,
+                                      __nv_bfloat16* __restrict__ out, int S) {
+  const long long bh = blockIdx.x;
+  const float* lse = part_lse + bh * S;
+  float M = -FLT_MAX;
+  for (int s = 0; s < S; ++s) M = fmaxf(M, lse[s]);
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float num = 0.f, den = 0.f;
+    for (int s = 0; s < S; ++s) {
+      if (lse[s] == -FLT_MAX) continue;
+      const float w = exp2f(lse[s] - M);
+      num += w * part_o[(bh * S + s) * D + d];
+      den += w;
+    }
+    out[bh * D + d] = __float2bfloat16(den > 0.f ? num / den : 0.f);
+  }
+}
+
+}  // namespace axr

@@ -15,7 +15,8 @@ void decode_attention(torch::Tensor q, int64_t k, int64_t v, int64_t km, int64_t
 void prefill_attention(torch::Tensor q, int64_t k, int64_t v, int64_t km, int64_t vm, int64_t blk_stride,
                        int64_t head_stride, int64_t mblk_stride, int64_t mhead_stride, int64_t fmt,
                        torch::Tensor block_table, torch::Tensor cu_q, torch::Tensor seq_lens, int64_t Hkv,
-                       double scale, int64_t max_q, torch::Tensor out);
+                       double scale, int64_t max_q, torch::Tensor out, int64_t num_splits,
+                       c10::optional<torch::Tensor> part_o, c10::optional<torch::Tensor> part_lse);
 void rmsnorm(torch::Tensor x, c10::optional<torch::Tensor> residual, torch::Tensor w, double eps,
              torch::Tensor out);
 void rope_kv_write(torch::Tensor qkv, torch::Tensor pos, torch::Tensor slots, torch::Tensor cos_sin,

@@ -20,6 +20,7 @@
 
 #include <cfloat>
 
+#include "attn_combine.cuh"
 #include "common.cuh"
 
 namespace axr {
@@ -691,25 +692,6 @@ static void launch_tc(int G, dim3 grid, const DecodeParams& p, cudaStream_t st) 
     case 4: go(decode_tc_kernel<FMT, 4>); break;
     case 8: go(decode_tc_kernel<FMT, 8>); break;
     default: TORCH_CHECK(false, "decode_attention: GQA group ", G, " unsupported");
-  }
-}
-
-template <int D>
-__global__ void decode_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_lse,
-                                      __nv_bfloat16* __restrict__ out, int S) {
-  const long long bh = blockIdx.x;
-  const float* lse = part_lse + bh * S;
-  float M = -FLT_MAX;
-  for (int s = 0; s < S; ++s) M = fmaxf(M, lse[s]);
-  for (int d = threadIdx.x; d < D; d += blockDim.x) {
-    float num = 0.f, den = 0.f;
-    for (int s = 0; s < S; ++s) {
-      if (lse[s] == -FLT_MAX) continue;
-      const float w = exp2f(lse[s] - M);
-      num += w * part_o[(bh * S + s) * D + d];
-      den += w;
-    }
-    out[bh * D + d] = __float2bfloat16(den > 0.f ? num / den : 0.f);
   }
 }
 

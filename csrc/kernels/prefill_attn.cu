@@ -9,6 +9,11 @@
 // cp.async (bf16 pages) or dequantised on the way in (FP8 / INT4 pages); S = QK^T and
 // O += PV run from ldmatrix fragments with the online softmax in registers.
 //
+// Split-KV: when the (query tile, head, sequence) grid is too small to fill the GPU --
+// a short suffix prefilled against a long restored prefix -- every CTA takes one slice
+// of the KV tiles and writes a normalised partial output plus its log-sum-exp; a
+// combine kernel merges the slices.
+//
 // Reference counterpart: the prefill attention inside llama.cpp / vLLM (library
 // kernels the reference delegates to); the reference has no prefill kernel of its own.
 #include <torch/extension.h>
@@ -16,6 +21,7 @@
 
 #include <cfloat>
 
+#include "attn_combine.cuh"
 #include "common.cuh"
 
 namespace axr {
@@ -34,6 +40,9 @@ struct PrefillParams {
   const int* seq_lens;  // [B] total kv length (cached prefix + new tokens)
   int Hq, Hkv;
   float scale_log2;
+  int num_splits;   // KV slices per (query tile, head, sequence); 1 = no split
+  float* part_o;    // [T*Hq, S, D] normalised partial outputs (S > 1)
+  float* part_lse;  // [T*Hq, S] log2-domain log-sum-exps (S > 1)
 };
 
 constexpr int BM = 64, BN = 64, D_ = 128;
@@ -113,7 +122,8 @@ __global__ void __launch_bounds__(128, 2) prefill_attn_kernel(PrefillParams p) {
   char* sK[2] = {smem + BM * ROWB, smem + BM * ROWB + 2 * BN * ROWB};
   char* sV[2] = {smem + BM * ROWB + BN * ROWB, smem + BM * ROWB + 3 * BN * ROWB};
 
-  const int tile_m = blockIdx.x, hq = blockIdx.y, b = blockIdx.z;
+  const int S = p.num_splits;
+  const int tile_m = blockIdx.x, hq = blockIdx.y, b = blockIdx.z / S, split = blockIdx.z % S;
   const int q0 = p.cu_q[b], nq = p.cu_q[b + 1] - q0;
   if (tile_m * BM >= nq) return;
   const int kv_len = p.seq_lens[b];
@@ -138,10 +148,20 @@ __global__ void __launch_bounds__(128, 2) prefill_attn_kernel(PrefillParams p) {
 
   const int m_last = min(nq, (tile_m + 1) * BM) - 1;  // last valid q row of the tile
   const int kv_end = min(kv_len, pos0 + m_last + 1);
-  const int n_tiles = (kv_end + BN - 1) / BN;
+  const int n_all = (kv_end + BN - 1) / BN;
+  const int per = (n_all + S - 1) / S;
+  const int t_begin = split * per, t_end = min(n_all, t_begin + per);
+  if (t_begin >= t_end) {  // this slice has no keys for the tile: mark its partials empty
+    cp_async_wait<0>();
+    for (int r = threadIdx.x; r < BM; r += blockDim.x) {
+      const int qr = tile_m * BM + r;
+      if (qr < nq) p.part_lse[((long long)(q0 + qr) * p.Hq + hq) * S + split] = -FLT_MAX;
+    }
+    return;
+  }
 
-  load_kv_tile<FMT>(p, p.k, p.km, bt, kvh, 0, kv_len, sK[0]);
-  load_kv_tile<FMT>(p, p.v, p.vm, bt, kvh, 0, kv_len, sV[0]);
+  load_kv_tile<FMT>(p, p.k, p.km, bt, kvh, t_begin * BN, kv_len, sK[0]);
+  load_kv_tile<FMT>(p, p.v, p.vm, bt, kvh, t_begin * BN, kv_len, sV[0]);
   cp_async_commit();
 
   cp_async_wait<1>();
@@ -165,9 +185,9 @@ __global__ void __launch_bounds__(128, 2) prefill_attn_kernel(PrefillParams p) {
   const int qabs0 = pos0 + tile_m * BM + warp * 16 + g;  // absolute position of row g
   const int qabs1 = qabs0 + 8;
 
-  for (int it = 0; it < n_tiles; ++it) {
-    const int buf = it & 1;
-    if (it + 1 < n_tiles) {
+  for (int it = t_begin; it < t_end; ++it) {
+    const int buf = (it - t_begin) & 1;
+    if (it + 1 < t_end) {
       load_kv_tile<FMT>(p, p.k, p.km, bt, kvh, (it + 1) * BN, kv_len, sK[buf ^ 1]);
       load_kv_tile<FMT>(p, p.v, p.vm, bt, kvh, (it + 1) * BN, kv_len, sV[buf ^ 1]);
       cp_async_commit();
@@ -279,6 +299,21 @@ __global__ void __launch_bounds__(128, 2) prefill_attn_kernel(PrefillParams p) {
   const float inv0 = lrow[0] > 0.f ? 1.f / lrow[0] : 0.f;
   const float inv1 = lrow[1] > 0.f ? 1.f / lrow[1] : 0.f;
   const int r0 = tile_m * BM + warp * 16 + g, r1 = r0 + 8;
+  if (S > 1) {
+    const long long row0 = ((long long)(q0 + r0) * p.Hq + hq) * S + split;
+    const long long row1 = ((long long)(q0 + r1) * p.Hq + hq) * S + split;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int col = j * 8 + 2 * t4;
+      if (r0 < nq) *reinterpret_cast<float2*>(p.part_o + row0 * D_ + col) = make_float2(o[j][0] * inv0, o[j][1] * inv0);
+      if (r1 < nq) *reinterpret_cast<float2*>(p.part_o + row1 * D_ + col) = make_float2(o[j][2] * inv1, o[j][3] * inv1);
+    }
+    if (t4 == 0) {
+      if (r0 < nq) p.part_lse[row0] = lrow[0] > 0.f ? mrow[0] + __log2f(lrow[0]) : -FLT_MAX;
+      if (r1 < nq) p.part_lse[row1] = lrow[1] > 0.f ? mrow[1] + __log2f(lrow[1]) : -FLT_MAX;
+    }
+    return;
+  }
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
     const int col = j * 8 + 2 * t4;
@@ -294,7 +329,8 @@ __global__ void __launch_bounds__(128, 2) prefill_attn_kernel(PrefillParams p) {
 void prefill_attention(torch::Tensor q, int64_t k, int64_t v, int64_t km, int64_t vm, int64_t blk_stride,
                        int64_t head_stride, int64_t mblk_stride, int64_t mhead_stride, int64_t fmt,
                        torch::Tensor block_table, torch::Tensor cu_q, torch::Tensor seq_lens, int64_t Hkv,
-                       double scale, int64_t max_q, torch::Tensor out) {
+                       double scale, int64_t max_q, torch::Tensor out, int64_t num_splits,
+                       c10::optional<torch::Tensor> part_o, c10::optional<torch::Tensor> part_lse) {
   TORCH_CHECK(q.is_cuda() && q.scalar_type() == torch::kBFloat16 && q.is_contiguous() && q.dim() == 3,
               "q must be contiguous bf16 [T, Hq, D]");
   TORCH_CHECK(q.size(2) == D_, "prefill_attention: head_dim must be 128");
@@ -322,8 +358,22 @@ void prefill_attention(torch::Tensor q, int64_t k, int64_t v, int64_t km, int64_
   p.Hq = Hq;
   p.Hkv = static_cast<int>(Hkv);
   p.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
+  const int S = static_cast<int>(std::max<int64_t>(1, num_splits));
+  p.num_splits = S;
+  p.part_o = nullptr;
+  p.part_lse = nullptr;
+  const int T = q.size(0);
+  if (S > 1) {
+    TORCH_CHECK(part_o.has_value() && part_lse.has_value() && part_o->scalar_type() == torch::kFloat32 &&
+                    part_lse->scalar_type() == torch::kFloat32 &&
+                    part_o->numel() >= (int64_t)T * Hq * S * D_ && part_lse->numel() >= (int64_t)T * Hq * S,
+                "prefill_attention: split-KV scratch too small");
+    p.part_o = part_o->data_ptr<float>();
+    p.part_lse = part_lse->data_ptr<float>();
+  }
   const int smem = BM * ROWB + 4 * BN * ROWB;  // 80 KB
-  dim3 grid((max_q + BM - 1) / BM, Hq, B);
+  TORCH_CHECK((int64_t)B * S < 65536, "prefill_attention: too many sequences x splits");
+  dim3 grid((max_q + BM - 1) / BM, Hq, B * S);
   auto st = at::cuda::getCurrentCUDAStream();
   if (grid.x == 0 || B == 0) return;
   if (fmt == kBF16) {
@@ -339,6 +389,10 @@ void prefill_attention(torch::Tensor q, int64_t k, int64_t v, int64_t km, int64_
     TORCH_CHECK(false, "prefill_attention: unsupported cache format ", fmt);
   }
   AXR_CHECK_CUDA(cudaGetLastError());
+  if (S > 1 && T > 0) {
+    decode_combine_kernel<128><<<T * Hq, 128, 0, st>>>(p.part_o, p.part_lse, p.out, S);
+    AXR_CHECK_CUDA(cudaGetLastError());
+  }
 }
 
 }  // namespace axr

@@ -103,6 +103,29 @@ def test_prefill_attention(fmt):
     torch.testing.assert_close(out.cpu().float(), ref.float(), atol=3e-2, rtol=3e-2)
 
 
+@pytest.mark.parametrize("fmt", ["bf16", "fp8", "int4"])
+@pytest.mark.parametrize("splits", [2, 5, 40])
+def test_prefill_attention_split_kv(fmt, splits):
+    """Suffix over a long cached prefix with the KV range split across CTAs (40 splits
+    leaves some slices without keys for some query tiles)."""
+    L, H, D, G = 1, 2, 128, 4
+    NB = 214
+    cache = _fill_cache(KVCache(L, NB, H, D, fmt, DEV), seed=6)
+    seq = torch.tensor([1100, 700, 90], dtype=torch.int32)
+    nq = torch.tensor([100, 3, 90], dtype=torch.int32)
+    cu = torch.zeros(4, dtype=torch.int32)
+    cu[1:] = torch.cumsum(nq, 0)
+    bt = _block_table(3, 70, NB, 7)
+    q = torch.randn(int(cu[-1]), H * G, D).to(torch.bfloat16)
+    out = prefill_attention(q.to(DEV), cache, 0, bt.to(DEV), cu.to(DEV), seq.to(DEV), int(nq.max()),
+                            num_splits=splits)
+    ref = prefill_attention(q, _cpu_copy(cache), 0, bt, cu, seq, int(nq.max()))
+    torch.testing.assert_close(out.cpu().float(), ref.float(), atol=3e-2, rtol=3e-2)
+    auto = prefill_attention(q.to(DEV), cache, 0, bt.to(DEV), cu.to(DEV), seq.to(DEV), int(nq.max()),
+                             max_seq_len=1100)
+    torch.testing.assert_close(auto.cpu().float(), ref.float(), atol=3e-2, rtol=3e-2)
+
+
 def test_rmsnorm_residual():
     x = torch.randn(37, 4096).to(torch.bfloat16)
     r = torch.randn(37, 4096).to(torch.bfloat16)
