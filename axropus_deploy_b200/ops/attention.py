@@ -10,7 +10,11 @@ from typing import Optional
 import torch
 
 from ._ext import cuda_ext
-from .kvcache import KVCache
+from .gemm import error_flag
+from .kvcache import BF16, KVCache
+
+# prefill of bf16 pages on the tcgen05 kernel (False: the warp-level mma.sync kernel)
+PREFILL_TC = [True]
 
 _SMS = {}
 
@@ -127,6 +131,11 @@ def prefill_attention(q: torch.Tensor, cache: KVCache, layer: int, block_table: 
         k, v, km, vm, bs, hs, mbs, mhs = cache.layer_args(layer)
         S = num_splits if num_splits is not None else prefill_num_splits(seq_lens.shape[0], Hq, max_q, max_seq_len,
                                                                           q.device)
+        if S == 1 and cache.fmt == BF16 and D == 128 and PREFILL_TC[0]:
+            # tensor-core (tcgen05 / TMEM) kernel: bf16 pages, enough query tiles to fill the GPU
+            cuda_ext().prefill_attention_tc(q, k, v, bs, hs, cache.num_blocks, block_table, cu_q, seq_lens,
+                                            cache.num_kv_heads, scale, max_q, out, error_flag(q.device))
+            return out
         po, pl = _PREFILL_WS.get(T, Hq, S, D, q.device) if S > 1 else (None, None)
         cuda_ext().prefill_attention(q, k, v, km, vm, bs, hs, mbs, mhs, cache.fmt, block_table, cu_q, seq_lens,
                                      cache.num_kv_heads, scale, max_q, out, S, po, pl)

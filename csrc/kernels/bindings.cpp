@@ -34,6 +34,9 @@ void gemm_tp(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t mode, 
              c10::optional<torch::Tensor> ready, c10::optional<torch::Tensor> peer_ready,
              c10::optional<torch::Tensor> peer_recv, c10::optional<torch::Tensor> peer_cnt,
              c10::optional<torch::Tensor> recv, c10::optional<torch::Tensor> cnt, torch::Tensor err);
+void prefill_attention_tc(torch::Tensor q, int64_t k, int64_t v, int64_t blk_stride, int64_t head_stride,
+                          int64_t num_blocks, torch::Tensor block_table, torch::Tensor cu_q, torch::Tensor seq_lens,
+                          int64_t Hkv, double scale, int64_t max_q, torch::Tensor out, torch::Tensor err);
 }  // namespace axr
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -42,6 +45,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_num_splits", &axr::decode_num_splits);
   m.def("decode_attention", &axr::decode_attention);
   m.def("prefill_attention", &axr::prefill_attention);
+  m.def("prefill_attention_tc", &axr::prefill_attention_tc);
   m.def("rmsnorm", &axr::rmsnorm);
   m.def("rope_kv_write", &axr::rope_kv_write);
   m.def("silu_mul", &axr::silu_mul);

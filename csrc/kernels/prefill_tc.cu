@@ -1,0 +1,385 @@
+// Causal prefill attention on the 5th-generation tensor cores (tcgen05 + TMEM), bf16
+// paged KV cache, head_dim 128, GQA. One CTA = 128 query rows of one head.
+//
+//   warp 4     TMA producer: each 128-token K or V tile is 8 pages x 2 halves of
+//              [16 tokens x 64 dims] boxes, gathered through the block table into a
+//              128-byte-swizzled [128 x 128] tile (2 stages of K+V).
+//   warp 5     MMA issuer (one thread): S_j = Q K_j^T into one of two TMEM S buffers,
+//              O += P_j V_j into the TMEM O accumulator (V read MN-major from smem).
+//   warps 0-3  softmax, one thread per query row (= TMEM lane): load S_j from TMEM,
+//              causal mask, running max, exp2, row sum, write P_j (bf16) to a
+//              swizzled smem tile the next MMA reads. The running max is only moved
+//              when a tile's max exceeds it by more than 2^8 (then O is rescaled in
+//              TMEM), so the exponentials stay below 256 and the O rescale is rare.
+//   epilogue   O / l from TMEM straight to the output rows.
+//
+// S_{j+1} is computed while the softmax works on S_j, and PV_j while the softmax works
+// on S_{j+1}. Every mbarrier wait is bounded; on timeout the kernel records an error
+// code, drains its own TMA loads and MMAs, frees TMEM and returns.
+//
+// Reference counterpart: the prefill attention the reference delegates to llama.cpp /
+// vLLM library kernels; the reference has no prefill attention kernel of its own.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+
+#include <cfloat>
+
+#include "common.cuh"
+#include "tc_common.cuh"
+
+namespace axr {
+namespace fa {
+
+constexpr int BM = 128, BN = 128, HD = 128;
+constexpr int CHUNK = 128 * 128;     // one [128 rows x 64 bf16] swizzled chunk (16 KB)
+constexpr int TILE = 2 * CHUNK;      // [128 x 128] bf16 tile
+constexpr int KST = 2;               // K/V pipeline stages
+constexpr int SMEM = 1024 + TILE /*Q*/ + 2 * KST * TILE /*K,V*/ + 2 * TILE /*P*/ + 512;
+constexpr int THREADS = 192;
+constexpr float RESCALE_T = 8.f;     // log2 units
+
+struct Params {
+  const __nv_bfloat16* q;  // [T, Hq, 128]
+  __nv_bfloat16* out;      // [T, Hq, 128]
+  int Hq, Hkv;
+  const int* block_table;
+  int bt_stride;
+  const int* cu_q;
+  const int* seq_lens;
+  float scale_log2;
+  volatile int* err;
+};
+
+// byte offset of 16-byte unit u (0..15) of row r in a [128 x 128] bf16 K-major SW128 tile
+__device__ __forceinline__ uint32_t swz_off(int r, int u) {
+  return (u >> 3) * CHUNK + r * 128 + (((u & 7) ^ (r & 7)) << 4);
+}
+
+__device__ __forceinline__ bool warp_ok(bool ok, volatile int* err) {
+  return __all_sync(0xffffffffu, ok) && __shfl_sync(0xffffffffu, *err, 0) == 0;
+}
+
+__global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK,
+                                                                const __grid_constant__ CUtensorMap tmV, Params p) {
+  extern __shared__ __align__(1024) char fa_raw[];
+  char* base = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(fa_raw) + 1023) & ~uintptr_t(1023));
+  char* sQ = base;
+  char* sK = sQ + TILE;
+  char* sV = sK + KST * TILE;
+  char* sP = sV + KST * TILE;
+  uint64_t* full_k = reinterpret_cast<uint64_t*>(sP + 2 * TILE);
+  uint64_t* full_v = full_k + KST;
+  uint64_t* kv_free = full_v + KST;
+  uint64_t* s_full = kv_free + KST;  // [2]
+  uint64_t* s_free = s_full + 2;     // [2]
+  uint64_t* p_full = s_free + 2;     // [2]
+  uint64_t* o_done = p_full + 2;     // [2]
+  uint64_t* q_full = o_done + 2;
+  uint64_t* drain = q_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile_m = gridDim.x - 1 - blockIdx.x;  // longest (most KV tiles) first
+  const int hq = blockIdx.y, b = blockIdx.z;
+  const int q0 = p.cu_q[b], nq = p.cu_q[b + 1] - q0;
+  if (tile_m * BM >= nq) return;
+  const int kv_len = p.seq_lens[b];
+  const int pos0 = kv_len - nq;  // absolute position of query row 0
+  const int kvh = hq / (p.Hq / p.Hkv);
+  const int m_last = min(nq, (tile_m + 1) * BM) - 1;
+  const int kv_end = min(kv_len, pos0 + m_last + 1);
+  const int n_tiles = (kv_end + BN - 1) / BN;
+  const int* bt = p.block_table + (long long)b * p.bt_stride;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < KST; ++s) {
+      tc::mbar_init(&full_k[s], 1);
+      tc::mbar_init(&full_v[s], 1);
+      tc::mbar_init(&kv_free[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      tc::mbar_init(&s_full[i], 1);
+      tc::mbar_init(&s_free[i], 4);
+      tc::mbar_init(&p_full[i], 4);
+      tc::mbar_init(&o_done[i], 1);
+    }
+    tc::mbar_init(q_full, 4);
+    tc::mbar_init(drain, 1);
+    tc::fence_barrier_init();
+    tc::prefetch_tmap(&tmK);
+    tc::prefetch_tmap(&tmV);
+  }
+  if (warp == 5) {
+    tc::tmem_alloc(tmem_slot, 512);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tO = tmem + 256;
+
+  if (warp == 4) {
+    if (lane == 0) {  // ---------------- TMA producer
+      int issued = 0;
+      bool ok = true;
+      for (int j = 0; j < n_tiles; ++j) {
+        const int s = j % KST;
+        if (j >= KST && !tc::mbar_wait(&kv_free[s], ((j / KST) + 1) & 1, p.err, 11)) { ok = false; break; }
+        int ys[8];
+#pragma unroll
+        for (int pg = 0; pg < 8; ++pg) {
+          const int tok = j * BN + pg * 16;
+          const int blk = tok < kv_len ? bt[tok >> 4] : 0;
+          ys[pg] = (blk * p.Hkv + kvh) * 16;
+        }
+        tc::mbar_arrive_expect_tx(&full_k[s], TILE);
+#pragma unroll
+        for (int pg = 0; pg < 8; ++pg) {
+          tc::tma_load_2d(sK + s * TILE + pg * 2048, &tmK, 0, ys[pg], &full_k[s]);
+          tc::tma_load_2d(sK + s * TILE + CHUNK + pg * 2048, &tmK, 64, ys[pg], &full_k[s]);
+        }
+        tc::mbar_arrive_expect_tx(&full_v[s], TILE);
+#pragma unroll
+        for (int pg = 0; pg < 8; ++pg) {
+          tc::tma_load_2d(sV + s * TILE + pg * 2048, &tmV, 0, ys[pg], &full_v[s]);
+          tc::tma_load_2d(sV + s * TILE + CHUNK + pg * 2048, &tmV, 64, ys[pg], &full_v[s]);
+        }
+        issued = j + 1;
+      }
+      if (!ok) {  // let this thread's loads land before the CTA can exit
+        for (int j = max(0, issued - KST); j < issued; ++j) {
+          tc::mbar_wait_quiet(&full_k[j % KST], (j / KST) & 1);
+          tc::mbar_wait_quiet(&full_v[j % KST], (j / KST) & 1);
+        }
+      }
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {  // ---------------- MMA issuer
+      constexpr uint32_t idesc_s = tc::idesc_bf16_f32(BM, BN);
+      constexpr uint32_t idesc_pv = tc::idesc_bf16_f32_bmn(BM, HD);
+      const uint32_t q_addr = tc::smem_u32(sQ);
+      auto issue_s = [&](int j) {
+        const uint32_t k_addr = tc::smem_u32(sK + (j % KST) * TILE);
+        const uint32_t d = tmem + (j & 1) * 128;
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * CHUNK + (kk & 3) * 32;
+          tc::mma_f16_ss(d, tc::smem_desc_k_sw128(q_addr + off), tc::smem_desc_k_sw128(k_addr + off), idesc_s,
+                         kk != 0);
+        }
+        tc::mma_commit(&s_full[j & 1]);
+      };
+      bool ok = tc::mbar_wait(q_full, 0, p.err, 12) && tc::mbar_wait(&full_k[0], 0, p.err, 13);
+      if (ok) {
+        tc::tc_fence_after();
+        issue_s(0);
+      }
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        if (j + 1 < n_tiles) {
+          const int sb = (j + 1) & 1;
+          if (j + 1 >= 2 && !tc::mbar_wait(&s_free[sb], (((j + 1) >> 1) + 1) & 1, p.err, 14)) break;
+          if (!tc::mbar_wait(&full_k[(j + 1) % KST], ((j + 1) / KST) & 1, p.err, 15)) break;
+          tc::tc_fence_after();
+          issue_s(j + 1);
+        }
+        if (!tc::mbar_wait(&p_full[j & 1], (j >> 1) & 1, p.err, 16)) break;
+        if (!tc::mbar_wait(&full_v[j % KST], (j / KST) & 1, p.err, 17)) break;
+        tc::tc_fence_after();
+        const uint32_t p_addr = tc::smem_u32(sP + (j & 1) * TILE);
+        const uint32_t v_addr = tc::smem_u32(sV + (j % KST) * TILE);
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          tc::mma_f16_ss(tO, tc::smem_desc_k_sw128(p_addr + (kk >> 2) * CHUNK + (kk & 3) * 32),
+                         tc::smem_desc_mn_sw128(v_addr + kk * 2048, CHUNK), idesc_pv, (j | kk) != 0);
+        }
+        tc::mma_commit(&o_done[j & 1]);
+        tc::mma_commit(&kv_free[j % KST]);
+      }
+      tc::mma_commit(drain);
+      tc::mbar_wait_quiet(drain, 0);  // every MMA of this CTA has completed
+    }
+  } else {
+    // ---------------- softmax warps 0..3: thread = query row = TMEM lane
+    const int row = warp * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    const int qr = tile_m * BM + row;
+    const bool row_valid = qr < nq;
+    {
+      const char* src = reinterpret_cast<const char*>(p.q + ((long long)(q0 + (row_valid ? qr : 0)) * p.Hq + hq) * HD);
+#pragma unroll
+      for (int u = 0; u < 16; ++u) cp_async16_zfill(sQ + swz_off(row, u), src + u * 16, row_valid);
+      cp_async_commit();
+      cp_async_wait<0>();
+      tc::fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(q_full);
+    }
+    const int qpos = pos0 + qr;
+    const int qpos_min = pos0 + tile_m * BM;
+    float m_used = -FLT_MAX, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_tiles; ++j) {
+      const int sb = j & 1;
+      ok = warp_ok(tc::mbar_wait(&s_full[sb], (j >> 1) & 1, p.err, 18), p.err);
+      if (!ok) break;
+      tc::tc_fence_after();
+      float x[BN];
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tc::tmem_ld32(tmem + sb * 128 + lane_off + c * 32, r);
+        tc::tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) x[c * 32 + i] = __uint_as_float(r[i]) * p.scale_log2;
+      }
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&s_free[sb]);
+      const int n0 = j * BN;
+      if (n0 + BN - 1 > qpos_min || n0 + BN > kv_len) {
+#pragma unroll
+        for (int i = 0; i < BN; ++i)
+          if (n0 + i > qpos || n0 + i >= kv_len) x[i] = -FLT_MAX;
+      }
+      float mt = -FLT_MAX;
+#pragma unroll
+      for (int i = 0; i < BN; ++i) mt = fmaxf(mt, x[i]);
+      if (j == 0) {
+        m_used = mt;
+      } else {
+        const bool rescale = mt > m_used + RESCALE_T;
+        if (__any_sync(0xffffffffu, rescale)) {
+          // O must hold PV_{j-1} before it is rescaled
+          ok = warp_ok(tc::mbar_wait(&o_done[(j - 1) & 1], ((j - 1) >> 1) & 1, p.err, 19), p.err);
+          if (!ok) break;
+          tc::tc_fence_after();
+          const float alpha = rescale ? exp2f(m_used - mt) : 1.f;
+          if (rescale) {
+            m_used = mt;
+            l *= alpha;
+          }
+#pragma unroll 1
+          for (int c = 0; c < HD / 32; ++c) {
+            uint32_t r[32];
+            tc::tmem_ld32(tO + lane_off + c * 32, r);
+            tc::tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+            tc::tmem_st32(tO + lane_off + c * 32, r);
+          }
+          tc::tmem_st_wait();
+        }
+      }
+      // P buffer sb was last read by PV_{j-2}
+      if (j >= 2) {
+        ok = warp_ok(tc::mbar_wait(&o_done[sb], ((j - 2) >> 1) & 1, p.err, 20), p.err);
+        if (!ok) break;
+      }
+      char* pbuf = sP + sb * TILE;
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        float e[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float v = x[u * 8 + i];
+          e[i] = v == -FLT_MAX ? 0.f : exp2f(v - m_used);
+          l += e[i];
+        }
+        *reinterpret_cast<uint4*>(pbuf + swz_off(row, u)) =
+            make_uint4(pack_bf16x2(e[0], e[1]), pack_bf16x2(e[2], e[3]), pack_bf16x2(e[4], e[5]),
+                       pack_bf16x2(e[6], e[7]));
+      }
+      tc::fence_proxy_async_smem();
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&p_full[sb]);
+    }
+    // ---------------- epilogue: O / l -> out
+    if (ok) ok = warp_ok(tc::mbar_wait(&o_done[(n_tiles - 1) & 1], ((n_tiles - 1) >> 1) & 1, p.err, 21), p.err);
+    if (ok) {
+      tc::tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* dst = p.out + ((long long)(q0 + (row_valid ? qr : 0)) * p.Hq + hq) * HD;
+#pragma unroll 1
+      for (int c = 0; c < HD / 32; ++c) {
+        uint32_t r[32];
+        tc::tmem_ld32(tO + lane_off + c * 32, r);
+        tc::tmem_ld_wait();
+        if (row_valid) {
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            const uint32_t* w = &r[v * 8];
+            *reinterpret_cast<uint4*>(dst + c * 32 + v * 8) =
+                make_uint4(pack_bf16x2(__uint_as_float(w[0]) * inv, __uint_as_float(w[1]) * inv),
+                           pack_bf16x2(__uint_as_float(w[2]) * inv, __uint_as_float(w[3]) * inv),
+                           pack_bf16x2(__uint_as_float(w[4]) * inv, __uint_as_float(w[5]) * inv),
+                           pack_bf16x2(__uint_as_float(w[6]) * inv, __uint_as_float(w[7]) * inv));
+          }
+        }
+      }
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 5) tc::tmem_dealloc(tmem, 512);
+}
+
+void make_page_map(CUtensorMap* map, const void* ptr, int64_t rows) {
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(ptr) % 16 == 0, "prefill_tc: page base must be 16-byte aligned");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(HD), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(HD * 2)};
+  cuuint32_t box[2] = {64, 16};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult rc = cuTensorMapEncodeTiled(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims,
+                                             strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(rc == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", static_cast<int>(rc));
+}
+
+}  // namespace fa
+
+// q [T, Hq, 128] bf16; k/v: the layer's bf16 K and V page regions ([num_blocks, Hkv, 16, 128]
+// each, contiguous); block_table [B, max_blocks] int32; cu_q [B+1]; seq_lens [B]; err int32.
+void prefill_attention_tc(torch::Tensor q, int64_t k, int64_t v, int64_t blk_stride, int64_t head_stride,
+                          int64_t num_blocks, torch::Tensor block_table, torch::Tensor cu_q, torch::Tensor seq_lens,
+                          int64_t Hkv, double scale, int64_t max_q, torch::Tensor out, torch::Tensor err) {
+  using namespace fa;
+  TORCH_CHECK(q.is_cuda() && q.scalar_type() == torch::kBFloat16 && q.is_contiguous() && q.dim() == 3 &&
+                  q.size(2) == HD,
+              "prefill_tc: q must be contiguous bf16 [T, Hq, 128]");
+  TORCH_CHECK(out.is_contiguous() && out.scalar_type() == torch::kBFloat16, "prefill_tc: out must be contiguous bf16");
+  TORCH_CHECK(blk_stride == Hkv * 16 * HD * 2 && head_stride == 16 * HD * 2,
+              "prefill_tc: expects contiguous bf16 pages [blocks, Hkv, 16, 128]");
+  TORCH_CHECK(block_table.scalar_type() == torch::kInt32 && cu_q.scalar_type() == torch::kInt32 &&
+                  seq_lens.scalar_type() == torch::kInt32 && err.scalar_type() == torch::kInt32,
+              "prefill_tc: index tensors must be int32");
+  const int B = seq_lens.size(0), Hq = q.size(1);
+  TORCH_CHECK(Hq % Hkv == 0, "Hq must be a multiple of Hkv");
+  if (B == 0 || max_q == 0) return;
+  CUtensorMap tk, tv;
+  make_page_map(&tk, reinterpret_cast<const void*>(k), num_blocks * Hkv * 16);
+  make_page_map(&tv, reinterpret_cast<const void*>(v), num_blocks * Hkv * 16);
+  Params p;
+  p.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  p.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  p.Hq = Hq;
+  p.Hkv = static_cast<int>(Hkv);
+  p.block_table = block_table.data_ptr<int>();
+  p.bt_stride = block_table.stride(0);
+  p.cu_q = cu_q.data_ptr<int>();
+  p.seq_lens = seq_lens.data_ptr<int>();
+  p.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
+  p.err = err.data_ptr<int>();
+  static bool attr = false;
+  if (!attr) {
+    AXR_CHECK_CUDA(cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
+    attr = true;
+  }
+  dim3 grid((max_q + BM - 1) / BM, Hq, B);
+  prefill_tc_kernel<<<grid, THREADS, SMEM, at::cuda::getCurrentCUDAStream()>>>(tk, tv, p);
+  AXR_CHECK_CUDA(cudaGetLastError());
+}
+
+}  // namespace axr

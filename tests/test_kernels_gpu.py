@@ -126,6 +126,41 @@ def test_prefill_attention_split_kv(fmt, splits):
     torch.testing.assert_close(auto.cpu().float(), ref.float(), atol=3e-2, rtol=3e-2)
 
 
+@pytest.mark.parametrize("G", [4, 8])
+def test_prefill_attention_tcgen05_long(G):
+    """tcgen05 prefill kernel (bf16 pages) on multi-tile causal prefills and a suffix,
+    with per-block key magnitudes from 1x to 8x so the running max moves by more than
+    2^8 between KV tiles (the O rescale in TMEM runs)."""
+    from axropus_deploy_b200.ops import attention as att
+    from axropus_deploy_b200.ops.gemm import check_errors
+
+    L, H, D = 1, 2, 128
+    seq = torch.tensor([700, 300, 129], dtype=torch.int32)
+    nq = torch.tensor([700, 150, 129], dtype=torch.int32)
+    pages = 45
+    NB = 3 * pages + 5
+    vals = torch.randn(NB, L, 2, H, 16, D, generator=torch.Generator().manual_seed(9))
+    vals[:, :, 0] *= torch.linspace(1.0, 8.0, NB)[:, None, None, None, None]
+    cache = KVCache(L, NB, H, D, "bf16", DEV)
+    cache.write_units(torch.arange(NB), vals.to(DEV))
+    cu = torch.zeros(4, dtype=torch.int32)
+    cu[1:] = torch.cumsum(nq, 0)
+    bt = _block_table(3, pages, NB, 11)
+    q = (torch.randn(int(cu[-1]), H * G, D) * 2.0).to(torch.bfloat16)
+    assert att.PREFILL_TC[0]
+    out = prefill_attention(q.to(DEV), cache, 0, bt.to(DEV), cu.to(DEV), seq.to(DEV), int(nq.max()))
+    torch.cuda.synchronize()
+    assert check_errors(q.device if q.is_cuda else torch.device(DEV)) == 0
+    ref = prefill_attention(q, _cpu_copy(cache), 0, bt, cu, seq, int(nq.max()))
+    torch.testing.assert_close(out.cpu().float(), ref.float(), atol=3e-2, rtol=3e-2)
+    att.PREFILL_TC[0] = False
+    try:
+        legacy = prefill_attention(q.to(DEV), cache, 0, bt.to(DEV), cu.to(DEV), seq.to(DEV), int(nq.max()))
+    finally:
+        att.PREFILL_TC[0] = True
+    torch.testing.assert_close(out.float(), legacy.float(), atol=3e-2, rtol=3e-2)
+
+
 def test_rmsnorm_residual():
     x = torch.randn(37, 4096).to(torch.bfloat16)
     r = torch.randn(37, 4096).to(torch.bfloat16)
