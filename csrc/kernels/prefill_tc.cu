@@ -1,21 +1,27 @@
 // Causal prefill attention on the 5th-generation tensor cores (tcgen05 + TMEM), bf16
-// paged KV cache, head_dim 128, GQA. One CTA = 128 query rows of one head.
+// paged KV cache, head_dim 128, GQA. One CTA = 256 query rows of one head, as two
+// 128-row sub-tiles A and B that ping-pong on the tensor core:
 //
-//   warp 4     TMA producer: each 128-token K or V tile is 8 pages x 2 halves of
-//              [16 tokens x 64 dims] boxes, gathered through the block table into a
-//              128-byte-swizzled [128 x 128] tile (2 stages of K+V).
-//   warp 5     MMA issuer (one thread): S_j = Q K_j^T into one of two TMEM S buffers,
-//              O += P_j V_j into the TMEM O accumulator (V read MN-major from smem).
-//   warps 0-3  softmax, one thread per query row (= TMEM lane): load S_j from TMEM,
-//              causal mask, running max, exp2, row sum, write P_j (bf16) to a
-//              swizzled smem tile the next MMA reads. The running max is only moved
-//              when a tile's max exceeds it by more than 2^8 (then O is rescaled in
-//              TMEM), so the exponentials stay below 256 and the O rescale is rare.
+//   warp 8     TMA producer: K_j and V_j (128 tokens each) are gathered through the
+//              block table as 8 pages x 2 halves of [16 tokens x 64 dims] boxes into a
+//              ring of three 128-byte-swizzled [128 x 128] slots (K_0 V_0 K_1 V_1 ...).
+//   warp 9     MMA issuer (one thread), per KV tile j:
+//                PV_A(j), S_A(j+1), PV_B(j), S_B(j+1)
+//              S_x = Q_x K^T goes to sub-tile x's TMEM S columns, O_x += P_x V (V read
+//              MN-major from shared memory) to its TMEM O columns.
+//   warps 0-3 / 4-7   softmax of sub-tile A / B, one thread per query row (= TMEM
+//              lane): S from TMEM, causal mask, running max, exp2, row sum, P (bf16)
+//              into a swizzled shared tile. The running max only moves when a tile's
+//              max exceeds it by more than 2^8 (O is then rescaled in TMEM), so the
+//              exponentials stay below 256 and the rescale is rare.
 //   epilogue   O / l from TMEM straight to the output rows.
 //
-// S_{j+1} is computed while the softmax works on S_j, and PV_j while the softmax works
-// on S_{j+1}. Every mbarrier wait is bounded; on timeout the kernel records an error
-// code, drains its own TMA loads and MMAs, frees TMEM and returns.
+// Ordering comes from tcgen05.commit, which fires only when every earlier MMA of the
+// issuing thread has completed: when S_x(j+1) is ready, PV_x(j) is done, so the softmax
+// may overwrite P_x and rescale O_x without further waits. While one sub-tile's
+// softmax runs, the tensor core works on the other's MMAs. Every mbarrier wait is
+// bounded; on timeout the kernel records an error code, drains its own TMA loads and
+// MMAs, frees TMEM and returns.
 //
 // Reference counterpart: the prefill attention the reference delegates to llama.cpp /
 // vLLM library kernels; the reference has no prefill attention kernel of its own.
@@ -31,12 +37,12 @@ namespace axr {
 namespace fa {
 
 constexpr int BM = 128, BN = 128, HD = 128;
-constexpr int CHUNK = 128 * 128;     // one [128 rows x 64 bf16] swizzled chunk (16 KB)
-constexpr int TILE = 2 * CHUNK;      // [128 x 128] bf16 tile
-constexpr int KST = 2;               // K/V pipeline stages
-constexpr int SMEM = 1024 + TILE /*Q*/ + 2 * KST * TILE /*K,V*/ + 2 * TILE /*P*/ + 512;
-constexpr int THREADS = 192;
-constexpr float RESCALE_T = 8.f;     // log2 units
+constexpr int CHUNK = 128 * 128;  // one [128 rows x 64 bf16] swizzled chunk (16 KB)
+constexpr int TILE = 2 * CHUNK;   // [128 x 128] bf16 tile (32 KB)
+constexpr int RING = 3;           // K/V slots
+constexpr int SMEM = 1024 + 2 * TILE /*Q_A,Q_B*/ + 2 * TILE /*P_A,P_B*/ + RING * TILE + 256;
+constexpr int THREADS = 320;
+constexpr float RESCALE_T = 8.f;  // log2 units
 
 struct Params {
   const __nv_bfloat16* q;  // [T, Hq, 128]
@@ -63,18 +69,15 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
                                                                 const __grid_constant__ CUtensorMap tmV, Params p) {
   extern __shared__ __align__(1024) char fa_raw[];
   char* base = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(fa_raw) + 1023) & ~uintptr_t(1023));
-  char* sQ = base;
-  char* sK = sQ + TILE;
-  char* sV = sK + KST * TILE;
-  char* sP = sV + KST * TILE;
-  uint64_t* full_k = reinterpret_cast<uint64_t*>(sP + 2 * TILE);
-  uint64_t* full_v = full_k + KST;
-  uint64_t* kv_free = full_v + KST;
-  uint64_t* s_full = kv_free + KST;  // [2]
-  uint64_t* s_free = s_full + 2;     // [2]
-  uint64_t* p_full = s_free + 2;     // [2]
-  uint64_t* o_done = p_full + 2;     // [2]
-  uint64_t* q_full = o_done + 2;
+  char* sQ = base;             // [2][TILE]
+  char* sP = sQ + 2 * TILE;    // [2][TILE]
+  char* sR = sP + 2 * TILE;    // [RING][TILE]
+  uint64_t* slot_full = reinterpret_cast<uint64_t*>(sR + RING * TILE);
+  uint64_t* slot_free = slot_full + RING;
+  uint64_t* s_full = slot_free + RING;  // [2] (A, B)
+  uint64_t* p_full = s_full + 2;        // [2]
+  uint64_t* o_done = p_full + 2;
+  uint64_t* q_full = o_done + 1;
   uint64_t* drain = q_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
@@ -82,34 +85,34 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
   const int tile_m = gridDim.x - 1 - blockIdx.x;  // longest (most KV tiles) first
   const int hq = blockIdx.y, b = blockIdx.z;
   const int q0 = p.cu_q[b], nq = p.cu_q[b + 1] - q0;
-  if (tile_m * BM >= nq) return;
+  const int row0 = tile_m * 2 * BM;  // first query row of sub-tile A
+  if (row0 >= nq) return;
+  const bool has_b = row0 + BM < nq;
   const int kv_len = p.seq_lens[b];
   const int pos0 = kv_len - nq;  // absolute position of query row 0
   const int kvh = hq / (p.Hq / p.Hkv);
-  const int m_last = min(nq, (tile_m + 1) * BM) - 1;
+  const int m_last = min(nq, row0 + 2 * BM) - 1;
   const int kv_end = min(kv_len, pos0 + m_last + 1);
   const int n_tiles = (kv_end + BN - 1) / BN;
   const int* bt = p.block_table + (long long)b * p.bt_stride;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < KST; ++s) {
-      tc::mbar_init(&full_k[s], 1);
-      tc::mbar_init(&full_v[s], 1);
-      tc::mbar_init(&kv_free[s], 1);
+    for (int s = 0; s < RING; ++s) {
+      tc::mbar_init(&slot_full[s], 1);
+      tc::mbar_init(&slot_free[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
       tc::mbar_init(&s_full[i], 1);
-      tc::mbar_init(&s_free[i], 4);
       tc::mbar_init(&p_full[i], 4);
-      tc::mbar_init(&o_done[i], 1);
     }
-    tc::mbar_init(q_full, 4);
+    tc::mbar_init(o_done, 1);
+    tc::mbar_init(q_full, 8);
     tc::mbar_init(drain, 1);
     tc::fence_barrier_init();
     tc::prefetch_tmap(&tmK);
     tc::prefetch_tmap(&tmV);
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tc::tmem_alloc(tmem_slot, 512);
     tc::tmem_relinquish();
   }
@@ -117,98 +120,96 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tO = tmem + 256;
+  // TMEM columns: S_A 0-127, S_B 128-255, O_A 256-383, O_B 384-511
 
-  if (warp == 4) {
-    if (lane == 0) {  // ---------------- TMA producer
+  if (warp == 8) {
+    if (lane == 0) {  // ---------------- TMA producer: items K_0, V_0, K_1, V_1, ...
       int issued = 0;
       bool ok = true;
-      for (int j = 0; j < n_tiles; ++j) {
-        const int s = j % KST;
-        if (j >= KST && !tc::mbar_wait(&kv_free[s], ((j / KST) + 1) & 1, p.err, 11)) { ok = false; break; }
-        int ys[8];
+      for (int i = 0; i < 2 * n_tiles; ++i) {
+        const int s = i % RING, j = i >> 1;
+        if (i >= RING && !tc::mbar_wait(&slot_free[s], ((i / RING) + 1) & 1, p.err, 11)) { ok = false; break; }
+        const CUtensorMap* map = (i & 1) ? &tmV : &tmK;
+        tc::mbar_arrive_expect_tx(&slot_full[s], TILE);
 #pragma unroll
         for (int pg = 0; pg < 8; ++pg) {
           const int tok = j * BN + pg * 16;
           const int blk = tok < kv_len ? bt[tok >> 4] : 0;
-          ys[pg] = (blk * p.Hkv + kvh) * 16;
+          const int y = (blk * p.Hkv + kvh) * 16;
+          tc::tma_load_2d(sR + s * TILE + pg * 2048, map, 0, y, &slot_full[s]);
+          tc::tma_load_2d(sR + s * TILE + CHUNK + pg * 2048, map, 64, y, &slot_full[s]);
         }
-        tc::mbar_arrive_expect_tx(&full_k[s], TILE);
-#pragma unroll
-        for (int pg = 0; pg < 8; ++pg) {
-          tc::tma_load_2d(sK + s * TILE + pg * 2048, &tmK, 0, ys[pg], &full_k[s]);
-          tc::tma_load_2d(sK + s * TILE + CHUNK + pg * 2048, &tmK, 64, ys[pg], &full_k[s]);
-        }
-        tc::mbar_arrive_expect_tx(&full_v[s], TILE);
-#pragma unroll
-        for (int pg = 0; pg < 8; ++pg) {
-          tc::tma_load_2d(sV + s * TILE + pg * 2048, &tmV, 0, ys[pg], &full_v[s]);
-          tc::tma_load_2d(sV + s * TILE + CHUNK + pg * 2048, &tmV, 64, ys[pg], &full_v[s]);
-        }
-        issued = j + 1;
+        issued = i + 1;
       }
       if (!ok) {  // let this thread's loads land before the CTA can exit
-        for (int j = max(0, issued - KST); j < issued; ++j) {
-          tc::mbar_wait_quiet(&full_k[j % KST], (j / KST) & 1);
-          tc::mbar_wait_quiet(&full_v[j % KST], (j / KST) & 1);
-        }
+        for (int i = max(0, issued - RING); i < issued; ++i) tc::mbar_wait_quiet(&slot_full[i % RING], (i / RING) & 1);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     if (lane == 0) {  // ---------------- MMA issuer
       constexpr uint32_t idesc_s = tc::idesc_bf16_f32(BM, BN);
       constexpr uint32_t idesc_pv = tc::idesc_bf16_f32_bmn(BM, HD);
-      const uint32_t q_addr = tc::smem_u32(sQ);
-      auto issue_s = [&](int j) {
-        const uint32_t k_addr = tc::smem_u32(sK + (j % KST) * TILE);
-        const uint32_t d = tmem + (j & 1) * 128;
+      const int nsub = has_b ? 2 : 1;
+      auto issue_s = [&](int x, int j) {  // S_x(j) = Q_x K_j^T
+        const uint32_t q_addr = tc::smem_u32(sQ + x * TILE);
+        const uint32_t k_addr = tc::smem_u32(sR + ((2 * j) % RING) * TILE);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
           const uint32_t off = (kk >> 2) * CHUNK + (kk & 3) * 32;
-          tc::mma_f16_ss(d, tc::smem_desc_k_sw128(q_addr + off), tc::smem_desc_k_sw128(k_addr + off), idesc_s,
-                         kk != 0);
+          tc::mma_f16_ss(tmem + x * 128, tc::smem_desc_k_sw128(q_addr + off), tc::smem_desc_k_sw128(k_addr + off),
+                         idesc_s, kk != 0);
         }
-        tc::mma_commit(&s_full[j & 1]);
+        tc::mma_commit(&s_full[x]);
       };
-      bool ok = tc::mbar_wait(q_full, 0, p.err, 12) && tc::mbar_wait(&full_k[0], 0, p.err, 13);
-      if (ok) {
-        tc::tc_fence_after();
-        issue_s(0);
-      }
-      for (int j = 0; ok && j < n_tiles; ++j) {
-        if (j + 1 < n_tiles) {
-          const int sb = (j + 1) & 1;
-          if (j + 1 >= 2 && !tc::mbar_wait(&s_free[sb], (((j + 1) >> 1) + 1) & 1, p.err, 14)) break;
-          if (!tc::mbar_wait(&full_k[(j + 1) % KST], ((j + 1) / KST) & 1, p.err, 15)) break;
-          tc::tc_fence_after();
-          issue_s(j + 1);
-        }
-        if (!tc::mbar_wait(&p_full[j & 1], (j >> 1) & 1, p.err, 16)) break;
-        if (!tc::mbar_wait(&full_v[j % KST], (j / KST) & 1, p.err, 17)) break;
-        tc::tc_fence_after();
-        const uint32_t p_addr = tc::smem_u32(sP + (j & 1) * TILE);
-        const uint32_t v_addr = tc::smem_u32(sV + (j % KST) * TILE);
+      auto issue_pv = [&](int x, int j) {  // O_x += P_x V_j
+        const uint32_t p_addr = tc::smem_u32(sP + x * TILE);
+        const uint32_t v_addr = tc::smem_u32(sR + ((2 * j + 1) % RING) * TILE);
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
-          tc::mma_f16_ss(tO, tc::smem_desc_k_sw128(p_addr + (kk >> 2) * CHUNK + (kk & 3) * 32),
+          tc::mma_f16_ss(tmem + 256 + x * 128, tc::smem_desc_k_sw128(p_addr + (kk >> 2) * CHUNK + (kk & 3) * 32),
                          tc::smem_desc_mn_sw128(v_addr + kk * 2048, CHUNK), idesc_pv, (j | kk) != 0);
         }
-        tc::mma_commit(&o_done[j & 1]);
-        tc::mma_commit(&kv_free[j % KST]);
+      };
+      bool ok = tc::mbar_wait(q_full, 0, p.err, 12) && tc::mbar_wait(&slot_full[0], 0, p.err, 13);
+      if (ok) {
+        tc::tc_fence_after();
+        for (int x = 0; x < nsub; ++x) issue_s(x, 0);
+        tc::mma_commit(&slot_free[0]);  // K_0 consumed once the S MMAs complete
       }
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        const int iv = 2 * j + 1, ik = 2 * j + 2;  // ring items V_j, K_{j+1}
+        if (!tc::mbar_wait(&slot_full[iv % RING], (iv / RING) & 1, p.err, 14)) break;
+        for (int x = 0; x < nsub; ++x) {
+          if (!tc::mbar_wait(&p_full[x], j & 1, p.err, 16)) { ok = false; break; }
+          tc::tc_fence_after();
+          issue_pv(x, j);
+          if (j + 1 < n_tiles) {
+            if (x == 0 && !tc::mbar_wait(&slot_full[ik % RING], (ik / RING) & 1, p.err, 15)) { ok = false; break; }
+            tc::tc_fence_after();
+            issue_s(x, j + 1);
+          }
+        }
+        if (!ok) break;
+        tc::mma_commit(&slot_free[iv % RING]);                    // V_j
+        if (j + 1 < n_tiles) tc::mma_commit(&slot_free[ik % RING]);  // K_{j+1}
+      }
+      tc::mma_commit(o_done);
       tc::mma_commit(drain);
       tc::mbar_wait_quiet(drain, 0);  // every MMA of this CTA has completed
     }
   } else {
-    // ---------------- softmax warps 0..3: thread = query row = TMEM lane
-    const int row = warp * 32 + lane;
-    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
-    const int qr = tile_m * BM + row;
+    // ---------------- softmax warps: 0-3 sub-tile A, 4-7 sub-tile B; thread = row = TMEM lane
+    const int x = warp >> 2;
+    const int row = (warp & 3) * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + x * 128 + lane_off, tO = tmem + 256 + x * 128 + lane_off;
+    const int qr = row0 + x * BM + row;
     const bool row_valid = qr < nq;
+    const bool active = x == 0 || has_b;
     {
       const char* src = reinterpret_cast<const char*>(p.q + ((long long)(q0 + (row_valid ? qr : 0)) * p.Hq + hq) * HD);
 #pragma unroll
-      for (int u = 0; u < 16; ++u) cp_async16_zfill(sQ + swz_off(row, u), src + u * 16, row_valid);
+      for (int u = 0; u < 16; ++u) cp_async16_zfill(sQ + x * TILE + swz_off(row, u), src + u * 16, row_valid);
       cp_async_commit();
       cp_async_wait<0>();
       tc::fence_proxy_async_smem();
@@ -216,44 +217,39 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
       if (lane == 0) tc::mbar_arrive(q_full);
     }
     const int qpos = pos0 + qr;
-    const int qpos_min = pos0 + tile_m * BM;
+    const int qpos_min = pos0 + row0 + x * BM;
     float m_used = -FLT_MAX, l = 0.f;
-    bool ok = true;
-    for (int j = 0; j < n_tiles; ++j) {
-      const int sb = j & 1;
-      ok = warp_ok(tc::mbar_wait(&s_full[sb], (j >> 1) & 1, p.err, 18), p.err);
+    bool ok = active;
+    for (int j = 0; ok && j < n_tiles; ++j) {
+      ok = warp_ok(tc::mbar_wait(&s_full[x], j & 1, p.err, 18), p.err);
       if (!ok) break;
       tc::tc_fence_after();
-      float x[BN];
+      float v[BN];
+      {
+        uint32_t r[4][32];
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tc::tmem_ld32(tmem + sb * 128 + lane_off + c * 32, r);
+        for (int c = 0; c < 4; ++c) tc::tmem_ld32(tS + c * 32, r[c]);
         tc::tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) x[c * 32 + i] = __uint_as_float(r[i]) * p.scale_log2;
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[c * 32 + i] = __uint_as_float(r[c][i]) * p.scale_log2;
       }
-      tc::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&s_free[sb]);
       const int n0 = j * BN;
       if (n0 + BN - 1 > qpos_min || n0 + BN > kv_len) {
 #pragma unroll
         for (int i = 0; i < BN; ++i)
-          if (n0 + i > qpos || n0 + i >= kv_len) x[i] = -FLT_MAX;
+          if (n0 + i > qpos || n0 + i >= kv_len) v[i] = -FLT_MAX;
       }
       float mt = -FLT_MAX;
 #pragma unroll
-      for (int i = 0; i < BN; ++i) mt = fmaxf(mt, x[i]);
+      for (int i = 0; i < BN; ++i) mt = fmaxf(mt, v[i]);
       if (j == 0) {
         m_used = mt;
       } else {
+        // PV_x(j-1) completed before S_x(j) was signalled: O_x may be rescaled now
         const bool rescale = mt > m_used + RESCALE_T;
         if (__any_sync(0xffffffffu, rescale)) {
-          // O must hold PV_{j-1} before it is rescaled
-          ok = warp_ok(tc::mbar_wait(&o_done[(j - 1) & 1], ((j - 1) >> 1) & 1, p.err, 19), p.err);
-          if (!ok) break;
-          tc::tc_fence_after();
           const float alpha = rescale ? exp2f(m_used - mt) : 1.f;
           if (rescale) {
             m_used = mt;
@@ -262,30 +258,25 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
 #pragma unroll 1
           for (int c = 0; c < HD / 32; ++c) {
             uint32_t r[32];
-            tc::tmem_ld32(tO + lane_off + c * 32, r);
+            tc::tmem_ld32(tO + c * 32, r);
             tc::tmem_ld_wait();
 #pragma unroll
             for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-            tc::tmem_st32(tO + lane_off + c * 32, r);
+            tc::tmem_st32(tO + c * 32, r);
           }
           tc::tmem_st_wait();
         }
       }
-      // P buffer sb was last read by PV_{j-2}
-      if (j >= 2) {
-        ok = warp_ok(tc::mbar_wait(&o_done[sb], ((j - 2) >> 1) & 1, p.err, 20), p.err);
-        if (!ok) break;
-      }
-      char* pbuf = sP + sb * TILE;
+      char* pbuf = sP + x * TILE;
 #pragma unroll
       for (int u = 0; u < 16; ++u) {
         float e[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          const float v = x[u * 8 + i];
-          e[i] = v == -FLT_MAX ? 0.f : exp2f(v - m_used);
-          l += e[i];
+          const float t = v[u * 8 + i];
+          e[i] = t == -FLT_MAX ? 0.f : exp2f(t - m_used);
         }
+        l += ((e[0] + e[1]) + (e[2] + e[3])) + ((e[4] + e[5]) + (e[6] + e[7]));
         *reinterpret_cast<uint4*>(pbuf + swz_off(row, u)) =
             make_uint4(pack_bf16x2(e[0], e[1]), pack_bf16x2(e[2], e[3]), pack_bf16x2(e[4], e[5]),
                        pack_bf16x2(e[6], e[7]));
@@ -293,10 +284,10 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
       tc::fence_proxy_async_smem();
       tc::tc_fence_before();
       __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&p_full[sb]);
+      if (lane == 0) tc::mbar_arrive(&p_full[x]);
     }
     // ---------------- epilogue: O / l -> out
-    if (ok) ok = warp_ok(tc::mbar_wait(&o_done[(n_tiles - 1) & 1], ((n_tiles - 1) >> 1) & 1, p.err, 21), p.err);
+    if (ok) ok = warp_ok(tc::mbar_wait(o_done, 0, p.err, 21), p.err);
     if (ok) {
       tc::tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
@@ -304,13 +295,13 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
 #pragma unroll 1
       for (int c = 0; c < HD / 32; ++c) {
         uint32_t r[32];
-        tc::tmem_ld32(tO + lane_off + c * 32, r);
+        tc::tmem_ld32(tO + c * 32, r);
         tc::tmem_ld_wait();
         if (row_valid) {
 #pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            const uint32_t* w = &r[v * 8];
-            *reinterpret_cast<uint4*>(dst + c * 32 + v * 8) =
+          for (int w8 = 0; w8 < 4; ++w8) {
+            const uint32_t* w = &r[w8 * 8];
+            *reinterpret_cast<uint4*>(dst + c * 32 + w8 * 8) =
                 make_uint4(pack_bf16x2(__uint_as_float(w[0]) * inv, __uint_as_float(w[1]) * inv),
                            pack_bf16x2(__uint_as_float(w[2]) * inv, __uint_as_float(w[3]) * inv),
                            pack_bf16x2(__uint_as_float(w[4]) * inv, __uint_as_float(w[5]) * inv),
@@ -322,7 +313,7 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
   }
   tc::tc_fence_before();
   __syncthreads();
-  if (warp == 5) tc::tmem_dealloc(tmem, 512);
+  if (warp == 9) tc::tmem_dealloc(tmem, 512);
 }
 
 void make_page_map(CUtensorMap* map, const void* ptr, int64_t rows) {
@@ -377,7 +368,7 @@ void prefill_attention_tc(torch::Tensor q, int64_t k, int64_t v, int64_t blk_str
     AXR_CHECK_CUDA(cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
     attr = true;
   }
-  dim3 grid((max_q + BM - 1) / BM, Hq, B);
+  dim3 grid((max_q + 2 * BM - 1) / (2 * BM), Hq, B);
   prefill_tc_kernel<<<grid, THREADS, SMEM, at::cuda::getCurrentCUDAStream()>>>(tk, tv, p);
   AXR_CHECK_CUDA(cudaGetLastError());
 }
