@@ -16,6 +16,7 @@ import torch
 
 from .. import ops
 from ..ops.kvcache import KVCache
+from ..parallel.ep import EpMoE, experts_reference, route
 from .config import ModelConfig
 
 
@@ -28,8 +29,8 @@ class LayerWeights:
     w_gate_up: Optional[torch.Tensor] = None  # dense MLP [H, 2F]
     w_down: Optional[torch.Tensor] = None     # [F, H]
     w_router: Optional[torch.Tensor] = None   # MoE [H, E]
-    e_gate_up: Optional[torch.Tensor] = None  # [E, H, 2F]
-    e_down: Optional[torch.Tensor] = None     # [E, F, H]
+    w13: Optional[torch.Tensor] = None        # this GPU's experts [E_l, 2F, H], gate/up interleaved per 128 rows
+    w2: Optional[torch.Tensor] = None         # [E_l, H, F]
 
 
 @dataclass
@@ -50,11 +51,18 @@ class AttnMeta:
 
 class LlamaModel:
     def __init__(self, cfg: ModelConfig, device="cpu", dtype=torch.bfloat16, seed: int = 0,
-                 init_std: float = 0.02, layers: Optional[int] = None):
+                 init_std: float = 0.02, layers: Optional[int] = None, ep_info=None, ep_max_tokens: int = 16384):
+        """``ep_info`` (a ``DistInfo``) splits the experts of an MoE model over the GPUs of
+        an expert-parallel group: this process keeps ``E / world`` of them and every MoE
+        layer runs the fused dispatch / grouped GEMM / combine kernels."""
         self.cfg = cfg
         self.device = torch.device(device)
         self.dtype = dtype
+        self.ep = None
+        ep_world, ep_rank = (ep_info.world, ep_info.rank) if ep_info is not None else (1, 0)
+        self.expert0 = 0
         g = torch.Generator(device=self.device).manual_seed(seed)
+        g_exp = torch.Generator(device=self.device).manual_seed(seed * 7919 + 17 + ep_rank)
         H, F = cfg.hidden, cfg.ffn
         n_layers = layers if layers is not None else cfg.num_layers
 
@@ -66,14 +74,20 @@ class LlamaModel:
         def ones(n):
             return torch.ones(n, dtype=dtype, device=self.device)
 
+        def rnd_g(gen, *shape, std=init_std):
+            t = torch.empty(*shape, dtype=dtype, device=self.device)
+            t.normal_(0.0, std, generator=gen)
+            return t
+
         self.embed = rnd(cfg.vocab, H, std=1.0)
         self.layers: List[LayerWeights] = []
         for _ in range(n_layers):
             lw = LayerWeights(ones(H), rnd(H, cfg.q_size + 2 * cfg.kv_size), rnd(cfg.q_size, H), ones(H))
             if cfg.is_moe:
+                E_l = cfg.num_experts // ep_world
                 lw.w_router = rnd(H, cfg.num_experts)
-                lw.e_gate_up = rnd(cfg.num_experts, H, 2 * F)
-                lw.e_down = rnd(cfg.num_experts, F, H)
+                lw.w13 = rnd_g(g_exp, E_l, 2 * F, H)
+                lw.w2 = rnd_g(g_exp, E_l, H, F)
             else:
                 lw.w_gate_up = rnd(H, 2 * F)
                 lw.w_down = rnd(F, H)
@@ -83,6 +97,13 @@ class LlamaModel:
         self.cos_sin = ops.rope_cos_sin(min(cfg.max_position, 1 << 17), cfg.head_dim, cfg.rope_theta,
                                         cfg.rope_scaling, self.device)
         self.scale = 1.0 / math.sqrt(cfg.head_dim)
+        if cfg.is_moe:
+            self.expert0 = ep_rank * (cfg.num_experts // ep_world)
+            if self.device.type == "cuda" or ep_world > 1:
+                from ..parallel.dist import DistInfo
+
+                info = ep_info or DistInfo(0, 1, 0, 1, self.device)
+                self.ep = EpMoE(info, cfg.num_experts, H, F, cfg.top_k, ep_max_tokens)
 
     @property
     def num_layers(self) -> int:
@@ -92,7 +113,7 @@ class LlamaModel:
         n = self.embed.numel() + self.lm_head.numel() + self.final_norm.numel()
         for lw in self.layers:
             for t in (lw.attn_norm, lw.wqkv, lw.wo, lw.mlp_norm, lw.w_gate_up, lw.w_down, lw.w_router,
-                      lw.e_gate_up, lw.e_down):
+                      lw.w13, lw.w2):
                 if t is not None:
                     n += t.numel()
         return n * 2
@@ -105,24 +126,10 @@ class LlamaModel:
 
     def _moe(self, lw: LayerWeights, x: torch.Tensor) -> torch.Tensor:
         cfg = self.cfg
-        logits = (x @ lw.w_router).float()
-        w, idx = torch.topk(logits, cfg.top_k, dim=-1)
-        w = torch.softmax(w, dim=-1)  # Mixtral renormalises over the selected experts
-        out = torch.zeros(x.shape[0], cfg.hidden, dtype=torch.float32, device=x.device)
-        flat = idx.flatten()
-        order = torch.argsort(flat)
-        counts = torch.bincount(flat, minlength=cfg.num_experts).tolist()
-        tok = order // cfg.top_k
-        start = 0
-        for e, c in enumerate(counts):
-            if c == 0:
-                continue
-            sel = order[start:start + c]
-            t = tok[start:start + c]
-            h = ops.silu_mul(x[t] @ lw.e_gate_up[e]) @ lw.e_down[e]
-            out.index_add_(0, t, h.float() * w.flatten()[sel, None])
-            start += c
-        return out.to(x.dtype)
+        idx, w = route(x @ lw.w_router, cfg.top_k)
+        if self.ep is not None:
+            return self.ep.forward(x, idx, w, lw.w13, lw.w2)
+        return experts_reference(x, idx, w, lw.w13, lw.w2, self.expert0).to(x.dtype)
 
     # ------------------------------------------------------------------ forward
     def forward(self, tokens: torch.Tensor, meta: AttnMeta, cache: KVCache) -> torch.Tensor:

@@ -37,6 +37,17 @@ void gemm_tp(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t mode, 
 void prefill_attention_tc(torch::Tensor q, int64_t k, int64_t v, int64_t blk_stride, int64_t head_stride,
                           int64_t num_blocks, torch::Tensor block_table, torch::Tensor cu_q, torch::Tensor seq_lens,
                           int64_t Hkv, double scale, int64_t max_q, torch::Tensor out, torch::Tensor err);
+void moe_dispatch(torch::Tensor x, torch::Tensor topk_idx, torch::Tensor topk_w, int64_t E_l, int64_t rank,
+                  int64_t world, int64_t epoch, int64_t cap_rows, torch::Tensor pair_pos, torch::Tensor gcount,
+                  torch::Tensor grid_bar, torch::Tensor peers, torch::Tensor cnt_all, torch::Tensor cnt_flag,
+                  torch::Tensor err);
+void moe_gemm(torch::Tensor a, torch::Tensor w, int64_t mode, int64_t E_l, int64_t rank, int64_t world,
+              int64_t epoch, torch::Tensor cnt_all, torch::Tensor cnt_flag, torch::Tensor arr_flag,
+              c10::optional<torch::Tensor> h, c10::optional<torch::Tensor> recv_meta,
+              c10::optional<torch::Tensor> recv_w, c10::optional<torch::Tensor> peer_comb,
+              c10::optional<torch::Tensor> peer_comb_flag, torch::Tensor done_ctr, torch::Tensor err);
+void moe_combine(torch::Tensor comb, torch::Tensor out, torch::Tensor comb_flag, int64_t world, int64_t epoch,
+                 int64_t K, torch::Tensor err);
 }  // namespace axr
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -53,4 +64,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("spec_verify", &axr::spec_verify);
   m.def("gemm_tc", &axr::gemm_tc);
   m.def("gemm_tp", &axr::gemm_tp);
+  m.def("moe_dispatch", &axr::moe_dispatch);
+  m.def("moe_gemm", &axr::moe_gemm);
+  m.def("moe_combine", &axr::moe_combine);
 }

@@ -30,9 +30,12 @@
 #include <ATen/cuda/CUDAContext.h>
 
 #include "common.cuh"
+#include "peer_sync.cuh"
 #include "tc_common.cuh"
 
 namespace axr {
+
+__device__ __forceinline__ void comm_bar() { asm volatile("bar.sync 2, 128;" ::: "memory"); }
 
 constexpr int TBM = 128, TBN = 256, TBK = 64, TST = 4;
 constexpr int TA_BYTES = TBM * TBK * 2, TB_BYTES = TBN * TBK * 2;
@@ -65,42 +68,6 @@ struct TpArgs {
   __nv_bfloat16* out_rs;       // [rows_per_rank, N] reduced output of this GPU
   volatile int* err;
 };
-
-__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
-  int v;
-  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ int ld_acquire_sys(const int* p) {
-  int v;
-  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void st_release_gpu(int* p, int v) {
-  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ void st_release_sys(int* p, int v) {
-  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ void red_add_release_sys(int* p, int v) {
-  asm volatile("red.release.sys.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
-__device__ __forceinline__ void comm_bar() { asm volatile("bar.sync 2, 128;" ::: "memory"); }
-
-// bounded wait until *p >= target
-template <bool SYS>
-__device__ __forceinline__ bool wait_geq(const int* p, int target, volatile int* err, int code) {
-  const unsigned long long t0 = tc::globaltimer();
-  while ((SYS ? ld_acquire_sys(p) : ld_acquire_gpu(p)) < target) {
-    if (*err != 0) return false;
-    if (tc::globaltimer() - t0 > tc::kWaitLimitNs) {
-      atomicCAS(const_cast<int*>(err), 0, code);
-      return false;
-    }
-  }
-  return true;
-}
 
 // Thread 0 of the comm warps waits; the outcome reaches all 128 comm threads through
 // shared memory and the barrier, so the four warps always take the same branch.
