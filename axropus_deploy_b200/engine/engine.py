@@ -88,6 +88,9 @@ class EngineConfig:
     capture_on_miss: bool = True
     amf_min_tokens: int = 64
     cuda_graphs: bool = False
+    # expert parallelism: every GPU runs exactly one prefill and one decode forward per
+    # step (empty when it has nothing to do) so the MoE collectives of all GPUs line up
+    lockstep: bool = False
 
 
 class LLMEngine:
@@ -164,10 +167,20 @@ class LLMEngine:
         admitted = self._admit()
         if admitted:
             done += self._prefill(admitted)
+        elif self.cfg.lockstep:
+            self._idle_forward()
         decoding = [r for r in self.running if r.state == "running" and r not in admitted]
         if decoding:
             done += self._decode(decoding)
+        elif self.cfg.lockstep:
+            self._idle_forward()
         return done
+
+    def _idle_forward(self) -> None:
+        empty = torch.empty(0, dtype=torch.int32, device=self.device)
+        meta = AttnMeta(mode="decode", positions=empty, slots=empty, block_table=self.block_table[:0],
+                        seq_lens=empty)
+        self.model.forward(empty, meta, self.cache)
 
     # ------------------------------------------------------------------ admission
     def _amf_limit(self, r: Request) -> int:

@@ -136,6 +136,16 @@ class LlamaModel:
         """tokens [T] -> logits of the rows in ``meta.logits_idx`` ([B, vocab], fp32 on GPU)."""
         cfg = self.cfg
         T = tokens.shape[0]
+        if T == 0:
+            # nothing to compute here, but an expert-parallel group needs every GPU in every
+            # MoE layer: take part with no tokens
+            if self.ep is not None:
+                x = torch.empty(0, cfg.hidden, dtype=self.dtype, device=self.device)
+                idx = torch.empty(0, cfg.top_k, dtype=torch.int32, device=self.device)
+                w = torch.empty(0, cfg.top_k, dtype=torch.float32, device=self.device)
+                for lw in self.layers:
+                    self.ep.forward(x, idx, w, lw.w13, lw.w2)
+            return torch.empty(0, cfg.vocab, dtype=torch.float32, device=self.device)
         h = self.embed[tokens.long()]
         residual = h.clone()
         x = ops.rmsnorm(h, self.layers[0].attn_norm if self.layers else self.final_norm, cfg.rms_eps)
