@@ -295,8 +295,10 @@ class LLMEngine:
 
     def _prefill(self, reqs: List[Request]) -> List[Request]:
         toks, pos, slots, cu, lens = [], [], [], [0], []
+        prefilled_from = {}
         for r in reqs:
             s = r.num_computed
+            prefilled_from[r.req_id] = s
             n = len(r.prompt) - s
             toks.extend(r.prompt[s:])
             p = np.arange(s, len(r.prompt))
@@ -330,9 +332,11 @@ class LLMEngine:
             full = len(r.prompt) // PAGE
             hs = r.hashes if len(r.hashes) >= full else block_hashes(r.prompt_np, full)
             self.bm.register_computed(r.blocks[:full], hs[:full])
-            if self.amf is not None and self.cfg.capture_on_miss and r.amf_tier == "cold":
+            # capture when this step computed a real part of the prefix itself: a cold miss,
+            # or a shorter hit (G2 or AMF) that this prompt extended
+            if self.amf is not None and self.cfg.capture_on_miss:
                 lim = self._amf_limit(r)
-                if lim >= self.cfg.amf_min_tokens:
+                if lim >= self.cfg.amf_min_tokens and lim - prefilled_from[r.req_id] >= self.cfg.amf_min_tokens:
                     self.amf.capture(r.prompt_np[:lim], self.cache, torch.tensor(r.blocks[: lim // PAGE],
                                                                               dtype=torch.int32))
             r.num_computed = len(r.prompt)
