@@ -38,6 +38,7 @@ class LMCacheAdapter:
         self._mem: "OrderedDict[str, torch.Tensor]" = OrderedDict()
         self._bytes = 0
         self._lock = threading.RLock()
+        self._pending: Dict[str, Any] = {}  # key -> CUDA event of an in-flight device->host copy
         self._engine = None
         self.stat = {"hits": 0, "misses": 0, "stores": 0, "evictions": 0, "errors": 0}
         if self.enabled:
@@ -66,6 +67,9 @@ class LMCacheAdapter:
                     out = self._mem.get(key)
                     if out is not None:
                         self._mem.move_to_end(key)
+                        ev = self._pending.pop(key, None)
+                        if ev is not None:
+                            ev.synchronize()
             except Exception as exc:
                 self.stat["errors"] += 1
                 log.warning("LMCache lookup failed for %s: %s", key, exc)
@@ -94,15 +98,23 @@ class LMCacheAdapter:
                     torch.save(pages.cpu(), tmp)
                     os.replace(tmp, self._file(key))
                 else:
-                    host = pages if pages.device.type == "cpu" else pages.to("cpu", non_blocking=False)
-                    if torch.cuda.is_available() and not host.is_pinned():
-                        host = host.pin_memory()
+                    if pages.device.type == "cpu":
+                        host = pages
+                    else:
+                        # asynchronous device->host copy into pinned memory (the caching host
+                        # allocator reuses blocks); a lookup waits for the copy's event
+                        host = torch.empty(pages.shape, dtype=pages.dtype, pin_memory=True)
+                        host.copy_(pages, non_blocking=True)
+                        ev = torch.cuda.Event()
+                        ev.record()
+                        self._pending[key] = ev
                     n = host.numel() * host.element_size()
                     if key in self._mem:
                         old = self._mem.pop(key)
                         self._bytes -= old.numel() * old.element_size()
                     while self._mem and self._bytes + n > self.max_bytes:
-                        _, ev = self._mem.popitem(last=False)
+                        old_key, ev = self._mem.popitem(last=False)
+                        self._pending.pop(old_key, None)
                         self._bytes -= ev.numel() * ev.element_size()
                         self.stat["evictions"] += 1
                     self._mem[key] = host
@@ -123,6 +135,7 @@ class LMCacheAdapter:
                 except FileNotFoundError:
                     return False
             t = self._mem.pop(key, None)
+            self._pending.pop(key, None)
             if t is None:
                 return False
             self._bytes -= t.numel() * t.element_size()

@@ -174,7 +174,19 @@ class LLMEngine:
             done += self._decode(decoding)
         elif self.cfg.lockstep:
             self._idle_forward()
+        if self.device.type == "cuda":
+            self._check_kernel_errors()
         return done
+
+    def _check_kernel_errors(self) -> None:
+        """The tcgen05 / peer kernels record a code instead of hanging when a bounded wait
+        runs out; their outputs are then incomplete, so the step must not be used."""
+        from ..ops.gemm import error_flag
+
+        code = int(error_flag(self.device)[0].item())
+        if code:
+            raise RuntimeError(f"a fused kernel gave up waiting (error code {code}); outputs of this step are "
+                               "invalid (a peer GPU stopped or fell behind by more than the wait bound)")
 
     def _idle_forward(self) -> None:
         empty = torch.empty(0, dtype=torch.int32, device=self.device)

@@ -54,6 +54,7 @@ struct TpArgs {
   int rank, world, rows_per_rank;  // AG/RS: M = world * rows_per_rank
   int mode;
   int epoch;  // 1, 2, 3, ... per call of this mode on this communicator (same on every GPU)
+  unsigned long long wait_ns;  // bound of every wait in this kernel (peer-dependent)
   // AG
   const int64_t* peer_a;  // [world] base addresses of the peers' A shards [rows_per_rank, K]
   __nv_bfloat16* staging;   // local [M, K]; the TMA map of A covers it
@@ -72,8 +73,8 @@ struct TpArgs {
 // Thread 0 of the comm warps waits; the outcome reaches all 128 comm threads through
 // shared memory and the barrier, so the four warps always take the same branch.
 __device__ __forceinline__ bool comm_wait(const int* p, int target, volatile int* err, int code, int ct,
-                                          volatile int* shared_ok) {
-  if (ct == 0) *shared_ok = wait_geq<true>(p, target, err, code) ? 1 : 0;
+                                          volatile int* shared_ok, unsigned long long limit) {
+  if (ct == 0) *shared_ok = wait_geq<true>(p, target, err, code, limit) ? 1 : 0;
   comm_bar();
   const bool ok = *shared_ok != 0;
   comm_bar();  // nobody overwrites shared_ok before everyone has read it
@@ -167,13 +168,13 @@ __global__ void __launch_bounds__(TP_THREADS, 1) gemm_tp_kernel(const __grid_con
         int mt, nt;
         tp_tile(g, t, num_n, num_m, first_m, mt, nt);
         if (g.mode == MODE_AG && (mt * TBM) / g.rows_per_rank != g.rank) {
-          for (int ch = 0; ok && ch < AG_CH; ++ch) ok = wait_geq<false>(g.flags + mt * AG_CH + ch, g.epoch, g.err, 5);
+          for (int ch = 0; ok && ch < AG_CH; ++ch) ok = wait_geq<false>(g.flags + mt * AG_CH + ch, g.epoch, g.err, 5, g.wait_ns);
           if (!ok) break;
           fence_proxy_async_global();  // order the TMA reads after the pulled rows
         }
         for (int kt = 0; kt < num_k; ++kt, ++it) {
           const int s = it % TST;
-          if (it >= TST && !tc::mbar_wait(&empty[s], ((it / TST) + 1) & 1, g.err, 1)) { ok = false; break; }
+          if (it >= TST && !tc::mbar_wait(&empty[s], ((it / TST) + 1) & 1, g.err, 1, g.wait_ns)) { ok = false; break; }
           tc::mbar_arrive_expect_tx(&full[s], TA_BYTES + TB_BYTES);
           tc::tma_load_2d(sA + s * TA_BYTES, &tmA, kt * TBK, mt * TBM, &full[s]);
           tc::tma_load_2d(sB + s * TB_BYTES, &tmB, kt * TBK, nt * TBN, &full[s]);
@@ -189,12 +190,12 @@ __global__ void __launch_bounds__(TP_THREADS, 1) gemm_tp_kernel(const __grid_con
       int it = 0, i = 0;
       for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
         const int buf = i & 1;
-        if (i >= 2 && !tc::mbar_wait(&acce[buf], ((i >> 1) + 1) & 1, g.err, 6)) break;
+        if (i >= 2 && !tc::mbar_wait(&acce[buf], ((i >> 1) + 1) & 1, g.err, 6, g.wait_ns)) break;
         tc::tc_fence_after();
         bool ok = true;
         for (int kt = 0; kt < num_k; ++kt, ++it) {
           const int s = it % TST;
-          if (!tc::mbar_wait(&full[s], (it / TST) & 1, g.err, 2)) { ok = false; break; }
+          if (!tc::mbar_wait(&full[s], (it / TST) & 1, g.err, 2, g.wait_ns)) { ok = false; break; }
           tc::tc_fence_after();
           const uint32_t a_addr = tc::smem_u32(sA + s * TA_BYTES), b_addr = tc::smem_u32(sB + s * TB_BYTES);
 #pragma unroll
@@ -219,7 +220,7 @@ __global__ void __launch_bounds__(TP_THREADS, 1) gemm_tp_kernel(const __grid_con
       int mt, nt;
       tp_tile(g, t, num_n, num_m, first_m, mt, nt);
       const int buf = i & 1;
-      bool ok = tc::mbar_wait(&accf[buf], (i >> 1) & 1, g.err, 3);
+      bool ok = tc::mbar_wait(&accf[buf], (i >> 1) & 1, g.err, 3, g.wait_ns);
       ok = __all_sync(0xffffffffu, ok) && __shfl_sync(0xffffffffu, *g.err, 0) == 0;
       tc::tc_fence_after();
       if (!ok) break;
@@ -297,7 +298,7 @@ __global__ void __launch_bounds__(TP_THREADS, 1) gemm_tp_kernel(const __grid_con
       for (int item = blockIdx.x; item < items; item += gridDim.x) {
         const int b = (first_m + lbk + item / AG_CH) % nb, ch = item % AG_CH;
         const int p = (b * TBM) / g.rows_per_rank;
-        if (!comm_wait(g.ready + p, g.epoch, g.err, 7, ct, comm_ok)) break;
+        if (!comm_wait(g.ready + p, g.epoch, g.err, 7, ct, comm_ok, g.wait_ns)) break;
         const long long r0 = (long long)b * TBM - (long long)p * g.rows_per_rank + ch * 16;
         const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(g.peer_a[p]) + r0 * g.K * 2);
         uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<char*>(g.staging) +
@@ -326,7 +327,7 @@ __global__ void __launch_bounds__(TP_THREADS, 1) gemm_tp_kernel(const __grid_con
       const __nv_bfloat16* rbase = g.recv + (long long)parity * g.world * slot;
       for (int item = blockIdx.x; item < items; item += gridDim.x) {
         const int lb = item / RS_CH, ch = item % RS_CH;
-        if (!comm_wait(g.cnt + 2 * lb + parity, target, g.err, 8, ct, comm_ok)) break;
+        if (!comm_wait(g.cnt + 2 * lb + parity, target, g.err, 8, ct, comm_ok, g.wait_ns)) break;
         const long long e0 = ((long long)lb * TBM + ch * 8) * g.N;
         for (long long v = ct; v < vecs; v += 128 * 2) {
           float acc[2][8];
@@ -419,6 +420,7 @@ void gemm_tp(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t mode, 
   g.mode = static_cast<int>(mode);
   g.epoch = static_cast<int>(epoch);
   g.err = err.data_ptr<int>();
+  g.wait_ns = peer_wait_ns();
   const void* a_ptr;
   int64_t lda;
   int comm_items = 0;

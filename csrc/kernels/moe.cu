@@ -62,13 +62,14 @@ struct DispatchArgs {
   const int64_t* peer_recv_w;     // [world] -> float [cap_rows]
   const int64_t* peer_arr_flag;   // [world] -> int [world src]
   volatile int* err;
+  unsigned long long wait_ns;
 };
 
 __device__ __forceinline__ bool cta_wait_all(const int* flags, int n, int target, volatile int* err, int code,
-                                             int* s_ok) {
+                                             int* s_ok, unsigned long long limit) {
   if (threadIdx.x == 0) {
     bool ok = true;
-    for (int s = 0; ok && s < n; ++s) ok = wait_geq<true>(flags + s, target, err, code);
+    for (int s = 0; ok && s < n; ++s) ok = wait_geq<true>(flags + s, target, err, code, limit);
     *s_ok = ok ? 1 : 0;
   }
   __syncthreads();
@@ -97,7 +98,7 @@ __global__ void __launch_bounds__(256) moe_dispatch_kernel(DispatchArgs a) {
   __syncthreads();
   if (threadIdx.x == 0) {
     atomicAdd(&a.grid_bar[0], 1);
-    s_ok = wait_geq<false>(&a.grid_bar[0], gridDim.x, a.err, 31) ? 1 : 0;
+    s_ok = wait_geq<false>(&a.grid_bar[0], gridDim.x, a.err, 31, a.wait_ns) ? 1 : 0;
   }
   __syncthreads();
   if (!s_ok) return;
@@ -114,7 +115,7 @@ __global__ void __launch_bounds__(256) moe_dispatch_kernel(DispatchArgs a) {
       for (int p = 0; p < W; ++p) st_release_sys(reinterpret_cast<int*>(a.peer_cnt_flag[p]) + a.rank, a.epoch);
   }
   // 3. every CTA: wait for all sources' counts, derive this GPU's base row per (dst, e)
-  if (!cta_wait_all(a.cnt_flag, W, a.epoch, a.err, 32, &s_ok)) return;
+  if (!cta_wait_all(a.cnt_flag, W, a.epoch, a.err, 32, &s_ok, a.wait_ns)) return;
   if (threadIdx.x < W) {
     const int d = threadIdx.x;
     int off = 0;
@@ -189,6 +190,7 @@ struct GemmArgs {
   const int64_t* peer_comb_flag;  // [world] -> int [world]
   int* done_ctr;                  // local counter, zero on entry; reset by the last CTA
   volatile int* err;
+  unsigned long long wait_ns;
 };
 
 struct TileMap {
@@ -224,7 +226,7 @@ __global__ void __launch_bounds__(THREADS, 1) moe_gemm_kernel(const __grid_const
   // ---- tile map from the count matrix (wait until every source has published it)
   if (threadIdx.x == 0) {
     bool ok = true;
-    for (int s = 0; ok && s < W; ++s) ok = wait_geq<true>(g.cnt_flag + s, g.epoch, g.err, 41);
+    for (int s = 0; ok && s < W; ++s) ok = wait_geq<true>(g.cnt_flag + s, g.epoch, g.err, 41, g.wait_ns);
     *s_ok = ok ? 1 : 0;
     if (ok) {
       int off = 0, mb = 0;
@@ -297,7 +299,7 @@ __global__ void __launch_bounds__(THREADS, 1) moe_gemm_kernel(const __grid_const
           for (int s = 0; ok && s < W; ++s) {
             if (arrived >> s & 1) continue;
             if (tm.soff[e][s + 1] <= r0 || tm.soff[e][s] >= r0 + BM) continue;  // no rows of s here
-            ok = wait_geq<true>(g.arr_flag + s, g.epoch, g.err, 43);
+            ok = wait_geq<true>(g.arr_flag + s, g.epoch, g.err, 43, g.wait_ns);
             if (ok) arrived |= 1u << s;
           }
           if (!ok) break;
@@ -306,7 +308,7 @@ __global__ void __launch_bounds__(THREADS, 1) moe_gemm_kernel(const __grid_const
         const int ya = tm.roff[e] + r0, yb = e * g.N + nt * BN;
         for (int kt = 0; kt < num_k; ++kt, ++it) {
           const int s = it % ST;
-          if (it >= ST && !tc::mbar_wait(&empty[s], ((it / ST) + 1) & 1, g.err, 44)) { ok = false; break; }
+          if (it >= ST && !tc::mbar_wait(&empty[s], ((it / ST) + 1) & 1, g.err, 44, g.wait_ns)) { ok = false; break; }
           tc::mbar_arrive_expect_tx(&full[s], A_BYTES + B_BYTES);
           tc::tma_load_2d(sA + s * A_BYTES, &tmA, kt * BK, ya, &full[s]);
           tc::tma_load_2d(sB + s * B_BYTES, &tmB, kt * BK, yb, &full[s]);
@@ -322,12 +324,12 @@ __global__ void __launch_bounds__(THREADS, 1) moe_gemm_kernel(const __grid_const
       int it = 0, i = 0;
       for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
         const int buf = i & 1;
-        if (i >= 2 && !tc::mbar_wait(&acce[buf], ((i >> 1) + 1) & 1, g.err, 45)) break;
+        if (i >= 2 && !tc::mbar_wait(&acce[buf], ((i >> 1) + 1) & 1, g.err, 45, g.wait_ns)) break;
         tc::tc_fence_after();
         bool ok = true;
         for (int kt = 0; kt < num_k; ++kt, ++it) {
           const int s = it % ST;
-          if (!tc::mbar_wait(&full[s], (it / ST) & 1, g.err, 46)) { ok = false; break; }
+          if (!tc::mbar_wait(&full[s], (it / ST) & 1, g.err, 46, g.wait_ns)) { ok = false; break; }
           tc::tc_fence_after();
           const uint32_t a_addr = tc::smem_u32(sA + s * A_BYTES), b_addr = tc::smem_u32(sB + s * B_BYTES);
 #pragma unroll
@@ -353,7 +355,7 @@ __global__ void __launch_bounds__(THREADS, 1) moe_gemm_kernel(const __grid_const
       const int e = expert_of(tm, El, mb);
       const int r0 = (mb - tm.mb0[e]) * BM;
       const int buf = i & 1;
-      bool ok = tc::mbar_wait(&accf[buf], (i >> 1) & 1, g.err, 47);
+      bool ok = tc::mbar_wait(&accf[buf], (i >> 1) & 1, g.err, 47, g.wait_ns);
       ok = __all_sync(0xffffffffu, ok) && __shfl_sync(0xffffffffu, *g.err, 0) == 0;
       tc::tc_fence_after();
       if (!ok) break;
@@ -444,9 +446,9 @@ __global__ void __launch_bounds__(THREADS, 1) moe_gemm_kernel(const __grid_const
 __global__ void __launch_bounds__(256) moe_combine_kernel(const __nv_bfloat16* __restrict__ comb,
                                                           __nv_bfloat16* __restrict__ out, const int* comb_flag,
                                                           int world, int epoch, int T, int K, int H,
-                                                          volatile int* err) {
+                                                          volatile int* err, unsigned long long wait_ns) {
   __shared__ int s_ok;
-  if (!cta_wait_all(comb_flag, world, epoch, err, 51, &s_ok)) return;
+  if (!cta_wait_all(comb_flag, world, epoch, err, 51, &s_ok, wait_ns)) return;
   const long long n8 = (long long)T * H / 8;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
     const long long t = (i * 8) / H, c = (i * 8) % H;
@@ -522,6 +524,7 @@ void moe_dispatch(torch::Tensor x, torch::Tensor topk_idx, torch::Tensor topk_w,
   a.cnt_all = cnt_all.data_ptr<int>();
   a.cnt_flag = cnt_flag.data_ptr<int>();
   a.err = err.data_ptr<int>();
+  a.wait_ns = peer_wait_ns();
   int per_sm = 0;
   cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, moe_dispatch_kernel, 256, 0);
   const int grid = std::max(1, std::min(sm_count(x.device().index()) * std::max(1, per_sm), 4 * 148));
@@ -561,6 +564,7 @@ void moe_gemm(torch::Tensor a, torch::Tensor w, int64_t mode, int64_t E_l, int64
   g.arr_flag = arr_flag.data_ptr<int>();
   g.done_ctr = done_ctr.data_ptr<int>();
   g.err = err.data_ptr<int>();
+  g.wait_ns = peer_wait_ns();
   if (mode == 0) {
     TORCH_CHECK(h.has_value() && h->size(0) >= a.size(0) && h->size(1) == N / 2 && h->stride(1) == 1,
                 "moe_gemm: h [cap_rows, N/2]");
@@ -597,7 +601,7 @@ void moe_combine(torch::Tensor comb, torch::Tensor out, torch::Tensor comb_flag,
                                         static_cast<int>(((int64_t)T * H / 8 + 255) / 256)));
   moe_combine_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(comb.data_ptr()), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
-      comb_flag.data_ptr<int>(), world, epoch, T, K, H, err.data_ptr<int>());
+      comb_flag.data_ptr<int>(), world, epoch, T, K, H, err.data_ptr<int>(), peer_wait_ns());
   AXR_CHECK_CUDA(cudaGetLastError());
 }
 

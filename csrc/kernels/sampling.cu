@@ -28,7 +28,8 @@ __device__ int row_argmax(const T* __restrict__ row, int V) {
   float best = -FLT_MAX;
   int bi = 0x7fffffff;
   for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    const float x = to_f<T>(row[i]);
+    float x = to_f<T>(row[i]);
+    if ((__float_as_uint(x) & 0x7fffffffu) > 0x7f800000u) x = -FLT_MAX;  // NaN never wins
     if (x > best || (x == best && i < bi)) { best = x; bi = i; }
   }
 #pragma unroll
@@ -53,7 +54,7 @@ __device__ int row_argmax(const T* __restrict__ row, int V) {
     }
   }
   __syncthreads();
-  return bi;
+  return bi == 0x7fffffff ? 0 : bi;  // a row with no finite entry still yields a valid token
 }
 
 template <typename T>

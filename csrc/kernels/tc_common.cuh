@@ -16,7 +16,7 @@
 namespace axr {
 namespace tc {
 
-constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s per wait
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s per wait (waits inside one GPU)
 
 __device__ __forceinline__ unsigned long long globaltimer() {
   unsigned long long t;
@@ -58,13 +58,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
 
 // Bounded wait; returns false (and records `code` in *err) when the limit is reached
 // or another role has already failed.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, volatile int* err, int code) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, volatile int* err, int code,
+                                          unsigned long long limit = kWaitLimitNs) {
   if (mbar_try_wait(bar, phase)) return true;
   const unsigned long long t0 = globaltimer();
   while (true) {
     if (mbar_try_wait(bar, phase)) return true;
     if (*err != 0) return false;
-    if (globaltimer() - t0 > kWaitLimitNs) {
+    if (globaltimer() - t0 > limit) {
       atomicCAS(const_cast<int*>(err), 0, code);
       return false;
     }
