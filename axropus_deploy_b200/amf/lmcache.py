@@ -26,6 +26,41 @@ from ..config import env_bool, env_str
 log = logging.getLogger(__name__)
 
 
+class PinnedPageArena:
+    """One pinned host buffer of page slots handed out as contiguous runs (first fit).
+
+    Pinning host memory is slow (it page-locks every page); doing it per stored prefix
+    would stall the serving step for hundreds of milliseconds. The arena is pinned once
+    and entries are runs of its slots, so a store is one asynchronous device->host DMA
+    and a promotion back to the GPU one host->device DMA."""
+
+    def __init__(self, n_pages: int, page_shape, dtype=torch.bfloat16):
+        self.page_shape = tuple(page_shape)
+        self.n_pages = n_pages
+        self.buf = torch.empty(n_pages, *self.page_shape, dtype=dtype, pin_memory=torch.cuda.is_available())
+        self.free = [(0, n_pages)]  # sorted, non-adjacent (start, length) runs
+
+    def alloc(self, n: int) -> Optional[int]:
+        for i, (s, ln) in enumerate(self.free):
+            if ln >= n:
+                if ln == n:
+                    self.free.pop(i)
+                else:
+                    self.free[i] = (s + n, ln - n)
+                return s
+        return None
+
+    def release(self, start: int, n: int) -> None:
+        runs = sorted(self.free + [(start, n)])
+        merged = []
+        for s, ln in runs:
+            if merged and merged[-1][0] + merged[-1][1] == s:
+                merged[-1] = (merged[-1][0], merged[-1][1] + ln)
+            else:
+                merged.append((s, ln))
+        self.free = merged
+
+
 class LMCacheAdapter:
     def __init__(self, enabled: Optional[bool] = None, backend: Optional[str] = None, path: Optional[str] = None,
                  url: Optional[str] = None, max_bytes: int = 32 << 30, lookup_timeout_ms: int = 0):
@@ -39,6 +74,8 @@ class LMCacheAdapter:
         self._bytes = 0
         self._lock = threading.RLock()
         self._pending: Dict[str, Any] = {}  # key -> CUDA event of an in-flight device->host copy
+        self._arena: Optional[PinnedPageArena] = None
+        self._runs: Dict[str, tuple] = {}  # key -> (start, n) in the arena
         self._engine = None
         self.stat = {"hits": 0, "misses": 0, "stores": 0, "evictions": 0, "errors": 0}
         if self.enabled:
@@ -80,6 +117,50 @@ class LMCacheAdapter:
         self.stat["hits" if out is not None else "misses"] += 1
         return out
 
+    def reserve(self, page_shape, dtype=torch.bfloat16) -> None:
+        """Pin the CPU tier's memory once, as slots of ``page_shape`` (one KV page of every
+        layer: ``[L, 2, H, 16, D]``), instead of per store."""
+        if not self.enabled or self.backend != "cpu" or self._arena is not None:
+            return
+        page_bytes = int(torch.tensor([], dtype=dtype).element_size())
+        for d in page_shape:
+            page_bytes *= int(d)
+        n = max(1, self.max_bytes // page_bytes)
+        self._arena = PinnedPageArena(n, page_shape, dtype)
+
+    def _drop(self, key: str) -> None:
+        t = self._mem.pop(key, None)
+        self._pending.pop(key, None)
+        run = self._runs.pop(key, None)
+        if run is not None:
+            self._arena.release(*run)
+        if t is not None:
+            self._bytes -= t.numel() * t.element_size()
+
+    def _store_arena(self, key: str, pages: torch.Tensor) -> bool:
+        n = pages.shape[0]
+        if n > self._arena.n_pages:
+            return False
+        if key in self._mem:
+            self._drop(key)
+        start = self._arena.alloc(n)
+        while start is None and self._mem:
+            self._drop(next(iter(self._mem)))  # least recently used
+            self.stat["evictions"] += 1
+            start = self._arena.alloc(n)
+        if start is None:
+            return False
+        view = self._arena.buf[start:start + n]
+        view.copy_(pages, non_blocking=True)
+        if pages.is_cuda:
+            ev = torch.cuda.Event()
+            ev.record()
+            self._pending[key] = ev
+        self._mem[key] = view
+        self._runs[key] = (start, n)
+        self._bytes += view.numel() * view.element_size()
+        return True
+
     def contains(self, key: str) -> bool:
         if not self.enabled:
             return False
@@ -97,6 +178,10 @@ class LMCacheAdapter:
                     tmp = self._file(key) + ".tmp"
                     torch.save(pages.cpu(), tmp)
                     os.replace(tmp, self._file(key))
+                elif self._arena is not None and tuple(pages.shape[1:]) == self._arena.page_shape:
+                    if not self._store_arena(key, pages):
+                        self.stat["errors"] += 1
+                        return False
                 else:
                     if pages.device.type == "cpu":
                         host = pages
@@ -134,11 +219,9 @@ class LMCacheAdapter:
                     return True
                 except FileNotFoundError:
                     return False
-            t = self._mem.pop(key, None)
-            self._pending.pop(key, None)
-            if t is None:
+            if key not in self._mem:
                 return False
-            self._bytes -= t.numel() * t.element_size()
+            self._drop(key)
             return True
 
     def stats(self) -> Dict[str, Any]:

@@ -90,6 +90,9 @@ class AmfManager:
         self.lmcache_write_through = lmcache_write_through
         self.disable_restore = disable_restore
         g1 = raw_pool or comp_pool
+        if g1 is not None and self.lmcache.enabled and torch.cuda.is_available() and \
+                str(getattr(g1, "device", "cpu")).startswith("cuda"):
+            self.lmcache.reserve((g1.num_layers, 2, g1.num_kv_heads, PAGE, g1.head_dim))
         self.router = TieredCacheRouter(g1, self.lmcache, min_prefix_tokens=min_tokens,
                                         write_policy=WritePolicy(write_policy),
                                         large_write_threshold=large_write_threshold) if g1 is not None else None

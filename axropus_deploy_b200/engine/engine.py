@@ -165,14 +165,18 @@ class LLMEngine:
         self.stat["steps"] += 1
         done: List[Request] = []
         admitted = self._admit()
+        decoding = [r for r in self.running if r.state == "running" and r not in admitted]
+        any_prefill, any_decode = bool(admitted), bool(decoding)
+        if self.cfg.lockstep and hasattr(self.model, "ep_any"):
+            # a forward runs on every GPU when it runs on any (the MoE layers need all of them)
+            any_prefill, any_decode = self.model.ep_any([any_prefill, any_decode])
         if admitted:
             done += self._prefill(admitted)
-        elif self.cfg.lockstep:
+        elif self.cfg.lockstep and any_prefill:
             self._idle_forward()
-        decoding = [r for r in self.running if r.state == "running" and r not in admitted]
         if decoding:
             done += self._decode(decoding)
-        elif self.cfg.lockstep:
+        elif self.cfg.lockstep and any_decode:
             self._idle_forward()
         if self.device.type == "cuda":
             self._check_kernel_errors()

@@ -105,6 +105,17 @@ class LlamaModel:
                 info = ep_info or DistInfo(0, 1, 0, 1, self.device)
                 self.ep = EpMoE(info, cfg.num_experts, H, F, cfg.top_k, ep_max_tokens)
 
+    def ep_any(self, flags):
+        """Element-wise OR of small flags over the expert-parallel group (lockstep steps)."""
+        if self.ep is None or self.ep.world == 1:
+            return list(flags)
+        import torch.distributed as dist
+
+        dev = self.device if self.device.type == "cuda" else torch.device("cpu")
+        t = torch.tensor([1 if f else 0 for f in flags], dtype=torch.int32, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return [bool(v) for v in t.tolist()]
+
     @property
     def num_layers(self) -> int:
         return len(self.layers)

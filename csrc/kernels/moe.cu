@@ -527,7 +527,10 @@ void moe_dispatch(torch::Tensor x, torch::Tensor topk_idx, torch::Tensor topk_w,
   a.wait_ns = peer_wait_ns();
   int per_sm = 0;
   cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, moe_dispatch_kernel, 256, 0);
-  const int grid = std::max(1, std::min(sm_count(x.device().index()) * std::max(1, per_sm), 4 * 148));
+  // one warp per (token, k) pair, 8 per CTA; a small batch (decode) gets a small grid so
+  // the grid barrier stays cheap
+  const int want = static_cast<int>((static_cast<int64_t>(a.T) * a.K + 7) / 8);
+  const int grid = std::max(1, std::min({sm_count(x.device().index()) * std::max(1, per_sm), 4 * 148, want}));
   void* args[] = {&a};
   AXR_CHECK_CUDA(cudaLaunchCooperativeKernel(reinterpret_cast<void*>(moe_dispatch_kernel), dim3(grid), dim3(256),
                                              args, 0, at::cuda::getCurrentCUDAStream()));

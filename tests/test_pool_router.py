@@ -128,3 +128,34 @@ def test_nvme_tier(tmp_path):
     assert lm.store("k1", pages) and lm.contains("k1")
     assert torch.equal(lm.lookup("k1"), pages)
     assert (tmp_path / "k1.pt").exists()
+
+
+def test_cpu_tier_page_arena_runs_and_lru():
+    """CPU tier on a pre-pinned page arena: entries are contiguous runs, LRU entries are
+    evicted until a run fits, freed runs merge back."""
+    from axropus_deploy_b200.amf.lmcache import LMCacheAdapter, PinnedPageArena
+
+    shape = (2, 2, 1, 16, 8)
+    page_bytes = 2 * 2 * 1 * 16 * 8 * 2
+    lm = LMCacheAdapter(enabled=True, backend="cpu", max_bytes=10 * page_bytes)
+    lm.reserve(shape)
+    assert lm._arena is not None and lm._arena.n_pages == 10
+    pages = {k: torch.full((n, *shape), float(i + 1)).to(torch.bfloat16) for i, (k, n) in
+             enumerate([("a", 4), ("b", 3), ("c", 3)])}
+    for k, v in pages.items():
+        assert lm.store(k, v)
+    assert lm._arena.free == []
+    assert torch.equal(lm.lookup("b"), pages["b"])  # b becomes most recently used
+    assert lm.store("d", torch.zeros(4, *shape, dtype=torch.bfloat16))  # evicts a (LRU) only
+    assert lm.lookup("a") is None
+    assert torch.equal(lm.lookup("b"), pages["b"]) and torch.equal(lm.lookup("c"), pages["c"])
+    # LRU order is now d, b, c; 5 contiguous pages need d's run (0-3) and b's (4-6) merged
+    assert lm.store("e", torch.zeros(5, *shape, dtype=torch.bfloat16))
+    assert lm.lookup("d") is None and lm.lookup("b") is None
+    assert torch.equal(lm.lookup("c"), pages["c"])
+    assert lm.evict("e") and lm.evict("c")
+    assert lm._arena.free == [(0, 10)]
+    ar = PinnedPageArena(8, (1,))
+    s1, s2 = ar.alloc(3), ar.alloc(3)
+    ar.release(s1, 3)
+    assert ar.alloc(4) is None and ar.alloc(3) == s1
