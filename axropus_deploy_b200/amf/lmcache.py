@@ -76,6 +76,7 @@ class LMCacheAdapter:
         self._pending: Dict[str, Any] = {}  # key -> CUDA event of an in-flight device->host copy
         self._arena: Optional[PinnedPageArena] = None
         self._runs: Dict[str, tuple] = {}  # key -> (start, n) in the arena
+        self._copy_stream = None
         self._engine = None
         self.stat = {"hits": 0, "misses": 0, "stores": 0, "evictions": 0, "errors": 0}
         if self.enabled:
@@ -151,11 +152,20 @@ class LMCacheAdapter:
         if start is None:
             return False
         view = self._arena.buf[start:start + n]
-        view.copy_(pages, non_blocking=True)
         if pages.is_cuda:
-            ev = torch.cuda.Event()
-            ev.record()
+            # the PCIe copy runs on a side stream so the serving stream does not wait for it
+            if self._copy_stream is None:
+                self._copy_stream = torch.cuda.Stream(device=pages.device)
+            side = self._copy_stream
+            side.wait_stream(torch.cuda.current_stream(pages.device))
+            with torch.cuda.stream(side):
+                view.copy_(pages, non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(side)
+            pages.record_stream(side)
             self._pending[key] = ev
+        else:
+            view.copy_(pages)
         self._mem[key] = view
         self._runs[key] = (start, n)
         self._bytes += view.numel() * view.element_size()
