@@ -24,6 +24,7 @@ bf16 cache, for comparison.
 from __future__ import annotations
 
 import argparse
+import faulthandler
 import json
 import math
 import os
@@ -79,7 +80,14 @@ def main():
     ap.add_argument("--decode-tokens", type=int, default=512)
     ap.add_argument("--graphs", type=int, default=1)
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--verbose", action="store_true", help="progress lines on stderr")
     args = ap.parse_args()
+    faulthandler.enable()
+
+    def note(msg):
+        if args.verbose:
+            print(f"[long_context] {msg}", file=sys.stderr, flush=True)
+
     info = init_distributed(timeout_s=900.0)
     dev, W, R = info.device, info.world, info.rank
     cfg = get_config(args.model)
@@ -90,6 +98,7 @@ def main():
     blk_int4 = KVCache.bytes_per_block(L, H, D, "int4")
     b_local = args.batch // W + (1 if R < args.batch % W else 0)
 
+    note("model ready")
     # ---- bf16 comparison first (its buffers are freed before the INT4 run)
     free0, _ = torch.cuda.mem_get_info(dev)
     bf_pages = pages
@@ -105,6 +114,7 @@ def main():
     del bf_cache, bf_store
     torch.cuda.empty_cache()
 
+    note("bf16 restore measured")
     # ---- INT4 pool (sharded): every sequence gets its own prefix entry, on its own GPU's
     # shard (prefix keys drawn until their owner is that GPU). One GPU cannot hold 32
     # sequences of 128K INT4 KV plus their pool entries: the batch per GPU is capped at
@@ -132,6 +142,7 @@ def main():
     torch.cuda.synchronize()
     barrier(info)
 
+    note("pool populated")
     nb = int(b_local * math.ceil(seq / PAGE) * 1.02) + 64
     eng = LLMEngine(model, EngineConfig(num_blocks=nb, kv_fmt="int4", max_batch=max(1, b_local),
                                         max_prefill_tokens=4096, max_model_len=seq + PAGE,
@@ -143,6 +154,7 @@ def main():
         reqs.append(eng.add_request(p, SamplingParams(max_tokens=args.decode_tokens), amf_prefix_len=args.prefix_len))
     torch.cuda.synchronize()
     barrier(info)
+    note("requests added")
     # admission (lookup + restore + register) and suffix prefill of every sequence
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
@@ -153,6 +165,7 @@ def main():
     admit_ms = all_reduce_max(e0.elapsed_time(e1), info)
     tiers = [r.amf_tier for r in reqs]
     restore_ms = [r.restore_ms for r in reqs]
+    note("admitted")
     # decode: every remaining token of every sequence (the first decode step, which also
     # captures the decode CUDA graph of this batch size, is left out of the timing)
     eng.step()
