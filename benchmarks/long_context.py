@@ -35,7 +35,7 @@ import torch
 
 sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
-from axropus_deploy_b200.amf.keys import pool_key  # noqa: E402
+from axropus_deploy_b200.amf.keys import pool_key, pool_key2  # noqa: E402
 from axropus_deploy_b200.amf.manager import AmfManager  # noqa: E402
 from axropus_deploy_b200.amf.pool import PoolSlab  # noqa: E402
 from axropus_deploy_b200.engine import EngineConfig, LLMEngine, SamplingParams  # noqa: E402
@@ -137,7 +137,7 @@ def main():
     fill_random(scratch, 2)
     src = (torch.arange(pages, dtype=torch.int32) % 512)
     for p in prefixes:
-        assert pool.capture(pool_key(p), scratch, src, args.prefix_len), "pool full"
+        assert pool.capture(pool_key(p), scratch, src, args.prefix_len, key2=pool_key2(p)), "pool full"
     del scratch
     torch.cuda.synchronize()
     barrier(info)
