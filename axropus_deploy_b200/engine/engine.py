@@ -91,10 +91,14 @@ class EngineConfig:
     # expert parallelism: every GPU runs exactly one prefill and one decode forward per
     # step (empty when it has nothing to do) so the MoE collectives of all GPUs line up
     lockstep: bool = False
+    # speculative decoding of greedy requests: "" (off), "ngram" (prompt lookup) or
+    # "model" (needs a draft model); depth adapts between 1 and spec_max_depth
+    spec: str = ""
+    spec_max_depth: int = 8
 
 
 class LLMEngine:
-    def __init__(self, model: LlamaModel, cfg: EngineConfig, amf: Optional[AmfManager] = None):
+    def __init__(self, model: LlamaModel, cfg: EngineConfig, amf: Optional[AmfManager] = None, draft_model=None):
         self.model = model
         self.cfg = cfg
         self.amf = amf
@@ -116,6 +120,19 @@ class LLMEngine:
             from .cuda_graph import DecodeGraphRunner
 
             self._graphs = DecodeGraphRunner(self)
+        self.spec = None
+        if cfg.spec:
+            from .spec import ModelDrafter, SpecDecoder
+
+            if cfg.spec == "model":
+                if draft_model is None:
+                    raise ValueError("spec='model' needs a draft_model")
+                drafter = ModelDrafter(draft_model, cfg.num_blocks)
+            elif cfg.spec == "ngram":
+                drafter = None
+            else:
+                raise ValueError(f"unknown spec mode {cfg.spec!r}")
+            self.spec = SpecDecoder(self, cfg.spec_max_depth, drafter)
         self.stat = {"steps": 0, "prefill_tokens": 0, "decode_tokens": 0, "restored_tokens": 0,
                      "local_cached_tokens": 0, "cold_prefill_tokens": 0}
 
@@ -370,6 +387,8 @@ class LLMEngine:
         return toks, pos, slots, lens
 
     def _decode(self, reqs: List[Request]) -> List[Request]:
+        if self.spec is not None and all(r.params.temperature <= 0 for r in reqs):
+            return self.spec.step(reqs)
         toks, pos, slots, lens = self.decode_meta(reqs)
         self.stat["decode_tokens"] += len(reqs)
         if self._graphs is not None:
@@ -394,4 +413,6 @@ class LLMEngine:
         out["blocks"] = self.bm.stats()
         if self.amf is not None:
             out["amf"] = self.amf.stats()
+        if self.spec is not None:
+            out["spec"] = self.spec.stats()
         return out
