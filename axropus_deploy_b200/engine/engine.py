@@ -102,6 +102,8 @@ class LLMEngine:
         self.model = model
         self.cfg = cfg
         self.amf = amf
+        if hasattr(model, "ensure_positions"):
+            model.ensure_positions(cfg.max_model_len + PAGE)
         mc = model.cfg
         self.device = model.device
         kv_heads = getattr(model, "cache_kv_heads", mc.num_kv_heads)  # tensor parallel: this GPU's heads
@@ -127,6 +129,8 @@ class LLMEngine:
             if cfg.spec == "model":
                 if draft_model is None:
                     raise ValueError("spec='model' needs a draft_model")
+                if hasattr(draft_model, "ensure_positions"):
+                    draft_model.ensure_positions(cfg.max_model_len + PAGE)
                 drafter = ModelDrafter(draft_model, cfg.num_blocks)
             elif cfg.spec == "ngram":
                 drafter = None

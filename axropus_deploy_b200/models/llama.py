@@ -116,6 +116,18 @@ class LlamaModel:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return [bool(v) for v in t.tolist()]
 
+    def ensure_positions(self, n: int) -> None:
+        """Grow the RoPE table to cover positions [0, n) (e.g. a 128K prefix plus its
+        suffix and decode tokens, past the architecture's nominal context)."""
+        if n > self.cos_sin.shape[0]:
+            cfg = self.cfg
+            self.cos_sin = ops.rope_cos_sin(n, cfg.head_dim, cfg.rope_theta, cfg.rope_scaling, self.device)
+
+    def _check_positions(self, meta: AttnMeta) -> None:
+        if meta.max_seq_len and meta.max_seq_len > self.cos_sin.shape[0]:
+            raise ValueError(f"position {meta.max_seq_len - 1} is beyond the RoPE table "
+                             f"({self.cos_sin.shape[0]} rows); call ensure_positions()")
+
     @property
     def num_layers(self) -> int:
         return len(self.layers)
@@ -157,6 +169,7 @@ class LlamaModel:
                 for lw in self.layers:
                     self.ep.forward(x, idx, w, lw.w13, lw.w2)
             return torch.empty(0, cfg.vocab, dtype=torch.float32, device=self.device)
+        self._check_positions(meta)
         h = self.embed[tokens.long()]
         residual = h.clone()
         x = ops.rmsnorm(h, self.layers[0].attn_norm if self.layers else self.final_norm, cfg.rms_eps)

@@ -118,6 +118,11 @@ class TpLlamaModel:
         self.final_norm = m.final_norm
         self.lm_head = m.lm_head[:, r * self.vocab_local:(r + 1) * self.vocab_local].t().contiguous()
 
+    def ensure_positions(self, n: int) -> None:
+        if n > self.cos_sin.shape[0]:
+            cfg = self.cfg
+            self.cos_sin = ops.rope_cos_sin(n, cfg.head_dim, cfg.rope_theta, cfg.rope_scaling, self.device)
+
     @property
     def num_layers(self) -> int:
         return len(self.layers)
@@ -170,6 +175,8 @@ class TpLlamaModel:
     def forward(self, tokens: torch.Tensor, meta: AttnMeta, cache: KVCache) -> torch.Tensor:
         """tokens [T] (the same on every rank) -> logits [B, vocab] fp32 of ``meta.logits_idx``."""
         T = tokens.shape[0]
+        if meta.max_seq_len and meta.max_seq_len > self.cos_sin.shape[0]:
+            raise ValueError(f"position {meta.max_seq_len - 1} is beyond the RoPE table; call ensure_positions()")
         if self.tp is not None and self.world > 1 and meta.mode == "prefill" and T >= self.sp_min_tokens \
                 and -(-T // (TILE_M * self.world)) * TILE_M <= self.max_rows:
             return self._forward_sp(tokens, meta, cache)

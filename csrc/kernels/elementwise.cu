@@ -112,6 +112,7 @@ struct RopeKvParams {
   char* vm;
   long long blk_stride, head_stride, mblk_stride, mhead_stride;
   int Hq, Hkv, T;
+  int n_pos;  // rows of cos_sin; positions are clamped into it (the host checks them first)
 };
 
 // One warp per (token, head row). Lane holds dims {2l, 2l+1} and {64+2l, 64+2l+1}
@@ -131,7 +132,8 @@ __global__ void __launch_bounds__(256) rope_kv_kernel(RopeKvParams p) {
   float x[4] = {bf16_lo(lo), bf16_hi(lo), bf16_lo(hi), bf16_hi(hi)};  // d, d+1, d+64, d+65
   const bool is_v = hr >= p.Hq + p.Hkv;
   if (!is_v) {
-    const float* cs = p.cos_sin + (long long)p.pos[tok] * D;
+    const int ps = min(max(p.pos[tok], 0), p.n_pos - 1);
+    const float* cs = p.cos_sin + (long long)ps * D;
     const float c0 = cs[2 * lane], c1 = cs[2 * lane + 1];
     const float s0 = cs[64 + 2 * lane], s1 = cs[64 + 2 * lane + 1];
     const float a0 = x[0] * c0 - x[2] * s0, b0 = x[2] * c0 + x[0] * s0;
@@ -204,7 +206,8 @@ void rope_kv_write(torch::Tensor qkv, torch::Tensor pos, torch::Tensor slots, to
                  slots.data_ptr<int>(), cos_sin.data_ptr<float>(),
                  reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr()), reinterpret_cast<char*>(k),
                  reinterpret_cast<char*>(v), reinterpret_cast<char*>(km), reinterpret_cast<char*>(vm),
-                 blk_stride, head_stride, mblk_stride, mhead_stride, (int)Hq, (int)Hkv, T};
+                 blk_stride, head_stride, mblk_stride, mhead_stride, (int)Hq, (int)Hkv, T,
+                 static_cast<int>(cos_sin.size(0))};
   const long long warps = (long long)T * (Hq + 2 * Hkv);
   const int grid = static_cast<int>((warps + 7) / 8);
   auto st = at::cuda::getCurrentCUDAStream();
