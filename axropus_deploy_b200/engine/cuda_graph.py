@@ -48,7 +48,7 @@ class DecodeGraphRunner:
     def _capture(self, b: int) -> None:
         eng = self.eng
         cache = eng.cache
-        self.splits[b] = decode_num_splits(b, cache.num_kv_heads, (self.max_seq + 15) // 16, eng.device)
+        self.splits[b] = decode_num_splits(b, cache.num_kv_heads, (self.max_seq + 15) // 16, eng.device, cache.fmt)
         # pre-size the split scratch for the largest bucket so every graph shares it
         from ..ops import attention as att
 

@@ -69,8 +69,8 @@ class DecodeWorkspace:
 _WS = DecodeWorkspace()
 
 
-def decode_num_splits(batch: int, kv_heads: int, max_pages: int, device: torch.device) -> int:
-    return int(cuda_ext().decode_num_splits(batch, kv_heads, max_pages, _num_sms(device)))
+def decode_num_splits(batch: int, kv_heads: int, max_pages: int, device: torch.device, fmt: int = -1) -> int:
+    return int(cuda_ext().decode_num_splits(batch, kv_heads, max_pages, _num_sms(device), fmt))
 
 
 def decode_attention(q: torch.Tensor, cache: KVCache, layer: int, block_table: torch.Tensor, seq_lens: torch.Tensor,
@@ -86,7 +86,7 @@ def decode_attention(q: torch.Tensor, cache: KVCache, layer: int, block_table: t
         if max_seq_len is None:
             max_seq_len = int(seq_lens.max().item()) if B else 0
         max_pages = (max_seq_len + 15) // 16
-        S = num_splits if num_splits is not None else decode_num_splits(B, cache.num_kv_heads, max_pages, q.device)
+        S = num_splits if num_splits is not None else decode_num_splits(B, cache.num_kv_heads, max_pages, q.device, cache.fmt)
         ws = workspace or _WS
         po, pl = ws.get(B, Hq, S, D, q.device) if S > 1 else (out, out)
         k, v, km, vm, bs, hs, mbs, mhs = cache.layer_args(layer)

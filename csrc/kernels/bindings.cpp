@@ -6,7 +6,7 @@ void page_transfer(int64_t src_data, int64_t src_meta, std::vector<int64_t> src_
                    int64_t dst_data, int64_t dst_meta, std::vector<int64_t> dst_strides, int64_t dst_fmt,
                    torch::Tensor src_ids, torch::Tensor dst_ids, int64_t n_lk, int64_t H, int64_t D,
                    int64_t max_ctas);
-int64_t decode_num_splits(int64_t batch, int64_t kv_heads, int64_t max_pages, int64_t sms);
+int64_t decode_num_splits(int64_t batch, int64_t kv_heads, int64_t max_pages, int64_t sms, int64_t fmt);
 void decode_attention(torch::Tensor q, int64_t k, int64_t v, int64_t km, int64_t vm, int64_t blk_stride,
                       int64_t head_stride, int64_t mblk_stride, int64_t mhead_stride, int64_t fmt,
                       torch::Tensor block_table, torch::Tensor seq_lens, int64_t Hkv, double scale,
@@ -53,7 +53,8 @@ void moe_combine(torch::Tensor comb, torch::Tensor out, torch::Tensor comb_flag,
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sm_100a kernels of axropus_deploy_b200";
   m.def("page_transfer", &axr::page_transfer);
-  m.def("decode_num_splits", &axr::decode_num_splits);
+  m.def("decode_num_splits", &axr::decode_num_splits, py::arg("batch"), py::arg("kv_heads"), py::arg("max_pages"),
+        py::arg("sms"), py::arg("fmt") = -1);
   m.def("decode_attention", &axr::decode_attention);
   m.def("prefill_attention", &axr::prefill_attention);
   m.def("prefill_attention_tc", &axr::prefill_attention_tc);

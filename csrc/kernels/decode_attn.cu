@@ -353,11 +353,21 @@ __device__ __forceinline__ uint32_t fp8x2_h2(uint32_t two_codes) {
   __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(two_codes & 0xffff), __NV_E4M3);
   return *reinterpret_cast<uint32_t*>(&h);
 }
-// one byte of two nibbles -> f16x2 (lo, hi) holding the integers 0..15
-__device__ __forceinline__ uint32_t nib2_h2(uint32_t byte) {
-  const uint32_t x = (byte & 0x0Fu) | ((byte & 0xF0u) << 12) | 0x64006400u;  // 1024 + n
-  __half2 h = *reinterpret_cast<const __half2*>(&x);
-  h = __hsub2(h, __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400)));
+// Byte Q of `word` (two nibbles) -> f16x2 (lo, hi) holding the integers 0..15, without
+// int->float conversions: one byte permute puts the byte in both 16-bit halves, one
+// mask+or builds the f16 bit patterns 1024 + lo and 1024 + 16*hi, and one f16x2 FMA
+// (scale 1 and 1/16, bias -1024 and -64) leaves the exact integers.
+template <int Q>
+__device__ __forceinline__ __half2 nib_pair(uint32_t word) {
+  uint32_t t = __byte_perm(word, 0u, Q | (4 << 4) | (Q << 8) | (4 << 12));  // bytes [bQ, 0, bQ, 0]
+  t = (t & 0x00F0000Fu) | 0x64006400u;
+  const __half2 h = *reinterpret_cast<const __half2*>(&t);
+  return __hfma2(h, __halves2half2(__ushort_as_half(0x3C00), __ushort_as_half(0x2C00)),   // 1, 1/16
+                 __halves2half2(__ushort_as_half(0xE400), __ushort_as_half(0xD400)));  // -1024, -64
+}
+template <int Q>
+__device__ __forceinline__ uint32_t nib2_h2w(uint32_t word) {
+  __half2 h = nib_pair<Q>(word);
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
@@ -493,13 +503,14 @@ __global__ void __launch_bounds__(128) decode_tc_kernel(DecodeParams p) {
           }
         } else {
           const uint2 x = *reinterpret_cast<const uint2*>(sk + ksw<FMT>(r, gr * 2 + (t >> 1)) + (t & 1) * 8);
-          const uint32_t w[2] = {x.x, x.y};
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const uint32_t word = w[q >> 1] >> ((q & 1) * 16);
-            ka[h][2 * q] = nib2_h2(word & 0xff);
-            ka[h][2 * q + 1] = nib2_h2((word >> 8) & 0xff);
-          }
+          ka[h][0] = nib2_h2w<0>(x.x);
+          ka[h][1] = nib2_h2w<1>(x.x);
+          ka[h][2] = nib2_h2w<2>(x.x);
+          ka[h][3] = nib2_h2w<3>(x.x);
+          ka[h][4] = nib2_h2w<0>(x.y);
+          ka[h][5] = nib2_h2w<1>(x.y);
+          ka[h][6] = nib2_h2w<2>(x.y);
+          ka[h][7] = nib2_h2w<3>(x.y);
         }
       }
 #pragma unroll
@@ -596,12 +607,14 @@ __global__ void __launch_bounds__(128) decode_tc_kernel(DecodeParams p) {
         } else {
           const uint32_t x = *reinterpret_cast<const uint32_t*>(sv + r * 64 + cc * 4);
           const uint32_t mm = reinterpret_cast<const uint32_t*>(vm)[r * 2 + (cc >> 3)];
-          const float a = half_bits_to_float(mm & 0xffff), z = half_bits_to_float(mm >> 16);
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const uint32_t byte = (x >> (8 * q)) & 0xff;
-            h4[q] = pack_h2(float(byte & 0xf) * a + z, float(byte >> 4) * a + z);
-          }
+          const __half2 sz = *reinterpret_cast<const __half2*>(&mm);  // (scale, zero)
+          const __half2 a2 = __low2half2(sz), z2 = __high2half2(sz);
+          const __half2 v0 = __hfma2(nib_pair<0>(x), a2, z2), v1 = __hfma2(nib_pair<1>(x), a2, z2);
+          const __half2 v2 = __hfma2(nib_pair<2>(x), a2, z2), v3 = __hfma2(nib_pair<3>(x), a2, z2);
+          h4[0] = *reinterpret_cast<const uint32_t*>(&v0);
+          h4[1] = *reinterpret_cast<const uint32_t*>(&v1);
+          h4[2] = *reinterpret_cast<const uint32_t*>(&v2);
+          h4[3] = *reinterpret_cast<const uint32_t*>(&v3);
         }
         *reinterpret_cast<uint4*>(vtile + vsw(r, cc)) = make_uint4(h4[0], h4[1], h4[2], h4[3]);
       }
@@ -707,13 +720,31 @@ static void launch_g(int G, dim3 grid, const DecodeParams& p, cudaStream_t st) {
   }
 }
 
-// Chooses the number of KV splits so batch x kv_heads x splits fills the GPU.
-int64_t decode_num_splits(int64_t batch, int64_t kv_heads, int64_t max_pages, int64_t sms) {
+// Chooses the number of KV splits so that batch x kv_heads x splits fills the GPU in
+// whole waves: with `fmt` given, a wave is SMs x the CTAs of that page format's kernel
+// that fit one SM (shared memory bound); the split count in [fill/2, 2*fill] with the
+// best last-wave occupancy wins (fewest splits on ties), keeping >= 4 pages per split.
+int64_t decode_num_splits(int64_t batch, int64_t kv_heads, int64_t max_pages, int64_t sms, int64_t fmt) {
   const int64_t base = std::max<int64_t>(1, batch * kv_heads);
-  const int64_t target = sms * 4;  // ~4 resident CTAs per SM
-  int64_t s = (target + base - 1) / base;
-  s = std::min<int64_t>(s, std::max<int64_t>(1, max_pages / 4));  // >= 4 pages per split
-  return std::max<int64_t>(1, std::min<int64_t>(s, 64));
+  int64_t per_sm = 4;
+  if (fmt == kBF16) per_sm = (227 * 1024) / TcCfg<kBF16>::SMEM;
+  else if (fmt == kFP8Token) per_sm = (227 * 1024) / TcCfg<kFP8Token>::SMEM;
+  else if (fmt == kINT4G64) per_sm = (227 * 1024) / TcCfg<kINT4G64>::SMEM;
+  const int64_t cap = sms * std::max<int64_t>(1, std::min<int64_t>(per_sm, 16));
+  const int64_t s_max = std::max<int64_t>(1, std::min<int64_t>(64, max_pages / 4));
+  const int64_t fill = (cap + base - 1) / base;
+  int64_t best = 1;
+  double best_eff = -1.0;
+  for (int64_t s = std::max<int64_t>(1, fill / 2); s <= std::min<int64_t>(s_max, 2 * fill); ++s) {
+    const int64_t ctas = base * s;
+    const int64_t waves = (ctas + cap - 1) / cap;
+    const double eff = static_cast<double>(ctas) / static_cast<double>(waves * cap);
+    if (eff > best_eff + 1e-9) {
+      best_eff = eff;
+      best = s;
+    }
+  }
+  return std::max<int64_t>(1, std::min<int64_t>(best, s_max));
 }
 
 // q [B,Hq,D] bf16; k/v: page data of one layer as raw addresses with strides; meta
