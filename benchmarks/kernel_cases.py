@@ -3,7 +3,7 @@
 whole run stays within a few GB of device memory.
 
     python benchmarks/kernel_cases.py decode|decode_int4|decode_fp8|restore|restore_fp8|capture_int4|
-                                      prefill|gemm|rmsnorm|rope
+                                      prefill|prefill_split|gemm|gemm_tp|moe|rmsnorm|rope
 """
 import os
 import sys
@@ -97,10 +97,49 @@ def rope():
         ops.rope_kv_write(qkv, pos, pos.clone(), cs, cache, 0, 32, 8)
 
 
+def prefill_split():
+    # 128-token suffix over an 8192-token cached prefix (hit TTFT case): split-KV prefill
+    T, n = 8320, 128
+    cache = KVCache(1, T // 16 + 1, 8, 128, "bf16", "cuda")
+    cache.data.normal_()
+    bt = torch.arange(T // 16 + 1, dtype=torch.int32, device="cuda").view(1, -1)
+    cu = torch.tensor([0, n], dtype=torch.int32, device="cuda")
+    sl = torch.tensor([T], dtype=torch.int32, device="cuda")
+    q = torch.randn(n, 32, 128, device="cuda").to(torch.bfloat16)
+    for _ in range(3):
+        ops.prefill_attention(q, cache, 0, bt, cu, sl, n, max_seq_len=T)
+
+
+def gemm_tp_plain():
+    from axropus_deploy_b200.parallel.tp import TpGemm
+
+    a = torch.randn(8192, 8192, device="cuda").to(torch.bfloat16)
+    w = torch.randn(7168, 8192, device="cuda").to(torch.bfloat16)
+    for _ in range(3):
+        TpGemm.gemm(a, w)
+
+
+def moe():
+    # one Mixtral MoE layer, all 8 experts on this GPU (expert-parallel group of one), 4096 tokens
+    from axropus_deploy_b200.parallel.dist import DistInfo
+    from axropus_deploy_b200.parallel.ep import EpMoE, route
+
+    E, H, F, T = 8, 4096, 14336, 4096
+    dev = torch.device("cuda", 0)
+    m = EpMoE(DistInfo(0, 1, 0, 1, dev), E, H, F, 2, max_tokens=T)
+    w13 = (torch.randn(E, 2 * F, H, device=dev) * 0.02).to(torch.bfloat16)
+    w2 = (torch.randn(E, H, F, device=dev) * 0.02).to(torch.bfloat16)
+    x = torch.randn(T, H, device=dev).to(torch.bfloat16)
+    idx, w = route(torch.randn(T, E, device=dev), 2)
+    for _ in range(3):
+        m.forward(x, idx, w, w13, w2)
+
+
 CASES = {"decode": lambda: decode("bf16"), "decode_int4": lambda: decode("int4"),
          "decode_fp8": lambda: decode("fp8"), "restore": lambda: restore("raw", "bf16"),
          "restore_fp8": lambda: restore("fp8", "bf16"), "capture_int4": lambda: capture("int4"),
-         "prefill": prefill, "gemm": gemm_case, "rmsnorm": rmsnorm, "rope": rope}
+         "prefill": prefill, "gemm": gemm_case, "rmsnorm": rmsnorm, "rope": rope,
+         "prefill_split": prefill_split, "gemm_tp": gemm_tp_plain, "moe": moe}
 
 if __name__ == "__main__":
     for name in sys.argv[1:] or ["decode"]:
