@@ -100,17 +100,28 @@ def decode_attention(q: torch.Tensor, cache: KVCache, layer: int, block_table: t
     return out
 
 
-def prefill_num_splits(batch: int, heads: int, max_q: int, max_seq_len: Optional[int], device) -> int:
+def prefill_num_splits(batch: int, heads: int, max_q: int, max_seq_len: Optional[int], device,
+                       q_tile: int = 64, kv_tile: int = 64, per_sm: int = 2) -> int:
     """KV slices per query tile so that a short suffix over a long prefix still fills
-    the GPU (about two 80 KB CTAs per SM); 1 when the query tiles alone do."""
+    the GPU (``per_sm`` resident CTAs per SM); 1 when the query tiles alone do. Each
+    slice keeps at least 4 KV tiles (2 for the 128-token tiles of the tensor-core kernel)."""
     if not max_seq_len:
         return 1
-    ctas = max(1, -(-max_q // 64)) * heads * max(1, batch)
-    target = 2 * _num_sms(device)
+    ctas = max(1, -(-max_q // q_tile)) * heads * max(1, batch)
+    target = per_sm * _num_sms(device)
     if ctas >= target:
         return 1
-    kv_tiles = -(-max_seq_len // 64)
-    return int(max(1, min(-(-target // ctas), kv_tiles // 4, 32)))
+    kv_tiles = -(-max_seq_len // kv_tile)
+    if kv_tile == 64:
+        return int(max(1, min(-(-target // ctas), kv_tiles // 4, 32)))
+    # one CTA per SM: pick the split count with the least estimated time, waves x (tiles
+    # per slice + a per-CTA overhead of about two tiles)
+    best, best_t = 1, None
+    for s in range(1, max(1, min(32, kv_tiles // 2)) + 1):
+        t = -(-ctas * s // target) * (-(-kv_tiles // s) + 2)
+        if best_t is None or t < best_t:
+            best, best_t = s, t
+    return best
 
 
 _PREFILL_WS = DecodeWorkspace()
@@ -129,13 +140,17 @@ def prefill_attention(q: torch.Tensor, cache: KVCache, layer: int, block_table: 
         out = torch.empty_like(q)
     if q.is_cuda:
         k, v, km, vm, bs, hs, mbs, mhs = cache.layer_args(layer)
+        if cache.fmt == BF16 and D == 128 and PREFILL_TC[0] and max_q >= 64:
+            # tensor-core (tcgen05 / TMEM) kernel on bf16 pages: 256-row query tiles, one CTA
+            # per SM; short suffixes over long prefixes split the KV range
+            S = num_splits if num_splits is not None else prefill_num_splits(
+                seq_lens.shape[0], Hq, max_q, max_seq_len, q.device, q_tile=256, kv_tile=128, per_sm=1)
+            po, pl = _PREFILL_WS.get(T, Hq, S, D, q.device) if S > 1 else (None, None)
+            cuda_ext().prefill_attention_tc(q, k, v, bs, hs, cache.num_blocks, block_table, cu_q, seq_lens,
+                                            cache.num_kv_heads, scale, max_q, out, error_flag(q.device), S, po, pl)
+            return out
         S = num_splits if num_splits is not None else prefill_num_splits(seq_lens.shape[0], Hq, max_q, max_seq_len,
                                                                           q.device)
-        if S == 1 and cache.fmt == BF16 and D == 128 and PREFILL_TC[0]:
-            # tensor-core (tcgen05 / TMEM) kernel: bf16 pages, enough query tiles to fill the GPU
-            cuda_ext().prefill_attention_tc(q, k, v, bs, hs, cache.num_blocks, block_table, cu_q, seq_lens,
-                                            cache.num_kv_heads, scale, max_q, out, error_flag(q.device))
-            return out
         po, pl = _PREFILL_WS.get(T, Hq, S, D, q.device) if S > 1 else (None, None)
         cuda_ext().prefill_attention(q, k, v, km, vm, bs, hs, mbs, mhs, cache.fmt, block_table, cu_q, seq_lens,
                                      cache.num_kv_heads, scale, max_q, out, S, po, pl)

@@ -30,6 +30,7 @@
 
 #include <cfloat>
 
+#include "attn_combine.cuh"
 #include "common.cuh"
 #include "tc_common.cuh"
 
@@ -54,6 +55,9 @@ struct Params {
   const int* seq_lens;
   float scale_log2;
   volatile int* err;
+  int num_splits;   // KV slices per (query tile, head, sequence); 1 = no split
+  float* part_o;    // [T*Hq, S, 128] normalised partial outputs (S > 1)
+  float* part_lse;  // [T*Hq, S] log2-domain log-sum-exps (S > 1)
 };
 
 // byte offset of 16-byte unit u (0..15) of row r in a [128 x 128] bf16 K-major SW128 tile
@@ -83,7 +87,8 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile_m = gridDim.x - 1 - blockIdx.x;  // longest (most KV tiles) first
-  const int hq = blockIdx.y, b = blockIdx.z;
+  const int S = p.num_splits;
+  const int hq = blockIdx.y, b = blockIdx.z / S, split = blockIdx.z % S;
   const int q0 = p.cu_q[b], nq = p.cu_q[b + 1] - q0;
   const int row0 = tile_m * 2 * BM;  // first query row of sub-tile A
   if (row0 >= nq) return;
@@ -93,7 +98,16 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
   const int kvh = hq / (p.Hq / p.Hkv);
   const int m_last = min(nq, row0 + 2 * BM) - 1;
   const int kv_end = min(kv_len, pos0 + m_last + 1);
-  const int n_tiles = (kv_end + BN - 1) / BN;
+  const int n_all = (kv_end + BN - 1) / BN;
+  // split-KV: this CTA takes KV tiles [t_begin, t_begin + n_tiles) of the query tile's range
+  const int per = (n_all + S - 1) / S;
+  const int t_begin = split * per;
+  const int n_tiles = max(0, min(n_all, t_begin + per) - t_begin);
+  if (n_tiles == 0) {  // no keys for this slice: mark its partials empty
+    for (int r = threadIdx.x; r < 2 * BM; r += blockDim.x)
+      if (row0 + r < nq) p.part_lse[((long long)(q0 + row0 + r) * p.Hq + hq) * S + split] = -FLT_MAX;
+    return;
+  }
   const int* bt = p.block_table + (long long)b * p.bt_stride;
 
   if (threadIdx.x == 0) {
@@ -133,7 +147,7 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
         tc::mbar_arrive_expect_tx(&slot_full[s], TILE);
 #pragma unroll
         for (int pg = 0; pg < 8; ++pg) {
-          const int tok = j * BN + pg * 16;
+          const int tok = (t_begin + j) * BN + pg * 16;
           const int blk = tok < kv_len ? bt[tok >> 4] : 0;
           const int y = (blk * p.Hkv + kvh) * 16;
           tc::tma_load_2d(sR + s * TILE + pg * 2048, map, 0, y, &slot_full[s]);
@@ -235,7 +249,7 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[c * 32 + i] = __uint_as_float(r[c][i]) * p.scale_log2;
       }
-      const int n0 = j * BN;
+      const int n0 = (t_begin + j) * BN;
       if (n0 + BN - 1 > qpos_min || n0 + BN > kv_len) {
 #pragma unroll
         for (int i = 0; i < BN; ++i)
@@ -288,7 +302,25 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
     }
     // ---------------- epilogue: O / l -> out
     if (ok) ok = warp_ok(tc::mbar_wait(o_done, 0, p.err, 21), p.err);
-    if (ok) {
+    if (ok && S > 1) {  // normalised partial output + log-sum-exp of this KV slice
+      tc::tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const long long pr = ((long long)(q0 + (row_valid ? qr : 0)) * p.Hq + hq) * S + split;
+#pragma unroll 1
+      for (int c = 0; c < HD / 32; ++c) {
+        uint32_t r[32];
+        tc::tmem_ld32(tO + c * 32, r);
+        tc::tmem_ld_wait();
+        if (row_valid) {
+          float4* dst = reinterpret_cast<float4*>(p.part_o + pr * HD + c * 32);
+#pragma unroll
+          for (int w4 = 0; w4 < 8; ++w4)
+            dst[w4] = make_float4(__uint_as_float(r[4 * w4]) * inv, __uint_as_float(r[4 * w4 + 1]) * inv,
+                                  __uint_as_float(r[4 * w4 + 2]) * inv, __uint_as_float(r[4 * w4 + 3]) * inv);
+        }
+      }
+      if (row_valid) p.part_lse[pr] = l > 0.f ? m_used + __log2f(l) : -FLT_MAX;
+    } else if (ok) {
       tc::tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       __nv_bfloat16* dst = p.out + ((long long)(q0 + (row_valid ? qr : 0)) * p.Hq + hq) * HD;
@@ -335,7 +367,9 @@ void make_page_map(CUtensorMap* map, const void* ptr, int64_t rows) {
 // each, contiguous); block_table [B, max_blocks] int32; cu_q [B+1]; seq_lens [B]; err int32.
 void prefill_attention_tc(torch::Tensor q, int64_t k, int64_t v, int64_t blk_stride, int64_t head_stride,
                           int64_t num_blocks, torch::Tensor block_table, torch::Tensor cu_q, torch::Tensor seq_lens,
-                          int64_t Hkv, double scale, int64_t max_q, torch::Tensor out, torch::Tensor err) {
+                          int64_t Hkv, double scale, int64_t max_q, torch::Tensor out, torch::Tensor err,
+                          int64_t num_splits, c10::optional<torch::Tensor> part_o,
+                          c10::optional<torch::Tensor> part_lse) {
   using namespace fa;
   TORCH_CHECK(q.is_cuda() && q.scalar_type() == torch::kBFloat16 && q.is_contiguous() && q.dim() == 3 &&
                   q.size(2) == HD,
@@ -363,14 +397,33 @@ void prefill_attention_tc(torch::Tensor q, int64_t k, int64_t v, int64_t blk_str
   p.seq_lens = seq_lens.data_ptr<int>();
   p.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
   p.err = err.data_ptr<int>();
+  const int S = static_cast<int>(std::max<int64_t>(1, num_splits));
+  const int T = q.size(0);
+  p.num_splits = S;
+  p.part_o = nullptr;
+  p.part_lse = nullptr;
+  if (S > 1) {
+    TORCH_CHECK(part_o.has_value() && part_lse.has_value() && part_o->scalar_type() == torch::kFloat32 &&
+                    part_lse->scalar_type() == torch::kFloat32 &&
+                    part_o->numel() >= (int64_t)T * Hq * S * HD && part_lse->numel() >= (int64_t)T * Hq * S,
+                "prefill_tc: split-KV scratch too small");
+    p.part_o = part_o->data_ptr<float>();
+    p.part_lse = part_lse->data_ptr<float>();
+  }
+  TORCH_CHECK((int64_t)B * S < 65536, "prefill_tc: too many sequences x splits");
   static bool attr = false;
   if (!attr) {
     AXR_CHECK_CUDA(cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
     attr = true;
   }
-  dim3 grid((max_q + 2 * BM - 1) / (2 * BM), Hq, B);
-  prefill_tc_kernel<<<grid, THREADS, SMEM, at::cuda::getCurrentCUDAStream()>>>(tk, tv, p);
+  dim3 grid((max_q + 2 * BM - 1) / (2 * BM), Hq, B * S);
+  auto st = at::cuda::getCurrentCUDAStream();
+  prefill_tc_kernel<<<grid, THREADS, SMEM, st>>>(tk, tv, p);
   AXR_CHECK_CUDA(cudaGetLastError());
+  if (S > 1 && T > 0) {
+    decode_combine_kernel<128><<<T * Hq, 128, 0, st>>>(p.part_o, p.part_lse, p.out, S);
+    AXR_CHECK_CUDA(cudaGetLastError());
+  }
 }
 
 }  // namespace axr
