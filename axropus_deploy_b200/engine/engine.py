@@ -95,6 +95,8 @@ class EngineConfig:
     # "model" (needs a draft model); depth adapts between 1 and spec_max_depth
     spec: str = ""
     spec_max_depth: int = 8
+    # [AMF_*] trace lines (None: KORITH_AMF_TRACE decides)
+    trace: Optional[bool] = None
 
 
 class LLMEngine:
@@ -122,6 +124,9 @@ class LLMEngine:
             from .cuda_graph import DecodeGraphRunner
 
             self._graphs = DecodeGraphRunner(self)
+        from .trace import AmfTrace
+
+        self.trace = AmfTrace(cfg.trace)
         self.spec = None
         if cfg.spec:
             from .spec import ModelDrafter, SpecDecoder
@@ -169,6 +174,29 @@ class LLMEngine:
         while self.has_unfinished():
             self.step()
         return [r.output for r in reqs]
+
+    def _trace_key(self, r: Request, limit: int, hit) -> None:
+        from ..amf.keys import amf_hash_tokens
+
+        disk = getattr(self.amf, "disk", None)
+        ctx = getattr(disk, "ctx", None)
+        self.trace.key("hit" if hit is not None else "miss", getattr(ctx, "model_hash", 0),
+                       getattr(ctx, "tenant_hash", 0), amf_hash_tokens(r.prompt[:limit]), self.cfg.max_model_len,
+                       self.cfg.max_prefill_tokens, getattr(ctx, "rope_base_bits", 0),
+                       getattr(ctx, "rope_scale_bits", 0), getattr(ctx, "sampling_hash", 0), getattr(ctx, "rng_hash", 0))
+        if hit is None:
+            r.amf_miss_reason = "first_request" if self.amf.stat.get("captures", 0) == 0 else "not_found"
+
+    def run_summary(self) -> dict:
+        """``[KORITH_RUN_SUMMARY]`` line (when tracing) and its fields."""
+        gen = sum(len(r.output) for r in self.finished) + sum(len(r.output) for r in self.running)
+        if self.amf is not None and self.trace.enabled:
+            a = self.amf.stat
+            self.trace.stats({"saved_ms": self.trace.n["saved_ms"], "saved_tokens": self.stat["restored_tokens"],
+                              "hits": self.trace.n["hits"], "misses": self.trace.n["misses"],
+                              "blocks": self.stat["restored_tokens"] // PAGE,
+                              "failures": a.get("capture_failures", 0), "admit": a.get("captures", 0)})
+        return self.trace.summary(gen)
 
     def close(self) -> None:
         """Release CUDA graphs (they hold device memory and must go before the
@@ -248,6 +276,8 @@ class LLMEngine:
                 if hit is not None and hit.n_pages <= n_local:
                     hit.release()
                     hit = None
+                if self.trace.enabled:
+                    self._trace_key(r, limit, hit)
             computed_pages = max(n_local, hit.n_pages if hit else 0)
             new_tokens = len(r.prompt) - computed_pages * PAGE
             if admitted and new_tokens > budget:
@@ -286,6 +316,7 @@ class LLMEngine:
                                      promote_from=hit.tier)
                 self.amf.note_restored(hit, r.restore_ms, 0.0)
                 self.stat["restored_tokens"] += r.restored_tokens
+                self.trace.hit(len(r.prompt), hit.n_tokens, hit.n_tokens, r.restore_ms, hit.tier)
             elif n_local:
                 r.amf_tier = "apc"
             r.num_computed = computed_pages * PAGE
@@ -361,9 +392,19 @@ class LLMEngine:
             max_seq_len=max(lens),
             logits_idx=torch.tensor([c - 1 for c in cu[1:]], dtype=torch.int32).to(dev, non_blocking=True),
         )
+        t_pf = time.perf_counter()
         logits = self.model.forward(torch.tensor(toks, dtype=torch.int32).to(dev, non_blocking=True), meta,
                                     self.cache)
-        new = self._sample(logits, reqs)
+        new = self._sample(logits, reqs)  # synchronises with the forward
+        pf_ms = (time.perf_counter() - t_pf) * 1e3
+        n_new = len(toks)
+        cold = [r for r in reqs if r.amf_tier == "cold"]
+        if cold and len(cold) == len(reqs):
+            self.trace.note_prefill(n_new, pf_ms)
+        if self.amf is not None and self.trace.enabled:
+            for r in cold:
+                share = (len(r.prompt) - prefilled_from[r.req_id]) / max(1, n_new)
+                self.trace.miss(getattr(r, "amf_miss_reason", "first_request"), pf_ms * share, len(r.prompt))
         done: List[Request] = []
         for r, t in zip(reqs, new):
             full = len(r.prompt) // PAGE

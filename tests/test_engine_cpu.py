@@ -77,3 +77,33 @@ def test_hashes_are_chained():
     a = block_hashes(list(range(48)))
     b = block_hashes([7] + list(range(1, 48)))
     assert all(x != y for x, y in zip(a, b))  # a change in block 0 changes every later hash
+
+
+def test_amf_trace_lines(model, tmp_path, monkeypatch):
+    """[AMF_KEY] / [AMF_MISS] / [AMF_SKIP] / [AMF_HIT] / [AMF_STATS] / [KORITH_RUN_SUMMARY]
+    lines with the reference's field names, engine events as JSON lines."""
+    import io
+    import json
+
+    events = tmp_path / "events.jsonl"
+    monkeypatch.setenv("KORITH_ENGINE_EVENTS_PATH", str(events))
+    cfg = model.cfg
+    pool = G1Pool(cfg.num_layers, cfg.num_kv_heads, cfg.head_dim, "raw", slots_per_shard=64)
+    eng = LLMEngine(model, EngineConfig(num_blocks=160, max_model_len=1024, trace=True), AmfManager(raw_pool=pool))
+    buf = io.StringIO()
+    eng.trace.stream = buf
+    prefix = list(range(7, 7 + 256))
+    eng.generate([prefix + [1, 2, 3]], SamplingParams(max_tokens=3))
+    eng.evict_live_cache()
+    eng.generate([prefix + [4, 5, 6, 7]], SamplingParams(max_tokens=3))
+    summ = eng.run_summary()
+    out = buf.getvalue().splitlines()
+    tags = [ln.split(" ", 1)[0] for ln in out]
+    assert tags.count("[AMF_KEY]") == 2 and "[AMF_MISS]" in tags and "[AMF_HIT]" in tags and "[AMF_SKIP]" in tags
+    assert tags[-2:] == ["[AMF_STATS]", "[KORITH_RUN_SUMMARY]"]
+    hit = next(ln for ln in out if ln.startswith("[AMF_HIT]"))
+    assert "prefix_tokens=256 skipped_tokens=256 baseline_ms=" in hit and " roi=" in hit
+    assert out[0].startswith("[AMF_KEY] result=miss model_hash=") and " prompt_hash=" in out[0]
+    assert summ["amf_hit"] == 1 and summ["tokens_generated"] == 6
+    kinds = [json.loads(ln)["type"] for ln in events.read_text().splitlines()]
+    assert kinds == ["amf_miss", "amf_hit"]
