@@ -124,7 +124,13 @@ class LLMEngine:
             from .cuda_graph import DecodeGraphRunner
 
             self._graphs = DecodeGraphRunner(self)
+        from .scheduler import AdmissionPolicy
         from .trace import AmfTrace
+
+        self.policy = AdmissionPolicy()
+        if getattr(model, "agree_min", None) is not None:
+            # tensor-parallel ranks must admit identically; their pool views may differ
+            self.policy.enabled = False
 
         self.trace = AmfTrace(cfg.trace)
         self.spec = None
@@ -254,9 +260,26 @@ class LLMEngine:
             lim = min(lim, r.amf_prefix_len // PAGE * PAGE)
         return max(0, lim)
 
+    def _held(self, r: Request) -> bool:
+        """Is r's prefix held by the live prefix cache or a G1 tier (admission order only)?"""
+        if len(r.prompt) > PAGE:
+            first = block_hashes(r.prompt_np, 1)
+            if first and first[0] in self.bm.by_hash:
+                return True
+        if self.amf is not None and self.amf.router is not None and r.amf_prefix_len:
+            from ..amf.keys import pool_key
+
+            g1 = self.amf.raw_pool or self.amf.comp_pool
+            return bool(g1 is not None and g1.contains(pool_key(r.prompt[: r.amf_prefix_len // PAGE * PAGE])))
+        return False
+
     def _admit(self) -> List[Request]:
         admitted: List[Request] = []
-        budget = self.cfg.max_prefill_tokens
+        if len(self.waiting) > 1:
+            self.waiting = self.policy.order(self.waiting, self._held, spec=self.spec is not None)
+        decoding = sum(1 for r in self.running if r.state == "running")
+        head_hit = bool(self.waiting) and bool(self.waiting[0].__dict__.get("_held"))
+        budget = self.policy.budget(self.cfg.max_prefill_tokens, decoding, self.cfg.max_batch, head_hit)
         while self.waiting and self.free_rows:
             r = self.waiting[0]
             limit = self._amf_limit(r)

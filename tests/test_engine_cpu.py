@@ -107,3 +107,25 @@ def test_amf_trace_lines(model, tmp_path, monkeypatch):
     assert summ["amf_hit"] == 1 and summ["tokens_generated"] == 6
     kinds = [json.loads(ln)["type"] for ln in events.read_text().splitlines()]
     assert kinds == ["amf_miss", "amf_hit"]
+
+
+def test_admission_policy_prefers_hits_and_scales_budget(monkeypatch):
+    from types import SimpleNamespace
+
+    from axropus_deploy_b200.engine.scheduler import AdmissionPolicy
+
+    monkeypatch.setenv("KORITH_VLLM_STARVATION_S", "100")
+    pol = AdmissionPolicy()
+    mk = lambda i, n, t: SimpleNamespace(prompt=[0] * n, t_arrival=t, params=SimpleNamespace(), i=i)
+    w = [mk(0, 4000, 0.0), mk(1, 300, 0.1), mk(2, 5000, 0.2), mk(3, 800, 0.3)]
+    held = {0: False, 1: False, 2: True, 3: False}
+    order = [r.i for r in pol.order(w, lambda r: held[r.i], now=1.0)]
+    assert order == [2, 1, 3, 0]  # the restorable prompt first, then shorter cold prompts
+    old = mk(9, 9000, -200.0)  # starving: goes first whatever its cost
+    assert pol.order(w + [old], lambda r: held.get(r.i, False), now=1.0)[0].i == 9
+    assert pol.budget(16384, decoding=10, max_batch=64, head_is_hit=False) == 16384
+    assert pol.budget(16384, decoding=60, max_batch=64, head_is_hit=False) == 12288
+    assert pol.budget(16384, decoding=60, max_batch=64, head_is_hit=True) == 16384
+    monkeypatch.setenv("KORITH_VLLM_DECODE_FIRST", "0")
+    off = AdmissionPolicy()
+    assert [r.i for r in off.order(w, lambda r: True)] == [0, 1, 2, 3]
