@@ -33,7 +33,7 @@ import torch.nn.functional as F
 from .. import ops
 from ..ops.kvcache import KVCache
 from ..parallel.dist import DistInfo
-from ..parallel.tp import TILE_M, TpGemm, ag_gemm_nccl, gemm_rs_nccl
+from ..parallel.tp import TILE_M, PeerAllReduce, TpGemm, ag_gemm_nccl, gemm_rs_nccl
 from .config import ModelConfig
 from .llama import AttnMeta, LlamaModel
 
@@ -97,6 +97,8 @@ class TpLlamaModel:
         self.scale = 1.0 / math.sqrt(D)
         self.max_rows = -(-max(max_tokens, 1) // (TILE_M * W)) * TILE_M
         self.tp = TpGemm(info, self.max_rows, H, H) if W > 1 else None
+        # decode / short-prefill all-reduces: one kernel over peer memory (NCCL beyond 1M elements)
+        self.ar = PeerAllReduce(info, 1 << 20) if W > 1 else None
 
     # ------------------------------------------------------------------ weights
     def _shard_from(self, m: LlamaModel) -> None:
@@ -145,6 +147,8 @@ class TpLlamaModel:
     def _all_reduce(self, x: torch.Tensor) -> torch.Tensor:
         if self.world == 1:
             return x
+        if self.ar is not None and self.ar.on_gpu:
+            return self.ar(x)
         if x.device.type == "cpu":  # gloo ranks: reduce in fp32
             t = x.float()
             dist.all_reduce(t)

@@ -148,6 +148,44 @@ def _gemm_rs_host(a, w, world, rank, out=None):
     return y
 
 
+class PeerAllReduce:
+    """Sum of a bf16 tensor over the group with one kernel over NVLink peer memory
+    (``csrc/kernels/allreduce.cu``) -- for decode-sized activations, where a collective
+    library's launch and protocol latency dominates. Larger tensors, odd sizes and CPU
+    ranks go to ``torch.distributed.all_reduce``. The epoch is kept on the device, so the
+    call can be captured in a CUDA graph."""
+
+    def __init__(self, info: DistInfo, cap_elems: int = 1 << 20):
+        self.info, self.world, self.rank = info, info.world, info.rank
+        self.cap = int(cap_elems)
+        self.on_gpu = info.device.type == "cuda" and info.world > 1
+        if not self.on_gpu:
+            return
+        dev = info.device
+        self.buf, p_buf = _symm(2 * self.world * self.cap, torch.bfloat16, info)
+        self.flag, p_flag = _symm(2 * self.world, torch.int32, info)
+        self.peers = torch.tensor([p_buf, p_flag], dtype=torch.int64, device=dev).view(-1).contiguous()
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.bar = torch.zeros(2, dtype=torch.int32, device=dev)
+        self.err = error_flag(dev)
+
+    def __call__(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if self.world == 1:
+            return x if out is None else out.copy_(x)
+        if not self.on_gpu or x.dtype != torch.bfloat16 or x.numel() % 8 or x.numel() > self.cap:
+            t = x.float() if x.device.type == "cpu" else x
+            dist.all_reduce(t)
+            if t is not x:
+                x.copy_(t)
+            return x if out is None else out.copy_(x)
+        x = x.contiguous()
+        if out is None:
+            out = x  # in place: the input is fully pushed before any GPU sums
+        cuda_ext().peer_allreduce(x, out, self.rank, self.world, self.peers, self.buf, self.flag, self.epoch,
+                                  self.bar, self.cap, self.err)
+        return out
+
+
 # ---------------------------------------------------------------------- NCCL baselines
 def ag_gemm_nccl(x_shard: torch.Tensor, w: torch.Tensor, world: int) -> torch.Tensor:
     full = torch.empty(world * x_shard.shape[0], x_shard.shape[1], dtype=x_shard.dtype, device=x_shard.device)

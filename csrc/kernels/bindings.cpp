@@ -50,6 +50,9 @@ void moe_gemm(torch::Tensor a, torch::Tensor w, int64_t mode, int64_t E_l, int64
               c10::optional<torch::Tensor> peer_comb_flag, torch::Tensor done_ctr, torch::Tensor err);
 void moe_combine(torch::Tensor comb, torch::Tensor out, torch::Tensor comb_flag, int64_t world, int64_t epoch,
                  int64_t K, torch::Tensor err);
+void peer_allreduce(torch::Tensor x, torch::Tensor out, int64_t rank, int64_t world, torch::Tensor peers,
+                    torch::Tensor buf, torch::Tensor flag, torch::Tensor epoch, torch::Tensor bar, int64_t cap,
+                    torch::Tensor err);
 }  // namespace axr
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -68,6 +71,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_tc", &axr::gemm_tc);
   m.def("gemm_tp", &axr::gemm_tp);
   m.def("moe_dispatch", &axr::moe_dispatch);
+  m.def("peer_allreduce", &axr::peer_allreduce);
   m.def("moe_gemm", &axr::moe_gemm);
   m.def("moe_combine", &axr::moe_combine);
 }

@@ -81,3 +81,16 @@ def test_tp_llama_two_gpus():
     r = subprocess.run(cmd, capture_output=True, text=True, env=env, cwd=ROOT)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert "TP_LLAMA_CHECK ok" in r.stdout
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_peer_allreduce_two_gpus():
+    """One-shot peer all-reduce vs NCCL, repeated and from a captured CUDA graph."""
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "20", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr", "127.0.0.1", "--master-port", "29535",
+           os.path.join(ROOT, "benchmarks", "allreduce.py"), "--check"]
+    r = subprocess.run(cmd, capture_output=True, text=True, env=env, cwd=ROOT)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert "AR_CHECK ok" in r.stdout
