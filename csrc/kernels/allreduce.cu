@@ -50,9 +50,10 @@ __global__ void __launch_bounds__(256) peer_allreduce_kernel(ArArgs a) {
       dst[v] = x;
     }
   }
-  __threadfence_system();
   __syncthreads();
-  // 2. the last CTA to finish its pushes raises this GPU's flag on every peer
+  // 2. the last CTA to finish its pushes raises this GPU's flag on every peer (the
+  //    barrier + system fence order the whole CTA's peer stores before the flags)
+  if (threadIdx.x == 0) __threadfence_system();
   if (threadIdx.x == 0 && atomicAdd(&a.bar[0], 1) == gridDim.x - 1) {
     a.bar[0] = 0;
     __threadfence_system();
@@ -115,10 +116,13 @@ void peer_allreduce(torch::Tensor x, torch::Tensor out, int64_t rank, int64_t wo
   a.bar = bar.data_ptr<int>();
   a.err = err.data_ptr<int>();
   a.wait_ns = peer_wait_ns();
-  const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>(32, (a.n8 + 1023) / 1024)));
-  void* args[] = {&a};
-  AXR_CHECK_CUDA(cudaLaunchCooperativeKernel(reinterpret_cast<void*>(peer_allreduce_kernel), dim3(grid), dim3(256),
-                                             args, 0, at::cuda::getCurrentCUDAStream()));
+  // A CTA waits for this GPU's own flag, which the last CTA to push raises: every CTA
+  // must be resident at once. With at most 32 CTAs of 256 threads (one per 4096 vectors)
+  // they all fit on the GPU at any time, so a plain launch suffices; were one to be held
+  // back anyway, the others' waits end at the bound with an error code, not a hang.
+  const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>(32, (a.n8 + 4095) / 4096)));
+  peer_allreduce_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+  AXR_CHECK_CUDA(cudaGetLastError());
 }
 
 }  // namespace axr
