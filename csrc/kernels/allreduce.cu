@@ -117,10 +117,10 @@ void peer_allreduce(torch::Tensor x, torch::Tensor out, int64_t rank, int64_t wo
   a.err = err.data_ptr<int>();
   a.wait_ns = peer_wait_ns();
   // A CTA waits for this GPU's own flag, which the last CTA to push raises: every CTA
-  // must be resident at once. With at most 32 CTAs of 256 threads (one per 4096 vectors)
-  // they all fit on the GPU at any time, so a plain launch suffices; were one to be held
+  // must be resident at once. With at most 32 CTAs of 256 threads
+  // they all fit on the GPU at any time, so a plain launch suffices (one CTA per 1024 vectors); were one to be held
   // back anyway, the others' waits end at the bound with an error code, not a hang.
-  const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>(32, (a.n8 + 4095) / 4096)));
+  const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>(32, (a.n8 + 1023) / 1024)));
   peer_allreduce_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(a);
   AXR_CHECK_CUDA(cudaGetLastError());
 }
