@@ -139,6 +139,7 @@ def run(args) -> None:
 
     for _ in range(args.warmup):
         gen([wl.request()[0] for _ in range(args.batch)], sp)
+    choice_state = wl.choice_state()
     waves = [[wl.request()[0] for _ in range(args.batch)] for _ in range(args.steps)]
     sampler = ClockSampler(local)
     ranks.gather("sync")
@@ -151,8 +152,9 @@ def run(args) -> None:
         n_out += sum(len(o.outputs[0].token_ids) for o in outs)
     clocks = sampler.stop()
     res = ranks.gather({"ms": total_ms, "n_out": n_out, "hit": ttft_hit, "cold": ttft_cold, "clocks": clocks})
-    # e2e: same waves on the host clock
-    e2e_w = [[wl.request()[0] for _ in range(args.batch)] for _ in range(args.e2e_waves)]
+    # e2e on the host clock: the timed waves' hit/cold mix and prefix picks, new tokens
+    wl.set_choice_state(choice_state)
+    e2e_w = [[wl.request()[0] for _ in range(args.batch)] for _ in range(args.e2e_waves or args.steps)]
     t0 = time.perf_counter()
     n_e2e = sum(len(o.outputs[0].token_ids) for w in e2e_w for o in gen(w, sp))
     torch.cuda.synchronize()

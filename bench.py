@@ -62,7 +62,7 @@ def parse_args(argv=None):
     p.add_argument("--pool", default="raw", choices=["raw", "fp8", "int4"])
     p.add_argument("--kv-fmt", default="bf16", choices=["bf16", "fp8", "int4"])
     p.add_argument("--ttft-samples", type=int, default=12)
-    p.add_argument("--e2e-waves", type=int, default=2)
+    p.add_argument("--e2e-waves", type=int, default=0, help="0: as many as --steps")
     p.add_argument("--graphs", type=int, default=1)
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--layers", type=int, default=None, help="debug only: fewer layers (invalidates the number)")
@@ -135,7 +135,10 @@ class Workload:
         ranks = np.arange(1, args.prefixes + 1, dtype=np.float64)
         p = ranks ** (-args.zipf)
         self.zipf_p = p / p.sum()
+        # reuse decisions and Zipf picks, and the random tokens, come from separate streams:
+        # replaying the choice stream gives a wave of the same hit/cold mix with new tokens
         self.rng = np.random.default_rng(args.seed * 1000 + 17 + rank)
+        self.tok_rng = np.random.default_rng(args.seed * 1000 + 29 + rank)
 
     def request(self, force: str = ""):
         a = self.args
@@ -144,9 +147,15 @@ class Workload:
             i = int(self.rng.choice(a.prefixes, p=self.zipf_p))
             prefix = self.prefixes[i]
         else:
-            prefix = self.rng.integers(0, self.vocab, a.prefix_len, dtype=np.int64).tolist()
-        suffix = self.rng.integers(0, self.vocab, a.suffix_len, dtype=np.int64).tolist()
+            prefix = self.tok_rng.integers(0, self.vocab, a.prefix_len, dtype=np.int64).tolist()
+        suffix = self.tok_rng.integers(0, self.vocab, a.suffix_len, dtype=np.int64).tolist()
         return prefix + suffix, reuse
+
+    def choice_state(self):
+        return self.rng.bit_generator.state
+
+    def set_choice_state(self, state) -> None:
+        self.rng.bit_generator.state = state
 
 
 def pct(xs, q):
@@ -280,6 +289,7 @@ def run_ours(args) -> None:
     # ---- 3. throughput waves
     for _ in range(args.warmup):
         run_requests([wl.request()[0] for _ in range(args.batch)])
+    choice_state = wl.choice_state()
     waves = [[wl.request()[0] for _ in range(args.batch)] for _ in range(args.steps)]
     sampler = ClockSampler(dev.index)
     torch.cuda.synchronize()
@@ -309,7 +319,11 @@ def run_ours(args) -> None:
     hits = {k: amf.stat[k] - amf0.get(k, 0) for k in ("hits_g1_raw", "hits_g1_pool", "misses")}
 
     # ---- 4. e2e through the public API on the host clock
-    e2e_waves = [[wl.request()[0] for _ in range(args.batch)] for _ in range(args.e2e_waves)]
+    # same hit/cold mix and prefix picks as the timed waves (replayed choice stream), new
+    # suffixes and fresh cold prefixes
+    wl.set_choice_state(choice_state)
+    n_e2e = args.e2e_waves or args.steps
+    e2e_waves = [[wl.request()[0] for _ in range(args.batch)] for _ in range(n_e2e)]
     torch.cuda.synchronize()
     barrier(info)
     h0 = time.perf_counter()
@@ -321,7 +335,7 @@ def run_ours(args) -> None:
     torch.cuda.synchronize()
     e2e_s = time.perf_counter() - h0
     e2e_s = all_reduce_max(e2e_s, info)
-    e2e_val = args.e2e_waves * args.batch * args.out_tokens * info.world / e2e_s
+    e2e_val = n_e2e * args.batch * args.out_tokens * info.world / e2e_s
 
     gathered = all_gather_object({"ttft_hit": ttft_hit, "ttft_cold": ttft_cold, "restore_ms": restore_ms,
                                   "rest_gbps": rest_gbps, "rest_remote": rest_gbps_remote, "clocks": clocks, "ms": ms, "waves": wave_stats,
@@ -364,8 +378,8 @@ def run_ours(args) -> None:
             "wave_mix": gathered[0]["waves"], "amf_hits_rank0": gathered[0]["hits"],
             "clocks": {"sm_mhz": ck.get("sm_mhz"), "sm_max_mhz": ck.get("sm_max_mhz"), "reasons": reasons},
             "e2e": {"value": round(e2e_val, 2), "unit": "output tokens/s (whole job)",
-                    "h2d_bytes_per_step": int(h2d / max(1, args.e2e_waves)),
-                    "d2h_bytes_per_step": int(d2h / max(1, args.e2e_waves))},
+                    "h2d_bytes_per_step": int(h2d / n_e2e),
+                    "d2h_bytes_per_step": int(d2h / n_e2e)},
             "gpu_launches": int(launches_timed),
             "baseline_note": "vs_baseline divides by the reference's published warm decode rate "
                              "(286.83 tok/s, llama.cpp 1B q4, batch 1, GPU not stated)",
