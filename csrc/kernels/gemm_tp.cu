@@ -45,6 +45,7 @@ constexpr int TSMEM = 1024 + TST * (TA_BYTES + TB_BYTES) + STG_BYTES + 256;
 constexpr int TP_THREADS = 320;
 constexpr int AG_CH = 8;   // a remote 128-row block is pulled as 8 chunks of 16 rows
 constexpr int RS_CH = 16;  // an owned 128-row block is reduced as 16 chunks of 8 rows
+constexpr int RS_MAXW = 8;  // partials loaded together per reduction step
 constexpr int MODE_PLAIN = 0, MODE_AG = 1, MODE_RS = 2;
 
 struct TpArgs {
@@ -329,25 +330,32 @@ __global__ void __launch_bounds__(TP_THREADS, 1) gemm_tp_kernel(const __grid_con
         const int lb = item / RS_CH, ch = item % RS_CH;
         if (!comm_wait(g.cnt + 2 * lb + parity, target, g.err, 8, ct, comm_ok, g.wait_ns)) break;
         const long long e0 = ((long long)lb * TBM + ch * 8) * g.N;
+        // every partial of a vector is loaded before any is summed (up to 8 GPUs x 2 vectors
+        // in flight per thread): the reduction is bound by memory-level parallelism
         for (long long v = ct; v < vecs; v += 128 * 2) {
           float acc[2][8];
 #pragma unroll
           for (int u = 0; u < 2; ++u)
 #pragma unroll
             for (int j = 0; j < 8; ++j) acc[u][j] = 0.f;
-          for (int p = 0; p < g.world; ++p) {
-            uint4 x[2];
+          for (int p0 = 0; p0 < g.world; p0 += RS_MAXW) {
+            uint4 x[RS_MAXW][2];
 #pragma unroll
-            for (int u = 0; u < 2; ++u)
-              if (v + u * 128 < vecs)
-                x[u] = *reinterpret_cast<const uint4*>(rbase + p * slot + e0 + (v + u * 128) * 8);
+            for (int q = 0; q < RS_MAXW; ++q)
 #pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              if (v + u * 128 < vecs) {
-                acc[u][0] += bf16_lo(x[u].x); acc[u][1] += bf16_hi(x[u].x);
-                acc[u][2] += bf16_lo(x[u].y); acc[u][3] += bf16_hi(x[u].y);
-                acc[u][4] += bf16_lo(x[u].z); acc[u][5] += bf16_hi(x[u].z);
-                acc[u][6] += bf16_lo(x[u].w); acc[u][7] += bf16_hi(x[u].w);
+              for (int u = 0; u < 2; ++u)
+                if (p0 + q < g.world && v + u * 128 < vecs)
+                  x[q][u] = *reinterpret_cast<const uint4*>(rbase + (p0 + q) * slot + e0 + (v + u * 128) * 8);
+#pragma unroll
+            for (int q = 0; q < RS_MAXW; ++q) {
+#pragma unroll
+              for (int u = 0; u < 2; ++u) {
+                if (p0 + q < g.world && v + u * 128 < vecs) {
+                  acc[u][0] += bf16_lo(x[q][u].x); acc[u][1] += bf16_hi(x[q][u].x);
+                  acc[u][2] += bf16_lo(x[q][u].y); acc[u][3] += bf16_hi(x[q][u].y);
+                  acc[u][4] += bf16_lo(x[q][u].z); acc[u][5] += bf16_hi(x[q][u].z);
+                  acc[u][6] += bf16_lo(x[q][u].w); acc[u][7] += bf16_hi(x[q][u].w);
+                }
               }
             }
           }
