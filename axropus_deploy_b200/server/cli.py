@@ -27,6 +27,13 @@ def build_parser() -> argparse.ArgumentParser:
     b.add_argument("--output", default=None)
     b.add_argument("--quick", action="store_true")
     sub.add_parser("info", help="print system information")
+    ab = sub.add_parser("amf-bench", help="cold then warm generation of one prompt through the AMF tiers, "
+                                          "with [AMF_*] trace lines and a run summary")
+    ab.add_argument("--model", default="tiny128")
+    ab.add_argument("--prompt-tokens", type=int, default=2048)
+    ab.add_argument("--max-tokens", type=int, default=32)
+    ab.add_argument("--warm-runs", type=int, default=3)
+    ab.add_argument("--device", default=None)
     return p
 
 
@@ -118,9 +125,47 @@ def _cmd_info(a) -> int:
     return 0
 
 
+def _cmd_amf_bench(a) -> int:
+    """Benchmark mode of the reference's vLLM server (korith_vllm_server.py:52-180): one
+    cold run captures the prompt's prefix, the live cache is dropped, warm runs restore it.
+    Trace lines go to stderr, the summary JSON to stdout."""
+    import numpy as np
+    import torch
+
+    from ..config import KorithConfig
+    from ..engine.engine import SamplingParams
+
+    dev = a.device or ("cuda" if torch.cuda.is_available() else "cpu")
+    kcfg = KorithConfig.from_env()
+    kcfg.enable_amf = False  # G1 pool only; the disk store is opted into through KORITH_* variables
+    kcfg.vram_cache_gb = kcfg.vram_cache_gb or 1.0
+    from .app import build_engine
+
+    eng = build_engine(AxropusConfig.load(None, {"model": a.model, "device": dev}), kcfg)
+    eng.trace.enabled = True
+    rng = np.random.default_rng(0)
+    prompt = rng.integers(0, eng.model.cfg.vocab, a.prompt_tokens).tolist()
+    sp = SamplingParams(max_tokens=a.max_tokens)
+    runs = []
+    for i in range(1 + a.warm_runs):
+        if i == 1:
+            eng.evict_live_cache()
+        r = eng.add_request(prompt, sp, amf_prefix_len=a.prompt_tokens - 1)
+        while eng.has_unfinished():
+            eng.step()
+        if i > 0:
+            eng.evict_live_cache()
+        runs.append({"run": "cold" if i == 0 else "warm", "tier": r.amf_tier, "ttft_ms": round(r.ttft_ms, 3),
+                     "restored_tokens": r.restored_tokens, "restore_ms": round(r.restore_ms, 3)})
+    summary = eng.run_summary()
+    print(json.dumps({"model": eng.model.cfg.name, "device": str(eng.device), "runs": runs, "summary": summary},
+                     indent=2, default=str))
+    return 0
+
+
 def main(argv=None) -> int:
     a = build_parser().parse_args(argv)
-    return {"serve": _cmd_serve, "bench": _cmd_bench, "info": _cmd_info}[a.command](a)
+    return {"serve": _cmd_serve, "bench": _cmd_bench, "info": _cmd_info, "amf-bench": _cmd_amf_bench}[a.command](a)
 
 
 if __name__ == "__main__":

@@ -286,3 +286,16 @@ def test_dynamo_components():
     sub.run([KvBlockEvent("created", "w0", "p1", 8192), KvBlockEvent("evicted", "w0", "p1", 8192),
              KvBlockEvent("created", "w0", "p2", 256), KvBlockEvent("evicted", "w0", "p2", 256)])
     assert [k["prefix_hash"] for k in kept] == ["p1"] and sub.stat["skipped"] == 1
+
+
+def test_codec_ids_and_amf_bench_cli(capsys):
+    from axropus_deploy_b200.codecs import AMF_CODEC_FP8, AMF_CODEC_INT4, codec_from_id, codec_id
+    from axropus_deploy_b200.server.cli import main
+
+    assert codec_id("int4_g64") == AMF_CODEC_INT4 and codec_from_id(AMF_CODEC_FP8) == "fp8_e4m3"
+    with pytest.raises(KeyError):
+        codec_id("nvfp4")
+    assert main(["amf-bench", "--model", "tiny", "--prompt-tokens", "256", "--max-tokens", "2", "--warm-runs", "1",
+                 "--device", "cpu"]) == 0
+    out = json.loads(capsys.readouterr().out)
+    assert out["runs"][0]["tier"] == "cold" and out["runs"][1]["tier"].startswith("g1")
