@@ -292,7 +292,7 @@ def test_codec_ids_and_amf_bench_cli(capsys):
     from axropus_deploy_b200.codecs import AMF_CODEC_FP8, AMF_CODEC_INT4, codec_from_id, codec_id
     from axropus_deploy_b200.server.cli import main
 
-    assert codec_id("int4_g64") == AMF_CODEC_INT4 and codec_from_id(AMF_CODEC_FP8) == "fp8_e4m3"
+    assert codec_id("int4_g64_asym") == AMF_CODEC_INT4 and codec_from_id(AMF_CODEC_FP8) == "fp8_e4m3"
     with pytest.raises(KeyError):
         codec_id("nvfp4")
     assert main(["amf-bench", "--model", "tiny", "--prompt-tokens", "256", "--max-tokens", "2", "--warm-runs", "1",
