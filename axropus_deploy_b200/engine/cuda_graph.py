@@ -109,3 +109,125 @@ class DecodeGraphRunner:
         self.graphs.clear()
         self.outs.clear()
         self.pool = None
+
+
+PREFILL_BUCKETS = [64, 128, 256, 512]
+
+
+class PrefillGraphRunner:
+    """CUDA-graph replay of a one-sequence prefill of at most 512 new tokens -- the step
+    that decides the TTFT of an AMF hit (a short suffix over a restored prefix), where a
+    ~300-kernel forward of small GEMMs is bound by the host launching it.
+
+    One graph per (token bucket, context bucket): the new tokens are padded up to the
+    bucket with slot -1 (no KV write, rows never read back), the attention grids are
+    sized for the bucket's query rows and the context bucket's longest KV range (split-
+    KV slices past the sequence's real length find no keys and mark their partials
+    empty), and the real lengths reach the kernels through device tensors refreshed
+    with one pinned copy before each replay. On CPU, :meth:`run` executes the same
+    padded step eagerly, which is how the padding is tested without a GPU.
+    """
+
+    def __init__(self, engine, max_tokens: int = 512, max_graphs: int = 24):
+        self.eng = engine
+        dev = engine.device
+        self.buckets = [b for b in PREFILL_BUCKETS if b <= max_tokens] or [PREFILL_BUCKETS[0]]
+        self.max_t = self.buckets[-1]
+        self.max_graphs = max_graphs
+        self.on_gpu = dev.type == "cuda"
+        self.ints = torch.zeros(3, self.max_t, dtype=torch.int32, device=dev)   # tok, pos, slot
+        self.small = torch.zeros(4, dtype=torch.int32, device=dev)               # seq_len, 0, n, n-1
+        pin = self.on_gpu
+        self.host = torch.zeros(3, self.max_t, dtype=torch.int32, pin_memory=pin)
+        self.small_host = torch.zeros(4, dtype=torch.int32, pin_memory=pin)
+        self.bt = torch.zeros(1, engine.max_blocks_per_seq, dtype=torch.int32, device=dev)
+        self.graphs: Dict[tuple, torch.cuda.CUDAGraph] = {}
+        self.outs: Dict[tuple, torch.Tensor] = {}
+        self.kernels: Dict[tuple, int] = {}
+        self.pool = None
+        self.ws = DecodeWorkspace()
+        self.stat = {"replays": 0, "captures": 0, "eager": 0}
+
+    def ctx_bucket(self, seq_len: int) -> int:
+        c = 2048
+        while c < seq_len:
+            c *= 2
+        return min(c, max(seq_len, self.eng.cfg.max_model_len))
+
+    def supports(self, reqs, n_tokens: int, seq_len: int) -> bool:
+        return len(reqs) == 1 and 0 < n_tokens <= self.max_t and seq_len <= self.eng.cfg.max_model_len and \
+            all(r.params.temperature <= 0 for r in reqs)
+
+    def _meta(self, tb: int, cb: int) -> AttnMeta:
+        return AttnMeta(mode="prefill", positions=self.ints[1, :tb], slots=self.ints[2, :tb], block_table=self.bt,
+                        seq_lens=self.small[0:1], cu_q=self.small[1:3], max_q=tb, max_seq_len=cb,
+                        logits_idx=self.small[3:4])
+
+    def _capture(self, key: tuple) -> None:
+        from ..ops import attention as att
+        from ..ops._ext import LAUNCHES
+
+        tb, cb = key
+        eng = self.eng
+        cfg = eng.model.cfg
+        hq = getattr(eng.model, "hq", cfg.num_heads)
+        # split scratch sized once for the largest bucket, shared by every graph
+        self.ws.get(self.max_t, hq, 32, cfg.head_dim, eng.device)
+        prev = att._PREFILL_WS
+        att._PREFILL_WS = self.ws
+        try:
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                eng.model.forward(self.ints[0, :tb], self._meta(tb, cb), eng.cache)  # warm-up (lazy init)
+            torch.cuda.current_stream().wait_stream(s)
+            g = torch.cuda.CUDAGraph()
+            n0 = LAUNCHES[0]
+            with torch.cuda.graph(g, pool=self.pool):
+                out = eng.model.forward(self.ints[0, :tb], self._meta(tb, cb), eng.cache)
+            self.kernels[key] = LAUNCHES[0] - n0
+            LAUNCHES[0] = n0
+            if self.pool is None:
+                self.pool = g.pool()
+        finally:
+            att._PREFILL_WS = prev
+        self.graphs[key] = g
+        self.outs[key] = out
+        self.stat["captures"] += 1
+
+    def run(self, r, toks: List[int], pos: List[int], slots: List[int], seq_len: int) -> torch.Tensor:
+        n = len(toks)
+        tb = self.buckets[bisect.bisect_left(self.buckets, n)]
+        cb = self.ctx_bucket(seq_len)
+        h = self.host
+        h[0, :n] = torch.tensor(toks, dtype=torch.int32)
+        h[1, :n] = torch.tensor(pos, dtype=torch.int32)
+        h[2, :n] = torch.tensor(slots, dtype=torch.int32)
+        if tb > n:
+            h[0, n:tb] = 0
+            h[1, n:tb] = pos[-1]
+            h[2, n:tb] = -1
+        self.small_host[0], self.small_host[1], self.small_host[2], self.small_host[3] = seq_len, 0, n, n - 1
+        self.ints[:, :tb].copy_(h[:, :tb], non_blocking=True)
+        self.small.copy_(self.small_host, non_blocking=True)
+        self.bt.copy_(self.eng.block_table[r.row:r.row + 1])
+        key = (tb, cb)
+        if not self.on_gpu:
+            self.stat["eager"] += 1
+            return self.eng.model.forward(self.ints[0, :tb], self._meta(tb, cb), self.eng.cache)
+        if key not in self.graphs:
+            if len(self.graphs) >= self.max_graphs:
+                self.stat["eager"] += 1
+                return self.eng.model.forward(self.ints[0, :tb], self._meta(tb, cb), self.eng.cache)
+            self._capture(key)
+        self.graphs[key].replay()
+        from ..ops._ext import LAUNCHES
+
+        LAUNCHES[0] += self.kernels[key]
+        self.stat["replays"] += 1
+        return self.outs[key]
+
+    def close(self) -> None:
+        self.graphs.clear()
+        self.outs.clear()
+        self.pool = None

@@ -88,6 +88,9 @@ class EngineConfig:
     capture_on_miss: bool = True
     amf_min_tokens: int = 64
     cuda_graphs: bool = False
+    # with cuda_graphs: one-sequence prefills of <= 512 new tokens (AMF-hit suffixes) replay
+    # CUDA graphs too (dense single-GPU models)
+    prefill_graphs: bool = True
     # expert parallelism: every GPU runs exactly one prefill and one decode forward per
     # step (empty when it has nothing to do) so the MoE collectives of all GPUs line up
     lockstep: bool = False
@@ -124,6 +127,12 @@ class LLMEngine:
             from .cuda_graph import DecodeGraphRunner
 
             self._graphs = DecodeGraphRunner(self)
+        self._prefill_graphs = None
+        if cfg.cuda_graphs and cfg.prefill_graphs and self.device.type == "cuda" and type(model) is LlamaModel \
+                and not model.cfg.is_moe:
+            from .cuda_graph import PrefillGraphRunner
+
+            self._prefill_graphs = PrefillGraphRunner(self)
         from .scheduler import AdmissionPolicy
         from .trace import AmfTrace
 
@@ -210,6 +219,9 @@ class LLMEngine:
         if self._graphs is not None:
             self._graphs.close()
             self._graphs = None
+        if self._prefill_graphs is not None:
+            self._prefill_graphs.close()
+            self._prefill_graphs = None
 
     def evict_live_cache(self, fraction: float = 1.0) -> int:
         """Drop cached (unreferenced) KV blocks -- forces later requests to restore from AMF."""
@@ -416,8 +428,11 @@ class LLMEngine:
             logits_idx=torch.tensor([c - 1 for c in cu[1:]], dtype=torch.int32).to(dev, non_blocking=True),
         )
         t_pf = time.perf_counter()
-        logits = self.model.forward(torch.tensor(toks, dtype=torch.int32).to(dev, non_blocking=True), meta,
-                                    self.cache)
+        if self._prefill_graphs is not None and self._prefill_graphs.supports(reqs, len(toks), lens[0]):
+            logits = self._prefill_graphs.run(reqs[0], toks, pos, slots, lens[0])
+        else:
+            logits = self.model.forward(torch.tensor(toks, dtype=torch.int32).to(dev, non_blocking=True), meta,
+                                        self.cache)
         new = self._sample(logits, reqs)  # synchronises with the forward
         pf_ms = (time.perf_counter() - t_pf) * 1e3
         n_new = len(toks)

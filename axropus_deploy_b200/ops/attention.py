@@ -5,6 +5,7 @@ CUDA tensors run the sm_100a kernels; CPU tensors run the fp32 PyTorch oracle
 from __future__ import annotations
 
 import math
+import os
 from typing import Optional
 
 import torch
@@ -15,6 +16,9 @@ from .kvcache import BF16, KVCache
 
 # prefill of bf16 pages on the tcgen05 kernel (False: the warp-level mma.sync kernel)
 PREFILL_TC = [True]
+# new tokens per sequence up to which the tcgen05 prefill packs the query heads of a KV head
+# into one tile's rows (AXR_PREFILL_GQA_PACK_MAX_Q; 0 turns packing off)
+GQA_PACK_MAX_Q = [int(os.environ.get("AXR_PREFILL_GQA_PACK_MAX_Q", "2048"))]
 
 _SMS = {}
 
@@ -140,14 +144,19 @@ def prefill_attention(q: torch.Tensor, cache: KVCache, layer: int, block_table: 
         out = torch.empty_like(q)
     if q.is_cuda:
         k, v, km, vm, bs, hs, mbs, mhs = cache.layer_args(layer)
-        if cache.fmt == BF16 and D == 128 and PREFILL_TC[0] and max_q >= 64:
-            # tensor-core (tcgen05 / TMEM) kernel on bf16 pages: 256-row query tiles, one CTA
-            # per SM; short suffixes over long prefixes split the KV range
+        G = Hq // cache.num_kv_heads
+        pack = G > 1 and max_q <= GQA_PACK_MAX_Q[0]
+        if cache.fmt == BF16 and D == 128 and PREFILL_TC[0] and max_q * (G if pack else 1) >= 64:
+            # tensor-core (tcgen05 / TMEM) kernel on bf16 pages: 256-row tiles, one CTA per
+            # SM; up to GQA_PACK_MAX_Q new tokens the G query heads of a KV head share the
+            # tiles (rows = token x head), and short suffixes over long prefixes split the KV range
+            rows, heads = (max_q * G, cache.num_kv_heads) if pack else (max_q, Hq)
             S = num_splits if num_splits is not None else prefill_num_splits(
-                seq_lens.shape[0], Hq, max_q, max_seq_len, q.device, q_tile=256, kv_tile=128, per_sm=1)
+                seq_lens.shape[0], heads, rows, max_seq_len, q.device, q_tile=256, kv_tile=128, per_sm=1)
             po, pl = _PREFILL_WS.get(T, Hq, S, D, q.device) if S > 1 else (None, None)
             cuda_ext().prefill_attention_tc(q, k, v, bs, hs, cache.num_blocks, block_table, cu_q, seq_lens,
-                                            cache.num_kv_heads, scale, max_q, out, error_flag(q.device), S, po, pl)
+                                            cache.num_kv_heads, scale, max_q, out, error_flag(q.device), S, po, pl,
+                                            G if pack else 1)
             return out
         S = num_splits if num_splits is not None else prefill_num_splits(seq_lens.shape[0], Hq, max_q, max_seq_len,
                                                                           q.device)

@@ -38,7 +38,7 @@ void prefill_attention_tc(torch::Tensor q, int64_t k, int64_t v, int64_t blk_str
                           int64_t num_blocks, torch::Tensor block_table, torch::Tensor cu_q, torch::Tensor seq_lens,
                           int64_t Hkv, double scale, int64_t max_q, torch::Tensor out, torch::Tensor err,
                           int64_t num_splits, c10::optional<torch::Tensor> part_o,
-                          c10::optional<torch::Tensor> part_lse);
+                          c10::optional<torch::Tensor> part_lse, int64_t gqa_pack);
 void moe_dispatch(torch::Tensor x, torch::Tensor topk_idx, torch::Tensor topk_w, int64_t E_l, int64_t rank,
                   int64_t world, int64_t epoch, int64_t cap_rows, torch::Tensor pair_pos, torch::Tensor gcount,
                   torch::Tensor grid_bar, torch::Tensor peers, torch::Tensor cnt_all, torch::Tensor cnt_flag,

@@ -1,6 +1,9 @@
 // Causal prefill attention on the 5th-generation tensor cores (tcgen05 + TMEM), bf16
-// paged KV cache, head_dim 128, GQA. One CTA = 256 query rows of one head, as two
-// 128-row sub-tiles A and B that ping-pong on the tensor core:
+// paged KV cache, head_dim 128, GQA. One CTA = 256 query rows, as two 128-row sub-tiles
+// A and B that ping-pong on the tensor core. A row is one (token, query head): either
+// the rows of one head (gpack = 1), or -- for short suffixes over long prefixes -- the
+// G = Hq / Hkv heads that share a KV head packed token-major (gpack = G), so a 128-token
+// suffix fills both sub-tiles and every KV tile loaded serves G heads.
 //
 //   warp 8     TMA producer: K_j and V_j (128 tokens each) are gathered through the
 //              block table as 8 pages x 2 halves of [16 tokens x 64 dims] boxes into a
@@ -56,6 +59,7 @@ struct Params {
   float scale_log2;
   volatile int* err;
   int num_splits;   // KV slices per (query tile, head, sequence); 1 = no split
+  int gpack;        // 1: grid.y = query heads; G = Hq/Hkv: grid.y = KV heads, rows = (token, head of the group)
   float* part_o;    // [T*Hq, S, 128] normalised partial outputs (S > 1)
   float* part_lse;  // [T*Hq, S] log2-domain log-sum-exps (S > 1)
 };
@@ -88,15 +92,17 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile_m = gridDim.x - 1 - blockIdx.x;  // longest (most KV tiles) first
   const int S = p.num_splits;
-  const int hq = blockIdx.y, b = blockIdx.z / S, split = blockIdx.z % S;
+  const int G = p.gpack;
+  const int hy = blockIdx.y, b = blockIdx.z / S, split = blockIdx.z % S;
   const int q0 = p.cu_q[b], nq = p.cu_q[b + 1] - q0;
-  const int row0 = tile_m * 2 * BM;  // first query row of sub-tile A
-  if (row0 >= nq) return;
-  const bool has_b = row0 + BM < nq;
+  const int nrow = nq * G;           // rows of this sequence: tokens x packed heads
+  const int row0 = tile_m * 2 * BM;  // first row of sub-tile A
+  if (row0 >= nrow) return;
+  const bool has_b = row0 + BM < nrow;
   const int kv_len = p.seq_lens[b];
-  const int pos0 = kv_len - nq;  // absolute position of query row 0
-  const int kvh = hq / (p.Hq / p.Hkv);
-  const int m_last = min(nq, row0 + 2 * BM) - 1;
+  const int pos0 = kv_len - nq;  // absolute position of token 0
+  const int kvh = G > 1 ? hy : hy / (p.Hq / p.Hkv);
+  const int m_last = (min(nrow, row0 + 2 * BM) - 1) / G;  // last token of the tile
   const int kv_end = min(kv_len, pos0 + m_last + 1);
   const int n_all = (kv_end + BN - 1) / BN;
   // split-KV: this CTA takes KV tiles [t_begin, t_begin + n_tiles) of the query tile's range
@@ -104,8 +110,13 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
   const int t_begin = split * per;
   const int n_tiles = max(0, min(n_all, t_begin + per) - t_begin);
   if (n_tiles == 0) {  // no keys for this slice: mark its partials empty
-    for (int r = threadIdx.x; r < 2 * BM; r += blockDim.x)
-      if (row0 + r < nq) p.part_lse[((long long)(q0 + row0 + r) * p.Hq + hq) * S + split] = -FLT_MAX;
+    for (int r = threadIdx.x; r < 2 * BM; r += blockDim.x) {
+      const int rr = row0 + r;
+      if (rr < nrow) {
+        const int head = G > 1 ? kvh * G + rr % G : hy;
+        p.part_lse[((long long)(q0 + rr / G) * p.Hq + head) * S + split] = -FLT_MAX;
+      }
+    }
     return;
   }
   const int* bt = p.block_table + (long long)b * p.bt_stride;
@@ -217,11 +228,13 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
     const int row = (warp & 3) * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t tS = tmem + x * 128 + lane_off, tO = tmem + 256 + x * 128 + lane_off;
-    const int qr = row0 + x * BM + row;
-    const bool row_valid = qr < nq;
+    const int qr = row0 + x * BM + row;  // row of the sequence
+    const bool row_valid = qr < nrow;
+    const int qt = row_valid ? qr / G : 0;  // its token
+    const int hq = G > 1 ? kvh * G + qr % G : hy;
     const bool active = x == 0 || has_b;
     {
-      const char* src = reinterpret_cast<const char*>(p.q + ((long long)(q0 + (row_valid ? qr : 0)) * p.Hq + hq) * HD);
+      const char* src = reinterpret_cast<const char*>(p.q + ((long long)(q0 + qt) * p.Hq + hq) * HD);
 #pragma unroll
       for (int u = 0; u < 16; ++u) cp_async16_zfill(sQ + x * TILE + swz_off(row, u), src + u * 16, row_valid);
       cp_async_commit();
@@ -230,8 +243,8 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(q_full);
     }
-    const int qpos = pos0 + qr;
-    const int qpos_min = pos0 + row0 + x * BM;
+    const int qpos = pos0 + qt;
+    const int qpos_min = pos0 + (row0 + x * BM) / G;
     float m_used = -FLT_MAX, l = 0.f;
     bool ok = active;
     for (int j = 0; ok && j < n_tiles; ++j) {
@@ -305,7 +318,7 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
     if (ok && S > 1) {  // normalised partial output + log-sum-exp of this KV slice
       tc::tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      const long long pr = ((long long)(q0 + (row_valid ? qr : 0)) * p.Hq + hq) * S + split;
+      const long long pr = ((long long)(q0 + qt) * p.Hq + hq) * S + split;
 #pragma unroll 1
       for (int c = 0; c < HD / 32; ++c) {
         uint32_t r[32];
@@ -323,7 +336,7 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
     } else if (ok) {
       tc::tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      __nv_bfloat16* dst = p.out + ((long long)(q0 + (row_valid ? qr : 0)) * p.Hq + hq) * HD;
+      __nv_bfloat16* dst = p.out + ((long long)(q0 + qt) * p.Hq + hq) * HD;
 #pragma unroll 1
       for (int c = 0; c < HD / 32; ++c) {
         uint32_t r[32];
@@ -369,7 +382,7 @@ void prefill_attention_tc(torch::Tensor q, int64_t k, int64_t v, int64_t blk_str
                           int64_t num_blocks, torch::Tensor block_table, torch::Tensor cu_q, torch::Tensor seq_lens,
                           int64_t Hkv, double scale, int64_t max_q, torch::Tensor out, torch::Tensor err,
                           int64_t num_splits, c10::optional<torch::Tensor> part_o,
-                          c10::optional<torch::Tensor> part_lse) {
+                          c10::optional<torch::Tensor> part_lse, int64_t gqa_pack) {
   using namespace fa;
   TORCH_CHECK(q.is_cuda() && q.scalar_type() == torch::kBFloat16 && q.is_contiguous() && q.dim() == 3 &&
                   q.size(2) == HD,
@@ -400,6 +413,8 @@ void prefill_attention_tc(torch::Tensor q, int64_t k, int64_t v, int64_t blk_str
   const int S = static_cast<int>(std::max<int64_t>(1, num_splits));
   const int T = q.size(0);
   p.num_splits = S;
+  const int G = Hq / static_cast<int>(Hkv);
+  p.gpack = gqa_pack > 1 ? G : 1;
   p.part_o = nullptr;
   p.part_lse = nullptr;
   if (S > 1) {
@@ -416,7 +431,9 @@ void prefill_attention_tc(torch::Tensor q, int64_t k, int64_t v, int64_t blk_str
     AXR_CHECK_CUDA(cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
     attr = true;
   }
-  dim3 grid((max_q + 2 * BM - 1) / (2 * BM), Hq, B * S);
+  const int64_t rows = max_q * p.gpack;
+  dim3 grid(static_cast<unsigned>((rows + 2 * BM - 1) / (2 * BM)), p.gpack > 1 ? static_cast<unsigned>(Hkv) : Hq,
+            B * S);
   auto st = at::cuda::getCurrentCUDAStream();
   prefill_tc_kernel<<<grid, THREADS, SMEM, st>>>(tk, tv, p);
   AXR_CHECK_CUDA(cudaGetLastError());

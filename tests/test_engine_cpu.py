@@ -129,3 +129,22 @@ def test_admission_policy_prefers_hits_and_scales_budget(monkeypatch):
     monkeypatch.setenv("KORITH_VLLM_DECODE_FIRST", "0")
     off = AdmissionPolicy()
     assert [r.i for r in off.order(w, lambda r: True)] == [0, 1, 2, 3]
+
+
+def test_prefill_graph_runner_padding_matches_eager(model):
+    """The graph runner's padded one-sequence prefill (bucketed token count, slot -1
+    padding, device-side lengths) gives the same tokens as the plain prefill. On CPU the
+    padded step runs eagerly; on a GPU the same step is what the CUDA graph replays."""
+    from axropus_deploy_b200.engine.cuda_graph import PrefillGraphRunner
+
+    g = torch.Generator().manual_seed(3)
+    prefix = torch.randint(0, 32000, (256,), generator=g).tolist()
+    prompts = [prefix + torch.randint(0, 32000, (n,), generator=g).tolist() for n in (37, 100)]
+    ref = LLMEngine(model, EngineConfig(num_blocks=96, max_model_len=1024)).generate(prompts, SamplingParams(max_tokens=4))
+    eng = LLMEngine(model, EngineConfig(num_blocks=96, max_model_len=1024))
+    eng._prefill_graphs = PrefillGraphRunner(eng, max_tokens=512)
+    out = [eng.generate([p], SamplingParams(max_tokens=4))[0] for p in prompts]  # one sequence per prefill
+    assert out == ref
+    assert eng._prefill_graphs.stat["eager"] >= 1
+    # the second prompt reuses the first one's cached prefix: its prefill is the 100-token suffix
+    assert eng.stat["local_cached_tokens"] == 256

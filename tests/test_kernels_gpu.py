@@ -126,11 +126,24 @@ def test_prefill_attention_split_kv(fmt, splits):
     torch.testing.assert_close(auto.cpu().float(), ref.float(), atol=3e-2, rtol=3e-2)
 
 
+@pytest.mark.parametrize("pack", [True, False])
 @pytest.mark.parametrize("G", [4, 8])
-def test_prefill_attention_tcgen05_long(G):
+def test_prefill_attention_tcgen05_long(G, pack):
     """tcgen05 prefill kernel (bf16 pages) on multi-tile causal prefills and a suffix,
     with per-block key magnitudes from 1x to 8x so the running max moves by more than
-    2^8 between KV tiles (the O rescale in TMEM runs)."""
+    2^8 between KV tiles (the O rescale in TMEM runs); rows one head at a time, or the
+    G query heads of a KV head packed into the same tiles."""
+    from axropus_deploy_b200.ops import attention as att
+
+    saved = att.GQA_PACK_MAX_Q[0]
+    att.GQA_PACK_MAX_Q[0] = 2048 if pack else 0
+    try:
+        _tcgen05_long_case(G)
+    finally:
+        att.GQA_PACK_MAX_Q[0] = saved
+
+
+def _tcgen05_long_case(G):
     from axropus_deploy_b200.ops import attention as att
     from axropus_deploy_b200.ops.gemm import check_errors
 
@@ -159,6 +172,25 @@ def test_prefill_attention_tcgen05_long(G):
     finally:
         att.PREFILL_TC[0] = True
     torch.testing.assert_close(out.float(), legacy.float(), atol=3e-2, rtol=3e-2)
+
+
+@pytest.mark.parametrize("splits", [None, 1, 7])
+def test_prefill_attention_tcgen05_packed_suffix(splits):
+    """A 128-token suffix over a 4 K-token cached prefix (the AMF-hit shape), GQA-packed
+    rows, with and without split KV, against the float32 reference."""
+    L, H, D, G = 1, 8, 128, 4
+    pages = 265
+    NB = pages + 3
+    cache = _fill_cache(KVCache(L, NB, H, D, "bf16", DEV), seed=12)
+    seq = torch.tensor([4224], dtype=torch.int32)
+    nq = torch.tensor([128], dtype=torch.int32)
+    cu = torch.tensor([0, 128], dtype=torch.int32)
+    bt = _block_table(1, pages, NB, 13)
+    q = torch.randn(128, H * G, D).to(torch.bfloat16)
+    out = prefill_attention(q.to(DEV), cache, 0, bt.to(DEV), cu.to(DEV), seq.to(DEV), 128, max_seq_len=4224,
+                            num_splits=splits)
+    ref = prefill_attention(q, _cpu_copy(cache), 0, bt, cu, seq, 128)
+    torch.testing.assert_close(out.cpu().float(), ref.float(), atol=3e-2, rtol=3e-2)
 
 
 def test_rmsnorm_residual():
