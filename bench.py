@@ -135,16 +135,28 @@ class Workload:
         ranks = np.arange(1, args.prefixes + 1, dtype=np.float64)
         p = ranks ** (-args.zipf)
         self.zipf_p = p / p.sum()
-        # reuse decisions and Zipf picks, and the random tokens, come from separate streams:
-        # replaying the choice stream gives a wave of the same hit/cold mix with new tokens
-        self.rng = np.random.default_rng(args.seed * 1000 + 17 + rank)
+        # Reuse-or-fresh is decided by an exact schedule, not a coin: request k of the
+        # stream brings a fresh prefix when floor((k+1) q) > floor(k q), q = 1 - reuse, so
+        # every wave holds the configured share of cold 8 K prefills (3 or 4 of 32 at
+        # q = 0.1) on every GPU -- weak scaling with equal per-GPU work, and no sampling
+        # noise in a run of a few waves. The Zipf picks of reused prefixes and the random
+        # tokens are per-rank random streams. Replaying the schedule position and the pick
+        # stream gives a wave of the same mix with new tokens.
+        self.k = 0
+        self.pick_rng = np.random.default_rng(args.seed * 1000 + 23 + rank)
         self.tok_rng = np.random.default_rng(args.seed * 1000 + 29 + rank)
+
+    def _fresh_next(self) -> bool:
+        q = 1.0 - self.args.reuse
+        fresh = math.floor((self.k + 1) * q + 1e-9) > math.floor(self.k * q + 1e-9)
+        self.k += 1
+        return fresh
 
     def request(self, force: str = ""):
         a = self.args
-        reuse = force == "hit" or (force != "cold" and self.rng.random() < a.reuse)
+        reuse = force == "hit" or (force != "cold" and not self._fresh_next())
         if reuse:
-            i = int(self.rng.choice(a.prefixes, p=self.zipf_p))
+            i = int(self.pick_rng.choice(a.prefixes, p=self.zipf_p))
             prefix = self.prefixes[i]
         else:
             prefix = self.tok_rng.integers(0, self.vocab, a.prefix_len, dtype=np.int64).tolist()
@@ -152,10 +164,10 @@ class Workload:
         return prefix + suffix, reuse
 
     def choice_state(self):
-        return self.rng.bit_generator.state
+        return self.k, self.pick_rng.bit_generator.state
 
     def set_choice_state(self, state) -> None:
-        self.rng.bit_generator.state = state
+        self.k, self.pick_rng.bit_generator.state = state
 
 
 def pct(xs, q):
@@ -363,7 +375,7 @@ def run_ours(args) -> None:
             "config": {"model": cfg.name + ("" if args.layers is None else f"-{args.layers}L-INVALID"),
                        "global_batch": args.batch * info.world, "seq_len": args.prefix_len + args.suffix_len,
                        "parallelism": f"dp{info.world}", "output_tokens": args.out_tokens,
-                       "prefixes": args.prefixes, "reuse": args.reuse, "zipf": args.zipf,
+                       "prefixes": args.prefixes, "reuse": args.reuse, "reuse_schedule": "exact share of fresh prefixes per wave, same on every GPU", "zipf": args.zipf,
                        "pool": args.pool, "kv_cache": args.kv_fmt, "pool_sharding": f"{info.world} shards by prefix hash",
                        "l2": "inputs larger than L2 (every decode step reads >30 GB of KV and weights)",
                        "step": "one wave of batch requests per GPU: restore/prefill + 128 decode steps"},
@@ -376,6 +388,7 @@ def run_ours(args) -> None:
                                  "another GPU's shard (fused pull over NVLink + scatter)",
             "pool_slots_per_shard": slots_per_shard,
             "wave_mix": gathered[0]["waves"], "amf_hits_rank0": gathered[0]["hits"],
+            "ms_per_step_by_rank": [round(g["ms"] / args.steps, 1) for g in gathered],
             "clocks": {"sm_mhz": ck.get("sm_mhz"), "sm_max_mhz": ck.get("sm_max_mhz"), "reasons": reasons},
             "e2e": {"value": round(e2e_val, 2), "unit": "output tokens/s (whole job)",
                     "h2d_bytes_per_step": int(h2d / n_e2e),
