@@ -311,14 +311,17 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(DecodeParams p) {
 // and 0..15 are exact in f16) with the per-token scales applied to the scores, and
 // their V page is dequantised into an f16 tile for the ldmatrix.trans PV operand.
 // ======================================================================================
+constexpr float kDecodeRescaleLog2 = 8.f;
+
 template <int FMT>
 struct TcCfg {
   static constexpr int KB = FMT == kBF16 ? 4096 : (FMT == kFP8Token ? 2048 : 1024);  // K (=V) unit bytes
   static constexpr int MB = FMT == kBF16 ? 0 : (FMT == kFP8Token ? 64 : 128);        // meta bytes per unit
   static constexpr int STAGE = 2 * KB + 2 * MB;
   static constexpr int STAGES = FMT == kBF16 ? 3 : 4;
-  static constexpr int VT = FMT == kBF16 ? 0 : 4096;  // f16 V tile (dequantised)
-  static constexpr int WARP = STAGES * STAGE + VT + 256;
+  static constexpr int VT = FMT == kBF16 ? 0 : 4096;  // f16 V tile (the codes as f16)
+  static constexpr int PT = FMT == kINT4G64 ? 512 : 256;  // P^T tile(s): INT4 one per 64-dim group
+  static constexpr int WARP = STAGES * STAGE + VT + PT;
   static constexpr int SMEM = 4 * WARP;
 };
 
@@ -353,21 +356,21 @@ __device__ __forceinline__ uint32_t fp8x2_h2(uint32_t two_codes) {
   __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(two_codes & 0xffff), __NV_E4M3);
   return *reinterpret_cast<uint32_t*>(&h);
 }
-// Byte Q of `word` (two nibbles) -> f16x2 (lo, hi) holding the integers 0..15, without
-// int->float conversions: one byte permute puts the byte in both 16-bit halves, one
-// mask+or builds the f16 bit patterns 1024 + lo and 1024 + 16*hi, and one f16x2 FMA
-// (scale 1 and 1/16, bias -1024 and -64) leaves the exact integers.
-template <int Q>
-__device__ __forceinline__ __half2 nib_pair(uint32_t word) {
-  uint32_t t = __byte_perm(word, 0u, Q | (4 << 4) | (Q << 8) | (4 << 12));  // bytes [bQ, 0, bQ, 0]
-  t = (t & 0x00F0000Fu) | 0x64006400u;
-  const __half2 h = *reinterpret_cast<const __half2*>(&t);
-  return __hfma2(h, __halves2half2(__ushort_as_half(0x3C00), __ushort_as_half(0x2C00)),   // 1, 1/16
-                 __halves2half2(__ushort_as_half(0xE400), __ushort_as_half(0xD400)));  // -1024, -64
+// Nibble K (0..3) of both 16-bit halves of `word` -> f16x2 (1024 + n_lo, 1024 + n_hi): a
+// shift and one and-or. The halves hold dims K and K + 4 of the word's 8 dims (byte j
+// holds dims 2j, 2j+1), so a word yields the pairs (0,4) (1,5) (2,6) (3,7). For K the
+// 1024 offset is folded into the zero point: a*(1024 + n) + (z - 1024 a) = a*n + z.
+template <int K>
+__device__ __forceinline__ uint32_t nib_sh(uint32_t word) {
+  return ((word >> (4 * K)) & 0x000F000Fu) | 0x64006400u;
 }
-template <int Q>
-__device__ __forceinline__ uint32_t nib2_h2w(uint32_t word) {
-  __half2 h = nib_pair<Q>(word);
+// As nib_sh, minus the offset: the exact integers n (one more f16x2 subtraction). The V
+// operand takes these, since its scale is folded into P in f16 and an offset of 1024
+// would cancel against that rounding.
+template <int K>
+__device__ __forceinline__ uint32_t nib_sh_exact(uint32_t word) {
+  uint32_t w = nib_sh<K>(word);
+  __half2 h = __hsub2(*reinterpret_cast<__half2*>(&w), __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400)));
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
@@ -430,10 +433,19 @@ __global__ void __launch_bounds__(128) decode_tc_kernel(DecodeParams p) {
     const __nv_bfloat16* qrow = p.q + ((long long)b * p.Hq + kvh * G + (g < G ? g : 0)) * 128;
 #pragma unroll
     for (int kk = 0; kk < 8; ++kk) {
-      const int base = (kk >> 2) * 64 + t * 16 + (kk & 3) * 4;
+      // dims of this lane's k-step: 4 consecutive; INT4 takes the nib_sh pairs
+      // (d, d+4) and (d+1, d+5) with d = 8 * ((kk & 3) >> 1) + 2 * (kk & 1)
+      int dd[4];
+      if constexpr (FMT == kINT4G64) {
+        const int d0 = (kk >> 2) * 64 + t * 16 + ((kk & 3) >> 1) * 8 + (kk & 1) * 2;
+        dd[0] = d0; dd[1] = d0 + 4; dd[2] = d0 + 1; dd[3] = d0 + 5;
+      } else {
+        const int base = (kk >> 2) * 64 + t * 16 + (kk & 3) * 4;
+        dd[0] = base; dd[1] = base + 1; dd[2] = base + 2; dd[3] = base + 3;
+      }
       float f[4];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) f[e] = g < G ? __bfloat162float(qrow[base + e]) * p.scale_log2 : 0.f;
+      for (int e = 0; e < 4; ++e) f[e] = g < G ? __bfloat162float(qrow[dd[e]]) * p.scale_log2 : 0.f;
       if constexpr (F16) {
         qb[kk][0] = pack_h2(f[0], f[1]);
         qb[kk][1] = pack_h2(f[2], f[3]);
@@ -460,6 +472,8 @@ __global__ void __launch_bounds__(128) decode_tc_kernel(DecodeParams p) {
   float o[8][4];
 #pragma unroll
   for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  // INT4: sum over tokens of p * z per (head 2t+j, group); added to O at the end
+  float zacc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
   float m[2] = {-FLT_MAX, -FLT_MAX}, l[2] = {0.f, 0.f};
 
   // prologue
@@ -503,14 +517,14 @@ __global__ void __launch_bounds__(128) decode_tc_kernel(DecodeParams p) {
           }
         } else {
           const uint2 x = *reinterpret_cast<const uint2*>(sk + ksw<FMT>(r, gr * 2 + (t >> 1)) + (t & 1) * 8);
-          ka[h][0] = nib2_h2w<0>(x.x);
-          ka[h][1] = nib2_h2w<1>(x.x);
-          ka[h][2] = nib2_h2w<2>(x.x);
-          ka[h][3] = nib2_h2w<3>(x.x);
-          ka[h][4] = nib2_h2w<0>(x.y);
-          ka[h][5] = nib2_h2w<1>(x.y);
-          ka[h][6] = nib2_h2w<2>(x.y);
-          ka[h][7] = nib2_h2w<3>(x.y);
+          ka[h][0] = nib_sh<0>(x.x);
+          ka[h][1] = nib_sh<1>(x.x);
+          ka[h][2] = nib_sh<2>(x.x);
+          ka[h][3] = nib_sh<3>(x.x);
+          ka[h][4] = nib_sh<0>(x.y);
+          ka[h][5] = nib_sh<1>(x.y);
+          ka[h][6] = nib_sh<2>(x.y);
+          ka[h][7] = nib_sh<3>(x.y);
         }
       }
 #pragma unroll
@@ -539,8 +553,8 @@ __global__ void __launch_bounds__(128) decode_tc_kernel(DecodeParams p) {
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const uint32_t m0 = km[(g + 8 * h) * 2 + 0], m1 = km[(g + 8 * h) * 2 + 1];
-        const float a0 = half_bits_to_float(m0 & 0xffff), z0 = half_bits_to_float(m0 >> 16);
-        const float a1 = half_bits_to_float(m1 & 0xffff), z1 = half_bits_to_float(m1 >> 16);
+        const float a0 = half_bits_to_float(m0 & 0xffff), z0 = half_bits_to_float(m0 >> 16) - 1024.f * a0;
+        const float a1 = half_bits_to_float(m1 & 0xffff), z1 = half_bits_to_float(m1 >> 16) - 1024.f * a1;
 #pragma unroll
         for (int j = 0; j < 2; ++j)
           sc[2 * h + j] = s0[2 * h + j] * a0 + qs_col[0][j] * z0 + s1[2 * h + j] * a1 + qs_col[1][j] * z1;
@@ -548,40 +562,85 @@ __global__ void __launch_bounds__(128) decode_tc_kernel(DecodeParams p) {
     }
     if (tok0 >= seq_len) { sc[0] = -FLT_MAX; sc[1] = -FLT_MAX; }
     if (tok1 >= seq_len) { sc[2] = -FLT_MAX; sc[3] = -FLT_MAX; }
-    // ---- online softmax (columns = heads 2t, 2t+1)
-    float pv[4];
+    // ---- online softmax (columns = heads 2t, 2t+1). The reference maximum only moves
+    // when a page's maximum exceeds it by more than 2^8 (log2 units), so p <= 256 and the
+    // rescale of O -- 34 multiplies per lane -- is skipped on almost every page.
+    float pv[4], alpha[2];
+    bool resc = false;
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
       float mx = fmaxf(sc[j], sc[2 + j]);
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-      const float mn = fmaxf(m[j], mx);
-      const float alpha = exp2f(m[j] - mn);
+      const bool up = mx > m[j] + kDecodeRescaleLog2;
+      const float mn = up ? mx : m[j];
+      alpha[j] = up ? exp2f(m[j] - mn) : 1.f;
+      resc |= up;
       m[j] = mn;
       pv[j] = sc[j] == -FLT_MAX ? 0.f : exp2f(sc[j] - mn);
       pv[2 + j] = sc[2 + j] == -FLT_MAX ? 0.f : exp2f(sc[2 + j] - mn);
-      l[j] = l[j] * alpha + pv[j] + pv[2 + j];
+      l[j] = l[j] * alpha[j] + pv[j] + pv[2 + j];
+    }
+    if (__any_sync(0xffffffffu, resc)) {
 #pragma unroll
-      for (int mt = 0; mt < 8; ++mt) {
-        o[mt][j] *= alpha;
-        o[mt][2 + j] *= alpha;
+      for (int j = 0; j < 2; ++j) {
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+          o[mt][j] *= alpha[j];
+          o[mt][2 + j] *= alpha[j];
+        }
+        if constexpr (FMT == kINT4G64) {
+          zacc[j][0] *= alpha[j];
+          zacc[j][1] *= alpha[j];
+        }
       }
     }
-    // ---- P^T to shared (for the B operand)
+    // ---- P^T to shared (for the B operand). FP8 / INT4: the V tile holds the raw codes,
+    // so each token's V scale is folded into its P entry (INT4: one P^T per 64-dim group,
+    // and the zero point of the group goes to zacc).
+    if constexpr (FMT == kINT4G64) {
+      const uint32_t* vmeta = reinterpret_cast<const uint32_t*>(st + 2 * C::KB + C::MB);  // [tok][group]
+      float va[2][2], vz[2][2];  // [token g | g+8][group]
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const int hcol = 2 * t + j;
-      uint16_t a, c;
-      if constexpr (F16) {
-        a = __half_as_ushort(__float2half_rn(pv[j]));
-        c = __half_as_ushort(__float2half_rn(pv[2 + j]));
-      } else {
-        a = __bfloat16_as_ushort(__float2bfloat16(pv[j]));
-        c = __bfloat16_as_ushort(__float2bfloat16(pv[2 + j]));
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int gr = 0; gr < 2; ++gr) {
+          const uint32_t mm = vmeta[(g + 8 * h) * 2 + gr];
+          va[h][gr] = half_bits_to_float(mm & 0xffff);
+          vz[h][gr] = half_bits_to_float(mm >> 16);
+        }
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int hcol = 2 * t + j;
+#pragma unroll
+        for (int gr = 0; gr < 2; ++gr) {
+          pt[gr * 128 + hcol * 16 + g] = __half_as_ushort(__float2half_rn(pv[j] * va[0][gr]));
+          pt[gr * 128 + hcol * 16 + g + 8] = __half_as_ushort(__float2half_rn(pv[2 + j] * va[1][gr]));
+          zacc[j][gr] += pv[j] * vz[0][gr] + pv[2 + j] * vz[1][gr];
+        }
       }
-      pt[hcol * 16 + g] = a;
-      pt[hcol * 16 + g + 8] = c;
+    } else {
+      float vs0 = 1.f, vs1 = 1.f;
+      if constexpr (FMT == kFP8Token) {
+        const float* vsc = reinterpret_cast<const float*>(st + 2 * C::KB + C::MB);
+        vs0 = vsc[g];
+        vs1 = vsc[g + 8];
+      }
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int hcol = 2 * t + j;
+        uint16_t a, c;
+        if constexpr (F16) {
+          a = __half_as_ushort(__float2half_rn(pv[j] * vs0));
+          c = __half_as_ushort(__float2half_rn(pv[2 + j] * vs1));
+        } else {
+          a = __bfloat16_as_ushort(__float2bfloat16(pv[j]));
+          c = __bfloat16_as_ushort(__float2bfloat16(pv[2 + j]));
+        }
+        pt[hcol * 16 + g] = a;
+        pt[hcol * 16 + g + 8] = c;
+      }
     }
     // ---- V tile (FP8 / INT4: dequantise into the f16 ldmatrix tile)
     const char* vt;
@@ -589,32 +648,23 @@ __global__ void __launch_bounds__(128) decode_tc_kernel(DecodeParams p) {
       vt = st + C::KB;
     } else {
       const char* sv = st + C::KB;
-      const char* vm = st + 2 * C::KB + C::MB;
       const int cc = lane & 15;
 #pragma unroll
       for (int i2 = 0; i2 < 8; ++i2) {
         const int r = (lane >> 4) + 2 * i2;
         uint32_t h4[4];
-        if constexpr (FMT == kFP8Token) {
+        if constexpr (FMT == kFP8Token) {  // e4m3 codes are exact in f16
           const uint2 x = *reinterpret_cast<const uint2*>(sv + r * 128 + cc * 8);
-          const float vs = reinterpret_cast<const float*>(vm)[r];
-          const uint32_t w[2] = {x.x, x.y};
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const float2 f = e4m3x2_to_float2((w[q >> 1] >> ((q & 1) * 16)) & 0xffff);
-            h4[q] = pack_h2(f.x * vs, f.y * vs);
-          }
-        } else {
+          h4[0] = fp8x2_h2(x.x);
+          h4[1] = fp8x2_h2(x.x >> 16);
+          h4[2] = fp8x2_h2(x.y);
+          h4[3] = fp8x2_h2(x.y >> 16);
+        } else {  // codes 0..15; tile columns of each 8-dim chunk hold dims 0,4,1,5,2,6,3,7
           const uint32_t x = *reinterpret_cast<const uint32_t*>(sv + r * 64 + cc * 4);
-          const uint32_t mm = reinterpret_cast<const uint32_t*>(vm)[r * 2 + (cc >> 3)];
-          const __half2 sz = *reinterpret_cast<const __half2*>(&mm);  // (scale, zero)
-          const __half2 a2 = __low2half2(sz), z2 = __high2half2(sz);
-          const __half2 v0 = __hfma2(nib_pair<0>(x), a2, z2), v1 = __hfma2(nib_pair<1>(x), a2, z2);
-          const __half2 v2 = __hfma2(nib_pair<2>(x), a2, z2), v3 = __hfma2(nib_pair<3>(x), a2, z2);
-          h4[0] = *reinterpret_cast<const uint32_t*>(&v0);
-          h4[1] = *reinterpret_cast<const uint32_t*>(&v1);
-          h4[2] = *reinterpret_cast<const uint32_t*>(&v2);
-          h4[3] = *reinterpret_cast<const uint32_t*>(&v3);
+          h4[0] = nib_sh_exact<0>(x);
+          h4[1] = nib_sh_exact<1>(x);
+          h4[2] = nib_sh_exact<2>(x);
+          h4[3] = nib_sh_exact<3>(x);
         }
         *reinterpret_cast<uint4*>(vtile + vsw(r, cc)) = make_uint4(h4[0], h4[1], h4[2], h4[3]);
       }
@@ -623,6 +673,11 @@ __global__ void __launch_bounds__(128) decode_tc_kernel(DecodeParams p) {
     __syncwarp();
     const uint32_t b0 = *reinterpret_cast<const uint32_t*>(pt + g * 16 + 2 * t);
     const uint32_t b1 = *reinterpret_cast<const uint32_t*>(pt + g * 16 + 2 * t + 8);
+    uint32_t c0 = b0, c1 = b1;  // group 1 (dims 64-127) of INT4
+    if constexpr (FMT == kINT4G64) {
+      c0 = *reinterpret_cast<const uint32_t*>(pt + 128 + g * 16 + 2 * t);
+      c1 = *reinterpret_cast<const uint32_t*>(pt + 128 + g * 16 + 2 * t + 8);
+    }
     // ---- O^T += V^T . P^T
     {
       const uint32_t vbase = static_cast<uint32_t>(__cvta_generic_to_shared(vt));
@@ -633,7 +688,7 @@ __global__ void __launch_bounds__(128) decode_tc_kernel(DecodeParams p) {
         asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
                      : "=r"(a0), "=r"(a1), "=r"(a2), "=r"(a3)
                      : "r"(vbase + vsw(r, 2 * mt + (mi & 1))));
-        mma16816(o[mt], a0, a1, a2, a3, b0, b1, F16);
+        mma16816(o[mt], a0, a1, a2, a3, mt < 4 ? b0 : c0, mt < 4 ? b1 : c1, F16);
       }
     }
     __syncwarp();
@@ -658,12 +713,28 @@ __global__ void __launch_bounds__(128) decode_tc_kernel(DecodeParams p) {
       wl[warp * 8 + 2 * t + j] = l[j];
     }
   }
+  if constexpr (FMT == kINT4G64) {
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int gr = 0; gr < 2; ++gr) {
+        zacc[j][gr] += __shfl_xor_sync(0xffffffffu, zacc[j][gr], 4);
+        zacc[j][gr] += __shfl_xor_sync(0xffffffffu, zacc[j][gr], 8);
+        zacc[j][gr] += __shfl_xor_sync(0xffffffffu, zacc[j][gr], 16);
+      }
+  }
 #pragma unroll
   for (int mt = 0; mt < 8; ++mt) {
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const int head = 2 * t + (e & 1), dim = mt * 16 + g + (e >> 1) * 8;
-      wacc[(warp * 8 + head) * 128 + dim] = o[mt][e];
+      const int head = 2 * t + (e & 1);
+      int dim = mt * 16 + g + (e >> 1) * 8;
+      float val = o[mt][e];
+      if constexpr (FMT == kINT4G64) {
+        dim = (dim & ~7) + ((g >> 1) | ((g & 1) << 2));  // tile column -> dim (nib_sh pairs)
+        val += zacc[e & 1][mt >> 2];
+      }
+      wacc[(warp * 8 + head) * 128 + dim] = val;
     }
   }
   __syncthreads();
