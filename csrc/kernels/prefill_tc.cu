@@ -268,9 +268,16 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
         for (int i = 0; i < BN; ++i)
           if (n0 + i > qpos || n0 + i >= kv_len) v[i] = -FLT_MAX;
       }
-      float mt = -FLT_MAX;
+      // row maximum as 8 independent chains (a single 128-long fmax chain is latency-bound)
+      float mx8[8];
 #pragma unroll
-      for (int i = 0; i < BN; ++i) mt = fmaxf(mt, v[i]);
+      for (int c = 0; c < 8; ++c) mx8[c] = v[c];
+#pragma unroll
+      for (int i = 8; i < BN; i += 8)
+#pragma unroll
+        for (int c = 0; c < 8; ++c) mx8[c] = fmaxf(mx8[c], v[i + c]);
+      const float mt = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       if (j == 0) {
         m_used = mt;
       } else {
@@ -295,14 +302,14 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
         }
       }
       char* pbuf = sP + x * TILE;
+      // masked scores are -FLT_MAX: exp2 of (-FLT_MAX - m) is 0 for any finite m, and
+      // while every score so far was masked (m = -FLT_MAX) subtracting 0 gives 0 as well
+      const float msub = m_used == -FLT_MAX ? 0.f : m_used;
 #pragma unroll
       for (int u = 0; u < 16; ++u) {
         float e[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float t = v[u * 8 + i];
-          e[i] = t == -FLT_MAX ? 0.f : exp2f(t - m_used);
-        }
+        for (int i = 0; i < 8; ++i) e[i] = exp2f(v[u * 8 + i] - msub);
         l += ((e[0] + e[1]) + (e[2] + e[3])) + ((e[4] + e[5]) + (e[6] + e[7]));
         *reinterpret_cast<uint4*>(pbuf + swz_off(row, u)) =
             make_uint4(pack_bf16x2(e[0], e[1]), pack_bf16x2(e[2], e[3]), pack_bf16x2(e[4], e[5]),
