@@ -33,7 +33,6 @@ Reference: platform/runtime/cluster_worker.py:455-621 (lane budgets), :924-1114 
 """
 from __future__ import annotations
 
-import collections
 import hashlib
 import os
 import threading
@@ -41,12 +40,13 @@ import time
 import traceback
 import uuid
 from pathlib import Path
-from typing import Any, Deque, Dict, List, Optional
+from typing import Any, Dict, List, Optional
 
 from .adapters import AdapterRegistry
 from .engine_client import validate_snapshot_metadata, write_snapshot_metadata
 from .nodes import estimate_transfer_ms, fetch_snapshot_bytes, should_transfer_snapshot, store_snapshot_bytes
 from .observability import GLOBAL_METRICS, ArtifactStore, emit_log, error_fields, utc_now
+from .queues import InProcQueue
 from .runtime import DecodeCache, ReplayGovernor, SpecGovernor, SpecKController
 
 LANES = ("SPEC_HIT", "HIT", "SPEC_MISS", "MISS")
@@ -69,7 +69,8 @@ class ClusterWorker:
     def __init__(self, worker_id: str, node_id: str, adapters: AdapterRegistry, ledger, artifacts: ArtifactStore, *,
                  snapshot_index=None, node_registry=None, coordinator=None, decode_cache: Optional[DecodeCache] = None,
                  metrics=GLOBAL_METRICS, snapshot_dir: Optional[str] = None, link_gbps: Optional[float] = None,
-                 rtt_ms: Optional[float] = None, transfer_threshold: Optional[float] = None, gpu_index: int = 0):
+                 rtt_ms: Optional[float] = None, transfer_threshold: Optional[float] = None, gpu_index: int = 0,
+                 queue_factory=None):
         self.worker_id, self.node_id, self.gpu_index = worker_id, node_id, gpu_index
         self.adapters = adapters
         self.ledger = ledger
@@ -90,7 +91,10 @@ class ClusterWorker:
         self.replay = ReplayGovernor(ledger)
         self.spec_gov = SpecGovernor(ledger)
         self.spec_k = SpecKController(_env_int("KORITH_SPEC_K", SpecKController.DEFAULT_K))
-        self.queues: Dict[str, Deque[Dict[str, Any]]] = {l: collections.deque() for l in LANES}
+        # one queue per lane: in-process by default; with a factory (e.g. one SqliteQueue per
+        # lane) jobs survive the worker -- a job taken but never acked (the worker died in
+        # the middle of it) becomes ready again after the queue's visibility timeout
+        self.queues: Dict[str, Any] = {l: (queue_factory(l) if queue_factory else InProcQueue()) for l in LANES}
         self.budget = lane_budgets()
         self._left = dict(self.budget)
         self._mu = threading.Lock()
@@ -107,49 +111,62 @@ class ClusterWorker:
     def enqueue(self, job: Dict[str, Any]) -> None:
         lane = str(job.get("lane", "MISS")).upper()
         with self._cv:
-            self.queues[lane if lane in self.queues else "MISS"].append(job)
+            self.queues[lane if lane in self.queues else "MISS"].enqueue(job)
             self.queued_tokens += int(job.get("prompt_tokens", 0)) + int(job.get("max_tokens", 0))
             self._cv.notify()
         self.metrics.set_gauge("korith_worker_queue_depth", self.depth(lane), {"worker": self.worker_id,
                                                                                "lane": lane})
 
+    @staticmethod
+    def _ready(q) -> int:
+        st = q.stats()
+        return int(st.get("ready", 0)) + int(st.get("delayed", 0))
+
     def depth(self, lane: Optional[str] = None) -> int:
         if lane is not None:
-            return len(self.queues.get(lane, ()))
-        return sum(len(q) for q in self.queues.values())
+            q = self.queues.get(lane)
+            return self._ready(q) if q is not None else 0
+        return sum(self._ready(q) for q in self.queues.values())
 
     def queue_status(self) -> Dict[str, Any]:
-        return {"worker_id": self.worker_id, "depths": {l: len(q) for l, q in self.queues.items()},
+        return {"worker_id": self.worker_id, "depths": {l: self._ready(q) for l, q in self.queues.items()},
                 "budget_left": dict(self._left), "inflight": self.inflight, "done": self.done, "failed": self.failed}
 
-    def _next(self) -> Optional[Dict[str, Any]]:
-        """Weighted round robin over the non-empty lanes (caller holds the lock)."""
+    def _next(self) -> Optional[tuple]:
+        """(lane, item id, job) by weighted round robin over the lanes that have work
+        (caller holds the lock)."""
         for _ in range(2):
             for lane in LANES:
-                if self.queues[lane] and self._left[lane] > 0:
-                    self._left[lane] -= 1
-                    return self.queues[lane].popleft()
-            if not any(self.queues.values()):
+                if self._left[lane] > 0:
+                    got = self.queues[lane].dequeue()
+                    if got is not None:
+                        self._left[lane] -= 1
+                        return lane, got[0], got[1]
+            if self.depth() == 0:
                 return None
-            self._left = dict(self.budget)  # every non-empty lane spent its budget: new round
+            self._left = dict(self.budget)  # every lane with work spent its budget: new round
         return None
 
     # ------------------------------------------------------------------ loop
     def run_once(self, block: bool = False, timeout: float = 0.5) -> Optional[Dict[str, Any]]:
         with self._cv:
-            job = self._next()
-            if job is None and block:
+            got = self._next()
+            if got is None and block:
                 self._cv.wait(timeout)
-                job = self._next()
-            if job is None:
+                got = self._next()
+            if got is None:
                 return None
             self.inflight += 1
+        lane, iid, job = got
         try:
-            return self._process(job)
+            out = self._process(job)
+            self.queues[lane].ack(iid)  # terminal state (succeeded or failed) recorded in the ledger
+            return out
         finally:
             with self._mu:
                 self.inflight -= 1
-                self.queued_tokens -= int(job.get("prompt_tokens", 0)) + int(job.get("max_tokens", 0))
+                self.queued_tokens = max(0, self.queued_tokens - int(job.get("prompt_tokens", 0))
+                                         - int(job.get("max_tokens", 0)))
 
     def drain(self) -> List[Dict[str, Any]]:
         out = []

@@ -299,3 +299,34 @@ def test_codec_ids_and_amf_bench_cli(capsys):
                  "--device", "cpu"]) == 0
     out = json.loads(capsys.readouterr().out)
     assert out["runs"][0]["tier"] == "cold" and out["runs"][1]["tier"].startswith("g1")
+
+
+def test_worker_crash_jobs_reclaimed_from_durable_queue(tmp_path):
+    """Lane queues on SQLite: a worker that dies holding a job (taken, never acked) loses
+    nothing -- a replacement worker over the same queue file picks the job up once the
+    visibility timeout has passed, and every submitted job ends succeeded."""
+    from axropus_deploy_b200.cluster.adapters import AdapterRegistry
+    from axropus_deploy_b200.cluster.control import ControlPlane
+    from axropus_deploy_b200.cluster.queues import SqliteQueue
+    from axropus_deploy_b200.cluster.worker import ClusterWorker
+
+    ledger = SqliteLedger(str(tmp_path / "ledger.db"))
+    qdb = str(tmp_path / "queues.db")
+    art = ArtifactStore(tmp_path / "art")
+    factory = lambda lane: SqliteQueue(qdb, name=f"w0:{lane}", visibility_s=0.5)  # noqa: E731
+    eng = _engine()
+    w1 = ClusterWorker("w0", "n0", AdapterRegistry(eng), ledger, art, metrics=MetricsRegistry(), queue_factory=factory)
+    plane = ControlPlane(ledger, {"w0": w1}, metrics=w1.metrics)
+    ids = [plane.submit({"prompt": f"job {i} " * 8, "max_tokens": 2}, org_id="o") for i in range(3)]
+    assert w1.depth() == 3
+    assert w1.run_once() is not None                       # one job done and acked
+    lane, iid, job = w1._next()                            # the worker takes a second job ...
+    assert job["job_id"] in ids
+    del w1                                                 # ... and dies without acking it
+    w2 = ClusterWorker("w0", "n0", AdapterRegistry(eng), ledger, art, metrics=MetricsRegistry(), queue_factory=factory)
+    assert w2.depth() == 1                                 # the abandoned job is in flight, not ready
+    time.sleep(0.7)                                        # past the visibility timeout
+    done = w2.drain()
+    assert len(done) == 2 and all(r["exit_code"] == 0 for r in done)
+    assert [ledger.get_job(j)["status"] for j in ids] == ["succeeded"] * 3
+    assert w2.depth() == 0
