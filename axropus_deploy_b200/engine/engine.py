@@ -213,6 +213,18 @@ class LLMEngine:
                               "failures": a.get("capture_failures", 0), "admit": a.get("captures", 0)})
         return self.trace.summary(gen)
 
+    def warmup_graphs(self) -> int:
+        """Capture the decode CUDA graph of every batch bucket now (start-up work), so no
+        capture lands in the middle of serving; returns the number captured."""
+        if self._graphs is None:
+            return 0
+        n = 0
+        for b in self._graphs.buckets:
+            if b not in self._graphs.graphs:
+                self._graphs._capture(b)
+                n += 1
+        return n
+
     def close(self) -> None:
         """Release CUDA graphs (they hold device memory and must go before the
         process group is destroyed)."""

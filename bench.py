@@ -64,6 +64,7 @@ def parse_args(argv=None):
     p.add_argument("--ttft-samples", type=int, default=12)
     p.add_argument("--e2e-waves", type=int, default=0, help="0: as many as --steps")
     p.add_argument("--graphs", type=int, default=1)
+    p.add_argument("--prefill-graphs", type=int, default=1, help="CUDA-graph one-sequence prefills (with --graphs)")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--layers", type=int, default=None, help="debug only: fewer layers (invalidates the number)")
     return p.parse_args(argv)
@@ -205,7 +206,8 @@ def run_ours(args) -> None:
     pages_per_prefix = args.prefix_len // PAGE
     ecfg = EngineConfig(num_blocks=num_blocks, kv_fmt=args.kv_fmt, max_batch=args.batch,
                         max_prefill_tokens=2 * (args.prefix_len + args.suffix_len),
-                        max_model_len=tok_per_req + PAGE, cuda_graphs=bool(args.graphs))
+                        max_model_len=tok_per_req + PAGE, cuda_graphs=bool(args.graphs),
+                        prefill_graphs=bool(args.prefill_graphs))
     eng = LLMEngine(model, ecfg, None)
     # G1 pool: at least 1.25x the prefix set over the node, grown into the HBM left after
     # weights and the live cache (keeping 12 GB of headroom for activations and graphs)
@@ -238,6 +240,7 @@ def run_ours(args) -> None:
         while eng.has_unfinished():
             eng.step()
     eng.evict_live_cache()
+    eng.warmup_graphs()  # every decode batch bucket captured before anything is timed
     torch.cuda.synchronize()
     barrier(info)
 
@@ -313,6 +316,13 @@ def run_ours(args) -> None:
     amf0 = dict(amf.stat)
     from axropus_deploy_b200.ops._ext import launches as n_launches
 
+    def n_graphs():
+        d = len(eng._graphs.graphs) if eng._graphs is not None else 0
+        p_ = eng._prefill_graphs.stat["captures"] if eng._prefill_graphs is not None else 0
+        return d, p_
+
+    graphs0 = n_graphs()
+
     t_start.record()
     launches_before = n_launches()
     for w in waves:
@@ -320,6 +330,7 @@ def run_ours(args) -> None:
     t_end.record()
     torch.cuda.synchronize()
     launches_timed = n_launches() - launches_before
+    graphs1 = n_graphs()
     barrier(info)
     clocks = sampler.stop()
     ms = t_start.elapsed_time(t_end)
@@ -389,6 +400,8 @@ def run_ours(args) -> None:
             "pool_slots_per_shard": slots_per_shard,
             "wave_mix": gathered[0]["waves"], "amf_hits_rank0": gathered[0]["hits"],
             "ms_per_step_by_rank": [round(g["ms"] / args.steps, 1) for g in gathered],
+            "graph_captures_in_timed_region_rank0": {"decode": graphs1[0] - graphs0[0],
+                                                     "prefill": graphs1[1] - graphs0[1]},
             "clocks": {"sm_mhz": ck.get("sm_mhz"), "sm_max_mhz": ck.get("sm_max_mhz"), "reasons": reasons},
             "e2e": {"value": round(e2e_val, 2), "unit": "output tokens/s (whole job)",
                     "h2d_bytes_per_step": int(h2d / n_e2e),
