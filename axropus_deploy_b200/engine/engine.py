@@ -347,13 +347,25 @@ class LLMEngine:
             if hit is not None:
                 t0 = time.perf_counter()
                 blk = torch.tensor(r.blocks[n_local:hit.n_pages], dtype=torch.int32)
+                ev = None
+                if self.device.type == "cuda":
+                    ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                    ev[0].record()
                 try:
                     hit.restore(self.cache, blk, first_page=n_local)
-                    if self.device.type == "cuda":
-                        torch.cuda.current_stream().synchronize()
-                finally:
+                except BaseException:
                     hit.release()
+                    raise
                 r.restore_ms = (time.perf_counter() - t0) * 1e3
+                if ev is not None:
+                    # the restore runs on the GPU while this step builds and launches the
+                    # prefill; the source entry stays pinned until the step's first
+                    # synchronisation (_settle_restores), which also reads the device time
+                    ev[1].record()
+                    r._restore = (hit, ev)
+                else:
+                    hit.release()
+                    self._note_restore(r, hit)
                 r.restored_tokens = (hit.n_pages - n_local) * PAGE
                 r.amf_tier = hit.tier
                 self.bm.register_computed(r.blocks[n_local:hit.n_pages], hashes[n_local:hit.n_pages])
@@ -361,9 +373,7 @@ class LLMEngine:
                     self.amf.capture(r.prompt_np[:hit.n_tokens], self.cache,
                                      torch.tensor(r.blocks[:hit.n_pages], dtype=torch.int32),
                                      promote_from=hit.tier)
-                self.amf.note_restored(hit, r.restore_ms, 0.0)
                 self.stat["restored_tokens"] += r.restored_tokens
-                self.trace.hit(len(r.prompt), hit.n_tokens, hit.n_tokens, r.restore_ms, hit.tier)
             elif n_local:
                 r.amf_tier = "apc"
             r.num_computed = computed_pages * PAGE
@@ -374,6 +384,26 @@ class LLMEngine:
             admitted.append(r)
             budget -= new_tokens
         return admitted
+
+    def _note_restore(self, r: Request, hit) -> None:
+        self.amf.note_restored(hit, r.restore_ms, 0.0)
+        self.trace.hit(len(r.prompt), hit.n_tokens, hit.n_tokens, r.restore_ms, hit.tier)
+
+    def _settle_restores(self, reqs: List[Request], ok: bool = True) -> None:
+        """After the step's first synchronisation: device time of each restore, release of
+        the pinned source entries, statistics and trace lines."""
+        for r in reqs:
+            pending = r.__dict__.pop("_restore", None)
+            if pending is None:
+                continue
+            hit, (e0, e1) = pending
+            if ok:
+                r.restore_ms = e0.elapsed_time(e1)
+            else:
+                e1.synchronize()  # the copy must be done before its source may be reused
+            hit.release()
+            if ok:
+                self._note_restore(r, hit)
 
     # ------------------------------------------------------------------ forward helpers
     def _sample(self, logits: torch.Tensor, reqs: List[Request]) -> List[int]:
@@ -440,12 +470,17 @@ class LLMEngine:
             logits_idx=torch.tensor([c - 1 for c in cu[1:]], dtype=torch.int32).to(dev, non_blocking=True),
         )
         t_pf = time.perf_counter()
-        if self._prefill_graphs is not None and self._prefill_graphs.supports(reqs, len(toks), lens[0]):
-            logits = self._prefill_graphs.run(reqs[0], toks, pos, slots, lens[0])
-        else:
-            logits = self.model.forward(torch.tensor(toks, dtype=torch.int32).to(dev, non_blocking=True), meta,
-                                        self.cache)
-        new = self._sample(logits, reqs)  # synchronises with the forward
+        try:
+            if self._prefill_graphs is not None and self._prefill_graphs.supports(reqs, len(toks), lens[0]):
+                logits = self._prefill_graphs.run(reqs[0], toks, pos, slots, lens[0])
+            else:
+                logits = self.model.forward(torch.tensor(toks, dtype=torch.int32).to(dev, non_blocking=True), meta,
+                                            self.cache)
+            new = self._sample(logits, reqs)  # synchronises with the forward (and the restores)
+        except BaseException:
+            self._settle_restores(reqs, ok=False)
+            raise
+        self._settle_restores(reqs)
         pf_ms = (time.perf_counter() - t_pf) * 1e3
         n_new = len(toks)
         cold = [r for r in reqs if r.amf_tier == "cold"]
