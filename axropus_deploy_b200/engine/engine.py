@@ -20,8 +20,10 @@ and save are per-layer PyTorch index-puts synchronous with the forward pass.
 """
 from __future__ import annotations
 
+import contextlib
 import itertools
 import logging
+import os
 import time
 from dataclasses import dataclass, field
 from typing import Dict, List, Optional, Sequence
@@ -100,6 +102,22 @@ class EngineConfig:
     spec_max_depth: int = 8
     # [AMF_*] trace lines (None: KORITH_AMF_TRACE decides)
     trace: Optional[bool] = None
+
+
+_NVTX = os.environ.get("AXR_NVTX", "0") == "1"
+
+
+@contextlib.contextmanager
+def _nvtx(name: str):
+    """NVTX range around an engine phase when AXR_NVTX=1 (for nsys / ncu range filters)."""
+    if _NVTX and torch.cuda.is_available():
+        torch.cuda.nvtx.range_push(name)
+        try:
+            yield
+        finally:
+            torch.cuda.nvtx.range_pop()
+    else:
+        yield
 
 
 class LLMEngine:
@@ -243,18 +261,21 @@ class LLMEngine:
     def step(self) -> List[Request]:
         self.stat["steps"] += 1
         done: List[Request] = []
-        admitted = self._admit()
+        with _nvtx("admit"):
+            admitted = self._admit()
         decoding = [r for r in self.running if r.state == "running" and r not in admitted]
         any_prefill, any_decode = bool(admitted), bool(decoding)
         if self.cfg.lockstep and hasattr(self.model, "ep_any"):
             # a forward runs on every GPU when it runs on any (the MoE layers need all of them)
             any_prefill, any_decode = self.model.ep_any([any_prefill, any_decode])
         if admitted:
-            done += self._prefill(admitted)
+            with _nvtx("prefill"):
+                done += self._prefill(admitted)
         elif self.cfg.lockstep and any_prefill:
             self._idle_forward()
         if decoding:
-            done += self._decode(decoding)
+            with _nvtx("decode"):
+                done += self._decode(decoding)
         elif self.cfg.lockstep and any_decode:
             self._idle_forward()
         if self.device.type == "cuda":
@@ -304,6 +325,7 @@ class LLMEngine:
         decoding = sum(1 for r in self.running if r.state == "running")
         head_hit = bool(self.waiting) and bool(self.waiting[0].__dict__.get("_held"))
         budget = self.policy.budget(self.cfg.max_prefill_tokens, decoding, self.cfg.max_batch, head_hit)
+        budget0 = budget
         while self.waiting and self.free_rows:
             r = self.waiting[0]
             limit = self._amf_limit(r)
@@ -383,6 +405,8 @@ class LLMEngine:
             self.running.append(r)
             admitted.append(r)
             budget -= new_tokens
+        self.policy.note(waiting=len(self.waiting), decoding=decoding, budget_tokens=budget0, head_is_hit=head_hit,
+                         admitted=len(admitted), held_waiting=sum(1 for w in self.waiting if w.__dict__.get("_held")))
         return admitted
 
     def _note_restore(self, r: Request, hit) -> None:

@@ -16,12 +16,18 @@ so running decodes keep a short step time -- except when the head of the queue i
 ``KORITH_VLLM_DECODE_FULL_BUDGET_ON_HIT`` is set. ``KORITH_VLLM_DECODE_FIRST=0`` turns the
 policy off (plain first-come first-served, full budget).
 
+Trace: with ``KORITH_VLLM_SCHED_TRACE_PATH`` and ``KORITH_VLLM_SCHED_TRACE_EVERY=N``, every
+N-th admission round appends one JSON line (queue length, requests decoding, prefill budget,
+whether the head of the queue is a hit, how many were admitted, how many waiting requests
+are held by a cache tier).
+
 Reference: korith_vllm_ext/decode_scheduler.py:89-147 (the knobs and their defaults) and
 :326-377 (the request score), a vLLM scheduler subclass there; here the engine's own
 admission loop consults it.
 """
 from __future__ import annotations
 
+import json
 import os
 import time
 from typing import List
@@ -51,6 +57,16 @@ class AdmissionPolicy:
         self.full_on_hit = _b("KORITH_VLLM_DECODE_FULL_BUDGET_ON_HIT", True)
         self.lane_bias = {lane: _f(f"KORITH_VLLM_LANE_BIAS_{lane}", d, 0.1, 10.0)
                           for lane, d in (("SPEC_HIT", 1.25), ("HIT", 1.1), ("SPEC_MISS", 0.95), ("MISS", 1.0))}
+        self.trace_path = os.environ.get("KORITH_VLLM_SCHED_TRACE_PATH", "")
+        self.trace_every = int(_f("KORITH_VLLM_SCHED_TRACE_EVERY", 0, 0, 1 << 30))
+        self.rounds = 0
+
+    def note(self, **fields) -> None:
+        """Count an admission round; every ``trace_every``-th one goes to the trace file."""
+        self.rounds += 1
+        if self.trace_path and self.trace_every > 0 and self.rounds % self.trace_every == 0:
+            with open(self.trace_path, "a") as f:
+                f.write(json.dumps({"ts": time.time(), "round": self.rounds, "enabled": self.enabled, **fields}) + "\n")
 
     def order(self, waiting: List, held, spec: bool = False, now: float = None) -> List:
         """Waiting requests in admission order; ``held(r)`` says whether r's prefix is

@@ -131,6 +131,23 @@ def test_admission_policy_prefers_hits_and_scales_budget(monkeypatch):
     assert [r.i for r in off.order(w, lambda r: True)] == [0, 1, 2, 3]
 
 
+def test_scheduler_trace_lines(model, tmp_path, monkeypatch):
+    """KORITH_VLLM_SCHED_TRACE_PATH / _EVERY: every N-th admission round of a running engine
+    appends one JSON line describing the queue."""
+    import json
+
+    path = tmp_path / "sched.jsonl"
+    monkeypatch.setenv("KORITH_VLLM_SCHED_TRACE_PATH", str(path))
+    monkeypatch.setenv("KORITH_VLLM_SCHED_TRACE_EVERY", "2")
+    eng = LLMEngine(model, EngineConfig(num_blocks=64, max_model_len=512, max_batch=4))
+    g = torch.Generator().manual_seed(7)
+    eng.generate([torch.randint(0, 32000, (40,), generator=g).tolist() for _ in range(3)], SamplingParams(max_tokens=5))
+    lines = [json.loads(x) for x in path.read_text().splitlines()]
+    assert lines and all(x["round"] % 2 == 0 for x in lines)
+    assert {"waiting", "decoding", "budget_tokens", "head_is_hit", "admitted", "held_waiting"} <= set(lines[0])
+    assert sum(x["admitted"] for x in lines) <= 3 and eng.policy.rounds >= 2 * len(lines)
+
+
 def test_prefill_graph_runner_padding_matches_eager(model):
     """The graph runner's padded one-sequence prefill (bucketed token count, slot -1
     padding, device-side lengths) gives the same tokens as the plain prefill. On CPU the
