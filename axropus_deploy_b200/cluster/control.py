@@ -21,7 +21,6 @@ billing and debug endpoints).
 """
 from __future__ import annotations
 
-import hashlib
 import json
 import statistics
 import uuid

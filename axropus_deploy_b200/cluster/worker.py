@@ -36,7 +36,6 @@ from __future__ import annotations
 import hashlib
 import os
 import threading
-import time
 import traceback
 import uuid
 from pathlib import Path
