@@ -16,14 +16,17 @@ names what a backend supports. Three backends:
   through :class:`~.engine_client.EngineClient`: one sequence, KV replay from
   snapshot files, logits, token verification.
 * :class:`OpenAICompatibleAdapter` (``openai_compatible``) -- any server speaking
-  ``POST /v1/completions`` (this framework's server among them), over HTTP.
+  ``POST /v1/completions`` (this framework's server among them), over HTTP;
+  :class:`VllmOpenAIAdapter` (``vllm_openai``) adds vLLM's request extras (``vllm_xargs``,
+  speculative tokens, ``kv_transfer_params`` pass-through).
+* :class:`TransformersAdapter` (``hf_transformers``) -- a Hugging Face causal LM in process.
 
 :class:`AdapterRegistry` builds adapters from a jobspec and caches them per
 (backend, model).
 
 Reference: platform/adapters/base.py:8-109 (interface, capability names),
 platform/adapters/registry.py (cache per backend/model), korith_local.py,
-openai_compatible.py, vllm_openai.py.
+openai_compatible.py, vllm_openai.py:388-425 (kv_transfer_params), transformers_local.py.
 """
 from __future__ import annotations
 
@@ -412,6 +415,148 @@ class OpenAICompatibleAdapter(BackendAdapter):
         return self._run(prompt, max_tokens, deterministic_cfg, use_amf=True)
 
 
+class VllmOpenAIAdapter(OpenAICompatibleAdapter):
+    """A vLLM OpenAI server. On top of the plain completion call: the job's lane and policy
+    travel as ``vllm_xargs`` (``KORITH_VLLM_*`` admission hints read by a decode-first
+    scheduler), a speculative run asks for ``num_speculative_tokens`` (and a draft model when
+    the policy names one), and ``kv_transfer_params`` returned by a KV connector are kept in
+    the result so a later request can hand them back."""
+
+    backend_id = "vllm_openai"
+    backend_version = "vllm-openai-v1"
+
+    @staticmethod
+    def _xargs(policy: Dict[str, Any], lane: str) -> Dict[str, Any]:
+        x: Dict[str, Any] = {"korith_lane": lane or "MISS"}
+        for k in ("priority", "replay_state", "tenant_id"):
+            v = (policy or {}).get(k)
+            if isinstance(v, (str, int, float)) and not isinstance(v, bool):
+                x[f"korith_{k}"] = v
+        return x
+
+    def _body(self, prompt, max_tokens, det, policy, use_amf: bool, spec_k: int = 0) -> Dict[str, Any]:
+        body = {"model": self.model_id, "prompt": prompt, "max_tokens": int(max_tokens),
+                "temperature": float((det or {}).get("temperature", 0.0)), "seed": (det or {}).get("seed"),
+                "vllm_xargs": self._xargs(policy, (policy or {}).get("lane", ""))}
+        if not use_amf:
+            body["amf_prefix_len"] = 0
+        if (policy or {}).get("kv_transfer_params"):
+            body["kv_transfer_params"] = policy["kv_transfer_params"]
+        if spec_k > 0:
+            body["num_speculative_tokens"] = int(spec_k)
+            if (policy or {}).get("draft_model"):
+                body["speculative_model"] = policy["draft_model"]
+        return body
+
+    def _run_v(self, prompt, max_tokens, det, policy, use_amf: bool, spec_k: int = 0) -> Dict:
+        t0 = time.perf_counter()
+        r = self._post(self._body(prompt, max_tokens, det, policy, use_amf, spec_k))
+        ax = r.get("axropus", {})
+        text = (r.get("choices") or [{}])[0].get("text", "")
+        toks = r.get("token_ids") or byte_tokens(text)
+        ttft = float(ax.get("ttft_ms", 0.0))
+        out = _result(list(toks), t0, ttft, ttft, {"decision": "hit" if ax.get("hit") else "miss",
+                                                   "tier": ax.get("tier", "remote"),
+                                                   "restored_tokens": ax.get("restored_tokens", 0), "saved_ms": 0.0})
+        kvp = r.get("kv_transfer_params") or (r.get("usage") or {}).get("kv_transfer_params")
+        if kvp:
+            out["kv_transfer_params"] = kvp
+        usage = r.get("usage") or {}
+        acc, prop = usage.get("accepted_speculative_tokens"), usage.get("proposed_speculative_tokens")
+        if spec_k > 0 and acc is not None and prop:
+            out["spec"] = {"drafted": int(prop), "accepted": int(acc), "acceptance": int(acc) / int(prop)}
+        return out
+
+    def get_capabilities(self) -> Capabilities:
+        return Capabilities(deterministic_seeding=True, batch_prefill=True, kv_replay=True, draft_supported=True)
+
+    def run_baseline(self, prompt, max_tokens, deterministic_cfg, policy, artifacts, mf_snapshot_in):
+        return self._run_v(prompt, max_tokens, deterministic_cfg, policy, use_amf=False)
+
+    def run_accel(self, prompt, max_tokens, deterministic_cfg, policy, artifacts, mf_snapshot_in, engine_cfg=None):
+        return self._run_v(prompt, max_tokens, deterministic_cfg, policy, use_amf=True)
+
+    def run_speculative(self, prompt, max_tokens, deterministic_cfg, policy, artifacts, mf_snapshot_in, spec_cfg=None,
+                        engine_cfg=None):
+        return self._run_v(prompt, max_tokens, deterministic_cfg, policy, use_amf=True,
+                           spec_k=int((spec_cfg or {}).get("k", 4)))
+
+
+class TransformersAdapter(BackendAdapter):
+    """A Hugging Face ``transformers`` causal LM in this process (``model_path`` of a local
+    checkpoint, or ``config`` -- a dict for ``LlamaConfig`` -- for a random-init model).
+    Baseline runs only: the KV cache lives inside ``generate`` and is not replayed; logits
+    and token verification are exposed. Text is tokenised byte-wise, as elsewhere here."""
+
+    backend_id = "hf_transformers"
+    backend_version = "transformers"
+
+    def __init__(self, model_path: str = "", config: Optional[Dict[str, Any]] = None, device: str = "cpu",
+                 seed: int = 0):
+        import torch
+        import transformers
+
+        if model_path:
+            self.model = transformers.AutoModelForCausalLM.from_pretrained(model_path)
+        else:
+            torch.manual_seed(seed)
+            cfg = transformers.LlamaConfig(**(config or {"vocab_size": 256, "hidden_size": 64, "intermediate_size": 128,
+                                                         "num_hidden_layers": 2, "num_attention_heads": 4,
+                                                         "num_key_value_heads": 2}))
+            self.model = transformers.LlamaForCausalLM(cfg)
+        self.model = self.model.to(device).eval()
+        self.device = device
+        self.name = model_path or "random-llama"
+        self.backend_version = f"transformers-{transformers.__version__}"
+
+    def get_fingerprint(self) -> Dict[str, str]:
+        c = self.model.config
+        shape = f"{c.model_type}:{c.num_hidden_layers}:{c.hidden_size}:{c.vocab_size}"
+        return {"backend_id": self.backend_id, "backend_version": self.backend_version, "model": self.name,
+                "model_hash": hashlib.sha256(shape.encode()).hexdigest()[:16], "tokenizer": "bytes-v1",
+                "kv_layout": "hf-dynamic"}
+
+    def get_capabilities(self) -> Capabilities:
+        return Capabilities(deterministic_seeding=True, logits_access=True, verify_tokens=True)
+
+    def tokenize(self, prompt: str) -> int:
+        return len(byte_tokens(prompt))
+
+    def _ids(self, toks):
+        import torch
+
+        v = self.model.config.vocab_size
+        return torch.tensor([[t % v for t in toks]], device=self.device)
+
+    def run_baseline(self, prompt, max_tokens, deterministic_cfg, policy, artifacts, mf_snapshot_in):
+        import torch
+
+        t0 = time.perf_counter()
+        ids = self._ids(byte_tokens(prompt))
+        with torch.no_grad():
+            first = self.model(ids).logits[0, -1].argmax().item()
+            ttft = (time.perf_counter() - t0) * 1e3
+            out = self.model.generate(ids, max_new_tokens=int(max_tokens), do_sample=False,
+                                      pad_token_id=0)[0, ids.shape[1]:].tolist()
+        if out and out[0] != first:
+            out = [first] + out[1:]
+        return _result(out, t0, ttft, ttft, {"decision": "miss", "tier": "cold", "restored_tokens": 0, "saved_ms": 0.0})
+
+    def verify_tokens(self, prompt, draft_tokens, deterministic_cfg, spec_cfg=None):
+        import torch
+
+        toks = byte_tokens(prompt)
+        ids = self._ids(toks + list(draft_tokens))
+        with torch.no_grad():
+            pred = self.model(ids).logits[0, len(toks) - 1:-1].argmax(-1).tolist()
+        acc = 0
+        for p, d in zip(pred, draft_tokens):
+            if p != d % self.model.config.vocab_size:
+                break
+            acc += 1
+        return {"accepted": acc, "accepted_tokens": list(draft_tokens[:acc])}
+
+
 class AdapterRegistry:
     """Adapters by jobspec ``backend_id`` + ``model``; one instance per (backend, model)."""
 
@@ -435,6 +580,11 @@ class AdapterRegistry:
         elif bid == "openai_compatible":
             a = OpenAICompatibleAdapter(str(model["endpoint"]), str(model.get("model_id", "")),
                                         str(model.get("api_key", "")))
+        elif bid in ("vllm", "vllm_openai"):
+            a = VllmOpenAIAdapter(str(model["endpoint"]), str(model.get("model_id", "")), str(model.get("api_key", "")))
+        elif bid == "hf_transformers":
+            a = TransformersAdapter(str(model.get("model_path", "")), model.get("config"),
+                                    str(model.get("device", "cpu")))
         else:
             raise ValueError(f"unknown backend_id {bid!r}")
         self._cache[key] = a

@@ -339,3 +339,86 @@ def serve(plane, host: str = "127.0.0.1", port: int = 8000, block: bool = True):
         return httpd
     threading.Thread(target=httpd.serve_forever, daemon=True).start()
     return httpd
+
+
+def serve_proxy(upstreams: Dict[str, str], router=None, host: str = "127.0.0.1", port: int = 0,
+                timeout_s: float = 300.0, block: bool = False):
+    """Reverse proxy in front of OpenAI-compatible servers (``upstreams``: worker id -> base
+    URL). ``POST /v1/completions`` and ``/v1/chat/completions`` go to the worker the
+    :class:`~.router.ClusterRouter` picks (the one holding the prompt's prefix, else the
+    least loaded; its worker ids must be the keys of ``upstreams``), with the choice in the
+    ``X-Korith-Route`` response header; every other request goes to the first upstream.
+    Reference: platform/gateway/proxy_server.py (a plain pass-through to the router)."""
+    import urllib.error
+    import urllib.request
+
+    from .control import render_messages
+
+    first = next(iter(upstreams.values()))
+    mu = threading.Lock()
+
+    class Proxy(BaseHTTPRequestHandler):
+        protocol_version = "HTTP/1.1"
+
+        def log_message(self, *a):
+            pass
+
+        def _forward(self, method: str) -> None:
+            n = int(self.headers.get("Content-Length", "0") or 0)
+            body = self.rfile.read(n) if n > 0 else None
+            base, route, wid, added = first, "default", None, 0.0
+            path = urlparse(self.path).path
+            if method == "POST" and router is not None and path in ("/v1/completions", "/v1/chat/completions"):
+                try:
+                    req = json.loads(body or b"{}")
+                    text = req.get("prompt") if path == "/v1/completions" else render_messages(req.get("messages") or [])
+                    if isinstance(text, str) and text:
+                        with mu:
+                            before = {k: w.load for k, w in router.workers.items()}
+                            r = router.submit(text, str(req.get("user", "default")), int(req.get("max_tokens", 16)))
+                            added = r.worker.load - before[r.worker.worker_id]
+                        if r.worker.worker_id in upstreams:
+                            wid, base, route = r.worker.worker_id, upstreams[r.worker.worker_id], r.kind
+                        else:
+                            with mu:
+                                r.worker.load -= added
+                except (ValueError, TypeError, RuntimeError):
+                    pass  # malformed or unroutable: the default upstream answers
+            fwd = urllib.request.Request(base.rstrip("/") + self.path, data=body, method=method)
+            for k in ("Content-Type", "Authorization", "X-Request-Id"):
+                if self.headers.get(k):
+                    fwd.add_header(k, self.headers[k])
+            try:
+                with urllib.request.urlopen(fwd, timeout=timeout_s) as resp:
+                    code, data, ctype = resp.status, resp.read(), resp.headers.get("Content-Type", "application/json")
+            except urllib.error.HTTPError as e:
+                code, data, ctype = e.code, e.read(), e.headers.get("Content-Type", "application/json")
+            except (urllib.error.URLError, OSError) as e:
+                code, data, ctype = 502, json.dumps({"error": f"upstream unreachable: {e}"}).encode(), "application/json"
+            finally:
+                if wid is not None:
+                    with mu:  # the request is done: its tokens leave the worker's load
+                        w = router.workers[wid]
+                        w.load = max(0.0, w.load - added)
+            self.send_response(code)
+            self.send_header("Content-Type", ctype)
+            self.send_header("Content-Length", str(len(data)))
+            self.send_header("X-Korith-Route", f"{route}:{wid or 'default'}")
+            self.end_headers()
+            self.wfile.write(data)
+
+        def do_GET(self):
+            self._forward("GET")
+
+        def do_POST(self):
+            self._forward("POST")
+
+        def do_DELETE(self):
+            self._forward("DELETE")
+
+    httpd = ThreadingHTTPServer((host, port), Proxy)
+    if block:
+        httpd.serve_forever()
+        return httpd
+    threading.Thread(target=httpd.serve_forever, daemon=True).start()
+    return httpd

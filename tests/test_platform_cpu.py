@@ -330,3 +330,77 @@ def test_worker_crash_jobs_reclaimed_from_durable_queue(tmp_path):
     assert len(done) == 2 and all(r["exit_code"] == 0 for r in done)
     assert [ledger.get_job(j)["status"] for j in ids] == ["succeeded"] * 3
     assert w2.depth() == 0
+
+
+def test_more_adapters_and_proxy(tmp_path):
+    """vLLM-style adapter request extras and the in-process transformers adapter, against a
+    stub OpenAI server; the reverse proxy routes a prompt to the worker that holds its prefix."""
+    import threading
+    from http.server import BaseHTTPRequestHandler, ThreadingHTTPServer
+
+    from axropus_deploy_b200.amf.keys import pool_key
+    from axropus_deploy_b200.cluster.adapters import AdapterRegistry, TransformersAdapter, VllmOpenAIAdapter
+    from axropus_deploy_b200.cluster.coordinator import AmfCoordinator
+    from axropus_deploy_b200.cluster.gateway import serve_proxy
+    from axropus_deploy_b200.cluster.router import ClusterRouter, WorkerInfo
+
+    seen = []
+
+    def stub(name):
+        class H(BaseHTTPRequestHandler):
+            def log_message(self, *a):
+                pass
+
+            def do_POST(self):
+                body = json.loads(self.rfile.read(int(self.headers["Content-Length"])))
+                seen.append((name, body))
+                out = json.dumps({"choices": [{"text": "ok"}], "token_ids": [111, 107], "server": name,
+                                  "usage": {"kv_transfer_params": {"blk": 3}, "accepted_speculative_tokens": 3,
+                                            "proposed_speculative_tokens": 4},
+                                  "axropus": {"hit": True, "tier": "g1_raw", "ttft_ms": 1.5}}).encode()
+                self.send_response(200)
+                self.send_header("Content-Type", "application/json")
+                self.send_header("Content-Length", str(len(out)))
+                self.end_headers()
+                self.wfile.write(out)
+        srv = ThreadingHTTPServer(("127.0.0.1", 0), H)
+        threading.Thread(target=srv.serve_forever, daemon=True).start()
+        return srv
+
+    a, b = stub("a"), stub("b")
+    try:
+        url_a, url_b = (f"http://127.0.0.1:{s.server_address[1]}" for s in (a, b))
+        v = VllmOpenAIAdapter(url_a, "m")
+        r = v.run_speculative("hello", 4, {"temperature": 0}, {"lane": "SPEC_HIT", "priority": 2}, {}, None,
+                              spec_cfg={"k": 4})
+        body = seen[-1][1]
+        assert body["num_speculative_tokens"] == 4 and body["vllm_xargs"]["korith_lane"] == "SPEC_HIT"
+        assert r["kv_transfer_params"] == {"blk": 3} and r["spec"]["accepted"] == 3 and r["amf"]["decision"] == "hit"
+        assert AdapterRegistry().get_adapter({"backend_id": "vllm_openai", "model": {"endpoint": url_a}}).backend_id \
+            == "vllm_openai"
+        hf = TransformersAdapter()
+        out = hf.run_baseline("abc", 3, {}, {}, {}, None)
+        assert out["tokens_out"] == 3
+        ver = hf.verify_tokens("abc", out["output_tokens"], {})
+        assert ver["accepted"] == 3  # the model's own greedy tokens verify in full
+        # proxy: the coordinator says worker "b" holds this prompt's prefix
+        text = "x" * 600
+        coord = AmfCoordinator()
+        coord.register("default", pool_key(list(text.encode())[:512]), "nb", "b", {})
+        router = ClusterRouter([WorkerInfo("a", "na"), WorkerInfo("b", "nb")], coordinator=coord, prefix_tokens=512)
+        px = serve_proxy({"a": url_a, "b": url_b}, router)
+        try:
+            purl = f"http://127.0.0.1:{px.server_address[1]}/v1/completions"
+            req = urllib.request.Request(purl, data=json.dumps({"prompt": text, "max_tokens": 4}).encode(),
+                                         method="POST", headers={"Content-Type": "application/json"})
+            with urllib.request.urlopen(req, timeout=30) as resp:
+                assert json.loads(resp.read())["server"] == "b"
+                assert resp.headers["X-Korith-Route"] == "amf_local:b"
+            assert router.workers["b"].load == 0
+        finally:
+            px.shutdown()
+            px.server_close()
+    finally:
+        for s in (a, b):
+            s.shutdown()
+            s.server_close()
