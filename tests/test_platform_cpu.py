@@ -404,3 +404,24 @@ def test_more_adapters_and_proxy(tmp_path):
         for s in (a, b):
             s.shutdown()
             s.server_close()
+
+
+def test_snapshot_sidecar_validation(tmp_path):
+    """The .meta.json sidecar refuses a snapshot for another model, tokenizer, layout,
+    context size or fingerprint, and a snapshot whose bytes changed."""
+    from axropus_deploy_b200.cluster.engine_client import validate_snapshot_metadata, write_snapshot_metadata
+
+    snap = tmp_path / "s.amfk"
+    snap.write_bytes(bytes(range(256)) * 64)
+    ctx = dict(fingerprint_hash="fp", model_hash="m", tokenizer_hash="t", kv_layout_version="paged16", n_ctx=4096)
+    write_snapshot_metadata(snap, backend_id="axr_engine", created_at="now", **ctx)
+    assert validate_snapshot_metadata(snap, **ctx)[:2] == (True, "ok")
+    for k, v, reason in (("model_hash", "m2", "snapshot_model_mismatch"), ("tokenizer_hash", "t2", "snapshot_tokenizer_mismatch"),
+                         ("kv_layout_version", "x", "snapshot_layout_mismatch"), ("n_ctx", 8192, "snapshot_ctx_mismatch"),
+                         ("fingerprint_hash", "other", "snapshot_fingerprint_mismatch")):
+        assert validate_snapshot_metadata(snap, **dict(ctx, **{k: v}))[1] == reason
+    raw = bytearray(snap.read_bytes())
+    raw[100] ^= 1
+    snap.write_bytes(bytes(raw))
+    assert validate_snapshot_metadata(snap, **ctx)[1] == "snapshot_checksum_mismatch"
+    assert validate_snapshot_metadata(tmp_path / "missing.amfk", **ctx)[1] == "snapshot_missing"
