@@ -28,6 +28,7 @@ from pathlib import Path
 from typing import Any, Dict, List, Optional
 
 from ..amf.keys import pool_key
+from ..amf.prompt_policy import amf_prefix_tokens, amf_tenant
 from .economics import TenantMeter, estimate_savings, target_report
 from .ledger import canonical_json, sha256_hex
 from .observability import GLOBAL_METRICS, utc_now
@@ -121,7 +122,12 @@ class ControlPlane:
                 return prev
         text = canonicalize(job["prompt"])
         toks = list(text.encode("utf-8"))
+        if job.get("amf_prefix_len") is None:  # KORITH_AMF_PREFIX_EXTRACTION: key on the part before the last turn
+            n = amf_prefix_tokens(toks, lambda s: list(s.encode("utf-8")))
+            if n:
+                job["amf_prefix_len"] = n
         fp = self.fingerprint_of(job, toks)
+        fp["tenant_ns"] = amf_tenant(tenant_id, text)  # isolated, shared (patterns) or one namespace
         fp_hash = sha256_hex(canonical_json(fp))
         det = job["deterministic"]
         sampling_hash = sha256_hex(canonical_json({"det": det, "max_tokens": job.get("max_tokens", 64)}))

@@ -225,7 +225,7 @@ class KorithConfig:
     amf_shared_prefix_patterns: str = ""
     amf_prefix_extraction: bool = False
     amf_prefix_boundary_token: str = "<|user|>"
-    amf_tenant_isolation: bool = True
+    amf_tenant_isolation: bool = False  # off: one key namespace (tenant hash 0), as the reference's store
     amf_normalize_whitespace: bool = False
     amf_normalize_unicode: bool = False
     amf_prompt_collapse_blanks: bool = False
@@ -323,7 +323,7 @@ class KorithConfig:
         e.amf_shared_prefix_patterns = env_str("KORITH_AMF_SHARED_PREFIX_PATTERNS", "")
         e.amf_prefix_extraction = env_bool("KORITH_AMF_PREFIX_EXTRACTION", False)
         e.amf_prefix_boundary_token = env_str("KORITH_AMF_PREFIX_BOUNDARY_TOKEN", e.amf_prefix_boundary_token)
-        e.amf_tenant_isolation = env_bool("KORITH_AMF_TENANT_ISOLATION", True)
+        e.amf_tenant_isolation = env_bool("KORITH_AMF_TENANT_ISOLATION", False)
         e.amf_normalize_whitespace = env_bool("KORITH_AMF_NORMALIZE_WHITESPACE", False)
         e.amf_normalize_unicode = env_bool("KORITH_AMF_NORMALIZE_UNICODE", False)
         e.amf_prompt_collapse_blanks = env_bool("KORITH_AMF_PROMPT_COLLAPSE_BLANKS", False)

@@ -18,6 +18,7 @@ from typing import Any, Dict, List, Optional
 from fastapi import FastAPI, Header, HTTPException, Request
 from fastapi.responses import Response
 
+from ..amf.prompt_policy import prepare_prompt
 from ..config import AxropusConfig, KorithConfig
 from ..engine import SamplingParams
 from .metrics import MetricRegistry
@@ -67,7 +68,8 @@ def build_engine(cfg: AxropusConfig, kcfg: Optional[KorithConfig] = None, *, num
                           max(1, int(kcfg.vram_pool_gb * (1 << 30) // chunk)), dev)
         if raw is None and comp is None:
             raw = G1Pool(mc.num_layers, mc.num_kv_heads, mc.head_dim, "raw", 256, dev)
-        ctx = AmfContext(model_hash=amf_hash_model_name(mc.name), tenant_hash=amf_hash_tenant_id(kcfg.tenant_id),
+        tenant_hash = amf_hash_tenant_id(kcfg.tenant_id) if kcfg.amf_tenant_isolation else 0
+        ctx = AmfContext(model_hash=amf_hash_model_name(mc.name), tenant_hash=tenant_hash,
                          n_ctx=kcfg.n_ctx, kv_version=1, rope_base_bits=amf_float_bits(mc.rope_theta),
                          rope_scale_bits=amf_float_bits(1.0))
         disk = DiskTier(kcfg.amf_path, ctx, from_env=True) if kcfg.enable_amf else None
@@ -145,7 +147,13 @@ def create_app(cfg: AxropusConfig, engine=None):
         ids = body.get("prompt_token_ids")
         if ids is None:
             p = body.get("prompt", "")
-            ids = p if isinstance(p, list) else byte_tokens(str(p))
+            if isinstance(p, list):
+                ids = p
+            else:  # canonical text, and the AMF prefix it keys on (KORITH_AMF_* prompt policy)
+                prep = prepare_prompt(str(p), byte_tokens)
+                ids = prep["tokens"]
+                if body.get("amf_prefix_len") is None and prep["amf_prefix_len"] is not None:
+                    body["amf_prefix_len"] = prep["amf_prefix_len"]
         out = await run(body, [int(x) for x in ids])
         metrics.requests.labels(endpoint="completions").inc()
         out.update(object="text_completion",
@@ -156,7 +164,12 @@ def create_app(cfg: AxropusConfig, engine=None):
     async def chat(request: Request, authorization: Optional[str] = Header(default=None)):
         check(authorization)
         body = await request.json()
-        ids = body.get("prompt_token_ids") or byte_tokens(render_messages(body.get("messages") or []))
+        ids = body.get("prompt_token_ids")
+        if not ids:
+            prep = prepare_prompt(render_messages(body.get("messages") or []), byte_tokens)
+            ids = prep["tokens"]
+            if body.get("amf_prefix_len") is None and prep["amf_prefix_len"] is not None:
+                body["amf_prefix_len"] = prep["amf_prefix_len"]
         out = await run(body, [int(x) for x in ids])
         metrics.requests.labels(endpoint="chat").inc()
         out.update(object="chat.completion",
