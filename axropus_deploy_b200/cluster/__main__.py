@@ -32,6 +32,7 @@ def _build_node(a):
     from .nodes import NodeRegistry, NodeServer, SnapshotIndex
     from .observability import ArtifactStore
     from .runtime import DecodeCache
+    from ..server.service import EngineService
     from .worker import ClusterWorker
 
     ledger = SqliteLedger(a.db)
@@ -47,10 +48,11 @@ def _build_node(a):
         eng = build_engine(AxropusConfig.load(None, {"model": a.model, "device": f"cuda:{g}" if g is not None
                                                      else "cpu"}))
         wid = f"{a.node_id}-gpu{g if g is not None else 'cpu'}"
-        workers[wid] = ClusterWorker(wid, a.node_id, AdapterRegistry(eng), ledger, art, snapshot_index=index,
-                                     node_registry=nodes, coordinator=coord,
+        svc = EngineService(eng)  # jobs of this GPU share engine steps (continuous batching)
+        workers[wid] = ClusterWorker(wid, a.node_id, AdapterRegistry(eng, service=svc), ledger, art,
+                                     snapshot_index=index, node_registry=nodes, coordinator=coord,
                                      decode_cache=DecodeCache(os.path.join(a.artifacts, "decode_cache.db")),
-                                     gpu_index=g or 0)
+                                     gpu_index=g or 0, concurrency=a.jobs_per_worker)
     plane = ControlPlane(ledger, workers, node_id=a.node_id, node_registry=nodes, snapshot_index=index,
                          coordinator=coord)
     status = lambda: {"gpu_count": len(gpus), "inflight": sum(w.inflight for w in workers.values()),  # noqa: E731
@@ -74,6 +76,7 @@ def main(argv=None) -> int:
     n.add_argument("--artifacts", default=os.environ.get("KORITH_PLATFORM_ARTIFACTS", "platform_data/artifacts"))
     n.add_argument("--coordinator", default=os.environ.get("AMF_COORDINATOR_URL", ""))
     n.add_argument("--max-workers", type=int, default=8)
+    n.add_argument("--jobs-per-worker", type=int, default=8, help="jobs in flight per GPU, batched by its engine")
     c = sub.add_parser("coordinator")
     c.add_argument("--db", default="platform_data/coordinator.db")
     c.add_argument("--host", default="127.0.0.1")

@@ -115,10 +115,18 @@ class EngineAdapter(BackendAdapter):
     backend_id = "axr_engine"
     backend_version = "b200-v1"
 
-    def __init__(self, engine, model_name: str = ""):
+    def __init__(self, engine, model_name: str = "", service=None):
         self.eng = engine
         self.model_name = model_name or engine.model.cfg.name
         self.cold_ms_per_token = 0.0  # measured on cold prefills, prices restored tokens
+        # with an EngineService driving the engine from its own thread, concurrent jobs are
+        # batched by the engine; every direct use of the engine then runs on that thread
+        self.svc = service
+
+    def _on_engine(self, fn, *args):
+        if self.svc is None:
+            return fn(*args)
+        return self.svc.run_in_engine(lambda _eng: fn(*args)).result()
 
     def get_fingerprint(self) -> Dict[str, str]:
         c = self.eng.model.cfg
@@ -138,6 +146,9 @@ class EngineAdapter(BackendAdapter):
     def import_snapshot(self, path: str) -> int:
         """Load an AMFK snapshot (``path`` + ``path.tok`` token ids) into the AMF tiers;
         returns the tokens made available."""
+        return self._on_engine(self._import_snapshot, path)
+
+    def _import_snapshot(self, path: str) -> int:
         import numpy as np
         import torch
 
@@ -164,6 +175,9 @@ class EngineAdapter(BackendAdapter):
 
     def export_snapshot(self, tokens: List[int], path: str) -> int:
         """Write the cached KV of ``tokens``' longest AMF-held prefix as an AMFK file."""
+        return self._on_engine(self._export_snapshot, tokens, path)
+
+    def _export_snapshot(self, tokens: List[int], path: str) -> int:
         import numpy as np
         import torch
 
@@ -201,20 +215,24 @@ class EngineAdapter(BackendAdapter):
         toks = byte_tokens(prompt)
         sp = SamplingParams(max_tokens=max_tokens, temperature=float(det.get("temperature", 0.0)),
                             seed=det.get("seed"))
-        saved_spec = eng.spec
         before = None
-        if spec_depth <= 0:
-            eng.spec = None
-        elif eng.spec is not None:
-            eng.spec.depth = max(1, min(int(spec_depth), eng.spec.max_depth))
-            before = dict(eng.spec.stat)
         t0 = time.perf_counter()
-        try:
-            r = eng.add_request(toks, sp, amf_prefix_len=prefix_len if use_amf else 0)
-            while not r.output or r.state != "finished":
-                eng.step()
-        finally:
-            eng.spec = saved_spec
+        if self.svc is not None:
+            # shared, batching engine: the engine's own speculative setting applies
+            r = self.svc.submit(toks, sp, amf_prefix_len=prefix_len if use_amf else 0).result()
+        else:
+            saved_spec = eng.spec
+            if spec_depth <= 0:
+                eng.spec = None
+            elif eng.spec is not None:
+                eng.spec.depth = max(1, min(int(spec_depth), eng.spec.max_depth))
+                before = dict(eng.spec.stat)
+            try:
+                r = eng.add_request(toks, sp, amf_prefix_len=prefix_len if use_amf else 0)
+                while not r.output or r.state != "finished":
+                    eng.step()
+            finally:
+                eng.spec = saved_spec
         ttft = (r.t_first_token - t0) * 1e3 if r.t_first_token else 0.0
         computed = len(toks) - r.restored_tokens - r.local_cached_tokens
         if r.amf_tier == "cold" and computed > 0:
@@ -270,6 +288,9 @@ class EngineAdapter(BackendAdapter):
     def verify_tokens(self, prompt, draft_tokens, deterministic_cfg, spec_cfg=None):
         """Greedy verification: the longest prefix of ``draft_tokens`` the model itself
         would produce after ``prompt`` (one forward over prompt + draft)."""
+        return self._on_engine(self._verify_tokens, prompt, draft_tokens)
+
+    def _verify_tokens(self, prompt, draft_tokens):
         import torch
 
         from .. import ops
@@ -560,8 +581,9 @@ class TransformersAdapter(BackendAdapter):
 class AdapterRegistry:
     """Adapters by jobspec ``backend_id`` + ``model``; one instance per (backend, model)."""
 
-    def __init__(self, engine=None):
+    def __init__(self, engine=None, service=None):
         self.engine = engine  # the worker's in-process engine, for axr_engine jobs
+        self.service = service  # optional EngineService driving that engine (batched jobs)
         self._cache: Dict[tuple, BackendAdapter] = {}
 
     def get_adapter(self, jobspec: Dict[str, Any]) -> BackendAdapter:
@@ -574,7 +596,7 @@ class AdapterRegistry:
         if bid == "axr_engine":
             if self.engine is None:
                 raise ValueError("axr_engine jobs need a worker with an engine")
-            a = EngineAdapter(self.engine, str(model.get("model_id", "")))
+            a = EngineAdapter(self.engine, str(model.get("model_id", "")), self.service)
         elif bid == "korith_capi":
             a = CAbiAdapter(str(model["model_path"]), int(model.get("n_ctx", 4096)))
         elif bid == "openai_compatible":

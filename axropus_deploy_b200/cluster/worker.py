@@ -26,6 +26,8 @@ A job (``_process``):
    coordinator; updates the replay / speculation governance and the metrics registry.
 
 Failures mark the job ``failed`` with the error in the run log; the worker keeps going.
+With ``concurrency`` > 1 several threads take jobs at once; over an adapter whose engine is
+driven by an ``EngineService`` their requests share engine steps (continuous batching).
 
 Reference: platform/runtime/cluster_worker.py:455-621 (lane budgets), :924-1114 and
 :2170-2410 (snapshot transfer into the tiered cache), :1413-1475 (run selection),
@@ -69,8 +71,9 @@ class ClusterWorker:
                  snapshot_index=None, node_registry=None, coordinator=None, decode_cache: Optional[DecodeCache] = None,
                  metrics=GLOBAL_METRICS, snapshot_dir: Optional[str] = None, link_gbps: Optional[float] = None,
                  rtt_ms: Optional[float] = None, transfer_threshold: Optional[float] = None, gpu_index: int = 0,
-                 queue_factory=None):
+                 queue_factory=None, concurrency: int = 1):
         self.worker_id, self.node_id, self.gpu_index = worker_id, node_id, gpu_index
+        self.concurrency = max(1, int(concurrency))  # jobs in flight (batched by an EngineService)
         self.adapters = adapters
         self.ledger = ledger
         self.artifacts = artifacts
@@ -180,16 +183,19 @@ class ClusterWorker:
             while not self._stop.is_set():
                 self.run_once(block=True)
 
-        self._thread = threading.Thread(target=loop, name=f"worker-{self.worker_id}", daemon=True)
-        self._thread.start()
+        self._threads = [threading.Thread(target=loop, name=f"worker-{self.worker_id}-{i}", daemon=True)
+                         for i in range(self.concurrency)]
+        for t in self._threads:
+            t.start()
+        self._thread = self._threads[0]
         return self
 
     def stop(self) -> None:
         self._stop.set()
         with self._cv:
             self._cv.notify_all()
-        if self._thread is not None:
-            self._thread.join(timeout=10)
+        for t in getattr(self, "_threads", []):
+            t.join(timeout=10)
 
     def health(self) -> Dict[str, Any]:
         return {"worker_id": self.worker_id, "node_id": self.node_id, "gpu_index": self.gpu_index,
@@ -345,8 +351,9 @@ class ClusterWorker:
         self.ledger.insert_run(uuid.uuid4().hex, job_id, started, finished, exit_code, str(paths["metrics"]),
                                str(paths["events"]), str(paths["output"]), str(paths["log"]), org_id=org)
         self.ledger.update_status(job_id, "succeeded" if exit_code == 0 else "failed")
-        self.done += exit_code == 0
-        self.failed += exit_code != 0
+        with self._mu:
+            self.done += exit_code == 0
+            self.failed += exit_code != 0
         self.metrics.inc("korith_jobs_total", 1, {"lane": lane, "status": "ok" if exit_code == 0 else "failed",
                                                   "org_id": org})
         self.metrics.inc("korith_amf_saved_ms_total", float((result.get("amf") or {}).get("saved_ms", 0.0)))

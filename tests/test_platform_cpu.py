@@ -425,3 +425,38 @@ def test_snapshot_sidecar_validation(tmp_path):
     snap.write_bytes(bytes(raw))
     assert validate_snapshot_metadata(snap, **ctx)[1] == "snapshot_checksum_mismatch"
     assert validate_snapshot_metadata(tmp_path / "missing.amfk", **ctx)[1] == "snapshot_missing"
+
+
+def test_concurrent_worker_batches_jobs(tmp_path):
+    """A worker with several jobs in flight over one EngineService: the engine runs them in
+    the same steps (continuous batching) and every job succeeds."""
+    from axropus_deploy_b200.cluster.adapters import AdapterRegistry
+    from axropus_deploy_b200.cluster.control import ControlPlane
+    from axropus_deploy_b200.cluster.worker import ClusterWorker
+    from axropus_deploy_b200.server.service import EngineService
+
+    eng = _engine()
+    peak = {"running": 0}
+    step = eng.step
+
+    def counting_step():
+        peak["running"] = max(peak["running"], len(eng.running) + len(eng.waiting))
+        return step()
+
+    eng.step = counting_step
+    svc = EngineService(eng)
+    ledger = SqliteLedger(str(tmp_path / "l.db"))
+    w = ClusterWorker("w0", "n0", AdapterRegistry(eng, service=svc), ledger, ArtifactStore(tmp_path / "art"),
+                      metrics=MetricsRegistry(), concurrency=4)
+    plane = ControlPlane(ledger, {"w0": w}, metrics=w.metrics)
+    ids = [plane.submit({"prompt": f"request {i} " * 6, "max_tokens": 8}, org_id="o") for i in range(6)]
+    w.start()
+    try:
+        deadline = time.time() + 120
+        while time.time() < deadline and any(ledger.get_job(j)["status"] != "succeeded" for j in ids):
+            time.sleep(0.05)
+    finally:
+        w.stop()
+        svc._stop.set()
+    assert [ledger.get_job(j)["status"] for j in ids] == ["succeeded"] * 6
+    assert peak["running"] >= 2  # jobs shared engine steps
