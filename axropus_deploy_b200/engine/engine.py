@@ -141,6 +141,8 @@ class LLMEngine:
         self.finished: List[Request] = []
         self._ids = itertools.count()
         self._graphs = None
+        self._pin: Optional[torch.Tensor] = None  # pinned staging buffer of step inputs
+        self._pin_ev = None                        # recorded after the last copy out of it
         if cfg.cuda_graphs and self.device.type == "cuda" and not model.cfg.is_moe:
             from .cuda_graph import DecodeGraphRunner
 
@@ -462,6 +464,33 @@ class LLMEngine:
             row = torch.tensor(r.blocks, dtype=torch.int32)
             self.block_table[r.row, : len(r.blocks)] = row.to(self.device, non_blocking=True)
 
+    def _stage_int32(self, *parts) -> List[torch.Tensor]:
+        """Host int32 arrays -> device tensors with one copy from a reused pinned buffer.
+        The buffer is rewritten only after the previous copy out of it has completed (its
+        event; normally long done, since the sampling of every step synchronises)."""
+        arrs = [np.asarray(p, dtype=np.int32).reshape(-1) for p in parts]
+        if self.device.type != "cuda":
+            return [torch.from_numpy(a.copy()) for a in arrs]
+        total = sum(a.size for a in arrs)
+        if self._pin_ev is not None:
+            self._pin_ev.synchronize()
+        if self._pin is None or self._pin.numel() < total:
+            self._pin = torch.empty(max(total, 1 << 16), dtype=torch.int32, pin_memory=True)
+        view = self._pin.numpy()
+        off = 0
+        for a in arrs:
+            view[off:off + a.size] = a
+            off += a.size
+        dev_all = self._pin[:total].to(self.device, non_blocking=True)
+        if self._pin_ev is None:
+            self._pin_ev = torch.cuda.Event()
+        self._pin_ev.record()
+        out, off = [], 0
+        for a in arrs:
+            out.append(dev_all[off:off + a.size])
+            off += a.size
+        return out
+
     def _prefill(self, reqs: List[Request]) -> List[Request]:
         toks, pos, slots, cu, lens = [], [], [], [0], []
         prefilled_from = {}
@@ -480,26 +509,19 @@ class LLMEngine:
             if r.amf_tier == "cold":
                 self.stat["cold_prefill_tokens"] += n
         self._set_rows(reqs)
-        dev = self.device
-        rows = torch.tensor([r.row for r in reqs], dtype=torch.long, device=dev)
-        meta = AttnMeta(
-            mode="prefill",
-            positions=torch.tensor(pos, dtype=torch.int32).to(dev, non_blocking=True),
-            slots=torch.tensor(slots, dtype=torch.int32).to(dev, non_blocking=True),
-            block_table=self.block_table.index_select(0, rows),
-            seq_lens=torch.tensor(lens, dtype=torch.int32).to(dev, non_blocking=True),
-            cu_q=torch.tensor(cu, dtype=torch.int32).to(dev, non_blocking=True),
-            max_q=max(cu[i + 1] - cu[i] for i in range(len(reqs))),
-            max_seq_len=max(lens),
-            logits_idx=torch.tensor([c - 1 for c in cu[1:]], dtype=torch.int32).to(dev, non_blocking=True),
-        )
         t_pf = time.perf_counter()
         try:
             if self._prefill_graphs is not None and self._prefill_graphs.supports(reqs, len(toks), lens[0]):
                 logits = self._prefill_graphs.run(reqs[0], toks, pos, slots, lens[0])
             else:
-                logits = self.model.forward(torch.tensor(toks, dtype=torch.int32).to(dev, non_blocking=True), meta,
-                                            self.cache)
+                # every input of the step in one copy from pinned host memory
+                d_toks, d_pos, d_slots, d_lens, d_cu, d_idx, d_rows = self._stage_int32(
+                    toks, pos, slots, lens, cu, [c - 1 for c in cu[1:]], [r.row for r in reqs])
+                meta = AttnMeta(mode="prefill", positions=d_pos, slots=d_slots,
+                                block_table=self.block_table.index_select(0, d_rows.long()), seq_lens=d_lens, cu_q=d_cu,
+                                max_q=max(cu[i + 1] - cu[i] for i in range(len(reqs))), max_seq_len=max(lens),
+                                logits_idx=d_idx)
+                logits = self.model.forward(d_toks, meta, self.cache)
             new = self._sample(logits, reqs)  # synchronises with the forward (and the restores)
         except BaseException:
             self._settle_restores(reqs, ok=False)
@@ -548,13 +570,11 @@ class LLMEngine:
         if self._graphs is not None:
             logits = self._graphs.run(reqs, toks, pos, slots, lens)
         else:
-            dev = self.device
-            rows = torch.tensor([r.row for r in reqs], dtype=torch.long, device=dev)
-            host = torch.tensor([toks, pos, slots, lens], dtype=torch.int32)
-            d = host.to(dev, non_blocking=True)
-            meta = AttnMeta(mode="decode", positions=d[1], slots=d[2], block_table=self.block_table.index_select(0, rows),
-                            seq_lens=d[3], max_seq_len=max(lens))
-            logits = self.model.forward(d[0], meta, self.cache)
+            d_toks, d_pos, d_slots, d_lens, d_rows = self._stage_int32(toks, pos, slots, lens, [r.row for r in reqs])
+            meta = AttnMeta(mode="decode", positions=d_pos, slots=d_slots,
+                            block_table=self.block_table.index_select(0, d_rows.long()), seq_lens=d_lens,
+                            max_seq_len=max(lens))
+            logits = self.model.forward(d_toks, meta, self.cache)
         new = self._sample(logits, reqs)
         done: List[Request] = []
         for r, t in zip(reqs, new):
