@@ -33,6 +33,7 @@ def _build_node(a):
     from .observability import ArtifactStore
     from .runtime import DecodeCache
     from ..server.service import EngineService
+    from .netqueues import build_queue
     from .worker import ClusterWorker
 
     ledger = SqliteLedger(a.db)
@@ -49,10 +50,14 @@ def _build_node(a):
                                                      else "cpu"}))
         wid = f"{a.node_id}-gpu{g if g is not None else 'cpu'}"
         svc = EngineService(eng)  # jobs of this GPU share engine steps (continuous batching)
+        # KORITH_QUEUE_BACKEND (sqlite / redis / redis_streams / nats / sqs / inproc) picks the lane queues;
+        # unset keeps them in this process
+        qf = ((lambda lane, wid=wid: build_queue(f"{wid}:{lane}")) if os.environ.get("KORITH_QUEUE_BACKEND")
+              else None)
         workers[wid] = ClusterWorker(wid, a.node_id, AdapterRegistry(eng, service=svc), ledger, art,
                                      snapshot_index=index, node_registry=nodes, coordinator=coord,
                                      decode_cache=DecodeCache(os.path.join(a.artifacts, "decode_cache.db")),
-                                     gpu_index=g or 0, concurrency=a.jobs_per_worker)
+                                     gpu_index=g or 0, concurrency=a.jobs_per_worker, queue_factory=qf)
     plane = ControlPlane(ledger, workers, node_id=a.node_id, node_registry=nodes, snapshot_index=index,
                          coordinator=coord)
     status = lambda: {"gpu_count": len(gpus), "inflight": sum(w.inflight for w in workers.values()),  # noqa: E731
