@@ -28,7 +28,7 @@ def _build_node(a):
     from .adapters import AdapterRegistry
     from .control import ControlPlane
     from .coordinator import CoordinatorClient
-    from .ledger import SqliteLedger
+    from .pgledger import build_ledger
     from .nodes import NodeRegistry, NodeServer, SnapshotIndex
     from .observability import ArtifactStore
     from .runtime import DecodeCache
@@ -36,7 +36,7 @@ def _build_node(a):
     from .netqueues import build_queue
     from .worker import ClusterWorker
 
-    ledger = SqliteLedger(a.db)
+    ledger = build_ledger(a.db)
     index = SnapshotIndex(ledger)
     nodes = NodeRegistry(a.node_db)
     coord = CoordinatorClient(a.coordinator) if a.coordinator else None
@@ -112,15 +112,15 @@ def main(argv=None) -> int:
             os.makedirs(os.path.dirname(path), exist_ok=True)
     if a.cmd == "create-key":
         from .gateway import issue_api_key
-        from .ledger import SqliteLedger
+        from .pgledger import build_ledger
 
-        print(issue_api_key(SqliteLedger(a.db), a.key_id, a.org_id, a.rpm, a.tpm))
+        print(issue_api_key(build_ledger(a.db), a.key_id, a.org_id, a.rpm, a.tpm))
         return 0
     if a.cmd == "report":
         from .economics import write_report
-        from .ledger import SqliteLedger
+        from .pgledger import build_ledger
 
-        rep = write_report(SqliteLedger(a.db), a.out, a.gpu_hourly_cost, a.org_id)
+        rep = write_report(build_ledger(a.db), a.out, a.gpu_hourly_cost, a.org_id)
         print(json.dumps(rep["targets"], indent=2))
         return 0
     if a.cmd == "coordinator":
