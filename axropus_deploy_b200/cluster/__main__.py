@@ -37,8 +37,9 @@ def _build_node(a):
     from .worker import ClusterWorker
 
     ledger = build_ledger(a.db)
-    index = SnapshotIndex(ledger)
-    nodes = NodeRegistry(a.node_db)
+    redis_url = os.environ.get("KORITH_REDIS_URL", "")
+    index = SnapshotIndex(ledger, redis_url=os.environ.get("KORITH_SNAPSHOT_INDEX_REDIS_URL", redis_url))
+    nodes = NodeRegistry(a.node_db, redis_url=os.environ.get("KORITH_NODE_REGISTRY_REDIS_URL", redis_url))
     coord = CoordinatorClient(a.coordinator) if a.coordinator else None
     art = ArtifactStore(a.artifacts)
     gpus = list(range(torch.cuda.device_count())) if torch.cuda.is_available() else [None]

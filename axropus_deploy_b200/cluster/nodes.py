@@ -24,6 +24,7 @@ platform/runtime/node_router.py:20-174.
 from __future__ import annotations
 
 import json
+import logging
 import os
 import sqlite3
 import threading
@@ -34,6 +35,8 @@ from datetime import datetime
 from http.server import BaseHTTPRequestHandler, ThreadingHTTPServer
 from pathlib import Path
 from typing import Any, Callable, Dict, List, Optional, Tuple
+
+log = logging.getLogger(__name__)
 
 NODE_TTL_S = 30.0
 TIERS = ("vram", "ram", "nvme")
@@ -61,9 +64,30 @@ class _Db:
             return [dict(zip(cols, r)) for r in cur.fetchall()]
 
 
+def _redis(url: str):
+    """A Redis client for the optional shared mirror, or None (no URL, or the server does not answer)."""
+    if not url:
+        return None
+    from .netqueues import RespClient
+
+    try:
+        c = RespClient(url, timeout_s=2.0)
+        c.call("PING")
+        return c
+    except Exception as e:  # the SQLite copy still serves this node
+        log.warning("redis mirror %s unavailable: %s", url, e)
+        return None
+
+
 class NodeRegistry:
-    def __init__(self, path: str = ":memory:", ttl_s: float = NODE_TTL_S):
+    """Nodes and their last heartbeat. With ``redis_url`` every heartbeat is also written to
+    Redis (``<prefix>:<node>`` with a TTL of ``ttl_s``, ids in ``<prefix>:ids``), so nodes that
+    share no SQLite file see each other; reads prefer Redis and fall back to SQLite."""
+
+    def __init__(self, path: str = ":memory:", ttl_s: float = NODE_TTL_S, redis_url: str = "",
+                 key_prefix: str = "korith:nodes"):
         self.ttl_s = ttl_s
+        self.redis, self.prefix = _redis(redis_url), key_prefix
         self.db = _Db(path, "CREATE TABLE IF NOT EXISTS nodes (node_id TEXT PRIMARY KEY, host TEXT NOT NULL, "
                             "router_port INTEGER NOT NULL, gpu_count INTEGER NOT NULL, inflight INTEGER NOT NULL, "
                             "queue_depth_hit INTEGER NOT NULL, queue_depth_miss INTEGER NOT NULL, "
@@ -72,9 +96,33 @@ class NodeRegistry:
     def register_or_heartbeat(self, node_id: str, host: str, router_port: int, gpu_count: int, inflight: int = 0,
                               queue_depth_hit: int = 0, queue_depth_miss: int = 0,
                               capabilities: Optional[Dict[str, Any]] = None, now: Optional[float] = None) -> None:
+        t = time.time() if now is None else now
         self.db.exec("INSERT OR REPLACE INTO nodes VALUES (?,?,?,?,?,?,?,?,?)",
                      (node_id, host, int(router_port), int(gpu_count), int(inflight), int(queue_depth_hit),
-                      int(queue_depth_miss), json.dumps(capabilities or {}), time.time() if now is None else now))
+                      int(queue_depth_miss), json.dumps(capabilities or {}), t))
+        if self.redis is not None:
+            row = {"node_id": node_id, "host": host, "router_port": int(router_port), "gpu_count": int(gpu_count),
+                   "inflight": int(inflight), "queue_depth_hit": int(queue_depth_hit),
+                   "queue_depth_miss": int(queue_depth_miss), "capabilities": capabilities or {}, "last_heartbeat": t}
+            try:
+                self.redis.call("SET", f"{self.prefix}:{node_id}", json.dumps(row), "EX", max(1, int(self.ttl_s)))
+                self.redis.call("SADD", f"{self.prefix}:ids", node_id)
+            except Exception as e:
+                log.warning("redis heartbeat of %s failed: %s", node_id, e)
+
+    def _redis_nodes(self) -> Optional[List[Dict[str, Any]]]:
+        if self.redis is None:
+            return None
+        try:
+            out = []
+            for nid in self.redis.call("SMEMBERS", f"{self.prefix}:ids") or []:
+                v = self.redis.call("GET", f"{self.prefix}:{nid.decode()}")
+                if v is not None:
+                    out.append(json.loads(v))
+            return sorted(out, key=lambda r: r["node_id"])
+        except Exception as e:
+            log.warning("redis node list failed, using SQLite: %s", e)
+            return None
 
     def _decode(self, r: Dict[str, Any]) -> Dict[str, Any]:
         r = dict(r)
@@ -83,10 +131,14 @@ class NodeRegistry:
 
     def list_nodes(self, healthy_only: bool = True, now: Optional[float] = None) -> List[Dict[str, Any]]:
         t = time.time() if now is None else now
-        rows = self.db.rows("SELECT * FROM nodes ORDER BY node_id")
-        return [self._decode(r) for r in rows if not healthy_only or t - r["last_heartbeat"] <= self.ttl_s]
+        shared = self._redis_nodes()
+        rows = shared if shared is not None else [self._decode(r) for r in self.db.rows("SELECT * FROM nodes ORDER BY node_id")]
+        return [r for r in rows if not healthy_only or t - r["last_heartbeat"] <= self.ttl_s]
 
     def get_node(self, node_id: str) -> Optional[Dict[str, Any]]:
+        for r in self._redis_nodes() or []:
+            if r["node_id"] == node_id:
+                return r
         rows = self.db.rows("SELECT * FROM nodes WHERE node_id=?", (node_id,))
         return self._decode(rows[0]) if rows else None
 
@@ -128,11 +180,33 @@ def _iso_ts(s: str) -> float:
 
 
 class SnapshotIndex:
-    """Snapshot locations over a ledger's ``snapshot_locations`` table."""
+    """Snapshot locations over a ledger's ``snapshot_locations`` table. With ``redis_url``
+    each (org, fingerprint) also has a Redis hash ``<prefix>:<org>:<fingerprint>`` of its
+    locations (field ``<node>:<snapshot>``), read first so that nodes with separate ledgers
+    find each other's snapshots; the ledger stays the durable copy."""
 
-    def __init__(self, ledger, tier_roots: Optional[Dict[str, str]] = None):
+    def __init__(self, ledger, tier_roots: Optional[Dict[str, str]] = None, redis_url: str = "",
+                 key_prefix: str = "korith:snapshots"):
         self.ledger = ledger
         self._roots = tier_roots
+        self.redis, self.prefix = _redis(redis_url), key_prefix
+
+    def _rkey(self, org_id: str, fingerprint_hash: str) -> str:
+        return f"{self.prefix}:{org_id}:{fingerprint_hash}"
+
+    def _mirror(self, fingerprint_hash: str, org_id: str) -> None:
+        if self.redis is None:
+            return
+        try:
+            args = []
+            for r in self.ledger.list_snapshot_locations(fingerprint_hash, org_id):
+                args += [f"{r['node_id']}:{r['snapshot_id']}", json.dumps(r, default=str)]
+            key = self._rkey(org_id, fingerprint_hash)
+            self.redis.call("DEL", key)  # rebuilt whole: locations the ledger pruned disappear too
+            if args:
+                self.redis.call("HSET", key, *args)
+        except Exception as e:
+            log.warning("redis snapshot mirror failed: %s", e)
 
     def tier_roots(self) -> Dict[str, Path]:
         if self._roots is not None:
@@ -164,10 +238,22 @@ class SnapshotIndex:
         now = utc_now()
         self.ledger.upsert_snapshot_location(fingerprint_hash, snapshot_id, org_id, node_id, worker_id,
                                              snapshot_path, size_bytes, now, now)
+        self._mirror(fingerprint_hash, org_id)
+
+    def _shared_rows(self, fingerprint_hash: str, org_id: str) -> Optional[List[Dict[str, Any]]]:
+        if self.redis is None:
+            return None
+        try:
+            flat = self.redis.call("HGETALL", self._rkey(org_id, fingerprint_hash)) or []
+            return [json.loads(flat[i + 1]) for i in range(0, len(flat), 2)] or None
+        except Exception as e:
+            log.warning("redis snapshot lookup failed, using the ledger: %s", e)
+            return None
 
     def get_locations(self, fingerprint_hash: str, org_id: str) -> List[Dict[str, Any]]:
         rows = []
-        for r in self.ledger.list_snapshot_locations(fingerprint_hash, org_id):
+        shared = self._shared_rows(fingerprint_hash, org_id)
+        for r in shared if shared is not None else self.ledger.list_snapshot_locations(fingerprint_hash, org_id):
             r = dict(r, storage_tier=self.detect_tier(r["snapshot_path"]))
             rows.append(r)
         rank = {t: i for i, t in enumerate(TIERS)}
@@ -177,6 +263,7 @@ class SnapshotIndex:
         from .observability import utc_now
 
         self.ledger.mark_snapshot_location_used(fingerprint_hash, org_id, node_id, snapshot_id, utc_now())
+        self._mirror(fingerprint_hash, org_id)
 
     def prune_old(self, max_entries_per_fingerprint: int = 8) -> int:
         return self.ledger.prune_snapshot_locations(max_entries_per_fingerprint)

@@ -124,6 +124,29 @@ class _FakeRedis:
             return 1 if self.zsets.get(a[0], {}).pop(a[1], None) is not None else 0
         if cmd == "ZCARD":
             return len(self.zsets.get(a[0], {}))
+        kv = self.__dict__.setdefault("kv", {})
+        if cmd == "SET":
+            kv[a[0]] = a[1]
+            return "+OK"
+        if cmd == "GET":
+            v = kv.get(a[0])
+            return v if isinstance(v, str) else None
+        if cmd == "DEL":
+            return 1 if kv.pop(a[0], None) is not None else 0
+        if cmd == "SADD":
+            st = kv.setdefault(a[0], set())
+            n = sum(1 for m in a[1:] if m not in st)
+            st.update(a[1:])
+            return n
+        if cmd == "SMEMBERS":
+            return sorted(kv.get(a[0], set()))
+        if cmd == "HSET":
+            h = kv.setdefault(a[0], {})
+            for i in range(1, len(a) - 1, 2):
+                h[a[i]] = a[i + 1]
+            return len(a) // 2
+        if cmd == "HGETALL":
+            return [x for k, v in kv.get(a[0], {}).items() for x in (k, v)]
         return Exception(f"ERR unknown command {cmd}")
 
     @staticmethod
@@ -471,3 +494,27 @@ def test_sqs_queue_over_signed_json_api(http_fake):
     assert q.retry(b, delay_s=0)                 # visible again at once
     assert q.dequeue() == (b, {"job": "b"}) and q.ack(b)
     assert q.stats()["ready"] == 0 and state["sqs"] == [] and state["rejected"] == 0
+
+
+def test_node_registry_and_snapshot_index_share_redis(redis_url, tmp_path):
+    from axropus_deploy_b200.cluster.ledger import SqliteLedger
+    from axropus_deploy_b200.cluster.nodes import NodeRegistry, SnapshotIndex
+
+    # two nodes with separate SQLite files see each other through the Redis mirror
+    a = NodeRegistry(str(tmp_path / "a.db"), redis_url=redis_url)
+    b = NodeRegistry(str(tmp_path / "b.db"), redis_url=redis_url)
+    a.register_or_heartbeat("node-a", "10.0.0.1", 9000, 8, inflight=2, capabilities={"gpu": "B200"})
+    b.register_or_heartbeat("node-b", "10.0.0.2", 9000, 8)
+    seen = a.list_nodes()
+    assert [n["node_id"] for n in seen] == ["node-a", "node-b"] and seen[0]["capabilities"] == {"gpu": "B200"}
+    assert b.get_node("node-a")["inflight"] == 2
+    ia = SnapshotIndex(SqliteLedger(str(tmp_path / "la.db")), tier_roots={}, redis_url=redis_url)
+    ib = SnapshotIndex(SqliteLedger(str(tmp_path / "lb.db")), tier_roots={}, redis_url=redis_url)
+    ia.upsert_location("fp", "s1", "default", "node-a", "w0", "/x/vram/s1.amfk", 1234)
+    locs = ib.get_locations("fp", "default")
+    assert [(r["node_id"], r["snapshot_id"], r["storage_tier"]) for r in locs] == [("node-a", "s1", "vram")]
+    # no Redis: the local copies still answer
+    lone = NodeRegistry(str(tmp_path / "c.db"), redis_url="redis://127.0.0.1:1/0")
+    assert lone.redis is None
+    lone.register_or_heartbeat("node-c", "h", 1, 1)
+    assert [n["node_id"] for n in lone.list_nodes()] == ["node-c"]
