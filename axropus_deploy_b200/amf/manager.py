@@ -89,6 +89,7 @@ class AmfManager:
         self.promote_lmcache_hits = promote_lmcache_hits
         self.lmcache_write_through = lmcache_write_through
         self.disable_restore = disable_restore
+        self.capture_enabled = True  # cache admission switch (the policy layer turns it off under negative ROI)
         g1 = raw_pool or comp_pool
         if g1 is not None and self.lmcache.enabled and torch.cuda.is_available() and \
                 str(getattr(g1, "device", "cpu")).startswith("cuda"):
@@ -170,7 +171,7 @@ class AmfManager:
         """Save the pages of ``tokens`` (a page-aligned prefix held in ``blocks``) into the
         hot tier, and mirror to LMCache / the disk store according to policy."""
         n = len(tokens) // PAGE
-        if n * PAGE < self.min_tokens or n == 0:
+        if n * PAGE < self.min_tokens or n == 0 or not self.capture_enabled:
             return False
         t = tokens[:n * PAGE]
         key = pool_key(t)

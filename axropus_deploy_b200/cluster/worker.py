@@ -71,9 +71,10 @@ class ClusterWorker:
                  snapshot_index=None, node_registry=None, coordinator=None, decode_cache: Optional[DecodeCache] = None,
                  metrics=GLOBAL_METRICS, snapshot_dir: Optional[str] = None, link_gbps: Optional[float] = None,
                  rtt_ms: Optional[float] = None, transfer_threshold: Optional[float] = None, gpu_index: int = 0,
-                 queue_factory=None, concurrency: int = 1):
+                 queue_factory=None, concurrency: int = 1, policy=None):
         self.worker_id, self.node_id, self.gpu_index = worker_id, node_id, gpu_index
         self.concurrency = max(1, int(concurrency))  # jobs in flight (batched by an EngineService)
+        self.policy = policy  # optional decision layer (PolicyOrchestrator): fail-closed hooks around each run
         self.adapters = adapters
         self.ledger = ledger
         self.artifacts = artifacts
@@ -298,6 +299,7 @@ class ClusterWorker:
                     snap_in = self._local_snapshot(fp, org, fingerprint, n_ctx) or \
                         self._remote_snapshot(job, fp, org, fingerprint, n_ctx, events)
                 events.append({"event": "snapshot", "path": snap_in, "replay_allowed": replay["replay_allowed"]})
+                ptok = self.policy.before_job(job) if self.policy is not None else None
                 spec_gate = self.spec_k.gate(caps, policy) if lane.startswith("SPEC") else {"enabled": False}
                 if spec_gate["enabled"] and not self.spec_gov.allowed(fp):
                     spec_gate = {"enabled": False, "reason": "governance"}
@@ -324,6 +326,8 @@ class ClusterWorker:
                     drafted, accepted = int(sp.get("drafted", 0)), int(sp.get("accepted", 0))
                     self.spec_k.update(drafted, accepted, 0.0, float(result["perf"].get("tok_s", 0.0)))
                     self.spec_gov.record(fp, org, accepted / max(1, drafted))
+                if self.policy is not None:
+                    self.policy.after_job(ptok, result, mode)
                 if self.dcache is not None and float(det.get("temperature", 0.0)) == 0.0:
                     self.dcache.put(**cache_key, output_text=result.get("output_text", ""),
                                     tokens_out=int(result.get("tokens_out", 0)),
