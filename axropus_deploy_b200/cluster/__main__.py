@@ -69,6 +69,12 @@ def _build_node(a):
 
 
 def main(argv=None) -> int:
+    if os.environ.get("KORITH_CONFIG"):
+        from .runtime import apply_config_to_env, load_platform_config
+
+        # the file fills KORITH_* variables that are not set yet; it is applied before the
+        # argument defaults below read them
+        apply_config_to_env(load_platform_config(os.environ["KORITH_CONFIG"]))
     p = argparse.ArgumentParser(prog="axropus-platform")
     sub = p.add_subparsers(dest="cmd", required=True)
     n = sub.add_parser("node")

@@ -172,14 +172,34 @@ class SpecGovernor:
 
 # ---------------------------------------------------------------------- config file -> environment
 CONFIG_ENV = {
+    "ledger.backend": "KORITH_LEDGER_BACKEND",
     "ledger.sqlite_path": "KORITH_PLATFORM_DB",
+    "ledger.postgres_dsn": "KORITH_LEDGER_DSN",
+    "artifacts.backend": "KORITH_ARTIFACT_BACKEND",
     "artifacts.local_path": "KORITH_PLATFORM_ARTIFACTS",
+    "artifacts.s3_bucket": "KORITH_S3_BUCKET",
+    "artifacts.s3_prefix": "KORITH_S3_PREFIX",
+    "artifacts.s3_endpoint": "KORITH_S3_ENDPOINT",
+    "artifacts.minio_endpoint": "KORITH_MINIO_ENDPOINT",
+    "artifacts.minio_access_key": "KORITH_MINIO_ACCESS_KEY",
+    "artifacts.minio_secret_key": "KORITH_MINIO_SECRET_KEY",
+    "artifacts.minio_bucket": "KORITH_MINIO_BUCKET",
+    "artifacts.minio_prefix": "KORITH_MINIO_PREFIX",
+    "artifacts.minio_secure": "KORITH_MINIO_SECURE",
     "queue.backend": "KORITH_QUEUE_BACKEND",
     "queue.sqlite_path": "KORITH_QUEUE_DB",
+    "queue.redis_url": "KORITH_REDIS_URL",
+    "queue.stream_prefix": "KORITH_STREAM_PREFIX",
+    "queue.consumer_group": "KORITH_STREAM_CONSUMER_GROUP",
+    "queue.nats_url": "KORITH_NATS_URL",
+    "queue.sqs_url": "KORITH_SQS_URL",
+    "queue.inflight_stale_s": "KORITH_QUEUE_INFLIGHT_STALE_S",
     "cluster.node_id": "KORITH_NODE_ID",
     "cluster.node_host": "KORITH_NODE_HOST",
     "cluster.node_router_port": "KORITH_NODE_ROUTER_PORT",
     "cluster.registry.sqlite_path": "KORITH_NODE_REGISTRY_DB",
+    "cluster.registry.redis_url": "KORITH_NODE_REGISTRY_REDIS_URL",
+    "cluster.snapshot_index.redis_url": "KORITH_SNAPSHOT_INDEX_REDIS_URL",
     "cluster.snapshot_bw_mbps": "KORITH_SNAPSHOT_BW_MBPS",
     "cluster.snapshot_rtt_ms": "KORITH_SNAPSHOT_RTT_MS",
     "cluster.transfer_vs_recompute_threshold": "KORITH_TRANSFER_VS_RECOMPUTE_THRESHOLD",

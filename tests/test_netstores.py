@@ -518,3 +518,24 @@ def test_node_registry_and_snapshot_index_share_redis(redis_url, tmp_path):
     assert lone.redis is None
     lone.register_or_heartbeat("node-c", "h", 1, 1)
     assert [n["node_id"] for n in lone.list_nodes()] == ["node-c"]
+
+
+def test_deploy_config_reaches_the_environment(monkeypatch, capsys):
+    import os
+
+    from axropus_deploy_b200.cluster.__main__ import main
+
+    saved = dict(os.environ)
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    try:
+        for k in [k for k in os.environ if k.startswith("KORITH_")]:
+            del os.environ[k]
+        os.environ["KORITH_CONFIG"] = os.path.join(root, "deploy", "config", "config.yaml")
+        os.environ["KORITH_QUEUE_BACKEND"] = "inproc"  # set variables win over the file
+        assert main(["apply-config", os.environ["KORITH_CONFIG"]]) == 0
+        assert os.environ["KORITH_STREAM_PREFIX"] == "korith:jobs" and os.environ["KORITH_LEDGER_BACKEND"] == "sqlite"
+        assert os.environ["KORITH_QUEUE_BACKEND"] == "inproc"
+        assert os.environ["KORITH_NODE_REGISTRY_REDIS_URL"] == "redis://redis:6379/0"
+    finally:
+        os.environ.clear()
+        os.environ.update(saved)
