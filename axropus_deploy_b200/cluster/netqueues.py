@@ -326,7 +326,7 @@ class NatsClient:
 
 class NatsQueue:
     def __init__(self, url: str = "nats://127.0.0.1:4222", name: str = "default", subject_prefix: str = "korith.queue",
-                 group: str = "korith", client: Optional[NatsClient] = None, wait_s: float = 0.05):
+                 group: str = "korith", client: Optional[NatsClient] = None, wait_s: float = 0.0):
         self.nc = client or NatsClient(url)
         self.subject = f"{subject_prefix}.{name}"
         self.sid = self.nc.subscribe(self.subject, group)

@@ -2,12 +2,12 @@
 execution, rewards, learned depth policy, federated averaging, curricula, and feedback
 controllers for batch size. Optional: a worker runs without it."""
 from .decide import AdaptivePolicy, Decision, DecisionExecutor, EndpointModel, read_decode_config
-from .learn import (REWARD_WEIGHTS, DepthPolicy, FederatedAverager, RewardLedger, RolloutBuffer, curriculum, fedavg,
-                    ppo_update, reinforce_update)
+from .learn import (REWARD_WEIGHTS, DepthPolicy, FederatedAverager, RewardLedger, RolloutBuffer, adversarial, curriculum,
+                    dpo_update, fedavg, ppo_update, reinforce_update, replay_trace)
 from .orchestrator import BatchController, Pid, PolicyOrchestrator, power_fraction
 from .state import WIDTH, PowerSampler, Slot, StateCollector
 
 __all__ = ["AdaptivePolicy", "Decision", "DecisionExecutor", "EndpointModel", "read_decode_config", "REWARD_WEIGHTS",
            "DepthPolicy", "FederatedAverager", "RewardLedger", "RolloutBuffer", "curriculum", "fedavg", "ppo_update",
-           "reinforce_update", "BatchController", "Pid", "PolicyOrchestrator", "power_fraction", "WIDTH",
+           "reinforce_update", "dpo_update", "adversarial", "replay_trace", "BatchController", "Pid", "PolicyOrchestrator", "power_fraction", "WIDTH",
            "PowerSampler", "Slot", "StateCollector"]

@@ -210,7 +210,26 @@ def reinforce_update(policy: DepthPolicy, opt: torch.optim.Optimizer, states: np
     opt.zero_grad()
     loss.backward()
     opt.step()
-    return float(loss)
+    return loss.item()
+
+
+def dpo_update(policy: DepthPolicy, ref: DepthPolicy, opt: torch.optim.Optimizer, states: np.ndarray,
+               chosen: np.ndarray, rejected: np.ndarray, beta: float = 0.1) -> float:
+    """One Direct Preference Optimization step (Rafailov et al. 2023) on (state, preferred
+    depth, rejected depth) pairs -- for example the depth of the higher-reward of two logged
+    decisions in the same state bucket: loss = -log sigmoid(beta * ((log pi(a_w) - log
+    pi_ref(a_w)) - (log pi(a_l) - log pi_ref(a_l)))), ``ref`` frozen."""
+    s = torch.as_tensor(states)
+    w, l = torch.as_tensor(chosen), torch.as_tensor(rejected)
+    dist, _ = policy(s)
+    with torch.no_grad():
+        rdist, _ = ref(s)
+    margin = (dist.log_prob(w) - rdist.log_prob(w)) - (dist.log_prob(l) - rdist.log_prob(l))
+    loss = -torch.nn.functional.logsigmoid(beta * margin).mean()
+    opt.zero_grad()
+    loss.backward()
+    opt.step()
+    return loss.item()
 
 
 # ---------------------------------------------------------------------- federation
@@ -304,3 +323,50 @@ def curriculum(level: int, n_requests: int = 256, vocab: int = 32000, seed: int 
                      "tenant": f"t{int(rng.integers(0, tenants))}", "max_tokens": 16 + 16 * (lv % 3),
                      "expect_hit": not fresh})
     return Workload(lv, reqs, n_pref, reuse, zipf)
+
+
+def adversarial(kind: str, n_requests: int = 256, vocab: int = 32000, pool_prefixes: int = 64,
+                prefix_len: int = 1024, seed: int = 0) -> List[Dict[str, Any]]:
+    """Workloads that stress the cache policy:
+
+    * ``thrash`` -- cycles through 2 x ``pool_prefixes`` prefixes in order, so an LRU pool
+      sized for ``pool_prefixes`` misses every time (admission should back off);
+    * ``near_duplicate`` -- prefixes that differ from one base in a single token near the end
+      (block hashing must not confuse them; only the shared leading blocks may hit);
+    * ``burst`` -- long runs of one prefix then a switch, to test hysteresis and pre-warming;
+    * ``one_shot`` -- every prefix seen once (admission should turn off)."""
+    rng = np.random.default_rng(seed)
+    base = rng.integers(0, vocab, prefix_len).tolist()
+    reqs: List[Dict[str, Any]] = []
+    if kind == "thrash":
+        pref = [rng.integers(0, vocab, prefix_len).tolist() for _ in range(2 * pool_prefixes)]
+        seq = [pref[i % len(pref)] for i in range(n_requests)]
+    elif kind == "near_duplicate":
+        seq = []
+        for i in range(n_requests):
+            p = list(base)
+            p[prefix_len - 1 - (i % 7)] = int((p[prefix_len - 1 - (i % 7)] + 1 + i) % vocab)
+            seq.append(p)
+    elif kind == "burst":
+        pref = [rng.integers(0, vocab, prefix_len).tolist() for _ in range(max(1, n_requests // 32))]
+        seq = [pref[(i // 32) % len(pref)] for i in range(n_requests)]
+    elif kind == "one_shot":
+        seq = [rng.integers(0, vocab, prefix_len).tolist() for _ in range(n_requests)]
+    else:
+        raise ValueError(f"unknown adversarial workload {kind!r}")
+    for p in seq:
+        reqs.append({"prompt": p + rng.integers(0, vocab, 32).tolist(), "amf_prefix_len": prefix_len,
+                     "tenant": "t0", "max_tokens": 16})
+    return reqs
+
+
+def replay_trace(ledger, limit: int = 1000, org_id: Optional[str] = None) -> List[Dict[str, Any]]:
+    """Requests of the most recent jobs in a ledger, oldest first, in the shape the
+    curricula use -- to replay production traffic against a new policy offline."""
+    out = []
+    for j in reversed(ledger.list_jobs(limit, org_id=org_id)):
+        spec = json.loads(j["jobspec_json"])
+        out.append({"prompt": spec.get("prompt"), "amf_prefix_len": spec.get("amf_prefix_len"),
+                    "tenant": j["org_id"], "max_tokens": int(spec.get("max_tokens", 16)),
+                    "fingerprint_hash": j["fingerprint_hash"]})
+    return out

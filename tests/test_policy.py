@@ -285,3 +285,46 @@ def test_orchestrator_hooks_fail_closed_and_train():
     assert bad.before_job({}) is None and bad.stat["hook_failures"] == 1
     bad.after_job(("x", None, "t", "p"), {})  # malformed token: swallowed
     assert bad.stat["hook_failures"] == 2
+
+
+def test_dpo_prefers_chosen_depth():
+    import copy
+
+    from axropus_deploy_b200.policy import dpo_update
+
+    torch.manual_seed(0)
+    pol = DepthPolicy()
+    ref = copy.deepcopy(pol)
+    opt = torch.optim.Adam(pol.parameters(), lr=1e-2)
+    rng = np.random.default_rng(0)
+    for _ in range(150):
+        s = np.zeros((32, WIDTH), np.float32)
+        s[:, Slot.ENTROPY_EMA] = rng.random(32)
+        low = s[:, Slot.ENTROPY_EMA] < 0.5
+        chosen = np.where(low, DEPTHS.index(12), DEPTHS.index(4))
+        rejected = np.where(low, DEPTHS.index(4), DEPTHS.index(12))
+        dpo_update(pol, ref, opt, s, chosen, rejected, beta=0.5)
+    assert pol.depth(_vec(ENTROPY_EMA=0.1)) == 12 and pol.depth(_vec(ENTROPY_EMA=0.9)) == 4
+
+
+def test_adversarial_workloads_and_trace_replay():
+    from axropus_deploy_b200.cluster.ledger import SqliteLedger
+    from axropus_deploy_b200.engine.block_manager import block_hashes
+    from axropus_deploy_b200.policy import adversarial, replay_trace
+
+    th = adversarial("thrash", 300, pool_prefixes=8, prefix_len=64)
+    keys = [tuple(r["prompt"][:64]) for r in th]
+    assert len(set(keys)) == 16 and keys[0] == keys[16] and keys[0] != keys[8]
+    nd = adversarial("near_duplicate", 8, prefix_len=256)
+    h0 = block_hashes(np.asarray(nd[0]["prompt"][:256]), 16)
+    h1 = block_hashes(np.asarray(nd[1]["prompt"][:256]), 16)
+    assert h0[:15] == h1[:15] and h0[15] != h1[15]  # only the last block differs
+    assert len({tuple(r["prompt"][:64]) for r in adversarial("one_shot", 20, prefix_len=64)}) == 20
+    with pytest.raises(ValueError):
+        adversarial("nope")
+    led = SqliteLedger(":memory:")
+    for i in range(3):
+        led.insert_job(f"j{i}", f"2026-01-0{i + 1}T00:00:00Z", {"prompt": [1, 2, i], "max_tokens": 8}, {}, "p", f"f{i}",
+                       None, "SUCCEEDED")
+    tr = replay_trace(led)
+    assert [r["prompt"] for r in tr] == [[1, 2, 0], [1, 2, 1], [1, 2, 2]] and tr[0]["max_tokens"] == 8
