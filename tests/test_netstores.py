@@ -539,3 +539,29 @@ def test_deploy_config_reaches_the_environment(monkeypatch, capsys):
     finally:
         os.environ.clear()
         os.environ.update(saved)
+
+
+def test_deploy_rules_and_dashboard_name_exported_metrics():
+    import os
+    import re
+
+    from axropus_deploy_b200.server.metrics import MetricRegistry as Metrics
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    obs = os.path.join(root, "deploy", "observability")
+    text = open(os.path.join(obs, "alerts.yml")).read() + open(os.path.join(obs, "grafana-axropus-b200.json")).read()
+    m = Metrics()
+    if m.registry is None:
+        pytest.skip("prometheus_client not installed")
+    m.observe_request("g1_raw", 7.0, 4096)
+    m.observe_request("cold", 120.0, 0)
+    rendered = m.render().decode()
+    src = "".join(open(os.path.join(root, "axropus_deploy_b200", "cluster", f)).read()
+                  for f in os.listdir(os.path.join(root, "axropus_deploy_b200", "cluster")) if f.endswith(".py"))
+    for name in sorted(set(re.findall(r"\b((?:axropus|korith)_[a-z_]+)", text))):
+        if name.startswith("axropus_"):
+            family = re.sub(r"_(total|sum|count)$", "", name)
+            assert (re.search(rf"^{name}[{{ ]", rendered, re.M) or f"# TYPE {name} " in rendered
+                    or f"# TYPE {family} " in rendered), name
+        else:
+            assert f'"{name}"' in src, name
