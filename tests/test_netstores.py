@@ -565,3 +565,19 @@ def test_deploy_rules_and_dashboard_name_exported_metrics():
                     or f"# TYPE {family} " in rendered), name
         else:
             assert f'"{name}"' in src, name
+
+
+def test_deploy_files_parse_and_agree():
+    import os
+
+    import yaml
+
+    root = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "deploy")
+    comp = yaml.safe_load(open(os.path.join(root, "docker-compose.yml")))
+    assert comp["services"]["node-b"]["image"] == comp["services"]["node-a"]["image"] == "axropus-b200:latest"
+    chart = os.path.join(root, "helm", "axropus-b200")
+    assert yaml.safe_load(open(os.path.join(chart, "Chart.yaml")))["name"] == "axropus-b200"
+    assert yaml.safe_load(open(os.path.join(chart, "values.yaml")))["nodes"]["gpusPerNode"] == 8
+    # the chart carries its own copy of the platform config (Helm reads files inside the chart only)
+    assert open(os.path.join(chart, "files", "config.yaml")).read() == open(os.path.join(root, "config",
+                                                                                           "config.yaml")).read()
