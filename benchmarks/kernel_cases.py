@@ -3,7 +3,8 @@
 whole run stays within a few GB of device memory.
 
     python benchmarks/kernel_cases.py decode|decode_int4|decode_fp8|restore|restore_fp8|capture_int4|
-                                      prefill|prefill_split|gemm|gemm_tp|moe|rmsnorm|rope
+                                      prefill|prefill_split|gemm|gemm_tp|moe|rmsnorm|rope|
+                                      silu_mul|argmax|spec_verify
 """
 import os
 import sys
@@ -135,11 +136,36 @@ def moe():
         m.forward(x, idx, w, w13, w2)
 
 
+def silu_mul():
+    # Llama-3-8B MLP of an 8K-token prefill: gate|up [8192, 2 x 14336] -> [8192, 14336]
+    gu = torch.randn(8192, 2 * 14336, device="cuda").to(torch.bfloat16)
+    out = torch.empty(8192, 14336, device="cuda", dtype=torch.bfloat16)
+    for _ in range(3):
+        ops.silu_mul(gu, out)
+
+
+def argmax():
+    # greedy sampling over the Llama-3 vocabulary, 1024 rows (263 MB of bf16 logits)
+    logits = torch.randn(1024, 128256, device="cuda").to(torch.bfloat16)
+    out = torch.empty(1024, dtype=torch.int32, device="cuda")
+    for _ in range(3):
+        ops.argmax(logits, out)
+
+
+def spec_verify():
+    # speculative verification: 64 sequences x (8 drafted + 1) positions over the vocabulary
+    logits = torch.randn(64, 9, 128256, device="cuda").to(torch.bfloat16)
+    draft = torch.randint(0, 128256, (64, 8), device="cuda", dtype=torch.int32)
+    for _ in range(3):
+        ops.spec_verify(logits, draft)
+
+
 CASES = {"decode": lambda: decode("bf16"), "decode_int4": lambda: decode("int4"),
          "decode_fp8": lambda: decode("fp8"), "restore": lambda: restore("raw", "bf16"),
          "restore_fp8": lambda: restore("fp8", "bf16"), "capture_int4": lambda: capture("int4"),
          "prefill": prefill, "gemm": gemm_case, "rmsnorm": rmsnorm, "rope": rope,
-         "prefill_split": prefill_split, "gemm_tp": gemm_tp_plain, "moe": moe}
+         "prefill_split": prefill_split, "gemm_tp": gemm_tp_plain, "moe": moe, "silu_mul": silu_mul,
+         "argmax": argmax, "spec_verify": spec_verify}
 
 if __name__ == "__main__":
     for name in sys.argv[1:] or ["decode"]:

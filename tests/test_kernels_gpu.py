@@ -237,3 +237,15 @@ def test_silu_mul_argmax_verify():
     got = spec_verify(lg.to(DEV), draft.to(DEV)).cpu()
     assert torch.equal(got, spec_verify(lg, draft))
     assert got[0, 0].item() == 4 and got[1, 0].item() == 2
+    # bf16 rows, ties (lowest index wins), rows not 16-byte aligned (V = 1001 bf16), tails
+    for V in (128256, 1001, 37):
+        lb = torch.randn(7, V).to(torch.bfloat16)
+        lb[3, V // 3] = 50.0
+        lb[3, V - 1] = 50.0
+        lb[5] = 1.0
+        assert torch.equal(argmax(lb.to(DEV)).cpu(), torch.argmax(lb.float(), -1).to(torch.int32)), V
+    lgb = torch.randn(3, 9, 1001).to(torch.bfloat16)
+    drb = torch.argmax(lgb[:, :8].float(), -1).to(torch.int32)
+    drb[0, 5] = (drb[0, 5] + 1) % 1001
+    gb = spec_verify(lgb.to(DEV), drb.to(DEV)).cpu()
+    assert gb[:, 0].tolist() == [5, 8, 8] and torch.equal(gb, spec_verify(lgb.float(), drb))
