@@ -4,7 +4,8 @@
   (speculative depth, draft temperature, back-pressure, pre-warm list, fleet hints), with
   the reference's field names so a model prompted with them answers in this shape.
 * :class:`AdaptivePolicy` -- the default decider, sub-millisecond and local: per-tenant
-  EMAs of hit rate and ROI; cache admission with a hysteresis band (on below
+  EMAs of hit rate and ROI (the ROI EMA seeded by the first evidence, admission kept on until
+  there is some); cache admission with a hysteresis band (on below
   ``ADMIT - BAND`` turns off, off above ``ADMIT + BAND`` turns on, so it does not flap);
   speculative depth by UCB1 over the arms ``DEPTHS`` (entropy picks the depth until every
   arm has data); rewards scaled by a streak multiplier (doubles on each correct admission,
@@ -139,6 +140,7 @@ class _Tenant:
     streak: int = 0
     mult: float = 1.0
     requests: int = 0
+    roi_seen: bool = False
 
 
 class AdaptivePolicy:
@@ -157,7 +159,11 @@ class AdaptivePolicy:
             t = self._t[tenant_id]
             t.requests += 1
             t.hit_ema = _ema(t.hit_ema, float(v[Slot.HIT_RATE]))
-            t.roi_ema = _ema(t.roi_ema, float(v[Slot.ROI_EMA_NORM]) * 10.0)
+            live_roi = float(v[Slot.ROI_EMA_NORM]) * 10.0
+            if t.roi_seen:
+                t.roi_ema = _ema(t.roi_ema, live_roi)
+            elif live_roi != 0.0:  # the first ROI evidence seeds the EMA instead of averaging with 0
+                t.roi_seen, t.roi_ema = True, live_roi
             ask = self.model is not None and (self.model_primary or self.uncertain[0] <= t.hit_ema <= self.uncertain[1])
         if ask:
             try:
@@ -172,8 +178,8 @@ class AdaptivePolicy:
                 self.stat["model_failures"] += 1
         with self._mu:
             self.stat["local"] += 1
-            # hysteresis admission on the ROI EMA; a tenant with no ROI signal yet stays admitted
-            if t.requests > 1 or t.roi_ema != 0.0:
+            # hysteresis admission on the ROI EMA; a tenant with no ROI evidence yet stays admitted
+            if t.roi_seen:
                 if t.admit and t.roi_ema < ADMIT - BAND:
                     t.admit = False
                 elif not t.admit and t.roi_ema > ADMIT + BAND:

@@ -82,6 +82,7 @@ class StateCollector:
         self._acc = {"ema": 0.0, "var": 0.0, "depth": 0.0, "entropy": 0.5, "bad": 0.0, "lat": 0.0}
         self._streak = [0, 0]  # hits, misses in a row
         self._roi = 0.0
+        self._roi_seen = False
         self._thread: Optional[threading.Thread] = None
         self._stop = threading.Event()
 
@@ -103,7 +104,9 @@ class StateCollector:
         with self._mu:
             self._streak = [self._streak[0] + 1, 0] if hit else [0, self._streak[1] + 1]
             if hit and savings_ms > 0:
-                self._roi = _ema(self._roi, (savings_ms - restore_ms) / max(savings_ms, 1e-3), 0.1)
+                x = (savings_ms - restore_ms) / max(savings_ms, 1e-3)  # net fraction of the prefill saved
+                self._roi = x if not self._roi_seen else _ema(self._roi, x, 0.1)
+                self._roi_seen = True
 
     # ------------------------------------------------------------------ sampling
     def _delta(self, key: str, now: float) -> float:

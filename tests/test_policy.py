@@ -328,3 +328,17 @@ def test_adversarial_workloads_and_trace_replay():
                        None, "SUCCEEDED")
     tr = replay_trace(led)
     assert [r["prompt"] for r in tr] == [[1, 2, 0], [1, 2, 1], [1, 2, 2]] and tr[0]["max_tokens"] == 8
+
+
+def test_policy_loop_example_drives_the_engine():
+    import importlib.util
+    import os
+
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "examples", "policy_loop.py")
+    spec = importlib.util.spec_from_file_location("policy_loop", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    out = mod.run(levels=(0,), n_requests=8)
+    lv = out["levels"][0]
+    assert lv["amf_hits"] >= 4 and lv["admit_now"] is True  # high reuse: restores happen, admission stays on
+    assert out["rewards"]["hit_admitted"]["count"] == lv["amf_hits"]
