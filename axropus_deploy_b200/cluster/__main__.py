@@ -42,6 +42,11 @@ def _build_node(a):
     nodes = NodeRegistry(a.node_db, redis_url=os.environ.get("KORITH_NODE_REGISTRY_REDIS_URL", redis_url))
     coord = CoordinatorClient(a.coordinator) if a.coordinator else None
     art = ArtifactStore(a.artifacts)
+    uploader = None
+    if os.environ.get("KORITH_ARTIFACT_BACKEND", "local").strip().lower() in ("s3", "minio"):
+        from .objstore import build_artifacts
+
+        uploader = build_artifacts(a.artifacts)  # jobs' files are written locally, then copied to the bucket
     gpus = list(range(torch.cuda.device_count())) if torch.cuda.is_available() else [None]
     workers = {}
     for g in gpus[: a.max_workers]:
@@ -58,7 +63,8 @@ def _build_node(a):
         workers[wid] = ClusterWorker(wid, a.node_id, AdapterRegistry(eng, service=svc), ledger, art,
                                      snapshot_index=index, node_registry=nodes, coordinator=coord,
                                      decode_cache=DecodeCache(os.path.join(a.artifacts, "decode_cache.db")),
-                                     gpu_index=g or 0, concurrency=a.jobs_per_worker, queue_factory=qf)
+                                     gpu_index=g or 0, concurrency=a.jobs_per_worker, queue_factory=qf,
+                                     uploader=uploader)
     plane = ControlPlane(ledger, workers, node_id=a.node_id, node_registry=nodes, snapshot_index=index,
                          coordinator=coord)
     status = lambda: {"gpu_count": len(gpus), "inflight": sum(w.inflight for w in workers.values()),  # noqa: E731

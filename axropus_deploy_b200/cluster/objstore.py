@@ -108,9 +108,9 @@ class S3ArtifactStore(LocalArtifactStore):
             token = root.findtext(f"{ns}NextContinuationToken")
 
 
-def build_artifacts():
+def build_artifacts(base_dir=None):
     backend = os.environ.get("KORITH_ARTIFACT_BACKEND", "local").strip().lower()
-    base = Path(os.environ.get("KORITH_PLATFORM_ARTIFACTS", "./platform_data/artifacts")).resolve()
+    base = Path(base_dir or os.environ.get("KORITH_PLATFORM_ARTIFACTS", "./platform_data/artifacts")).resolve()
     if backend == "s3":
         return S3ArtifactStore(base, os.environ.get("KORITH_S3_BUCKET", ""), os.environ.get("KORITH_S3_PREFIX", "korith"),
                                endpoint=os.environ.get("KORITH_S3_ENDPOINT") or None)

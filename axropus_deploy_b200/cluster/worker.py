@@ -71,10 +71,11 @@ class ClusterWorker:
                  snapshot_index=None, node_registry=None, coordinator=None, decode_cache: Optional[DecodeCache] = None,
                  metrics=GLOBAL_METRICS, snapshot_dir: Optional[str] = None, link_gbps: Optional[float] = None,
                  rtt_ms: Optional[float] = None, transfer_threshold: Optional[float] = None, gpu_index: int = 0,
-                 queue_factory=None, concurrency: int = 1, policy=None):
+                 queue_factory=None, concurrency: int = 1, policy=None, uploader=None):
         self.worker_id, self.node_id, self.gpu_index = worker_id, node_id, gpu_index
         self.concurrency = max(1, int(concurrency))  # jobs in flight (batched by an EngineService)
         self.policy = policy  # optional decision layer (PolicyOrchestrator): fail-closed hooks around each run
+        self.uploader = uploader  # optional object store (S3 / MinIO) that receives each finished job's files
         self.adapters = adapters
         self.ledger = ledger
         self.artifacts = artifacts
@@ -352,6 +353,13 @@ class ClusterWorker:
         if exit_code == 0:
             emit_log("worker", "job_done", {"job_id": job_id, "lane": lane}, artifact_log=Path(paths["log"]),
                      echo=False)
+        if self.uploader is not None:
+            try:  # the local files stay authoritative; a failed upload is counted, not fatal
+                self.uploader.upload_job(job_id, org)
+                self.metrics.inc("korith_artifact_uploads_total", 1, {"status": "ok"})
+            except Exception as e:
+                self.metrics.inc("korith_artifact_uploads_total", 1, {"status": "failed"})
+                emit_log("worker", "artifact_upload_failed", {"job_id": job_id, **error_fields(e)}, echo=False)
         self.ledger.insert_run(uuid.uuid4().hex, job_id, started, finished, exit_code, str(paths["metrics"]),
                                str(paths["events"]), str(paths["output"]), str(paths["log"]), org_id=org)
         self.ledger.update_status(job_id, "succeeded" if exit_code == 0 else "failed")

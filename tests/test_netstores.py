@@ -581,3 +581,32 @@ def test_deploy_files_parse_and_agree():
     # the chart carries its own copy of the platform config (Helm reads files inside the chart only)
     assert open(os.path.join(chart, "files", "config.yaml")).read() == open(os.path.join(root, "config",
                                                                                            "config.yaml")).read()
+
+
+def test_worker_uploads_job_files_to_object_store(http_fake, tmp_path):
+    import importlib.util
+    import os
+
+    from axropus_deploy_b200.cluster.objstore import S3ArtifactStore
+
+    ep, state = http_fake
+    here = os.path.dirname(os.path.abspath(__file__))
+    spec = importlib.util.spec_from_file_location("platform_cpu", os.path.join(here, "test_platform_cpu.py"))
+    pc = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(pc)
+    plane, w, _ = pc._plane(tmp_path)
+    w.uploader = S3ArtifactStore(w.artifacts.base, "jobs", "korith", endpoint=ep, creds=CREDS)
+    jid = plane.submit({"prompt": "hello there", "max_tokens": 2}, org_id="org1")
+    assert w.drain()[0]["exit_code"] == 0
+    keys = sorted(state["s3"]["jobs"])
+    assert f"korith/org1/{jid}/metrics" in keys and f"korith/org1/{jid}/output" in keys
+    assert state["rejected"] == 0
+
+    class Broken:
+        def upload_job(self, *a):
+            raise OSError("bucket unreachable")
+
+    w.uploader = Broken()
+    jid2 = plane.submit({"prompt": "hello again", "max_tokens": 2}, org_id="org1")
+    assert w.drain()[0]["exit_code"] == 0 and plane.get_job(jid2, "org1")["status"] == "succeeded"
+    assert any('status="failed"' in k for k in w.metrics.counters if k.startswith("korith_artifact_uploads_total"))
