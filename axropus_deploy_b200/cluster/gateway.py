@@ -88,13 +88,25 @@ def authenticate(headers, ledger) -> Dict[str, Any]:
 
 
 class RateLimiter:
-    """Requests and tokens per organisation in 60-second windows."""
+    """Requests and tokens per organisation in 60-second windows: in memory, in SQLite
+    (``KORITH_RATE_LIMIT_DB``), or in Redis (``KORITH_RATE_LIMIT_BACKEND=redis`` with
+    ``KORITH_REDIS_URL``), where every gateway of a deployment shares one budget: counters
+    ``korith:rl:{req,tok}:<org>:<window>`` are incremented, and rolled back when the request
+    is refused so that refusals do not use up the quota."""
 
-    def __init__(self, db_path: Optional[str] = None, burst_factor: Optional[float] = None):
+    def __init__(self, db_path: Optional[str] = None, burst_factor: Optional[float] = None,
+                 redis_url: Optional[str] = None):
         self.burst = max(1.0, float(burst_factor if burst_factor is not None else
                                     os.environ.get("KORITH_RATE_LIMIT_BURST", "2.0") or 2.0))
         self._mu = threading.Lock()
         self._mem: Dict[Tuple[str, int], list] = {}
+        if redis_url is None and os.environ.get("KORITH_RATE_LIMIT_BACKEND", "").strip().lower() == "redis":
+            redis_url = os.environ.get("KORITH_REDIS_URL", "redis://127.0.0.1:6379/0")
+        self._redis = None
+        if redis_url:
+            from .netqueues import RespClient
+
+            self._redis = RespClient(redis_url)
         path = db_path or os.environ.get("KORITH_RATE_LIMIT_DB", "")
         self._db = sqlite3.connect(path, check_same_thread=False, timeout=5.0) if path else None
         if self._db is not None:
@@ -108,6 +120,18 @@ class RateLimiter:
         t = int(time.time() if now is None else now)
         win = t - t % 60
         rcap, tcap = max(1, int(rpm * self.burst)), max(1, int(tpm * self.burst))
+        if self._redis is not None:
+            rk, tk = f"korith:rl:req:{org_id}:{win}", f"korith:rl:tok:{org_id}:{win}"
+            if int(self._redis.call("INCRBY", rk, 1)) > rcap:
+                self._redis.call("DECRBY", rk, 1)
+                return {"allowed": False, "reason": "rpm_exceeded", "retry_after": 60 - t % 60}
+            self._redis.call("EXPIRE", rk, 180)
+            if int(self._redis.call("INCRBY", tk, int(tokens))) > tcap:
+                self._redis.call("DECRBY", tk, int(tokens))
+                self._redis.call("DECRBY", rk, 1)
+                return {"allowed": False, "reason": "tpm_exceeded", "retry_after": 60 - t % 60}
+            self._redis.call("EXPIRE", tk, 180)
+            return {"allowed": True, "reason": "ok"}
         with self._mu:
             if self._db is not None:
                 self._db.execute("DELETE FROM rate_limit_windows WHERE window_epoch < ?", (win - 120,))

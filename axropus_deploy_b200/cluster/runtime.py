@@ -220,7 +220,9 @@ CONFIG_ENV = {
     "runtime.spec.k": "KORITH_SPEC_K",
     "runtime.spec.min_accept": "KORITH_SPEC_MIN_ACCEPT",
     "runtime.spec.disable_after_n": "KORITH_SPEC_DISABLE_AFTER_N",
+    "gateway.rate_limit.backend": "KORITH_RATE_LIMIT_BACKEND",
     "gateway.rate_limit.sqlite_path": "KORITH_RATE_LIMIT_DB",
+    "gateway.rate_limit.redis_url": "KORITH_REDIS_URL",
     "gateway.rate_limit.burst_factor": "KORITH_RATE_LIMIT_BURST",
     "security.api_key_salt": "KORITH_API_KEY_SALT",
 }

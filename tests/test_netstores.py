@@ -147,6 +147,12 @@ class _FakeRedis:
             return len(a) // 2
         if cmd == "HGETALL":
             return [x for k, v in kv.get(a[0], {}).items() for x in (k, v)]
+        if cmd in ("INCRBY", "DECRBY"):
+            n = int(kv.get(a[0], 0)) + (int(a[1]) if cmd == "INCRBY" else -int(a[1]))
+            kv[a[0]] = n
+            return n
+        if cmd == "EXPIRE":
+            return 1
         return Exception(f"ERR unknown command {cmd}")
 
     @staticmethod
@@ -610,3 +616,19 @@ def test_worker_uploads_job_files_to_object_store(http_fake, tmp_path):
     jid2 = plane.submit({"prompt": "hello again", "max_tokens": 2}, org_id="org1")
     assert w.drain()[0]["exit_code"] == 0 and plane.get_job(jid2, "org1")["status"] == "succeeded"
     assert any('status="failed"' in k for k in w.metrics.counters if k.startswith("korith_artifact_uploads_total"))
+
+
+def test_gateway_rate_limit_shared_in_redis(redis_url, monkeypatch):
+    from axropus_deploy_b200.cluster.gateway import RateLimiter
+
+    monkeypatch.setenv("KORITH_RATE_LIMIT_BACKEND", "redis")
+    monkeypatch.setenv("KORITH_REDIS_URL", redis_url)
+    g1, g2 = RateLimiter(burst_factor=1.0), RateLimiter(burst_factor=1.0)  # two gateways, one budget
+    now = 1_800_000_000.0
+    got = [g.check_and_consume("acme", 10, rpm=3, tpm=1000, now=now)["allowed"] for g in (g1, g2, g1, g2)]
+    assert got == [True, True, True, False]
+    assert g1.check_and_consume("acme", 10, rpm=3, tpm=1000, now=now + 60)["allowed"]  # next window
+    assert g2.check_and_consume("beta", 900, rpm=10, tpm=1000, now=now)["allowed"]
+    r = g1.check_and_consume("beta", 200, rpm=10, tpm=1000, now=now)
+    assert not r["allowed"] and r["reason"] == "tpm_exceeded"
+    assert g2.check_and_consume("beta", 100, rpm=10, tpm=1000, now=now)["allowed"]  # the refusal used no quota
