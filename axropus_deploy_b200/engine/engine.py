@@ -328,7 +328,8 @@ class LLMEngine:
         head_hit = bool(self.waiting) and bool(self.waiting[0].__dict__.get("_held"))
         budget = self.policy.budget(self.cfg.max_prefill_tokens, decoding, self.cfg.max_batch, head_hit)
         budget0 = budget
-        while self.waiting and self.free_rows:
+        # cfg.max_batch may be lowered at run time (a batch controller); rows stay allocated for the start value
+        while self.waiting and self.free_rows and len(self.running) < self.cfg.max_batch:
             r = self.waiting[0]
             limit = self._amf_limit(r)
             full_pages = (len(r.prompt) - 1) // PAGE

@@ -342,3 +342,20 @@ def test_policy_loop_example_drives_the_engine():
     lv = out["levels"][0]
     assert lv["amf_hits"] >= 4 and lv["admit_now"] is True  # high reuse: restores happen, admission stays on
     assert out["rewards"]["hit_admitted"]["count"] == lv["amf_hits"]
+
+
+def test_lowered_max_batch_caps_running_sequences():
+    from axropus_deploy_b200.engine import EngineConfig, LLMEngine, SamplingParams
+    from axropus_deploy_b200.models.config import get_config
+    from axropus_deploy_b200.models.llama import LlamaModel
+
+    eng = LLMEngine(LlamaModel(get_config("tiny"), "cpu", seed=0),
+                    EngineConfig(num_blocks=128, max_model_len=256, max_batch=8))
+    eng.cfg.max_batch = 2  # what BatchController does
+    reqs = [eng.add_request(list(range(1, 20 + i)), SamplingParams(max_tokens=3)) for i in range(5)]
+    peak = 0
+    while eng.has_unfinished():
+        eng.step()
+        peak = max(peak, len(eng.running))
+    assert peak == 2 and all(len(r.output) == 3 for r in reqs)
+    eng.close()
