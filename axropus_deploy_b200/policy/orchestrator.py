@@ -26,12 +26,11 @@ import logging
 import time
 from typing import Any, Callable, Dict, Optional, Tuple
 
-import numpy as np
 import torch
 
-from .decide import DEPTHS, AdaptivePolicy, Decision, DecisionExecutor
+from .decide import AdaptivePolicy, Decision, DecisionExecutor
 from .learn import DepthPolicy, RewardLedger, reinforce_update
-from .state import Slot, StateCollector
+from .state import StateCollector
 
 log = logging.getLogger(__name__)
 
