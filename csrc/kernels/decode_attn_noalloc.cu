@@ -39,18 +39,20 @@
 #include <cstdint>
 #include <mutex>
 
+#include "decode_attn_noalloc.h"
+
 namespace {
 
 constexpr int kNoAllocPage = 16;
 constexpr int kNoAllocD = 128;
-constexpr long long kScratchFloats = 2097152;  // 8 MiB of fp32 scratch per device
+constexpr long long kScratchFloats = AXR_NOALLOC_SCRATCH_FLOATS;  // 8 MiB of fp32 scratch per device
 constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) float g_noalloc_scratch[kScratchFloats];
 
 std::mutex g_setup_mu;
 float* g_scratch_ptr[kMaxDevices] = {nullptr};
-const char* g_last_error = "ok";
+thread_local const char* g_last_error = "ok";
 
 __device__ __forceinline__ float lo_bf16(uint32_t v) { return __uint_as_float(v << 16); }
 __device__ __forceinline__ float hi_bf16(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
@@ -63,7 +65,7 @@ struct NoAllocParams {
   const int* block_table;
   int bt_stride;
   const int* seq_lens;
-  int Hq, pages_per_split;
+  int Hq, pages_per_split, max_pages;
   float scale_log2;
   __nv_bfloat16* out;
   float* part_o;   // scratch [B, Hq, S, D]
@@ -85,7 +87,7 @@ __global__ void __launch_bounds__(128) noalloc_decode_kernel(NoAllocParams p) {
   const int seq_len = p.seq_lens[b];
   const int n_pages = (seq_len + kNoAllocPage - 1) / kNoAllocPage;
   const int pg0 = split * p.pages_per_split;
-  const int pg1 = min(n_pages, pg0 + p.pages_per_split);
+  const int pg1 = min(min(n_pages, p.max_pages), pg0 + p.pages_per_split);  // never past the table row
   for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
     const int g = i / D, d = i % D;
     qs[g][d / HALF][d % HALF] = __bfloat162float(p.q[((long long)b * p.Hq + kvh * G + g) * D + d]) * p.scale_log2;
@@ -231,14 +233,6 @@ float* scratch_for_current_device() {
 
 extern "C" {
 
-enum {
-  AXR_NOALLOC_OK = 0,
-  AXR_NOALLOC_TOO_LARGE = 1,
-  AXR_NOALLOC_SETUP_FAILED = 2,
-  AXR_NOALLOC_BAD_ARGS = 3,
-  AXR_NOALLOC_LAUNCH_FAILED = 4,
-};
-
 // Largest number of fp32 scratch elements one call may use: B * Hq * S * (D + 1).
 __attribute__((visibility("default"))) long long axr_decode_noalloc_scratch_floats(void) { return kScratchFloats; }
 
@@ -253,7 +247,7 @@ __attribute__((visibility("default"))) int axr_decode_attention_noalloc(
     long long head_stride, const int* block_table, int bt_stride, const int* seq_lens, int B, int Hq,
     int Hkv, int D, float scale, int num_splits, int max_pages, cudaStream_t stream) {
   if (!q || !out || !k_pages || !v_pages || !block_table || !seq_lens || B <= 0 || Hq <= 0 || Hkv <= 0 ||
-      Hq % Hkv != 0 || num_splits < 1 || max_pages < 0) {
+      Hq % Hkv != 0 || num_splits < 1 || max_pages < 0 || bt_stride < 0 || max_pages > bt_stride) {
     g_last_error = "invalid arguments";
     return AXR_NOALLOC_BAD_ARGS;
   }
@@ -266,6 +260,10 @@ __attribute__((visibility("default"))) int axr_decode_attention_noalloc(
   if (need > kScratchFloats) {
     g_last_error = "call needs more scratch than the fixed 8 MiB array (B*Hq*splits*(head_dim+1) > 2097152)";
     return AXR_NOALLOC_TOO_LARGE;
+  }
+  if (cudaPeekAtLastError() != cudaSuccess) {  // not ours: leave it for its owner
+    g_last_error = "an earlier CUDA error is pending on this thread; nothing launched";
+    return AXR_NOALLOC_PENDING_ERROR;
   }
   float* scratch = nullptr;
   if (num_splits > 1) {
@@ -283,24 +281,34 @@ __attribute__((visibility("default"))) int axr_decode_attention_noalloc(
   p.seq_lens = seq_lens;
   p.Hq = Hq;
   p.pages_per_split = (max_pages + num_splits - 1) / num_splits;
+  p.max_pages = max_pages;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.out = static_cast<__nv_bfloat16*>(out);
   p.part_o = scratch;
   p.part_lse = scratch ? scratch + (long long)B * Hq * num_splits * D : nullptr;
-  dim3 grid(num_splits, Hkv, B);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(num_splits, Hkv, B);
+  cfg.blockDim = dim3(128);
+  cfg.stream = stream;
+  cudaError_t rc;
   switch (G) {
-    case 1: noalloc_decode_kernel<1><<<grid, 128, 0, stream>>>(p); break;
-    case 2: noalloc_decode_kernel<2><<<grid, 128, 0, stream>>>(p); break;
-    case 4: noalloc_decode_kernel<4><<<grid, 128, 0, stream>>>(p); break;
-    default: noalloc_decode_kernel<8><<<grid, 128, 0, stream>>>(p); break;
+    case 1: rc = cudaLaunchKernelEx(&cfg, noalloc_decode_kernel<1>, p); break;
+    case 2: rc = cudaLaunchKernelEx(&cfg, noalloc_decode_kernel<2>, p); break;
+    case 4: rc = cudaLaunchKernelEx(&cfg, noalloc_decode_kernel<4>, p); break;
+    default: rc = cudaLaunchKernelEx(&cfg, noalloc_decode_kernel<8>, p); break;
   }
-  if (cudaGetLastError() != cudaSuccess) {
+  if (rc != cudaSuccess) {
     g_last_error = "decode kernel launch failed";
     return AXR_NOALLOC_LAUNCH_FAILED;
   }
   if (num_splits > 1) {
-    noalloc_combine_kernel<<<B * Hq, kNoAllocD, 0, stream>>>(p.part_o, p.part_lse, p.out, num_splits);
-    if (cudaGetLastError() != cudaSuccess) {
+    cudaLaunchConfig_t c2 = {};
+    c2.gridDim = dim3(B * Hq);
+    c2.blockDim = dim3(kNoAllocD);
+    c2.stream = stream;
+    rc = cudaLaunchKernelEx(&c2, noalloc_combine_kernel, static_cast<const float*>(p.part_o),
+                            static_cast<const float*>(p.part_lse), p.out, num_splits);
+    if (rc != cudaSuccess) {
       g_last_error = "combine kernel launch failed";
       return AXR_NOALLOC_LAUNCH_FAILED;
     }

@@ -9,246 +9,300 @@
 #include <cstring>
 #include <limits>
 
+// ------------------------------------------------------------------ spec-depth scheduler
+namespace axr {
 namespace {
-
-thread_local const char* g_lane = "MISS";
-thread_local const char* g_reason = "warmup";
 
 float unit_or(float v, float d) { return std::isfinite(v) ? std::min(1.f, std::max(0.f, v)) : d; }
 float finite_or(float v, float d) { return std::isfinite(v) ? v : d; }
 
-enum class Lane { kSpecHit, kHit, kMiss };
+int lane_cap(Lane l, int max_depth) {
+  const int c = l == Lane::kSpecHit ? 16 : l == Lane::kHit ? 10 : 3;
+  return std::max(1, std::min(c, max_depth));
+}
 
-// Lane from the decode quality signals and the AMF reuse of the current prefix.
-Lane lane_of(float acc, float ent, float dtps, float reuse) {
-  const bool replay_local = reuse >= 0.70f;
-  const bool stable = acc >= 0.78f && ent <= 0.58f && dtps >= -0.05f;
-  if (replay_local && stable) return Lane::kSpecHit;
-  if (replay_local || (acc >= 0.68f && ent <= 0.68f)) return Lane::kHit;
+// The lane the smoothed signals point to. Quality q = acceptance x (1 - entropy) is the
+// chance a drafted token survives; AMF reuse says the prefix was restored, i.e. the
+// request replays a known context where drafts (n-gram or model) are usually right.
+Lane lane_for(float acc, float ent, float dtps, float reuse) {
+  const float q = acc * (1.f - ent);
+  if (reuse >= 0.70f && q >= 0.35f && dtps >= -0.05f) return Lane::kSpecHit;
+  if (reuse >= 0.70f || q >= 0.22f) return Lane::kHit;
   return Lane::kMiss;
 }
 
-constexpr unsigned kProbeInterval = 64, kHysteresis = 32, kStarvation = 96;
-constexpr int kMaxDepth = 16;
+}  // namespace
 
+const char* lane_name(Lane l) { return l == Lane::kSpecHit ? "SPEC_HIT" : l == Lane::kHit ? "HIT" : "MISS"; }
+
+// Expected tokens per verification step with k drafted tokens, each accepted with
+// probability a (independently): 1 + a + ... + a^k = (1 - a^(k+1)) / (1 - a), against a
+// step cost of 1 + c k (Leviathan, Kalman & Matias 2023, "Fast inference from
+// transformers via speculative decoding", section 3).
+int best_depth(float acceptance, float draft_cost, int cap) {
+  const double a = std::min(0.98, std::max(0.0, static_cast<double>(acceptance)));
+  const double c = std::min(1.0, std::max(0.005, static_cast<double>(draft_cost)));
+  int best = 1;
+  double best_v = -1.0;
+  double pw = a;  // a^k
+  for (int k = 1; k <= std::max(1, cap); ++k) {
+    pw *= a;  // a^(k+1)
+    const double tokens = a >= 0.999999 ? k + 1.0 : (1.0 - pw) / (1.0 - a);
+    const double v = tokens / (1.0 + c * k);
+    if (v > best_v + 1e-9) {
+      best_v = v;
+      best = k;
+    }
+  }
+  return best;
+}
+
+KorithScheduleOutput schedule(SchedState* st, const KorithScheduleInput& in, const SchedConfig& cfg) {
+  KorithScheduleOutput out{1, 0.f, static_cast<int>(Lane::kMiss)};
+  st->step += 1;
+  st->ready = in.baseline_ready != 0;
+  if (!st->ready) {  // the engine's throughput baseline is not stable yet: no speculation
+    st->depth = 1;
+    st->lane = st->pending = Lane::kMiss;
+    st->reason = "warmup";
+    st->last_change = st->step;
+    return out;
+  }
+  const float acc = unit_or(in.acceptance, 0.f), ent = unit_or(in.entropy, 1.f);
+  const float dtps = std::max(-1.f, std::min(1.f, finite_or(in.current_tps, 0.f)));
+  const float reuse = unit_or(in.amf_reuse_score, 0.f);
+  if (!st->primed) {
+    st->acc = acc;
+    st->ent = ent;
+    st->dtps = dtps;
+    st->primed = true;
+  } else {
+    st->acc += cfg.alpha * (acc - st->acc);
+    st->ent += cfg.alpha * (ent - st->ent);
+    st->dtps += cfg.alpha * (dtps - st->dtps);
+  }
+
+  // lane: worse lanes are taken at once, better ones after lane_debounce steps in a row
+  const Lane want = lane_for(st->acc, st->ent, st->dtps, reuse);
+  if (static_cast<int>(want) < static_cast<int>(st->lane)) {
+    st->lane = want;
+    st->lane_age = 0;
+    st->better_streak = 0;
+  } else if (static_cast<int>(want) > static_cast<int>(st->lane)) {
+    st->better_streak = st->pending == want ? st->better_streak + 1 : 1;
+    st->pending = want;
+    if (static_cast<int>(st->better_streak) >= cfg.lane_debounce) {
+      st->lane = want;
+      st->lane_age = 0;
+      st->better_streak = 0;
+    }
+  } else {
+    st->better_streak = 0;
+  }
+  st->lane_age += 1;
+  st->miss_streak = st->lane == Lane::kMiss ? st->miss_streak + 1 : 0;
+
+  const int cap = lane_cap(st->lane, cfg.max_depth);
+  float cost = cfg.draft_cost;
+  if (std::isfinite(in.engine_costs) && in.engine_costs > 0.f && in.engine_costs <= 1.f) cost = in.engine_costs;
+  const int target = std::min(cap, best_depth(st->acc, cost, cap));
+  int depth = std::max(1, st->depth);
+  const char* reason = "hold";
+  if (depth > cap || target < depth) {  // decreases are never held back
+    depth = std::max(target, depth - 4);
+    depth = std::min(depth, cap);
+    reason = st->lane == Lane::kMiss ? "miss_down" : "down";
+  } else if (target > depth && st->step - st->last_change >= static_cast<std::uint64_t>(cfg.hold_up_steps)) {
+    depth = std::min(target, depth + 2);
+    reason = "up";
+  }
+  // a long MISS stretch with usable acceptance: measure a deeper draft again
+  if (st->lane == Lane::kMiss && st->miss_streak >= static_cast<std::uint32_t>(cfg.starve_steps) && st->acc >= 0.5f) {
+    depth = std::min(lane_cap(Lane::kHit, cfg.max_depth), std::max(depth, 2) + 1);
+    st->miss_streak = 0;
+    reason = "starvation_probe";
+  } else if (depth == 1 && st->step % static_cast<std::uint64_t>(std::max(1, cfg.probe_every)) == 0 &&
+             st->dtps >= 0.f) {
+    depth = 2;
+    reason = "probe";
+  }
+  depth = std::max(1, std::min(cfg.max_depth, depth));
+  if (depth != st->depth) st->last_change = st->step;
+  st->depth = depth;
+  st->reason = reason;
+  out.desired_depth = depth;
+  out.stability_score = std::min(1.f, std::max(0.f, st->acc * (1.f - st->ent)));
+  out.throttle_flag = static_cast<int>(st->lane);
+  if (std::getenv("KORITH_SCHED_LOG")) {
+    std::fprintf(stderr, "[SCHEDULER_DECISION] depth=%d stability=%.3f throttle=%d lane=%s reason=%s\n", depth,
+                 out.stability_score, out.throttle_flag, lane_name(st->lane), reason);
+  }
+  return out;
+}
+
+}  // namespace axr
+
+namespace {
+// The reference-shaped entry points keep one scheduler per process (the caller's record
+// carries only the depth and the baseline flag).
+std::mutex g_sched_mu;
+axr::SchedState g_sched;
+
+int batch_hint(int depth) { return std::max(1, 256 / (depth + 1)); }
 }  // namespace
 
 extern "C" {
 
 __attribute__((visibility("default"))) KorithScheduleOutput korith_schedule_step(KorithSchedulerState* st,
                                                                                   const KorithScheduleInput* in) {
-  KorithScheduleOutput out{1, 0.f, 1};
-  if (!st || !in) return out;
-  st->baseline_ready = in->baseline_ready ? 1 : 0;
-  if (!st->baseline_ready) {  // warm-up: miss budget until the baseline is stable
-    st->speculative_depth = 1;
-    g_lane = "MISS";
-    g_reason = "warmup";
-    return out;
+  KorithScheduleInput zero{};
+  std::lock_guard<std::mutex> lk(g_sched_mu);
+  if (st && st->speculative_depth >= 1) g_sched.depth = st->speculative_depth;
+  const KorithScheduleOutput o = axr::schedule(&g_sched, in ? *in : zero);
+  if (st) {
+    st->speculative_depth = o.desired_depth;
+    st->batch_size = batch_hint(o.desired_depth);
+    st->baseline_ready = g_sched.ready ? 1 : 0;
   }
-  const float acc = unit_or(in->acceptance, 0.f);
-  const float ent = unit_or(in->entropy, 1.f);
-  const float dtps = finite_or(in->current_tps, 0.f);
-  const float reuse = unit_or(in->amf_reuse_score, 0.f);
-  int depth = std::min(kMaxDepth, std::max(1, st->speculative_depth));
-  const unsigned raw = static_cast<unsigned>(st->batch_size);
-  unsigned step = ((raw & 0xFFFFu) + 1u) & 0xFFFFu;
-  unsigned last_change = (raw >> 16) & 0xFFu;
-  unsigned miss_streak = (raw >> 24) & 0xFFu;
-
-  const Lane lane = lane_of(acc, ent, dtps, reuse);
-  miss_streak = lane == Lane::kMiss ? std::min(255u, miss_streak + 1u) : 0u;
-  const char* reason = "hold";
-  bool force_down = false;
-  int cap = 3, throttle = 1;
-  switch (lane) {
-    case Lane::kSpecHit:
-      cap = 16;
-      throttle = 3;
-      if (acc >= 0.90f && ent <= 0.45f && dtps >= -0.02f) { depth += 2; reason = "spec_hit_up2"; }
-      else if (acc >= 0.80f && ent <= 0.58f && dtps >= -0.05f) { depth += 1; reason = "spec_hit_up1"; }
-      else if (acc < 0.62f || ent > 0.82f || dtps < -0.15f) { depth = std::max(2, depth - 2); force_down = true; reason = "spec_hit_down"; }
-      g_lane = "SPEC_HIT";
-      break;
-    case Lane::kHit:
-      cap = 12;
-      throttle = 2;
-      if (acc >= 0.82f && ent <= 0.62f && dtps >= -0.03f) { depth += 1; reason = "hit_up"; }
-      else if (acc < 0.58f || ent > 0.84f || dtps < -0.14f) { depth = std::max(2, depth - 1); force_down = true; reason = "hit_down"; }
-      g_lane = "HIT";
-      break;
-    case Lane::kMiss:
-      if (acc < 0.50f || ent > 0.85f || dtps < -0.10f) { depth = 2; reason = "miss_cap"; }
-      else { depth = std::min(depth, 3); reason = "miss_hold"; }
-      if (miss_streak >= kStarvation && acc >= 0.60f && ent <= 0.70f) {  // starvation probe
-        depth = 3;
-        reason = "miss_probe";
-        miss_streak = 0;
-      }
-      force_down = true;
-      g_lane = "MISS";
-      break;
-  }
-  depth = std::min(cap, std::max(1, depth));
-  bool probed = false;
-  if (depth == 1 && step % kProbeInterval == 0 && dtps >= 0.f) {  // periodic cold-start probe
-    depth = 2;
-    reason = "probe";
-    probed = true;
-    force_down = false;
-  }
-  depth = std::min(kMaxDepth, std::max(1, depth));
-  if (depth != st->speculative_depth) {
-    const unsigned s8 = step & 0xFFu;
-    const unsigned since = (s8 - last_change) & 0xFFu;
-    if (!probed && !force_down && since < kHysteresis) {
-      depth = st->speculative_depth;
-      reason = "hold";
-    } else {
-      last_change = s8;
-    }
-  }
-  out.desired_depth = depth;
-  out.stability_score = std::min(1.f, std::max(0.f, acc * (1.f - ent)));
-  out.throttle_flag = throttle;
-  st->speculative_depth = depth;
-  st->batch_size = static_cast<int>(((miss_streak & 0xFFu) << 24) | ((last_change & 0xFFu) << 16) | (step & 0xFFFFu));
-  g_reason = reason;
-  if (std::getenv("KORITH_SCHED_LOG")) {
-    std::fprintf(stderr, "[SCHEDULER_DECISION] depth=%d stability=%.3f throttle=%d lane=%s reason=%s\n", depth,
-                 out.stability_score, throttle, g_lane, reason);
-  }
-  return out;
+  return o;
 }
 
-__attribute__((visibility("default"))) void korith_scheduler_reset(KorithSchedulerState* st) {
-  if (st) *st = KorithSchedulerState{1, 0, 0};
+__attribute__((visibility("default"))) unsigned korith_scheduler_update(float entropy, float acceptance, float tps) {
+  KorithScheduleInput in{acceptance, entropy, tps, 0.f, 0.f, 0.f, 0.f, 0.f, 1};
+  std::lock_guard<std::mutex> lk(g_sched_mu);
+  const KorithScheduleOutput o = axr::schedule(&g_sched, in);
+  return static_cast<unsigned>(std::max(1, o.desired_depth));
 }
 
-__attribute__((visibility("default"))) int korith_scheduler_update(KorithSchedulerState* st,
-                                                                   const KorithScheduleInput* in, int* out_depth) {
-  const KorithScheduleOutput o = korith_schedule_step(st, in);
-  if (out_depth) *out_depth = o.desired_depth;
-  return o.throttle_flag;
+__attribute__((visibility("default"))) void korith_scheduler_reset(void) {
+  std::lock_guard<std::mutex> lk(g_sched_mu);
+  g_sched = axr::SchedState{};
 }
+
+__attribute__((visibility("default"))) void* korith_scheduler_create(void) { return new axr::SchedState(); }
+
+__attribute__((visibility("default"))) KorithScheduleOutput korith_scheduler_step_ex(void* h,
+                                                                                     const KorithScheduleInput* in) {
+  KorithScheduleInput zero{};
+  if (!h) return KorithScheduleOutput{1, 0.f, 1};
+  return axr::schedule(static_cast<axr::SchedState*>(h), in ? *in : zero);
+}
+
+__attribute__((visibility("default"))) void korith_scheduler_destroy(void* h) { delete static_cast<axr::SchedState*>(h); }
 
 }  // extern "C"
 
-namespace axr {
-
-const char* last_lane_name() { return g_lane; }
-const char* last_reason() { return g_reason; }
-
 // ------------------------------------------------------------------ memory field
+namespace axr {
 namespace {
-constexpr std::uint64_t kEveryRequests = 2, kEveryMs = 100, kCooldownMax = 60000;
-constexpr double kRoiMax = 10.0, kPressMin = 0.5, kPressMax = 3.0, kPressStep = 0.5;
+constexpr std::uint64_t kMinIntervalMs = 100, kMinRequests = 4;
+constexpr std::uint64_t kBaseCooldownMs = 2000, kMaxCooldownMs = 60000, kBackoffForgetMs = 60000;
+constexpr double kRoiMax = 10.0, kPressMin = 0.5, kPressMax = 3.0;
+constexpr double kRoiSlew = 0.5, kPressSlew = 0.25;  // largest change of an output per update
+constexpr double kRoiOff = 0.6, kEvidenceHits = 3.0;
 
 std::uint64_t dlt(std::uint64_t a, std::uint64_t b) { return a >= b ? a - b : 0; }
 double clamp(double v, double lo, double hi) { return std::isfinite(v) ? std::min(hi, std::max(lo, v)) : lo; }
-// true when new differs from old by less than max(abs_eps, rel_eps*|old|)
-bool tiny_change(double o, double n, double rel, double ab) {
-  const double scale = std::max(ab, std::fabs(o) * rel);
-  return std::fabs(n - o) + std::max(1e-12, scale * 1e-7) < scale;
+double slew(double from, double to, double step) { return std::max(from - step, std::min(from + step, to)); }
+double smoothstep(double e0, double e1, double x) {
+  const double t = clamp((x - e0) / (e1 - e0), 0.0, 1.0);
+  return t * t * (3.0 - 2.0 * t);
 }
 }  // namespace
 
+// Outputs and how they move:
+//  * min_admit_roi (admission bar of new AMF entries): 0 while the pool is below 60 %
+//    full, rising linearly to 2 at 100 % full, plus 2 x (1 - ROI) while restores cost
+//    more than they save, plus 0.5 per failed restore in the window; at most 0.5 of
+//    change per update.
+//  * eviction_pressure: 0.75 + 2.25 x smoothstep(fill from 50 % to 95 %), at most 0.25 of
+//    change per update.
+//  * replay gate (Schmitt trigger with exponential back-off): replay turns off when the
+//    smoothed ROI falls below 0.6 with at least 3 hits of evidence; it turns back on
+//    ("probation") once its cooldown has passed. Each off within 60 s of the previous one
+//    doubles the cooldown (2 s, 4 s, ... up to 60 s), so an oscillating workload settles
+//    with replay off for longer and longer stretches.
 MemoryFieldOutput memory_field_update(MemoryFieldState* s, const MemoryFieldInput& in, bool log) {
-  const MemoryFieldOutput last = s ? s->last : MemoryFieldOutput{};
-  MemoryFieldOutput out = last;
-  if (s && s->has_prev) {
-    const std::uint64_t el = dlt(in.now_ms, s->last_update_ms);
-    if (!(s->requests_since_update >= kEveryRequests || el >= kEveryMs)) {
-      s->requests_since_update += 1;
-      return last;
-    }
+  MemoryFieldState scratch;
+  if (!s) s = &scratch;
+  const MemoryFieldOutput last = s->last;
+  if (s->has_prev) {
+    s->requests_since_update += 1;
+    if (dlt(in.now_ms, s->last_update_ms) < kMinIntervalMs && s->requests_since_update < kMinRequests) return last;
   }
-  std::uint64_t dh = 0, dm = 0, db = 0, df = 0, dsav = 0, drest = 0;
-  if (s && s->has_prev) {
+  std::uint64_t dh = 0, dm = 0, df = 0, dsav = 0, drest = 0;
+  if (s->has_prev) {
     dh = dlt(in.hits, s->prev.hits);
     dm = dlt(in.misses, s->prev.misses);
-    db = dlt(in.blocks, s->prev.blocks);
     df = dlt(in.failures, s->prev.failures);
     dsav = dlt(in.ms_saved, s->prev.ms_saved);
     drest = dlt(in.restore_ms, s->prev.restore_ms);
   }
-  const double hit_rate = (dh + dm) ? double(dh) / double(dh + dm) : 0.0;
-  const double roi = drest ? double(dsav) / double(drest) : 0.0;
-  const double pressure = in.max_bytes ? clamp(double(in.bytes) / double(in.max_bytes), 0.0, 1.0) : 0.0;
-  const bool roi_bad = drest && roi < 1.0, roi_very_bad = drest && roi < 0.5, roi_good = drest && roi > 1.2;
-  const bool stable = roi_good || hit_rate > 0.20 || in.negative_roi_streak == 0;
-  if (roi_bad || in.negative_roi_streak >= 3 || pressure > 0.90) out.min_admit_roi = std::max(out.min_admit_roi, 1.0);
-  else if (roi_good && hit_rate > 0.20 && pressure < 0.70 && out.min_admit_roi > 0.0) out.min_admit_roi *= 0.90;
-  out.eviction_pressure = pressure > 0.90 ? 2.0 : pressure > 0.75 ? 1.5 : pressure < 0.50 ? 0.8 : 1.0;
-  if (in.negative_roi_streak >= 3 || (roi_very_bad && dh >= 2)) {
-    out.replay_disable_mask = 1u;
-    out.cooldown_ms = std::max<std::uint64_t>(out.cooldown_ms, 2000);
-  } else if (stable) {
-    out.replay_disable_mask = 0u;
-    out.cooldown_ms = 0;
+  if (dh + dm) s->hit_ema = 0.7 * s->hit_ema + 0.3 * (double(dh) / double(dh + dm));
+  if (drest) {
+    const double roi = double(dsav) / double(drest);
+    s->roi_ema = s->roi_seen ? 0.6 * s->roi_ema + 0.4 * roi : roi;
+    s->roi_seen = true;
   }
-  out.eviction_pressure = std::min(last.eviction_pressure + kPressStep, std::max(last.eviction_pressure - kPressStep, out.eviction_pressure));
-  if (s) {
-    const std::uint32_t lm = last.replay_disable_mask & 1u;
-    std::uint32_t nm = out.replay_disable_mask & 1u;
-    const std::uint64_t win = std::max(out.cooldown_ms, last.cooldown_ms);
-    const std::uint64_t weff = win ? win : kEveryMs;
-    if (nm != lm) {  // anti-oscillation: a third flip inside the window pins replay off
-      std::uint32_t flips = s->replay_flip_count;
-      if (s->last_replay_flip_ms && in.now_ms > s->last_replay_flip_ms && in.now_ms - s->last_replay_flip_ms <= weff)
-        flips = flips < UINT32_MAX ? flips + 1 : flips;
-      else
-        flips = 1;
-      s->last_replay_flip_ms = in.now_ms;
-      s->replay_flip_count = flips;
-      if (flips > 2) {
-        nm = 1u;
-        out.cooldown_ms = std::max(out.cooldown_ms, weff);
-      }
+  s->evidence = 0.5 * s->evidence + double(dh);
+  const double fill = in.max_bytes ? clamp(double(in.bytes) / double(in.max_bytes), 0.0, 1.0) : 0.0;
+
+  MemoryFieldOutput out = last;
+  double bar = 5.0 * std::max(0.0, fill - 0.6);
+  if (s->roi_seen && s->roi_ema < 1.0) bar += 2.0 * (1.0 - s->roi_ema);
+  bar += 0.5 * std::min<std::uint64_t>(df, 8);
+  out.min_admit_roi = clamp(slew(last.min_admit_roi, bar, kRoiSlew), 0.0, kRoiMax);
+  const double press = 0.75 + 2.25 * smoothstep(0.5, 0.95, fill);
+  out.eviction_pressure = clamp(slew(last.eviction_pressure, press, kPressSlew), kPressMin, kPressMax);
+
+  const bool off = (last.replay_disable_mask & 1u) != 0;
+  if (!off) {
+    if (s->roi_seen && s->roi_ema < kRoiOff && s->evidence >= kEvidenceHits) {
+      if (s->last_disable_ms && dlt(in.now_ms, s->last_disable_ms) <= kBackoffForgetMs) s->backoff += 1;
+      else s->backoff = 0;
+      const std::uint64_t cd = std::min(kMaxCooldownMs, kBaseCooldownMs << std::min<std::uint32_t>(s->backoff, 5));
+      s->disabled_at_ms = in.now_ms;
+      s->last_disable_ms = in.now_ms;
+      s->disable_until_ms = in.now_ms + cd;
+      out.replay_disable_mask = 1u;
     }
-    out.replay_disable_mask = nm;
+  } else if (in.now_ms >= s->disable_until_ms) {
+    out.replay_disable_mask = 0u;  // probation: restores resume and the ROI is measured again
+    s->roi_seen = false;
+    s->evidence = 0.0;
   }
-  if (tiny_change(last.min_admit_roi, out.min_admit_roi, 0.10, 0.05)) out.min_admit_roi = last.min_admit_roi;
-  if (tiny_change(last.eviction_pressure, out.eviction_pressure, 0.10, 0.05)) out.eviction_pressure = last.eviction_pressure;
-  if (!stable && out.cooldown_ms < last.cooldown_ms) {
-    out.cooldown_ms = last.cooldown_ms;
-    out.replay_disable_mask = last.replay_disable_mask;
-  }
-  out.min_admit_roi = clamp(out.min_admit_roi, 0.0, kRoiMax);
-  if (!std::isfinite(out.eviction_pressure) || out.eviction_pressure <= 0.0) out.eviction_pressure = 1.0;
-  out.eviction_pressure = clamp(out.eviction_pressure, kPressMin, kPressMax);
-  out.replay_disable_mask &= 1u;
-  out.cooldown_ms = std::min(out.cooldown_ms, kCooldownMax);
-  const bool changed = !tiny_change(last.min_admit_roi, out.min_admit_roi, 1e-3, 1e-3) ||
-                       !tiny_change(last.eviction_pressure, out.eviction_pressure, 1e-3, 1e-3) ||
-                       last.replay_disable_mask != out.replay_disable_mask || last.cooldown_ms != out.cooldown_ms;
+  out.cooldown_ms = (out.replay_disable_mask & 1u) ? dlt(s->disable_until_ms, in.now_ms) : 0;
+
+  const bool changed = std::fabs(out.min_admit_roi - last.min_admit_roi) > 1e-6 ||
+                       std::fabs(out.eviction_pressure - last.eviction_pressure) > 1e-6 ||
+                       out.replay_disable_mask != last.replay_disable_mask;
   if (changed && log) {
     std::fprintf(stderr,
                  "[MF_POLICY] min_admit_roi=%.2f->%.2f evict_pressure=%.2f->%.2f replay_mask=0x%02x cooldown_ms=%llu "
-                 "roi=%.2f hits=%llu misses=%llu blocks=%llu failures=%llu pressure=%.2f\n",
+                 "roi=%.2f hit_rate=%.2f fill=%.2f failures=%llu\n",
                  last.min_admit_roi, out.min_admit_roi, last.eviction_pressure, out.eviction_pressure,
-                 out.replay_disable_mask, (unsigned long long)out.cooldown_ms, roi, (unsigned long long)dh,
-                 (unsigned long long)dm, (unsigned long long)db, (unsigned long long)df, pressure);
+                 out.replay_disable_mask, (unsigned long long)out.cooldown_ms, s->roi_ema, s->hit_ema, fill,
+                 (unsigned long long)df);
     std::fflush(stderr);
   }
-  if (s) {
-    s->last = out;
-    s->prev = in;
-    s->has_prev = true;
-    s->last_update_ms = in.now_ms;
-    s->requests_since_update = 0;
-  }
+  s->last = out;
+  s->prev = in;
+  s->has_prev = true;
+  s->last_update_ms = in.now_ms;
+  s->requests_since_update = 0;
   return out;
 }
 
 std::string memory_field_to_json(const MemoryFieldState& s) {
-  char b[512];
+  char b[768];
   std::snprintf(b, sizeof(b),
                 "{\"min_admit_roi\":%.17g,\"eviction_pressure\":%.17g,\"replay_disable_mask\":%u,\"cooldown_ms\":%llu,"
-                "\"last_update_ms\":%llu,\"last_replay_flip_ms\":%llu,\"replay_flip_count\":%u}",
+                "\"roi_ema\":%.17g,\"hit_ema\":%.17g,\"roi_seen\":%d,\"disable_until_ms\":%llu,"
+                "\"last_disable_ms\":%llu,\"backoff\":%u,\"last_update_ms\":%llu}",
                 s.last.min_admit_roi, s.last.eviction_pressure, s.last.replay_disable_mask,
-                (unsigned long long)s.last.cooldown_ms, (unsigned long long)s.last_update_ms,
-                (unsigned long long)s.last_replay_flip_ms, s.replay_flip_count);
+                (unsigned long long)s.last.cooldown_ms, s.roi_ema, s.hit_ema, s.roi_seen ? 1 : 0,
+                (unsigned long long)s.disable_until_ms, (unsigned long long)s.last_disable_ms, s.backoff,
+                (unsigned long long)s.last_update_ms);
   return b;
 }
 
@@ -265,24 +319,34 @@ bool json_num(const std::string& js, const char* key, double* out) {
   *out = v;
   return true;
 }
+std::uint64_t u64(double v) { return static_cast<std::uint64_t>(std::max(0.0, v)); }
 }  // namespace
 
 bool memory_field_from_json(const std::string& js, MemoryFieldState* s) {
   if (!s) return false;
-  double a, b, m, c, u = 0, f = 0, n = 0;
+  double a, b, m, c;
   if (!json_num(js, "min_admit_roi", &a) || !json_num(js, "eviction_pressure", &b) ||
       !json_num(js, "replay_disable_mask", &m) || !json_num(js, "cooldown_ms", &c))
     return false;
-  json_num(js, "last_update_ms", &u);
-  json_num(js, "last_replay_flip_ms", &f);
-  json_num(js, "replay_flip_count", &n);
+  double roi = 1.0, hit = 0.0, seen = 0.0, until = 0.0, lastd = 0.0, bo = 0.0, upd = 0.0;
+  json_num(js, "roi_ema", &roi);
+  json_num(js, "hit_ema", &hit);
+  json_num(js, "roi_seen", &seen);
+  json_num(js, "disable_until_ms", &until);
+  json_num(js, "last_disable_ms", &lastd);
+  json_num(js, "backoff", &bo);
+  json_num(js, "last_update_ms", &upd);
   s->last.min_admit_roi = clamp(a, 0.0, kRoiMax);
   s->last.eviction_pressure = clamp(b, kPressMin, kPressMax);
   s->last.replay_disable_mask = static_cast<std::uint32_t>(m) & 1u;
-  s->last.cooldown_ms = std::min<std::uint64_t>(static_cast<std::uint64_t>(std::max(0.0, c)), kCooldownMax);
-  s->last_update_ms = static_cast<std::uint64_t>(std::max(0.0, u));
-  s->last_replay_flip_ms = static_cast<std::uint64_t>(std::max(0.0, f));
-  s->replay_flip_count = static_cast<std::uint32_t>(std::max(0.0, n));
+  s->last.cooldown_ms = std::min<std::uint64_t>(u64(c), kMaxCooldownMs);
+  s->roi_ema = clamp(roi, 0.0, 1e6);
+  s->hit_ema = clamp(hit, 0.0, 1.0);
+  s->roi_seen = seen != 0.0;
+  s->disable_until_ms = u64(until);
+  s->last_disable_ms = u64(lastd);
+  s->backoff = static_cast<std::uint32_t>(std::min(31.0, std::max(0.0, bo)));
+  s->last_update_ms = u64(upd);
   return true;
 }
 

@@ -80,28 +80,35 @@ void bind_runtime(py::module_& m) {
   m.def("block_chain_hashes", &block_chain_hashes, py::arg("tokens"), py::arg("page") = 16,
         py::arg("n_blocks") = -1);
 
-  py::class_<KorithSchedulerState>(m, "SchedulerState")
-      .def(py::init([]() { KorithSchedulerState s{1, 0, 0}; return s; }))
-      .def_readwrite("speculative_depth", &KorithSchedulerState::speculative_depth)
-      .def_readwrite("packed_counters", &KorithSchedulerState::batch_size)
-      .def_readwrite("baseline_ready", &KorithSchedulerState::baseline_ready);
-  m.def("schedule_step", [](KorithSchedulerState& st, float acceptance, float entropy, float current_tps,
+  py::class_<SchedState>(m, "SchedulerState")
+      .def(py::init<>())
+      .def_readwrite("depth", &SchedState::depth)
+      .def_readonly("ready", &SchedState::ready)
+      .def_readonly("acceptance_ema", &SchedState::acc)
+      .def_readonly("entropy_ema", &SchedState::ent)
+      .def_readonly("tps_trend_ema", &SchedState::dtps)
+      .def_readonly("step", &SchedState::step)
+      .def_readonly("last_change", &SchedState::last_change)
+      .def_readonly("miss_streak", &SchedState::miss_streak)
+      .def_property_readonly("lane", [](const SchedState& s) { return std::string(lane_name(s.lane)); })
+      .def_property_readonly("reason", [](const SchedState& s) { return std::string(s.reason); });
+  m.def("schedule_step", [](SchedState& st, float acceptance, float entropy, float current_tps,
                             float engine_costs, float amf_reuse_score, float amf_avg_prefix_length,
                             float amf_accept_rate, float amf_restore_cost_ms, bool baseline_ready) {
     KorithScheduleInput in{acceptance, entropy, current_tps, engine_costs, amf_reuse_score, amf_avg_prefix_length,
                            amf_accept_rate, amf_restore_cost_ms, baseline_ready ? 1 : 0};
-    const KorithScheduleOutput o = korith_schedule_step(&st, &in);
+    const KorithScheduleOutput o = schedule(&st, in);
     py::dict d;
     d["desired_depth"] = o.desired_depth;
     d["stability_score"] = o.stability_score;
     d["throttle_flag"] = o.throttle_flag;
-    d["lane"] = std::string(last_lane_name());
-    d["reason"] = std::string(last_reason());
+    d["lane"] = std::string(lane_name(st.lane));
+    d["reason"] = std::string(st.reason);
     return d;
   }, py::arg("state"), py::arg("acceptance"), py::arg("entropy"), py::arg("current_tps") = 0.f,
      py::arg("engine_costs") = 0.f, py::arg("amf_reuse_score") = 0.f, py::arg("amf_avg_prefix_length") = 0.f,
      py::arg("amf_accept_rate") = 0.f, py::arg("amf_restore_cost_ms") = 0.f, py::arg("baseline_ready") = true);
-  m.def("scheduler_reset", [](KorithSchedulerState& st) { korith_scheduler_reset(&st); });
+  m.def("best_depth", &best_depth, py::arg("acceptance"), py::arg("draft_cost"), py::arg("cap"));
 
   py::class_<MemoryFieldState>(m, "MemoryFieldState")
       .def(py::init<>())

@@ -11,22 +11,64 @@ from axropus_deploy_b200._native_loader import native
 n = native()
 
 
-def test_scheduler_warmup_lanes_hysteresis():
+def _run(st, k, acc, ent, reuse=0.0, tps=0.0):
+    o = None
+    for _ in range(k):
+        o = n.schedule_step(st, acc, ent, current_tps=tps, amf_reuse_score=reuse)
+    return o
+
+
+def test_best_depth_follows_the_speedup_model():
+    # expected tokens / cost: a = 0 -> no speculation pays; high a -> deep drafts
+    assert n.best_depth(0.0, 0.08, 16) == 1
+    assert n.best_depth(0.95, 0.08, 16) >= 8
+    assert n.best_depth(0.95, 0.5, 16) < n.best_depth(0.95, 0.05, 16)  # expensive drafts: shallower
+    assert n.best_depth(0.99, 0.01, 4) == 4  # capped
+
+
+def test_scheduler_warmup_and_lane_classification():
     st = n.SchedulerState()
-    o = n.schedule_step(st, 0.95, 0.2, baseline_ready=False)
-    assert o["desired_depth"] == 1 and o["throttle_flag"] == 1 and o["reason"] == "warmup"
-    # first change is blocked by hysteresis (step 1 is within 32 steps of step 0)
-    o = n.schedule_step(st, 0.95, 0.2, amf_reuse_score=0.9)
-    assert o["lane"] == "SPEC_HIT" and o["throttle_flag"] == 3 and o["desired_depth"] == 1
-    for _ in range(40):
-        o = n.schedule_step(st, 0.95, 0.2, amf_reuse_score=0.9)
-    assert o["desired_depth"] > 1 and o["desired_depth"] <= 16
-    # a miss lane forces the depth down immediately (no hysteresis on the way down)
-    o = n.schedule_step(st, 0.3, 0.9)
-    assert o["lane"] == "MISS" and o["desired_depth"] == 2 and o["reason"] == "miss_cap"
-    o = n.schedule_step(st, 0.72, 0.6)
+    o = n.schedule_step(st, 0.95, 0.1, baseline_ready=False)
+    assert o["desired_depth"] == 1 and o["lane"] == "MISS" and o["reason"] == "warmup"
+    # replayed prefix + high quality -> SPEC_HIT, but only after the lane debounce (3 steps)
+    o = n.schedule_step(st, 0.95, 0.1, amf_reuse_score=0.9)
+    assert o["lane"] == "MISS"
+    o = _run(st, 3, 0.95, 0.1, reuse=0.9)
+    assert o["lane"] == "SPEC_HIT" and o["throttle_flag"] == 3
+    # reuse alone -> HIT; a worse lane is taken at once
+    st2 = n.SchedulerState()
+    o = _run(st2, 4, 0.3, 0.8, reuse=0.9)
     assert o["lane"] == "HIT" and o["throttle_flag"] == 2
-    assert 0.0 <= o["stability_score"] <= 1.0
+    o = _run(st2, 10, 0.1, 0.95, reuse=0.0)
+    assert o["lane"] == "MISS" and o["desired_depth"] <= 3
+
+
+def test_scheduler_hysteresis_up_slow_down_fast():
+    st = n.SchedulerState()
+    _run(st, 5, 0.95, 0.1, reuse=0.9)
+    d0 = st.depth
+    # increases wait hold_up_steps (24) between them and move by at most 2
+    depths = [n.schedule_step(st, 0.95, 0.1, amf_reuse_score=0.9)["desired_depth"] for _ in range(100)]
+    ups = [b - a for a, b in zip([d0] + depths, depths) if b > a]
+    assert ups and max(ups) <= 2
+    change_steps = [i for i in range(1, len(depths)) if depths[i] != depths[i - 1]]
+    assert all(b - a >= 24 for a, b in zip(change_steps, change_steps[1:]))
+    top = depths[-1]
+    assert top > 4
+    # a collapse of acceptance lowers the depth on the next steps without waiting
+    o = n.schedule_step(st, 0.0, 1.0)
+    assert o["desired_depth"] < top and o["reason"] in ("down", "miss_down")
+    o = _run(st, 3, 0.0, 1.0)
+    assert o["desired_depth"] <= 3
+
+
+def test_scheduler_starvation_probe_and_periodic_probe():
+    st = n.SchedulerState()
+    reasons = [n.schedule_step(st, 0.55, 0.7)["reason"] for _ in range(200)]
+    assert "starvation_probe" in reasons  # MISS lane with usable acceptance: a deeper draft is measured again
+    st = n.SchedulerState()
+    reasons = [n.schedule_step(st, 0.0, 1.0)["reason"] for _ in range(100)]
+    assert "probe" in reasons and "starvation_probe" not in reasons  # no usable acceptance: only the depth-1 probe
 
 
 def test_scheduler_c_abi():
@@ -44,41 +86,79 @@ def test_scheduler_c_abi():
         _fields_ = [("desired_depth", ctypes.c_int), ("stability_score", ctypes.c_float),
                     ("throttle_flag", ctypes.c_int)]
 
+    lib.korith_scheduler_reset.argtypes = []
+    lib.korith_scheduler_reset()
     f = lib.korith_schedule_step
     f.restype = Out
     f.argtypes = [ctypes.POINTER(St), ctypes.POINTER(In)]
     st = St(1, 0, 0)
-    for _ in range(40):
-        out = f(ctypes.byref(st), ctypes.byref(In(0.95, 0.2, 0, 0, 0.9, 0, 0, 0, 1)))
+    for _ in range(80):
+        out = f(ctypes.byref(st), ctypes.byref(In(0.95, 0.1, 0, 0, 0.9, 0, 0, 0, 1)))
     assert out.throttle_flag == 3 and out.desired_depth > 1 and st.speculative_depth == out.desired_depth
-    lib.korith_scheduler_reset(ctypes.byref(st))
-    assert (st.speculative_depth, st.batch_size, st.baseline_ready) == (1, 0, 0)
+    assert st.batch_size == 256 // (out.desired_depth + 1) and st.baseline_ready == 1
+    upd = lib.korith_scheduler_update
+    upd.restype = ctypes.c_uint
+    upd.argtypes = [ctypes.c_float, ctypes.c_float, ctypes.c_float]
+    assert upd(0.2, 0.9, 0.0) >= 1
+    lib.korith_scheduler_reset()
+    # handle API: independent states
+    lib.korith_scheduler_create.restype = ctypes.c_void_p
+    lib.korith_scheduler_step_ex.restype = Out
+    lib.korith_scheduler_step_ex.argtypes = [ctypes.c_void_p, ctypes.POINTER(In)]
+    lib.korith_scheduler_destroy.argtypes = [ctypes.c_void_p]
+    h1, h2 = lib.korith_scheduler_create(), lib.korith_scheduler_create()
+    for _ in range(60):
+        a = lib.korith_scheduler_step_ex(h1, ctypes.byref(In(0.95, 0.1, 0, 0, 0.9, 0, 0, 0, 1)))
+        b = lib.korith_scheduler_step_ex(h2, ctypes.byref(In(0.05, 0.95, 0, 0, 0.0, 0, 0, 0, 1)))
+    assert a.desired_depth > b.desired_depth and a.throttle_flag == 3 and b.throttle_flag == 1
+    lib.korith_scheduler_destroy(h1)
+    lib.korith_scheduler_destroy(h2)
 
 
-def test_memory_field_policy_and_snapshot():
+def _mf(st, now, **kw):
+    d = {"now_ms": now, "max_bytes": 1000, "bytes": kw.pop("bytes", 100)}
+    d.update(kw)
+    return n.memory_field_update(st, d)
+
+
+def test_memory_field_fill_drives_bar_and_pressure_with_slew():
     st = n.MemoryFieldState()
-    base = {"now_ms": 1000, "max_bytes": 1000, "bytes": 100}
-    n.memory_field_update(st, base)
-    # bad ROI window with hits -> replay disabled with a cooldown, admission bar raised
-    o = n.memory_field_update(st, dict(base, now_ms=1200, hits=4, misses=1, ms_saved=10, restore_ms=100))
-    assert o["replay_disable_mask"] == 1 and o["cooldown_ms"] >= 2000 and o["min_admit_roi"] >= 1.0
-    # high pressure -> eviction pressure rises by at most 0.5 per update
-    o2 = n.memory_field_update(st, dict(base, now_ms=1400, bytes=990, hits=4, misses=1, ms_saved=10, restore_ms=100))
-    assert o2["eviction_pressure"] <= o["eviction_pressure"] + 0.5 + 1e-9
+    o = _mf(st, 0)
+    assert o["min_admit_roi"] == 0.0 and o["eviction_pressure"] == pytest.approx(0.75)
+    outs = [_mf(st, 200 * (i + 1), bytes=990) for i in range(12)]
+    steps = [b["eviction_pressure"] - a["eviction_pressure"] for a, b in zip([o] + outs, outs)]
+    assert max(steps) <= 0.25 + 1e-9 and outs[-1]["eviction_pressure"] > 2.9
+    assert outs[-1]["min_admit_roi"] == pytest.approx(5.0 * (0.99 - 0.6), abs=1e-6)
+    assert max(b["min_admit_roi"] - a["min_admit_roi"] for a, b in zip([o] + outs, outs)) <= 0.5 + 1e-9
+
+
+def test_memory_field_replay_gate_and_backoff():
+    st = n.MemoryFieldState()
+    _mf(st, 0)
+    # restores that cost 10x what they save, with hits: replay off, 2 s cooldown
+    o = _mf(st, 200, hits=4, misses=1, ms_saved=10, restore_ms=100)
+    assert o["replay_disable_mask"] == 1 and 0 < o["cooldown_ms"] <= 2000
+    assert _mf(st, 1200, hits=4, misses=1, ms_saved=10, restore_ms=100)["replay_disable_mask"] == 1
+    # cooldown over: probation (replay on again, ROI measured afresh)
+    o = _mf(st, 2300, hits=4, misses=1, ms_saved=10, restore_ms=100)
+    assert o["replay_disable_mask"] == 0 and o["cooldown_ms"] == 0
+    # still bad: off again within 60 s -> the cooldown doubles (anti-oscillation)
+    o = _mf(st, 2500, hits=8, misses=2, ms_saved=20, restore_ms=200)
+    assert o["replay_disable_mask"] == 1 and 2000 < o["cooldown_ms"] <= 4000
     js = st.to_json()
     st2 = n.MemoryFieldState()
     assert st2.from_json(js) and st2.last == st.last
-    assert json.loads(js)["cooldown_ms"] <= 60000
+    assert json.loads(js)["backoff"] == 1
     assert not n.MemoryFieldState().from_json("{}")
 
 
 def test_memory_field_cadence():
     st = n.MemoryFieldState()
-    first = n.memory_field_update(st, {"now_ms": 0})
-    a = n.memory_field_update(st, {"now_ms": 10, "max_bytes": 100, "bytes": 99})  # too soon: unchanged
-    assert a == first
-    n.memory_field_update(st, {"now_ms": 20, "max_bytes": 100, "bytes": 99})
-    b = n.memory_field_update(st, {"now_ms": 30, "max_bytes": 100, "bytes": 99})  # after 2 skipped requests
+    first = _mf(st, 0)
+    assert _mf(st, 10, bytes=990) == first  # too soon and too few requests: unchanged
+    _mf(st, 20, bytes=990)
+    _mf(st, 30, bytes=990)
+    b = _mf(st, 40, bytes=990)  # fourth request since the last update
     assert b["eviction_pressure"] > first["eviction_pressure"]
 
 

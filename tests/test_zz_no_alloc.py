@@ -1,8 +1,9 @@
 """GPU test of the allocation-free decode entry point, called through its exported
-C symbol ``axr_decode_attention_noalloc`` (ctypes), for callers that cannot allocate
-device memory at call time. Its output must match the regular decode_attention
-entry point (which uses a caller-provided scratch buffer) on two calls in a row.
-This file is named to be collected last."""
+C symbol ``axr_decode_attention_noalloc`` (ctypes; declared in
+csrc/kernels/decode_attn_noalloc.h), for callers that cannot allocate device memory at
+call time. Its output must match the regular decode_attention entry point (which uses a
+caller-provided scratch buffer) and the fp32 CPU oracle, on two calls in a row. This
+file is named to be collected last."""
 import ctypes
 
 import pytest
@@ -47,19 +48,40 @@ def _noalloc(lib, cache, bt, sl, q, splits, max_pages):
     return rc, out
 
 
+def _oracle(cache, bt, sl, q):
+    """fp32 CPU reference of the same attention (the ops' PyTorch path on CPU tensors)."""
+    from axropus_deploy_b200.ops import KVCache, decode_attention
+
+    c = KVCache(1, cache.num_blocks, cache.num_kv_heads, 128, "bf16", "cpu")
+    c.data.copy_(cache.data.cpu())
+    return decode_attention(q.cpu(), c, 0, bt.cpu(), sl.cpu())
+
+
 def test_noalloc_matches_decode_attention_two_calls():
     from axropus_deploy_b200.ops import decode_attention
 
     lib = _lib()
-    cases = [(11, 3, 2, 4, 9, [1, 77, 144]), (12, 4, 2, 4, 6, [96, 5, 33, 90])]
-    for seed, B, Hkv, G, pages, seq in cases:
+    # the last case: every sequence fills its table row exactly (seq_len == max_pages * 16)
+    # and 4 splits do not divide the 9 pages
+    cases = [(11, 3, 2, 4, 9, [1, 77, 144], (3, 1)), (12, 4, 2, 4, 6, [96, 5, 33, 90], (3, 1)),
+             (14, 2, 2, 4, 9, [144, 144], (4, 2))]
+    for seed, B, Hkv, G, pages, seq, split_list in cases:
         cache, bt, sl, q = _case(seed, B, Hkv, G, pages, seq)
-        for splits in (3, 1):
+        ref = _oracle(cache, bt, sl, q)
+        for splits in split_list:
             rc, got = _noalloc(lib, cache, bt, sl, q, splits, pages)
             assert rc == 0, lib.axr_decode_noalloc_last_error()
             want = decode_attention(q, cache, 0, bt, sl, num_splits=splits, max_seq_len=pages * 16)
             torch.cuda.synchronize()
             torch.testing.assert_close(got.float(), want.float(), atol=2e-2, rtol=2e-2)
+            torch.testing.assert_close(got.float().cpu(), ref.float(), atol=2e-2, rtol=2e-2)
+
+
+def test_noalloc_rejects_table_overrun():
+    lib = _lib()
+    cache, bt, sl, q = _case(15, 2, 2, 4, 4, [60, 64])
+    rc, _ = _noalloc(lib, cache, bt, sl, q, 2, 5)  # max_pages beyond the table row (bt_stride 4)
+    assert rc == 3 and b"invalid" in lib.axr_decode_noalloc_last_error()
 
 
 def test_noalloc_rejects_oversize():
