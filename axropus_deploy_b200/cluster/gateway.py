@@ -87,12 +87,32 @@ def authenticate(headers, ledger) -> Dict[str, Any]:
             "rpm": int(rec["rate_limit_rpm"]), "tpm": int(rec["rate_limit_tpm"])}
 
 
+# Atomic check-and-consume of one request and its tokens in a 60-second window. KEYS:
+# request counter, token counter; ARGV: request cap, token cap, tokens, TTL seconds.
+# Returns {1, 0} when consumed, {0, 1} over the request cap, {0, 2} over the token cap;
+# a refusal changes nothing. Redis runs a script atomically, so no other gateway can
+# interleave between the check and the increments, and the TTL is set in the same step.
+RATE_LIMIT_LUA = """
+local r = tonumber(redis.call('GET', KEYS[1]) or '0')
+local t = tonumber(redis.call('GET', KEYS[2]) or '0')
+if r + 1 > tonumber(ARGV[1]) then return {0, 1} end
+if t + tonumber(ARGV[3]) > tonumber(ARGV[2]) then return {0, 2} end
+redis.call('INCRBY', KEYS[1], 1)
+redis.call('EXPIRE', KEYS[1], ARGV[4])
+redis.call('INCRBY', KEYS[2], ARGV[3])
+redis.call('EXPIRE', KEYS[2], ARGV[4])
+return {1, 0}
+"""
+
+
 class RateLimiter:
     """Requests and tokens per organisation in 60-second windows: in memory, in SQLite
     (``KORITH_RATE_LIMIT_DB``), or in Redis (``KORITH_RATE_LIMIT_BACKEND=redis`` with
     ``KORITH_REDIS_URL``), where every gateway of a deployment shares one budget: counters
-    ``korith:rl:{req,tok}:<org>:<window>`` are incremented, and rolled back when the request
-    is refused so that refusals do not use up the quota."""
+    ``korith:rl:{req,tok}:<org>:<window>`` are checked and consumed by one atomic script
+    (:data:`RATE_LIMIT_LUA`; refusals use no quota). The script is sent at most once per
+    request: if the connection drops mid-call the request is decided by this gateway's
+    in-memory window instead, so quota is never spent twice."""
 
     def __init__(self, db_path: Optional[str] = None, burst_factor: Optional[float] = None,
                  redis_url: Optional[str] = None):
@@ -122,16 +142,16 @@ class RateLimiter:
         rcap, tcap = max(1, int(rpm * self.burst)), max(1, int(tpm * self.burst))
         if self._redis is not None:
             rk, tk = f"korith:rl:req:{org_id}:{win}", f"korith:rl:tok:{org_id}:{win}"
-            if int(self._redis.call("INCRBY", rk, 1)) > rcap:
-                self._redis.call("DECRBY", rk, 1)
-                return {"allowed": False, "reason": "rpm_exceeded", "retry_after": 60 - t % 60}
-            self._redis.call("EXPIRE", rk, 180)
-            if int(self._redis.call("INCRBY", tk, int(tokens))) > tcap:
-                self._redis.call("DECRBY", tk, int(tokens))
-                self._redis.call("DECRBY", rk, 1)
-                return {"allowed": False, "reason": "tpm_exceeded", "retry_after": 60 - t % 60}
-            self._redis.call("EXPIRE", tk, 180)
-            return {"allowed": True, "reason": "ok"}
+            try:
+                ok, why = self._redis.call("EVAL", RATE_LIMIT_LUA, 2, rk, tk, rcap, tcap, int(tokens), 180,
+                                           retry=False)
+            except (ConnectionError, OSError):
+                ok = None  # Redis unreachable: this gateway's own window decides
+            if ok is not None:
+                if int(ok):
+                    return {"allowed": True, "reason": "ok"}
+                return {"allowed": False, "reason": "rpm_exceeded" if int(why) == 1 else "tpm_exceeded",
+                        "retry_after": 60 - t % 60}
         with self._mu:
             if self._db is not None:
                 self._db.execute("DELETE FROM rate_limit_windows WHERE window_epoch < ?", (win - 120,))

@@ -45,7 +45,10 @@ class RedisError(RuntimeError):
 class RespClient:
     """Minimal Redis client: one socket, RESP2 requests as arrays of bulk strings, replies
     parsed into str / bytes / int / list / None. ``redis://[user:password@]host:port/db``.
-    A dropped connection is reopened once per call."""
+    A dropped connection is reopened and the call retried once, unless the call is
+    marked non-idempotent (``retry=False``): a command the server may already have
+    applied before the connection dropped (INCRBY, a script that writes) is then not
+    sent twice; the error reaches the caller instead."""
 
     def __init__(self, url: str = "redis://127.0.0.1:6379/0", timeout_s: float = 10.0):
         u = urllib.parse.urlsplit(url)
@@ -110,18 +113,20 @@ class RespClient:
             raise r
         return r
 
-    def call(self, *args) -> Any:
+    def call(self, *args, retry: bool = True) -> Any:
         with self._mu:
             for attempt in (0, 1):
+                sent = False
                 try:
                     if self._sock is None:
                         self._connect()
+                    sent = True
                     return self._call_locked(*args)
                 except (ConnectionError, OSError):
                     if self._sock is not None:
                         self._sock.close()
                     self._sock = None
-                    if attempt:
+                    if attempt or (sent and not retry):
                         raise
 
 

@@ -153,6 +153,21 @@ class _FakeRedis:
             return n
         if cmd == "EXPIRE":
             return 1
+        if cmd == "EVAL":
+            # no Lua here: the fake knows the one script the gateway sends and runs its
+            # semantics (check both windows, then consume) under the server lock
+            from axropus_deploy_b200.cluster.gateway import RATE_LIMIT_LUA
+
+            if a[0] != RATE_LIMIT_LUA:
+                return Exception("ERR unknown script")
+            rk, tk, rcap, tcap, toks = a[2], a[3], int(a[4]), int(a[5]), int(a[6])
+            r, t = int(kv.get(rk, 0)), int(kv.get(tk, 0))
+            if r + 1 > rcap:
+                return [0, 1]
+            if t + toks > tcap:
+                return [0, 2]
+            kv[rk], kv[tk] = r + 1, t + toks
+            return [1, 0]
         return Exception(f"ERR unknown command {cmd}")
 
     @staticmethod
@@ -632,3 +647,26 @@ def test_gateway_rate_limit_shared_in_redis(redis_url, monkeypatch):
     r = g1.check_and_consume("beta", 200, rpm=10, tpm=1000, now=now)
     assert not r["allowed"] and r["reason"] == "tpm_exceeded"
     assert g2.check_and_consume("beta", 100, rpm=10, tpm=1000, now=now)["allowed"]  # the refusal used no quota
+
+
+def test_resp_client_does_not_resend_non_idempotent_calls():
+    from axropus_deploy_b200.cluster import netqueues as nq2
+
+    c = nq2.RespClient("redis://127.0.0.1:1/0")
+    sent = []
+
+    def fake_connect():
+        c._sock = type("S", (), {"close": lambda self: None})()
+
+    def fake_call(*args):
+        sent.append(args)
+        raise ConnectionError("dropped after send")
+
+    c._connect, c._call_locked = fake_connect, fake_call
+    with pytest.raises(ConnectionError):
+        c.call("INCRBY", "k", 1, retry=False)
+    assert len(sent) == 1  # not sent a second time
+    sent.clear()
+    with pytest.raises(ConnectionError):
+        c.call("GET", "k")
+    assert len(sent) == 2  # idempotent: retried once
