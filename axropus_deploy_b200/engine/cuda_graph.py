@@ -16,7 +16,7 @@ from typing import Dict, List
 import torch
 
 from ..models.llama import AttnMeta
-from ..ops.attention import DecodeWorkspace, decode_num_splits
+from ..ops.attention import CascadeMeta, DecodeWorkspace, cascade_num_splits, decode_num_splits
 
 BUCKETS = [1, 2, 4, 8, 12, 16, 24, 32, 48, 64, 96, 128, 192, 256]
 
@@ -40,20 +40,67 @@ class DecodeGraphRunner:
         self.max_seq = engine.cfg.max_model_len
         self.splits: Dict[int, int] = {}
         self.kernels: Dict[int, int] = {}
+        # shared-prefix decode: every graph carries the grouped pass; a step without groups
+        # replays it with zero groups (its CTAs return at once)
+        self.cascade = bool(getattr(engine, "_cascade_on", False))
+        self.ng_max = max(1, self.max_b // 2)
+        self.cints = torch.zeros(3, self.max_b, dtype=torch.int32, device=dev)  # q_index, row_of, page_start
+        self.cgrp = torch.zeros(2, self.ng_max + 1, dtype=torch.int32, device=dev)  # cu_q, shared lengths
+        self.cbt = torch.zeros(self.ng_max, mb, dtype=torch.int32, device=dev)
+        self.chost = torch.zeros(3, self.max_b, dtype=torch.int32).pin_memory()
+        self.cgrp_host = torch.zeros(2, self.ng_max + 1, dtype=torch.int32).pin_memory()
+        self.cplan = ()  # identity of the plan in the cascade buffers
+        self.csplits: Dict[int, int] = {}
+
+    def _cascade(self, b: int):
+        if not self.cascade:
+            return None
+        ng = max(1, b // 2)
+        return CascadeMeta(q_index=self.cints[0, :b], cu_q=self.cgrp[0, :ng + 1], seq_lens=self.cgrp[1, :ng],
+                           block_table=self.cbt[:ng], row_of=self.cints[1, :b], page_start=self.cints[2, :b],
+                           max_q=b, num_splits=self.csplits[b])
 
     def _meta(self, b: int) -> AttnMeta:
         return AttnMeta(mode="decode", positions=self.ints[1, :b], slots=self.ints[2, :b], block_table=self.bt[:b],
-                        seq_lens=self.ints[3, :b], max_seq_len=self.max_seq, num_splits=self.splits[b])
+                        seq_lens=self.ints[3, :b], max_seq_len=self.max_seq, num_splits=self.splits[b],
+                        cascade=self._cascade(b))
+
+    def _load_plan(self, plan, n: int) -> None:
+        """Cascade buffers for this batch: the plan's groups, or none (row_of = -1)."""
+        ident = (plan["serial"] if plan is not None else 0, n)
+        if self.cplan == ident:
+            return
+        h, hg = self.chost, self.cgrp_host
+        h.zero_()
+        hg.zero_()
+        h[1].fill_(-1)
+        if plan is not None:
+            R, ng = len(plan["q_index"]), len(plan["seq_lens"])
+            h[0, :R] = torch.tensor(plan["q_index"], dtype=torch.int32)
+            h[1, :n] = torch.tensor(plan["row_of"], dtype=torch.int32)
+            h[2, :n] = torch.tensor(plan["page_start"], dtype=torch.int32)
+            hg[0, :ng + 1] = torch.tensor(plan["cu_q"], dtype=torch.int32)
+            hg[0, ng + 1:] = plan["cu_q"][-1]
+            hg[1, :ng] = torch.tensor(plan["seq_lens"], dtype=torch.int32)
+            rows = torch.tensor(plan["bt_rows"], dtype=torch.long, device=self.cbt.device)
+            self.cbt[:ng] = self.eng.block_table.index_select(0, rows)
+        self.cints.copy_(h, non_blocking=True)
+        self.cgrp.copy_(hg, non_blocking=True)
+        self.cplan = ident
 
     def _capture(self, b: int) -> None:
         eng = self.eng
         cache = eng.cache
         self.splits[b] = decode_num_splits(b, cache.num_kv_heads, (self.max_seq + 15) // 16, eng.device, cache.fmt)
+        self.csplits[b] = cascade_num_splits(max(1, b // 6), cache.num_kv_heads, self.max_seq, eng.device)
         # pre-size the split scratch for the largest bucket so every graph shares it
         from ..ops import attention as att
 
         D, Hq = eng.model.cfg.head_dim, getattr(eng.model, "hq", eng.model.cfg.num_heads)
         self.ws.get(self.max_b, Hq, max(self.splits[b], 64), D, eng.device)
+        if self.cascade:
+            att._CASCADE_WS.get(self.max_b, Hq, 16, D, eng.device)
+            self._load_plan(None, b)
         prev = att._WS
         att._WS = self.ws
         try:
@@ -80,11 +127,14 @@ class DecodeGraphRunner:
         self.graphs[b] = g
         self.outs[b] = out
 
-    def run(self, reqs, toks: List[int], pos: List[int], slots: List[int], lens: List[int]) -> torch.Tensor:
+    def run(self, reqs, toks: List[int], pos: List[int], slots: List[int], lens: List[int],
+            plan=None) -> torch.Tensor:
         n = len(reqs)
         b = self.buckets[bisect.bisect_left(self.buckets, n)]
         if b not in self.graphs:
             self._capture(b)
+        if self.cascade:
+            self._load_plan(plan, n)
         h = self.host
         h[0, :n] = torch.tensor(toks, dtype=torch.int32)
         h[1, :n] = torch.tensor(pos, dtype=torch.int32)

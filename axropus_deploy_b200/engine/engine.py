@@ -102,6 +102,10 @@ class EngineConfig:
     spec_max_depth: int = 8
     # [AMF_*] trace lines (None: KORITH_AMF_TRACE decides)
     trace: Optional[bool] = None
+    # shared-prefix decode: running sequences whose block tables start with the same
+    # (prefix-cache / AMF-restored) pages read those pages once per step for the whole
+    # group; groups need at least this many shared pages (0 turns it off)
+    cascade_min_pages: int = 32
 
 
 _NVTX = os.environ.get("AXR_NVTX", "0") == "1"
@@ -178,7 +182,15 @@ class LLMEngine:
                 raise ValueError(f"unknown spec mode {cfg.spec!r}")
             self.spec = SpecDecoder(self, cfg.spec_max_depth, drafter)
         self.stat = {"steps": 0, "prefill_tokens": 0, "decode_tokens": 0, "restored_tokens": 0,
-                     "local_cached_tokens": 0, "cold_prefill_tokens": 0}
+                     "local_cached_tokens": 0, "cold_prefill_tokens": 0, "cascade_steps": 0,
+                     "cascade_grouped_seqs": 0}
+        from ..ops.attention import cascade_supported
+
+        self._cascade_on = (cfg.cascade_min_pages > 0 and self.device.type == "cuda" and
+                            cascade_supported(self.cache, mc.head_dim) and type(model) is LlamaModel)
+        self._casc_key = None
+        self._casc_plan = None
+        self._casc_serial = itertools.count(1)
 
     # ------------------------------------------------------------------ API
     def add_request(self, prompt: Sequence[int], params: Optional[SamplingParams] = None, req_id: Optional[str] = None,
@@ -439,7 +451,7 @@ class LLMEngine:
         out = ops.argmax(logits).tolist()
         for i, r in enumerate(reqs):
             if r.params.temperature > 0:
-                p = torch.softmax(logits[i] / r.params.temperature, dim=-1)
+                p = torch.softmax(logits[i].float() / r.params.temperature, dim=-1)
                 g = torch.Generator(device=p.device)
                 g.manual_seed((r.params.seed or 0) + len(r.output))
                 out[i] = int(torch.multinomial(p, 1, generator=g))
@@ -563,18 +575,66 @@ class LLMEngine:
             lens.append(p + 1)
         return toks, pos, slots, lens
 
+    def cascade_plan(self, reqs: List[Request]) -> Optional[dict]:
+        """Shared-prefix groups of a decode batch (host arrays), or None. Recomputed only
+        when the batch changes: shared pages are full prompt pages, which never change."""
+        if not self._cascade_on:
+            return None
+        key = tuple(id(r) for r in reqs)
+        if key == self._casc_key:
+            return self._casc_plan
+        from ..ops.attention import cascade_groups
+
+        groups = cascade_groups([r.blocks for r in reqs], self.cfg.cascade_min_pages,
+                                [len(r.prompt) // PAGE for r in reqs])
+        plan = None
+        if groups:
+            B = len(reqs)
+            q_index, cu, lens, first_rows = [], [0], [], []
+            row_of, page_start = [-1] * B, [0] * B
+            for rows, shared in groups:
+                for i in rows:
+                    row_of[i] = len(q_index)
+                    page_start[i] = shared
+                    q_index.append(i)
+                cu.append(len(q_index))
+                lens.append(shared * PAGE)
+                first_rows.append(reqs[rows[0]].row)
+            plan = {"q_index": q_index, "cu_q": cu, "seq_lens": lens, "bt_rows": first_rows, "row_of": row_of,
+                    "page_start": page_start, "max_q": max(len(g[0]) for g in groups),
+                    "grouped": len(q_index), "serial": next(self._casc_serial)}
+        self._casc_key, self._casc_plan = key, plan
+        return plan
+
+    def _cascade_meta_eager(self, plan: Optional[dict], max_seq_len: int):
+        if plan is None:
+            return None
+        from ..ops.attention import CascadeMeta, cascade_num_splits
+
+        q_index, cu, lens, row_of, ps = self._stage_int32(plan["q_index"], plan["cu_q"], plan["seq_lens"],
+                                                         plan["row_of"], plan["page_start"])
+        rows = torch.tensor(plan["bt_rows"], dtype=torch.long, device=self.device)
+        ng = len(plan["seq_lens"])
+        return CascadeMeta(q_index, cu, lens, self.block_table.index_select(0, rows), row_of, ps, plan["max_q"],
+                           cascade_num_splits(ng, self.cache.num_kv_heads, max_seq_len, self.device))
+
     def _decode(self, reqs: List[Request]) -> List[Request]:
         if self.spec is not None and all(r.params.temperature <= 0 for r in reqs):
             return self.spec.step(reqs)
         toks, pos, slots, lens = self.decode_meta(reqs)
         self.stat["decode_tokens"] += len(reqs)
+        plan = self.cascade_plan(reqs)
+        if plan is not None:
+            self.stat["cascade_steps"] += 1
+            self.stat["cascade_grouped_seqs"] += plan["grouped"]
         if self._graphs is not None:
-            logits = self._graphs.run(reqs, toks, pos, slots, lens)
+            logits = self._graphs.run(reqs, toks, pos, slots, lens, plan)
         else:
+            casc = self._cascade_meta_eager(plan, max(lens))
             d_toks, d_pos, d_slots, d_lens, d_rows = self._stage_int32(toks, pos, slots, lens, [r.row for r in reqs])
             meta = AttnMeta(mode="decode", positions=d_pos, slots=d_slots,
                             block_table=self.block_table.index_select(0, d_rows.long()), seq_lens=d_lens,
-                            max_seq_len=max(lens))
+                            max_seq_len=max(lens), cascade=casc)
             logits = self.model.forward(d_toks, meta, self.cache)
         new = self._sample(logits, reqs)
         done: List[Request] = []

@@ -1,10 +1,14 @@
 """Llama-3 / Mixtral decoder with a paged KV cache.
 
-Weights are random-initialised at the real shapes (no checkpoints on these boxes).
-Projections are fused (QKV, gate/up) and stored ``[in, out]``; the dense GEMMs are
-library GEMMs (cuBLAS through torch.matmul), everything around them runs the
-framework's kernels: fused residual RMSNorm, RoPE + paged KV write, paged prefill /
-split-KV decode attention reading bf16/FP8/INT4 pages, SwiGLU, greedy argmax.
+Weights are random-initialised at the real shapes, or loaded from a checkpoint
+(``models/loader.py``). Projections are fused (QKV, gate/up) and stored ``[out, in]``
+(the layout of Hugging Face checkpoints and of the TMA loads). Every projection runs the
+framework's tcgen05 kernels (``ops/dense.py``) with the following element-wise step in
+its epilogue: RoPE + paged KV write after QKV (bf16 cache), the residual add after the
+o and down projections (the residual stream is updated in place), SwiGLU after gate/up.
+Around them: RMSNorm, paged prefill / split-KV decode attention reading bf16/FP8/INT4
+pages, greedy argmax. The gate/up rows are interleaved in groups of 64 (see
+``ops.dense.interleave_gate_up``).
 """
 from __future__ import annotations
 
@@ -15,6 +19,7 @@ from typing import List, Optional
 import torch
 
 from .. import ops
+from ..ops import dense
 from ..ops.kvcache import KVCache
 from ..parallel.ep import EpMoE, experts_reference, route
 from .config import ModelConfig
@@ -23,12 +28,12 @@ from .config import ModelConfig
 @dataclass
 class LayerWeights:
     attn_norm: torch.Tensor
-    wqkv: torch.Tensor
-    wo: torch.Tensor
+    wqkv: torch.Tensor                        # [Q + 2 KV, H]
+    wo: torch.Tensor                          # [H, Q]
     mlp_norm: torch.Tensor
-    w_gate_up: Optional[torch.Tensor] = None  # dense MLP [H, 2F]
-    w_down: Optional[torch.Tensor] = None     # [F, H]
-    w_router: Optional[torch.Tensor] = None   # MoE [H, E]
+    w_gate_up: Optional[torch.Tensor] = None  # dense MLP [2F, H], gate/up interleaved by 64 rows
+    w_down: Optional[torch.Tensor] = None     # [H, F]
+    w_router: Optional[torch.Tensor] = None   # MoE [E, H]
     w13: Optional[torch.Tensor] = None        # this GPU's experts [E_l, 2F, H], gate/up interleaved per 128 rows
     w2: Optional[torch.Tensor] = None         # [E_l, H, F]
 
@@ -47,6 +52,7 @@ class AttnMeta:
     max_seq_len: int = 0
     logits_idx: Optional[torch.Tensor] = None  # [B] rows of the hidden state to sample
     num_splits: Optional[int] = None
+    cascade: Optional[object] = None  # ops.attention.CascadeMeta: shared-prefix decode
 
 
 class LlamaModel:
@@ -82,18 +88,18 @@ class LlamaModel:
         self.embed = rnd(cfg.vocab, H, std=1.0)
         self.layers: List[LayerWeights] = []
         for _ in range(n_layers):
-            lw = LayerWeights(ones(H), rnd(H, cfg.q_size + 2 * cfg.kv_size), rnd(cfg.q_size, H), ones(H))
+            lw = LayerWeights(ones(H), rnd(cfg.q_size + 2 * cfg.kv_size, H), rnd(H, cfg.q_size), ones(H))
             if cfg.is_moe:
                 E_l = cfg.num_experts // ep_world
-                lw.w_router = rnd(H, cfg.num_experts)
+                lw.w_router = rnd(cfg.num_experts, H)
                 lw.w13 = rnd_g(g_exp, E_l, 2 * F, H)
                 lw.w2 = rnd_g(g_exp, E_l, H, F)
             else:
-                lw.w_gate_up = rnd(H, 2 * F)
-                lw.w_down = rnd(F, H)
+                lw.w_gate_up = rnd(2 * F, H)  # i.i.d. rows: already "interleaved"
+                lw.w_down = rnd(H, F)
             self.layers.append(lw)
         self.final_norm = ones(H)
-        self.lm_head = rnd(H, cfg.vocab)
+        self.lm_head = rnd(cfg.vocab, H)
         self.cos_sin = ops.rope_cos_sin(min(cfg.max_position, 1 << 17), cfg.head_dim, cfg.rope_theta,
                                         cfg.rope_scaling, self.device)
         self.scale = 1.0 / math.sqrt(cfg.head_dim)
@@ -104,6 +110,17 @@ class LlamaModel:
 
                 info = ep_info or DistInfo(0, 1, 0, 1, self.device)
                 self.ep = EpMoE(info, cfg.num_experts, H, F, cfg.top_k, ep_max_tokens)
+        dense.reserve(self.device, self.dense_shapes())
+
+    def dense_shapes(self):
+        """(N, K) of every projection (sizes the split-K scratch of the dense kernels)."""
+        cfg = self.cfg
+        shapes = [(cfg.q_size + 2 * cfg.kv_size, cfg.hidden), (cfg.hidden, cfg.q_size), (cfg.vocab, cfg.hidden)]
+        if cfg.is_moe:
+            shapes.append((cfg.num_experts, cfg.hidden))
+        else:
+            shapes += [(2 * cfg.ffn, cfg.hidden), (cfg.hidden, cfg.ffn)]
+        return shapes
 
     def ep_any(self, flags):
         """Element-wise OR of small flags over the expert-parallel group (lockstep steps)."""
@@ -142,21 +159,28 @@ class LlamaModel:
         return n * 2
 
     # ------------------------------------------------------------------ MLPs
-    def _mlp(self, lw: LayerWeights, x: torch.Tensor) -> torch.Tensor:
-        if lw.w_gate_up is not None:
-            return ops.silu_mul(x @ lw.w_gate_up) @ lw.w_down
-        return self._moe(lw, x)
-
     def _moe(self, lw: LayerWeights, x: torch.Tensor) -> torch.Tensor:
         cfg = self.cfg
-        idx, w = route(x @ lw.w_router, cfg.top_k)
+        idx, w = route(dense.linear(x, lw.w_router), cfg.top_k)
         if self.ep is not None:
             return self.ep.forward(x, idx, w, lw.w13, lw.w2)
         return experts_reference(x, idx, w, lw.w13, lw.w2, self.expert0).to(x.dtype)
 
+    def _qkv(self, li: int, lw: LayerWeights, x: torch.Tensor, meta: AttnMeta, cache: KVCache) -> torch.Tensor:
+        """QKV projection + RoPE + paged KV write -> rotated q [T, Hq, D]."""
+        cfg = self.cfg
+        T = x.shape[0]
+        if cache.fmt == 0 and cfg.head_dim == 128:
+            q = dense.linear(x, lw.wqkv, "rope", rope=(meta.positions, meta.slots, self.cos_sin, cache, li,
+                                                       cfg.num_heads, cfg.num_kv_heads))
+            return q.view(T, cfg.num_heads, cfg.head_dim)
+        qkv = dense.linear(x, lw.wqkv)
+        return ops.rope_kv_write(qkv, meta.positions, meta.slots, self.cos_sin, cache, li, cfg.num_heads,
+                                 cfg.num_kv_heads)
+
     # ------------------------------------------------------------------ forward
     def forward(self, tokens: torch.Tensor, meta: AttnMeta, cache: KVCache) -> torch.Tensor:
-        """tokens [T] -> logits of the rows in ``meta.logits_idx`` ([B, vocab], fp32 on GPU)."""
+        """tokens [T] -> logits of the rows in ``meta.logits_idx`` ([B, vocab], bf16)."""
         cfg = self.cfg
         T = tokens.shape[0]
         if T == 0:
@@ -168,28 +192,34 @@ class LlamaModel:
                 w = torch.empty(0, cfg.top_k, dtype=torch.float32, device=self.device)
                 for lw in self.layers:
                     self.ep.forward(x, idx, w, lw.w13, lw.w2)
-            return torch.empty(0, cfg.vocab, dtype=torch.float32, device=self.device)
+            return torch.empty(0, cfg.vocab, dtype=self.dtype, device=self.device)
         self._check_positions(meta)
-        h = self.embed[tokens.long()]
-        residual = h.clone()
-        x = ops.rmsnorm(h, self.layers[0].attn_norm if self.layers else self.final_norm, cfg.rms_eps)
+        residual = self.embed[tokens.long()]  # the residual stream, updated in place by the o / down epilogues
+        pending = None  # MoE output not yet added to the residual stream
         for li, lw in enumerate(self.layers):
-            if li > 0:
-                x = ops.rmsnorm(h, lw.attn_norm, cfg.rms_eps, residual=residual)
-            qkv = x @ lw.wqkv
-            q = ops.rope_kv_write(qkv, meta.positions, meta.slots, self.cos_sin, cache, li, cfg.num_heads,
-                                  cfg.num_kv_heads)
+            if pending is None:
+                x = ops.rmsnorm(residual, lw.attn_norm, cfg.rms_eps)
+            else:
+                x = ops.rmsnorm(pending, lw.attn_norm, cfg.rms_eps, residual=residual)
+            q = self._qkv(li, lw, x, meta, cache)
             if meta.mode == "decode":
                 a = ops.decode_attention(q, cache, li, meta.block_table, meta.seq_lens, self.scale,
-                                         max_seq_len=meta.max_seq_len, num_splits=meta.num_splits)
+                                         max_seq_len=meta.max_seq_len, num_splits=meta.num_splits,
+                                         cascade=meta.cascade)
             else:
                 a = ops.prefill_attention(q, cache, li, meta.block_table, meta.cu_q, meta.seq_lens, meta.max_q,
                                           self.scale, max_seq_len=meta.max_seq_len)
-            h = a.view(T, cfg.q_size) @ lw.wo
-            x = ops.rmsnorm(h, lw.mlp_norm, cfg.rms_eps, residual=residual)
-            h = self._mlp(lw, x)
-        idx = meta.logits_idx if meta.logits_idx is not None else torch.arange(T, device=tokens.device)
-        hs = h[idx.long()]
-        rs = residual[idx.long()].clone()
-        x = ops.rmsnorm(hs, self.final_norm, cfg.rms_eps, residual=rs)
-        return (x @ self.lm_head).float()
+            dense.linear(a.view(T, cfg.q_size), lw.wo, "resid", out=residual, res=residual)
+            x = ops.rmsnorm(residual, lw.mlp_norm, cfg.rms_eps)
+            if lw.w_gate_up is not None:
+                act = dense.linear(x, lw.w_gate_up, "swiglu")
+                dense.linear(act, lw.w_down, "resid", out=residual, res=residual)
+                pending = None
+            else:
+                pending = self._moe(lw, x)
+        idx = (meta.logits_idx if meta.logits_idx is not None else torch.arange(T, device=tokens.device)).long()
+        if pending is None:
+            x = ops.rmsnorm(residual[idx], self.final_norm, cfg.rms_eps)
+        else:
+            x = ops.rmsnorm(pending[idx], self.final_norm, cfg.rms_eps, residual=residual[idx].clone())
+        return dense.linear(x, self.lm_head)

@@ -105,20 +105,24 @@ class TpLlamaModel:
         """Take this rank's slices of a dense model's weights (tests compare against it)."""
         cfg, r, D = self.cfg, self.rank, self.cfg.head_dim
         hq, hkv, f = self.hq, self.hkv, self.f
-        Q, KV, Fd = cfg.q_size, cfg.kv_size, cfg.ffn
+        Q, KV = cfg.q_size, cfg.kv_size
         self.embed = m.embed
         self.layers = []
+        from ..ops.dense import split_gate_up
+
         for lw in m.layers:
-            q = lw.wqkv[:, r * hq * D:(r + 1) * hq * D]
-            k = lw.wqkv[:, Q + r * hkv * D:Q + (r + 1) * hkv * D]
-            v = lw.wqkv[:, Q + KV + r * hkv * D:Q + KV + (r + 1) * hkv * D]
-            wqkv = torch.cat([q, k, v], dim=1).t().contiguous()
-            wo = lw.wo[r * hq * D:(r + 1) * hq * D].t().contiguous()
-            gu = torch.cat([lw.w_gate_up[:, r * f:(r + 1) * f], lw.w_gate_up[:, Fd + r * f:Fd + (r + 1) * f]], dim=1)
-            down = lw.w_down[r * f:(r + 1) * f].t().contiguous()
-            self.layers.append(TpLayer(lw.attn_norm, wqkv, wo, lw.mlp_norm, gu.t().contiguous(), down))
+            # the dense model stores [out, in]: take this rank's output rows / input columns
+            q = lw.wqkv[r * hq * D:(r + 1) * hq * D]
+            k = lw.wqkv[Q + r * hkv * D:Q + (r + 1) * hkv * D]
+            v = lw.wqkv[Q + KV + r * hkv * D:Q + KV + (r + 1) * hkv * D]
+            wqkv = torch.cat([q, k, v], dim=0).contiguous()
+            wo = lw.wo[:, r * hq * D:(r + 1) * hq * D].contiguous()
+            gate, up = split_gate_up(lw.w_gate_up)
+            gu = torch.cat([gate[r * f:(r + 1) * f], up[r * f:(r + 1) * f]], dim=0).contiguous()
+            down = lw.w_down[:, r * f:(r + 1) * f].contiguous()
+            self.layers.append(TpLayer(lw.attn_norm, wqkv, wo, lw.mlp_norm, gu, down))
         self.final_norm = m.final_norm
-        self.lm_head = m.lm_head[:, r * self.vocab_local:(r + 1) * self.vocab_local].t().contiguous()
+        self.lm_head = m.lm_head[r * self.vocab_local:(r + 1) * self.vocab_local].contiguous()
 
     def ensure_positions(self, n: int) -> None:
         if n > self.cos_sin.shape[0]:

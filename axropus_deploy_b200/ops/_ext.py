@@ -14,7 +14,13 @@ _ERR = None
 # Kernels of this framework launched so far (per process). Each wrapper call adds the
 # number of kernels it launches; CUDA-graph replays add what their capture recorded.
 LAUNCHES = [0]
-_KERNELS_PER_CALL = {"decode_attention": lambda a: 2 if a[14] > 1 else 1}
+_KERNELS_PER_CALL = {
+    # split kernel + combine (split-KV or shared-prefix merge)
+    "decode_attention": lambda a: 2 if (a[14] > 1 or (len(a) > 19 and a[19] is not None)) else 1,
+    # attention kernel + combine unless the partials are kept for a later merge
+    "prefill_attention_tc": lambda a: 2 if (a[14] > 1 and not (len(a) > 20 and a[20])) else 1,
+    "prefill_attention": lambda a: 2 if a[17] > 1 else 1,
+}
 
 
 class _Counted:
@@ -24,7 +30,8 @@ class _Counted:
 
     def __getattr__(self, name):
         fn = getattr(self._mod, name)
-        if not callable(fn) or name in ("decode_num_splits",):
+        if not callable(fn) or name in ("decode_num_splits", "dense_stream_nt", "dense_stream_splits",
+                                                   "dense_stream_workspace"):
             return fn
         per = _KERNELS_PER_CALL.get(name)
 

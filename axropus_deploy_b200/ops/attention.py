@@ -6,7 +6,8 @@ from __future__ import annotations
 
 import math
 import os
-from typing import Optional
+from dataclasses import dataclass
+from typing import List, Optional, Sequence
 
 import torch
 
@@ -71,17 +72,83 @@ class DecodeWorkspace:
 
 
 _WS = DecodeWorkspace()
+_CASCADE_WS = DecodeWorkspace()
+
+
+@dataclass
+class CascadeMeta:
+    """Shared-prefix decode of one step: sequences whose block tables start with the same
+    pages form a group; the group's queries attend to those shared pages once (one pass
+    over them for every query of the group, on the tensor cores) and each sequence then
+    attends only to its own pages, the two partial results merged by log-sum-exp.
+
+    Device tensors (int32): ``q_index`` [R] decode rows of the groups' members, grouped;
+    ``cu_q`` [NG+1] group offsets into q_index; ``seq_lens`` [NG] shared tokens per group;
+    ``block_table`` [NG, max_blocks] the shared pages; ``row_of`` [B] packed row of each
+    sequence in q_index (-1: in no group); ``page_start`` [B] first page of each sequence's
+    own pass. ``max_q``: largest group (padded for CUDA graphs), ``num_splits``: KV slices
+    of the shared pass."""
+
+    q_index: torch.Tensor
+    cu_q: torch.Tensor
+    seq_lens: torch.Tensor
+    block_table: torch.Tensor
+    row_of: torch.Tensor
+    page_start: torch.Tensor
+    max_q: int
+    num_splits: int
+
+
+def cascade_groups(block_lists: Sequence[Sequence[int]], min_pages: int = 32,
+                   max_pages: Optional[Sequence[int]] = None) -> List[tuple]:
+    """Groups of batch rows that share leading pages: [(rows, shared_pages), ...] with at
+    least two rows and ``min_pages`` shared pages each. Rows are grouped by their first
+    block; the shared length is the longest common prefix of the group's block lists,
+    capped by ``max_pages[b]`` (a row's pages that hold prompt tokens), so that the pages
+    a sequence is still writing stay in its own pass."""
+    by_first = {}
+    for i, bl in enumerate(block_lists):
+        if len(bl) >= min_pages:
+            by_first.setdefault(bl[0], []).append(i)
+    groups = []
+    for rows in by_first.values():
+        if len(rows) < 2:
+            continue
+        n = min(len(block_lists[r]) if max_pages is None else min(len(block_lists[r]), max_pages[r]) for r in rows)
+        first = block_lists[rows[0]]
+        lcp = 0
+        while lcp < n and all(block_lists[r][lcp] == first[lcp] for r in rows[1:]):
+            lcp += 1
+        if lcp >= min_pages:
+            groups.append((rows, lcp))
+    return groups
+
+
+def cascade_num_splits(n_groups: int, kv_heads: int, max_seq_len: int, device: torch.device) -> int:
+    """KV slices of the shared pass: enough CTAs (groups x KV heads x slices) for a wave of
+    SMs, each slice keeping at least 4 KV tiles of 128 tokens."""
+    ctas = max(1, n_groups) * kv_heads
+    tiles = max(1, -(-max_seq_len // 128))
+    return int(max(1, min(16, -(-_num_sms(device) // ctas), tiles // 4)))
 
 
 def decode_num_splits(batch: int, kv_heads: int, max_pages: int, device: torch.device, fmt: int = -1) -> int:
     return int(cuda_ext().decode_num_splits(batch, kv_heads, max_pages, _num_sms(device), fmt))
 
 
+def cascade_supported(cache: KVCache, head_dim: int) -> bool:
+    """The shared pass runs on the tcgen05 prefill kernel: bf16 pages, head_dim 128."""
+    return cache.fmt == BF16 and head_dim == 128 and PREFILL_TC[0]
+
+
 def decode_attention(q: torch.Tensor, cache: KVCache, layer: int, block_table: torch.Tensor, seq_lens: torch.Tensor,
                      scale: Optional[float] = None, max_seq_len: Optional[int] = None,
                      num_splits: Optional[int] = None, out: Optional[torch.Tensor] = None,
-                     workspace: Optional[DecodeWorkspace] = None) -> torch.Tensor:
-    """q [B, Hq, D] (rotated) -> out [B, Hq, D]; attends to seq_lens[b] cached tokens."""
+                     workspace: Optional[DecodeWorkspace] = None,
+                     cascade: Optional[CascadeMeta] = None) -> torch.Tensor:
+    """q [B, Hq, D] (rotated) -> out [B, Hq, D]; attends to seq_lens[b] cached tokens.
+    With ``cascade`` the shared prefixes of grouped sequences are attended once per group
+    (same result; see :class:`CascadeMeta`)."""
     B, Hq, D = q.shape
     scale = scale if scale is not None else 1.0 / math.sqrt(D)
     if out is None:
@@ -92,10 +159,21 @@ def decode_attention(q: torch.Tensor, cache: KVCache, layer: int, block_table: t
         max_pages = (max_seq_len + 15) // 16
         S = num_splits if num_splits is not None else decode_num_splits(B, cache.num_kv_heads, max_pages, q.device, cache.fmt)
         ws = workspace or _WS
-        po, pl = ws.get(B, Hq, S, D, q.device) if S > 1 else (out, out)
+        po, pl = ws.get(B, Hq, S, D, q.device) if (S > 1 or cascade is not None) else (out, out)
         k, v, km, vm, bs, hs, mbs, mhs = cache.layer_args(layer)
-        cuda_ext().decode_attention(q, k, v, km, vm, bs, hs, mbs, mhs, cache.fmt, block_table, seq_lens,
-                                    cache.num_kv_heads, scale, S, max_pages, out, po, pl)
+        C = cuda_ext()
+        if cascade is None:
+            C.decode_attention(q, k, v, km, vm, bs, hs, mbs, mhs, cache.fmt, block_table, seq_lens,
+                               cache.num_kv_heads, scale, S, max_pages, out, po, pl, None, None, None, None, 0)
+            return out
+        S2 = cascade.num_splits
+        R = cascade.q_index.numel()
+        po2, pl2 = _CASCADE_WS.get(max(R, 1), Hq, S2, D, q.device)
+        C.prefill_attention_tc(q, k, v, bs, hs, cache.num_blocks, cascade.block_table, cascade.cu_q,
+                               cascade.seq_lens, cache.num_kv_heads, scale, cascade.max_q, out, error_flag(q.device),
+                               S2, po2, pl2, Hq // cache.num_kv_heads, 1, cascade.q_index, 1)
+        C.decode_attention(q, k, v, km, vm, bs, hs, mbs, mhs, cache.fmt, block_table, seq_lens, cache.num_kv_heads,
+                           scale, S, max_pages, out, po, pl, cascade.page_start, po2, pl2, cascade.row_of, S2)
         return out
     for b in range(B):
         n = int(seq_lens[b])
@@ -129,6 +207,64 @@ def prefill_num_splits(batch: int, heads: int, max_q: int, max_seq_len: Optional
 
 
 _PREFILL_WS = DecodeWorkspace()
+_CASCADE_WS = DecodeWorkspace()
+
+
+@dataclass
+class CascadeMeta:
+    """Shared-prefix decode of one step: sequences whose block tables start with the same
+    pages form a group; the group's queries attend to those shared pages once (one pass
+    over them for every query of the group, on the tensor cores) and each sequence then
+    attends only to its own pages, the two partial results merged by log-sum-exp.
+
+    Device tensors (int32): ``q_index`` [R] decode rows of the groups' members, grouped;
+    ``cu_q`` [NG+1] group offsets into q_index; ``seq_lens`` [NG] shared tokens per group;
+    ``block_table`` [NG, max_blocks] the shared pages; ``row_of`` [B] packed row of each
+    sequence in q_index (-1: in no group); ``page_start`` [B] first page of each sequence's
+    own pass. ``max_q``: largest group (padded for CUDA graphs), ``num_splits``: KV slices
+    of the shared pass."""
+
+    q_index: torch.Tensor
+    cu_q: torch.Tensor
+    seq_lens: torch.Tensor
+    block_table: torch.Tensor
+    row_of: torch.Tensor
+    page_start: torch.Tensor
+    max_q: int
+    num_splits: int
+
+
+def cascade_groups(block_lists: Sequence[Sequence[int]], min_pages: int = 32,
+                   max_pages: Optional[Sequence[int]] = None) -> List[tuple]:
+    """Groups of batch rows that share leading pages: [(rows, shared_pages), ...] with at
+    least two rows and ``min_pages`` shared pages each. Rows are grouped by their first
+    block; the shared length is the longest common prefix of the group's block lists,
+    capped by ``max_pages[b]`` (a row's pages that hold prompt tokens), so that the pages
+    a sequence is still writing stay in its own pass."""
+    by_first = {}
+    for i, bl in enumerate(block_lists):
+        if len(bl) >= min_pages:
+            by_first.setdefault(bl[0], []).append(i)
+    groups = []
+    for rows in by_first.values():
+        if len(rows) < 2:
+            continue
+        n = min(len(block_lists[r]) if max_pages is None else min(len(block_lists[r]), max_pages[r]) for r in rows)
+        first = block_lists[rows[0]]
+        lcp = 0
+        while lcp < n and all(block_lists[r][lcp] == first[lcp] for r in rows[1:]):
+            lcp += 1
+        if lcp >= min_pages:
+            groups.append((rows, lcp))
+    return groups
+
+
+def cascade_num_splits(n_groups: int, kv_heads: int, max_seq_len: int, device: torch.device) -> int:
+    """KV slices of the shared pass: enough CTAs (groups x KV heads x slices) for a wave of
+    SMs, each slice keeping at least 4 KV tiles of 128 tokens."""
+    ctas = max(1, n_groups) * kv_heads
+    tiles = max(1, -(-max_seq_len // 128))
+    return int(max(1, min(16, -(-_num_sms(device) // ctas), tiles // 4)))
 
 
 def prefill_attention(q: torch.Tensor, cache: KVCache, layer: int, block_table: torch.Tensor, cu_q: torch.Tensor,
@@ -156,7 +292,7 @@ def prefill_attention(q: torch.Tensor, cache: KVCache, layer: int, block_table: 
             po, pl = _PREFILL_WS.get(T, Hq, S, D, q.device) if S > 1 else (None, None)
             cuda_ext().prefill_attention_tc(q, k, v, bs, hs, cache.num_blocks, block_table, cu_q, seq_lens,
                                             cache.num_kv_heads, scale, max_q, out, error_flag(q.device), S, po, pl,
-                                            G if pack else 1)
+                                            G if pack else 1, 0, None, 0)
             return out
         S = num_splits if num_splits is not None else prefill_num_splits(seq_lens.shape[0], Hq, max_q, max_seq_len,
                                                                           q.device)

@@ -11,7 +11,9 @@ void decode_attention(torch::Tensor q, int64_t k, int64_t v, int64_t km, int64_t
                       int64_t head_stride, int64_t mblk_stride, int64_t mhead_stride, int64_t fmt,
                       torch::Tensor block_table, torch::Tensor seq_lens, int64_t Hkv, double scale,
                       int64_t num_splits, int64_t max_pages, torch::Tensor out, torch::Tensor part_o,
-                      torch::Tensor part_lse);
+                      torch::Tensor part_lse, c10::optional<torch::Tensor> page_start,
+                      c10::optional<torch::Tensor> part_o2, c10::optional<torch::Tensor> part_lse2,
+                      c10::optional<torch::Tensor> row_of, int64_t S2);
 void prefill_attention(torch::Tensor q, int64_t k, int64_t v, int64_t km, int64_t vm, int64_t blk_stride,
                        int64_t head_stride, int64_t mblk_stride, int64_t mhead_stride, int64_t fmt,
                        torch::Tensor block_table, torch::Tensor cu_q, torch::Tensor seq_lens, int64_t Hkv,
@@ -38,7 +40,8 @@ void prefill_attention_tc(torch::Tensor q, int64_t k, int64_t v, int64_t blk_str
                           int64_t num_blocks, torch::Tensor block_table, torch::Tensor cu_q, torch::Tensor seq_lens,
                           int64_t Hkv, double scale, int64_t max_q, torch::Tensor out, torch::Tensor err,
                           int64_t num_splits, c10::optional<torch::Tensor> part_o,
-                          c10::optional<torch::Tensor> part_lse, int64_t gqa_pack);
+                          c10::optional<torch::Tensor> part_lse, int64_t gqa_pack, int64_t noncausal,
+                          c10::optional<torch::Tensor> q_index, int64_t partial_only);
 void moe_dispatch(torch::Tensor x, torch::Tensor topk_idx, torch::Tensor topk_w, int64_t E_l, int64_t rank,
                   int64_t world, int64_t epoch, int64_t cap_rows, torch::Tensor pair_pos, torch::Tensor gcount,
                   torch::Tensor grid_bar, torch::Tensor peers, torch::Tensor cnt_all, torch::Tensor cnt_flag,
@@ -53,6 +56,16 @@ void moe_combine(torch::Tensor comb, torch::Tensor out, torch::Tensor comb_flag,
 void peer_allreduce(torch::Tensor x, torch::Tensor out, int64_t rank, int64_t world, torch::Tensor peers,
                     torch::Tensor buf, torch::Tensor flag, torch::Tensor epoch, torch::Tensor bar, int64_t cap,
                     torch::Tensor err);
+namespace dense {
+void dense_gemm(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t epi, c10::optional<torch::Tensor> res,
+                c10::optional<torch::Tensor> pos, c10::optional<torch::Tensor> slots,
+                c10::optional<torch::Tensor> cos_sin, int64_t kc, int64_t vc, int64_t blk_stride, int64_t head_stride,
+                int64_t Hq, int64_t Hkv, torch::Tensor ws, torch::Tensor cnt, torch::Tensor err, int64_t splits,
+                int64_t force_big);
+int64_t dense_stream_nt(int64_t M);
+int64_t dense_stream_splits(int64_t M, int64_t N, int64_t K, int64_t sms);
+std::vector<int64_t> dense_stream_workspace(int64_t M, int64_t N, int64_t K, int64_t sms);
+}  // namespace dense
 }  // namespace axr
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -74,4 +87,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("peer_allreduce", &axr::peer_allreduce);
   m.def("moe_gemm", &axr::moe_gemm);
   m.def("moe_combine", &axr::moe_combine);
+  m.def("dense_gemm", &axr::dense::dense_gemm);
+  m.def("dense_stream_nt", &axr::dense::dense_stream_nt);
+  m.def("dense_stream_splits", &axr::dense::dense_stream_splits);
+  m.def("dense_stream_workspace", &axr::dense::dense_stream_workspace);
 }

@@ -42,6 +42,10 @@ struct DecodeParams {
   __nv_bfloat16* out;      // [B, Hq, D] when splits == 1
   float* part_o;           // [B, Hq, S, D]
   float* part_lse;         // [B, Hq, S]
+  // Shared-prefix decode: sequence b attends only to its pages [page_start[b], ...) here
+  // (the shared prefix before them is attended by the grouped pass), and the result is
+  // always written as partials for the merge. nullptr: every page from 0.
+  const int* page_start;
 };
 
 template <int D, int G, int FMT>
@@ -62,7 +66,7 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(DecodeParams p) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int seq_len = p.seq_lens[b];
   const int n_pages = (seq_len + kPage - 1) / kPage;
-  const int pg0 = split * p.pages_per_split;
+  const int pg0 = (p.page_start != nullptr ? p.page_start[b] : 0) + split * p.pages_per_split;
   const int pg1 = min(n_pages, pg0 + p.pages_per_split);
 
   // Stage q (pre-scaled into the log2 domain) for the G heads of this KV head.
@@ -283,7 +287,7 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(DecodeParams p) {
     }
     const int hq = kvh * G + g;
     const float o = L > 0.f ? O / L : 0.f;
-    if (S == 1) {
+    if (S == 1 && p.page_start == nullptr) {
       p.out[((long long)b * p.Hq + hq) * D + d] = __float2bfloat16(o);
     } else {
       const long long base = ((long long)b * p.Hq + hq) * S + split;
@@ -421,7 +425,7 @@ __global__ void __launch_bounds__(128) decode_tc_kernel(DecodeParams p) {
 
   const int seq_len = p.seq_lens[b];
   const int n_pages = (seq_len + kPage - 1) / kPage;
-  const int pg0 = split * p.pages_per_split;
+  const int pg0 = (p.page_start != nullptr ? p.page_start[b] : 0) + split * p.pages_per_split;
   const int pg1 = min(n_pages, pg0 + p.pages_per_split);
   const int my_n = pg1 > pg0 + warp ? (pg1 - pg0 - warp + 3) / 4 : 0;
   const int* bt = p.block_table + (long long)b * p.bt_stride;
@@ -753,7 +757,7 @@ __global__ void __launch_bounds__(128) decode_tc_kernel(DecodeParams p) {
     }
     const int hq = kvh * G + hh;
     const float ov = L > 0.f ? O / L : 0.f;
-    if (S == 1) {
+    if (S == 1 && p.page_start == nullptr) {
       p.out[((long long)b * p.Hq + hq) * 128 + d] = __float2bfloat16(ov);
     } else {
       const long long base = ((long long)b * p.Hq + hq) * S + split;
@@ -825,7 +829,9 @@ void decode_attention(torch::Tensor q, int64_t k, int64_t v, int64_t km, int64_t
                       int64_t head_stride, int64_t mblk_stride, int64_t mhead_stride, int64_t fmt,
                       torch::Tensor block_table, torch::Tensor seq_lens, int64_t Hkv, double scale,
                       int64_t num_splits, int64_t max_pages, torch::Tensor out, torch::Tensor part_o,
-                      torch::Tensor part_lse) {
+                      torch::Tensor part_lse, c10::optional<torch::Tensor> page_start,
+                      c10::optional<torch::Tensor> part_o2, c10::optional<torch::Tensor> part_lse2,
+                      c10::optional<torch::Tensor> row_of, int64_t S2) {
   TORCH_CHECK(q.is_cuda() && q.scalar_type() == torch::kBFloat16 && q.is_contiguous(), "q must be contiguous bf16");
   TORCH_CHECK(q.dim() == 3, "q must be [B, Hq, D]");
   const int B = q.size(0), Hq = q.size(1), D = q.size(2);
@@ -834,9 +840,16 @@ void decode_attention(torch::Tensor q, int64_t k, int64_t v, int64_t km, int64_t
   TORCH_CHECK(seq_lens.scalar_type() == torch::kInt32, "seq_lens int32");
   TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.is_contiguous(), "out must be contiguous bf16");
   const int S = static_cast<int>(std::max<int64_t>(1, num_splits));
-  if (S > 1) {
+  const bool cascade = page_start.has_value();
+  if (S > 1 || cascade) {
     TORCH_CHECK(part_o.numel() >= (int64_t)B * Hq * S * D && part_lse.numel() >= (int64_t)B * Hq * S,
                 "split scratch too small");
+  }
+  if (cascade) {
+    TORCH_CHECK(page_start->scalar_type() == torch::kInt32 && page_start->numel() >= B && row_of.has_value() &&
+                    row_of->scalar_type() == torch::kInt32 && row_of->numel() >= B && part_o2.has_value() &&
+                    part_lse2.has_value() && S2 >= 1,
+                "decode_attention: shared-prefix inputs (page_start, row_of, shared partials)");
   }
   DecodeParams p;
   p.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
@@ -856,8 +869,9 @@ void decode_attention(torch::Tensor q, int64_t k, int64_t v, int64_t km, int64_t
   p.pages_per_split = static_cast<int>((max_pages + S - 1) / S);
   p.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
   p.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
-  p.part_o = S > 1 ? part_o.data_ptr<float>() : nullptr;
-  p.part_lse = S > 1 ? part_lse.data_ptr<float>() : nullptr;
+  p.part_o = S > 1 || cascade ? part_o.data_ptr<float>() : nullptr;
+  p.part_lse = S > 1 || cascade ? part_lse.data_ptr<float>() : nullptr;
+  p.page_start = cascade ? page_start->data_ptr<int>() : nullptr;
   const int G = Hq / static_cast<int>(Hkv);
   dim3 grid(S, Hkv, B);
   auto st = at::cuda::getCurrentCUDAStream();
@@ -875,7 +889,13 @@ void decode_attention(torch::Tensor q, int64_t k, int64_t v, int64_t km, int64_t
     TORCH_CHECK(false, "decode_attention: head_dim must be 64 or 128");
   }
   AXR_CHECK_CUDA(cudaGetLastError());
-  if (S > 1) {
+  if (cascade) {
+    TORCH_CHECK(D == 128, "shared-prefix decode: head_dim 128");
+    cascade_combine_kernel<128><<<B * Hq, 128, 0, st>>>(p.part_o, p.part_lse, S, part_o2->data_ptr<float>(),
+                                                        part_lse2->data_ptr<float>(), static_cast<int>(S2),
+                                                        row_of->data_ptr<int>(), Hq, p.out);
+    AXR_CHECK_CUDA(cudaGetLastError());
+  } else if (S > 1) {
     if (D == 128) decode_combine_kernel<128><<<B * Hq, 128, 0, st>>>(p.part_o, p.part_lse, p.out, S);
     else decode_combine_kernel<64><<<B * Hq, 64, 0, st>>>(p.part_o, p.part_lse, p.out, S);
     AXR_CHECK_CUDA(cudaGetLastError());

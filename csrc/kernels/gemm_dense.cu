@@ -1,0 +1,755 @@
+// Dense projections of the single-GPU / data-parallel models on tcgen05, with the
+// element-wise step that follows each projection fused into its epilogue.
+//
+//   out = epilogue(X W^T), X [M, K] bf16 activations, W [N, K] bf16 weights ("out x in"),
+//   fp32 accumulation in tensor memory.
+//
+// Two kernels, chosen by the number of token rows M:
+//
+// * gemm_stream_kernel (M <= 256: decode steps, AMF-hit suffix prefills). The weights
+//   are the only large operand, so the kernel is a weight stream: the MMA's M side is
+//   128 weight rows (swap-AB), its N side the M token rows padded to NT (16..256).
+//   The reduction is split over `splits` CTAs per 128-row tile so that every SM keeps
+//   TMA loads of weights in flight; the last CTA of a tile to finish (a per-tile
+//   arrival counter) sums all CTAs' fp32 partials in split order and runs the epilogue, then
+//   puts the counter back to zero for the next call. The kernel is launched with
+//   programmatic dependent launch: it fills its TMA ring with weight tiles before it
+//   waits for the previous kernel (griddepcontrol.wait), so the stream starts while
+//   the previous kernel drains; activations and every epilogue input are read after
+//   the wait.
+// * gemm_big_kernel (M > 256: prefills). Persistent, one CTA per SM, 128 x 256 output
+//   tiles in a grouped raster, a 4-stage TMA ring, two 256-column TMEM accumulators so
+//   the epilogue of tile i overlaps the MMAs of tile i + 1.
+//
+// Epilogues (both kernels):
+//   STORE  : out = acc
+//   RESID  : out = res + acc (res may be out itself: the residual stream updated in place)
+//   SWIGLU : W rows are gate/up interleaved in groups of 64 (rows 128j..128j+63 = gate
+//            features 64j.., rows 128j+64.. = up features 64j..); out[:, f] = silu(g) * u
+//   ROPE   : W = [q heads | k heads | v heads] x 128 dims; rotate-half RoPE on q and k at
+//            pos[m], q written to out, k and v stored at slots[m] of a bf16 paged cache
+//            (slot < 0: not stored).
+//
+// Every wait is bounded (tc::mbar_wait: records a code in err and winds down). Every
+// TMA load is a plain per-CTA load of this GPU's memory (no multicast).
+// Reference counterpart: the dense projections the reference leaves to vLLM / llama.cpp
+// library GEMMs (axropus/server.py:110, core/engine.cpp llama_decode).
+#include <algorithm>
+#include <string>
+
+#include "common.cuh"
+#include "gemm_dense.h"
+#include "tc_common.cuh"
+
+namespace axr {
+namespace dense {
+
+struct EpiArgs {
+  __nv_bfloat16* out;
+  long long ldo;
+  const __nv_bfloat16* res;  // RESID
+  long long ldr;
+  const int* pos;             // ROPE
+  const int* slots;
+  const float* cos_sin;       // [n_pos, 128]: cos [0, 64), sin [64, 128)
+  int n_pos;
+  char* kc;                   // bf16 paged cache of this layer: unit (blk, head) at blk*blk_stride + head*head_stride
+  char* vc;
+  long long blk_stride, head_stride;
+  int Hq, Hkv;
+};
+
+struct Args {
+  int M, N, K;
+  int splits;   // stream kernel: CTAs per 128-row weight tile
+  float* ws;    // stream kernel split-K partials [tiles * splits][NT][128]
+  int* cnt;     // stream kernel per-tile arrival counters (zero between calls)
+  volatile int* err;
+  EpiArgs e;
+};
+
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+__device__ __forceinline__ float silu(float g) { return g / (1.f + __expf(-g)); }
+
+__device__ __forceinline__ char* align1024(char* p) {
+  return reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+
+// Where row m of k/v head h goes in the paged cache (nullptr: not stored).
+__device__ __forceinline__ __nv_bfloat16* cache_row(const EpiArgs& e, bool is_v, int h, int m) {
+  const int slot = e.slots[m];
+  if (slot < 0) return nullptr;
+  char* unit = (is_v ? e.vc : e.kc) + (long long)(slot / kPage) * e.blk_stride + (long long)h * e.head_stride;
+  return reinterpret_cast<__nv_bfloat16*>(unit + (long long)(slot % kPage) * 128 * 2);
+}
+
+// =====================================================================================
+// weight-streaming kernel
+// =====================================================================================
+template <int NT>
+struct StreamCfg {
+  static constexpr int ST = NT <= 16 ? 6 : NT <= 32 ? 5 : NT <= 64 ? 4 : NT <= 128 ? 3 : 4;
+  static constexpr int A_BYTES = 128 * 64 * 2;  // 128 weight rows x 64 k
+  static constexpr int B_BYTES = NT * 64 * 2;   // NT token rows x 64 k
+  static constexpr int STAGE = A_BYTES + B_BYTES;
+  static constexpr int SMEM = 1024 + ST * STAGE + 128;
+  static constexpr int TMEM_COLS = NT < 32 ? 32 : NT;
+  static constexpr int CH = NT < 32 ? NT : 32;  // epilogue columns (tokens) per TMEM load
+  static constexpr int CTAS_PER_SM = NT <= 128 ? 2 : 1;
+};
+
+template <int CH>
+__device__ __forceinline__ void tmem_ld_chunk(uint32_t taddr, float (&v)[CH]) {
+  if constexpr (CH == 16) {
+    uint32_t r[16];
+    tc::tmem_ld16(taddr, r);
+    tc::tmem_ld_wait();
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
+  } else {
+    uint32_t r[32];
+    tc::tmem_ld32(taddr, r);
+    tc::tmem_ld_wait();
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+  }
+}
+
+// Epilogue of one chunk of CH token columns. Thread t holds weight row r = t of the tile
+// (feature n0 + r) for tokens c0 .. c0 + CH - 1. sx: [128][CH + 1] fp32 exchange space.
+template <int EPI, int CH>
+__device__ __forceinline__ void stream_epilogue(const Args& g, int tile, int c0, const float (&v)[CH], float* sx) {
+  const int r = threadIdx.x;
+  const EpiArgs& e = g.e;
+  if constexpr (EPI == kStore || EPI == kResid) {
+    const int n = tile * 128 + r;
+    if (n >= g.N) return;
+#pragma unroll
+    for (int j = 0; j < CH; ++j) {
+      const int m = c0 + j;
+      if (m < g.M) {
+        float x = v[j];
+        if constexpr (EPI == kResid) x += __bfloat162float(e.res[(long long)m * e.ldr + n]);
+        e.out[(long long)m * e.ldo + n] = __float2bfloat16(x);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < CH; ++j) sx[r * (CH + 1) + j] = v[j];
+    __syncthreads();
+    const int d = r & 63, jj = r >> 6;
+    if constexpr (EPI == kSwiGLU) {
+      const int f = tile * 64 + d;
+#pragma unroll 4
+      for (int j = jj; j < CH; j += 2) {
+        const int m = c0 + j;
+        if (m < g.M) {
+          const float gt = sx[d * (CH + 1) + j], up = sx[(d + 64) * (CH + 1) + j];
+          e.out[(long long)m * e.ldo + f] = __float2bfloat16(silu(gt) * up);
+        }
+      }
+    } else {  // ROPE: tile = head row hr of [q | k | v]
+      const int hr = tile;
+      const bool rot = hr < e.Hq + e.Hkv, is_q = hr < e.Hq, is_v = !rot;
+#pragma unroll 4
+      for (int j = jj; j < CH; j += 2) {
+        const int m = c0 + j;
+        if (m >= g.M) continue;
+        const float x1 = sx[d * (CH + 1) + j], x2 = sx[(d + 64) * (CH + 1) + j];
+        float o1 = x1, o2 = x2;
+        if (rot) {
+          const int ps = min(max(e.pos[m], 0), e.n_pos - 1);
+          const float co = e.cos_sin[(long long)ps * 128 + d], si = e.cos_sin[(long long)ps * 128 + 64 + d];
+          o1 = x1 * co - x2 * si;
+          o2 = x2 * co + x1 * si;
+        }
+        __nv_bfloat16* dst;
+        if (is_q) {
+          dst = e.out + (long long)m * e.ldo + hr * 128;
+        } else {
+          dst = cache_row(e, is_v, is_v ? hr - e.Hq - e.Hkv : hr - e.Hq, m);
+          if (dst == nullptr) continue;
+        }
+        dst[d] = __float2bfloat16(o1);
+        dst[d + 64] = __float2bfloat16(o2);
+      }
+    }
+    __syncthreads();
+  }
+}
+
+template <int NT, int EPI>
+__global__ void __launch_bounds__(128) gemm_stream_kernel(const __grid_constant__ CUtensorMap tmW,
+                                                          const __grid_constant__ CUtensorMap tmX, Args g) {
+  using C = StreamCfg<NT>;
+  extern __shared__ __align__(1024) char smem_raw[];
+  char* base = align1024(smem_raw);
+  uint64_t* full = reinterpret_cast<uint64_t*>(base + C::ST * C::STAGE);
+  uint64_t* empty = full + C::ST;
+  uint64_t* accb = empty + C::ST;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accb + 1);
+  int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x, split = blockIdx.y;
+  const int n0 = tile * 128;
+  const int nk = (g.K + 63) / 64;
+  const int kb0 = static_cast<int>((long long)split * nk / g.splits);
+  const int kb1 = static_cast<int>((long long)(split + 1) * nk / g.splits);
+  const int nkb = kb1 - kb0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::ST; ++s) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&empty[s], 1);
+    }
+    tc::mbar_init(accb, 1);
+    tc::fence_barrier_init();
+    tc::prefetch_tmap(&tmW);
+    tc::prefetch_tmap(&tmX);
+  }
+  if (warp == 2) {
+    tc::tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer: weights first (independent of earlier kernels), then activations
+    const int pre = min(C::ST, nkb);
+    for (int i = 0; i < pre; ++i) {
+      tc::mbar_arrive_expect_tx(&full[i], C::STAGE);
+      tc::tma_load_2d(base + i * C::STAGE, &tmW, (kb0 + i) * 64, n0, &full[i]);
+    }
+    griddep_wait();
+    for (int i = 0; i < pre; ++i) tc::tma_load_2d(base + i * C::STAGE + C::A_BYTES, &tmX, (kb0 + i) * 64, 0, &full[i]);
+    int issued = pre;
+    bool ok = true;
+    for (int i = pre; i < nkb; ++i) {
+      const int s = i % C::ST;
+      if (!tc::mbar_wait(&empty[s], ((i / C::ST) + 1) & 1, g.err, 1)) { ok = false; break; }
+      tc::mbar_arrive_expect_tx(&full[s], C::STAGE);
+      tc::tma_load_2d(base + s * C::STAGE, &tmW, (kb0 + i) * 64, n0, &full[s]);
+      tc::tma_load_2d(base + s * C::STAGE + C::A_BYTES, &tmX, (kb0 + i) * 64, 0, &full[s]);
+      issued = i + 1;
+    }
+    if (!ok) {  // let this thread's loads land before the CTA can exit
+      for (int i = max(0, issued - C::ST); i < issued; ++i) tc::mbar_wait_quiet(&full[i % C::ST], (i / C::ST) & 1);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer
+    constexpr uint32_t idesc = tc::idesc_bf16_f32(128, NT);
+    bool ok = true;
+    for (int i = 0; i < nkb; ++i) {
+      const int s = i % C::ST;
+      if (!tc::mbar_wait(&full[s], (i / C::ST) & 1, g.err, 2)) { ok = false; break; }
+      tc::tc_fence_after();
+      const uint32_t a_addr = tc::smem_u32(base + s * C::STAGE);
+      const uint32_t b_addr = a_addr + C::A_BYTES;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        tc::mma_f16_ss(tmem, tc::smem_desc_k_sw128(a_addr + kk * 32), tc::smem_desc_k_sw128(b_addr + kk * 32), idesc,
+                       (i | kk) != 0);
+      tc::mma_commit(&empty[s]);
+    }
+    tc::mma_commit(accb);
+    if (!ok) tc::mbar_wait_quiet(accb, 0);
+  }
+  __syncwarp();
+
+  // ---------------- epilogue (all 4 warps; warp w reads TMEM lanes 32w..32w+31)
+  bool ready = tc::mbar_wait(accb, 0, g.err, 3);
+  tc::tc_fence_after();
+  if (threadIdx.x == 0) griddep_launch();
+  griddep_wait();  // residual, positions and slots come from earlier kernels
+  ready = __syncthreads_and(ready && *g.err == 0) != 0;
+  const uint32_t trow = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+  const int r = threadIdx.x;
+  float* sx = reinterpret_cast<float*>(base);  // the TMA ring is idle once the accumulator is complete
+  bool write = ready;
+  if (g.splits > 1) {
+    if (ready) {
+      float* mine = g.ws + (long long)(tile * g.splits + split) * NT * 128;
+#pragma unroll 1
+      for (int c0 = 0; c0 < NT; c0 += C::CH) {
+        float v[C::CH];
+        tmem_ld_chunk<C::CH>(trow + c0, v);
+#pragma unroll
+        for (int j = 0; j < C::CH; ++j) __stcg(mine + (c0 + j) * 128 + r, v[j]);
+      }
+      __threadfence();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int last = 0;
+      if (ready) {
+        last = atomicAdd(g.cnt + tile, 1) == g.splits - 1;
+        if (last) g.cnt[tile] = 0;  // every split has arrived: ready for the next call
+      }
+      *last_flag = last;
+    }
+    __syncthreads();
+    write = *last_flag != 0;
+    if (write) __threadfence();
+  }
+  if (write) {
+#pragma unroll 1
+    for (int c0 = 0; c0 < NT; c0 += C::CH) {
+      float v[C::CH];
+      if (g.splits > 1) {
+        // every split's partial, own included, summed in split order: the result does not
+        // depend on which CTA finished last
+#pragma unroll
+        for (int j = 0; j < C::CH; ++j) v[j] = 0.f;
+        for (int s2 = 0; s2 < g.splits; ++s2) {
+          const float* p = g.ws + (long long)(tile * g.splits + s2) * NT * 128 + c0 * 128 + r;
+#pragma unroll
+          for (int j = 0; j < C::CH; ++j) v[j] += __ldcg(p + j * 128);
+        }
+      } else {
+        tmem_ld_chunk<C::CH>(trow + c0, v);
+      }
+      stream_epilogue<EPI, C::CH>(g, tile, c0, v, sx);
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 2) tc::tmem_dealloc(tmem, C::TMEM_COLS);
+}
+
+// =====================================================================================
+// persistent big-M kernel
+// =====================================================================================
+constexpr int BM = 128, BN = 256, BK = 64, BST = 4;
+constexpr int BA_BYTES = BM * BK * 2, BB_BYTES = BN * BK * 2;
+constexpr int BSMEM = 1024 + BST * (BA_BYTES + BB_BYTES) + 256;
+constexpr int BTHREADS = 192;
+constexpr int BGROUP_M = 16;
+
+__device__ __forceinline__ void big_tile(int t, int num_m, int num_n, int& mt, int& nt) {
+  const int group = BGROUP_M * num_n;
+  const int first = (t / group) * BGROUP_M;
+  const int gm = min(num_m - first, BGROUP_M);
+  const int in = t - (t / group) * group;
+  mt = first + in % gm;
+  nt = in / gm;
+}
+
+__device__ __forceinline__ void tmem_ld32f(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  tc::tmem_ld32(taddr, r);
+  tc::tmem_ld_wait();
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+}
+
+// 32 floats -> 32 bf16 at dst (16-byte aligned), or element-wise up to `n` valid columns.
+__device__ __forceinline__ void store32(__nv_bfloat16* dst, const float (&v)[32], int n) {
+  if (n >= 32 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      reinterpret_cast<uint4*>(dst)[q] =
+          make_uint4(pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]), pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]),
+                     pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]), pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]));
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < n) dst[j] = __float2bfloat16(v[j]);
+  }
+}
+
+// Epilogue of one tile: thread = token row m, TMEM columns = features of the tile.
+template <int EPI>
+__device__ __forceinline__ void big_epilogue(const Args& g, uint32_t tacc, int m, int mt, int nt) {
+  const EpiArgs& e = g.e;
+  const bool row_ok = m < g.M;
+  if constexpr (EPI == kStore || EPI == kResid) {
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      float v[32];
+      tmem_ld32f(tacc + c, v);
+      const int n = nt * BN + c;
+      if (!row_ok || n >= g.N) continue;
+      if constexpr (EPI == kResid) {
+        const __nv_bfloat16* rp = e.res + (long long)m * e.ldr + n;
+        if (n + 32 <= g.N && (reinterpret_cast<uintptr_t>(rp) & 15) == 0) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint4 x = reinterpret_cast<const uint4*>(rp)[q];
+            v[q * 8 + 0] += bf16_lo(x.x); v[q * 8 + 1] += bf16_hi(x.x);
+            v[q * 8 + 2] += bf16_lo(x.y); v[q * 8 + 3] += bf16_hi(x.y);
+            v[q * 8 + 4] += bf16_lo(x.z); v[q * 8 + 5] += bf16_hi(x.z);
+            v[q * 8 + 6] += bf16_lo(x.w); v[q * 8 + 7] += bf16_hi(x.w);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (n + j < g.N) v[j] += __bfloat162float(rp[j]);
+        }
+      }
+      store32(e.out + (long long)m * e.ldo + n, v, g.N - n);
+    }
+  } else if constexpr (EPI == kSwiGLU) {
+    // 256 columns = 2 gate/up pairs of 64 -> 128 outputs
+#pragma unroll 1
+    for (int q = 0; q < 2; ++q) {
+#pragma unroll 1
+      for (int p = 0; p < 64; p += 32) {
+        float gt[32], up[32];
+        tmem_ld32f(tacc + q * 128 + p, gt);
+        tmem_ld32f(tacc + q * 128 + 64 + p, up);
+        const int f = nt * 128 + q * 64 + p;
+        if (!row_ok || 2 * f >= g.N) continue;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) gt[j] = silu(gt[j]) * up[j];
+        store32(e.out + (long long)m * e.ldo + f, gt, g.N / 2 - f);
+      }
+    }
+  } else {  // ROPE: 256 columns = head rows 2nt, 2nt+1
+    const int ps = row_ok ? min(max(e.pos[m], 0), e.n_pos - 1) : 0;
+    const float* cs = e.cos_sin + (long long)ps * 128;
+#pragma unroll 1
+    for (int q = 0; q < 2; ++q) {
+      const int hr = nt * 2 + q;
+      const bool rot = hr < e.Hq + e.Hkv, is_q = hr < e.Hq, is_v = !rot;
+      __nv_bfloat16* dst = nullptr;
+      if (row_ok && hr < e.Hq + 2 * e.Hkv) {
+        dst = is_q ? e.out + (long long)m * e.ldo + hr * 128
+                   : cache_row(e, is_v, is_v ? hr - e.Hq - e.Hkv : hr - e.Hq, m);
+      }
+#pragma unroll 1
+      for (int p = 0; p < 64; p += 32) {
+        float x1[32], x2[32];
+        tmem_ld32f(tacc + q * 128 + p, x1);
+        tmem_ld32f(tacc + q * 128 + 64 + p, x2);
+        if (dst == nullptr) continue;
+        if (rot) {
+#pragma unroll
+          for (int j4 = 0; j4 < 32; j4 += 4) {
+            const float4 co = *reinterpret_cast<const float4*>(cs + p + j4);
+            const float4 si = *reinterpret_cast<const float4*>(cs + 64 + p + j4);
+            const float c4[4] = {co.x, co.y, co.z, co.w}, s4[4] = {si.x, si.y, si.z, si.w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const float a = x1[j4 + u], b = x2[j4 + u];
+              x1[j4 + u] = a * c4[u] - b * s4[u];
+              x2[j4 + u] = b * c4[u] + a * s4[u];
+            }
+          }
+        }
+        store32(dst + p, x1, 32);
+        store32(dst + 64 + p, x2, 32);
+      }
+    }
+  }
+}
+
+// Roles: warp 0 TMA producer, warp 1 MMA issuer, warps 2..5 epilogue (TMEM lane group
+// warp % 4), warp 2 also owns the 512 TMEM columns.
+template <int EPI>
+__global__ void __launch_bounds__(BTHREADS, 1) gemm_big_kernel(const __grid_constant__ CUtensorMap tmX,
+                                                               const __grid_constant__ CUtensorMap tmW, Args g) {
+  extern __shared__ __align__(1024) char smem_raw[];
+  char* base = align1024(smem_raw);
+  char* sA = base;
+  char* sB = base + BST * BA_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + BST * BB_BYTES);
+  uint64_t* empty = full + BST;
+  uint64_t* accf = empty + BST;  // [2]
+  uint64_t* acce = accf + 2;     // [2]
+  uint64_t* drain = acce + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_m = (g.M + BM - 1) / BM, num_n = (g.N + BN - 1) / BN;
+  const int tiles = num_m * num_n;
+  const int nk = (g.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < BST; ++s) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      tc::mbar_init(&accf[b], 1);
+      tc::mbar_init(&acce[b], 4);
+    }
+    tc::mbar_init(drain, 1);
+    tc::fence_barrier_init();
+    tc::prefetch_tmap(&tmX);
+    tc::prefetch_tmap(&tmW);
+  }
+  if (warp == 2) {
+    tc::tmem_alloc(tmem_slot, 512);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {  // ---------------- TMA producer
+      int it = 0;
+      bool ok = true;
+      bool waited = false;
+      for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
+        int mt, nt;
+        big_tile(t, num_m, num_n, mt, nt);
+        for (int kt = 0; kt < nk; ++kt, ++it) {
+          const int s = it % BST;
+          if (it >= BST && !tc::mbar_wait(&empty[s], ((it / BST) + 1) & 1, g.err, 1)) { ok = false; break; }
+          tc::mbar_arrive_expect_tx(&full[s], BA_BYTES + BB_BYTES);
+          tc::tma_load_2d(sB + s * BB_BYTES, &tmW, kt * BK, nt * BN, &full[s]);  // weights: no dependency
+          if (!waited) {
+            griddep_wait();
+            waited = true;
+          }
+          tc::tma_load_2d(sA + s * BA_BYTES, &tmX, kt * BK, mt * BM, &full[s]);
+        }
+      }
+      if (!waited) griddep_wait();
+      if (!ok) {
+        for (int j = max(0, it - BST); j < it; ++j) tc::mbar_wait_quiet(&full[j % BST], (j / BST) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // ---------------- MMA issuer
+      constexpr uint32_t idesc = tc::idesc_bf16_f32(BM, BN);
+      int it = 0, i = 0;
+      for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
+        const int buf = i & 1;
+        if (i >= 2 && !tc::mbar_wait(&acce[buf], ((i >> 1) + 1) & 1, g.err, 6)) break;
+        tc::tc_fence_after();
+        bool ok = true;
+        for (int kt = 0; kt < nk; ++kt, ++it) {
+          const int s = it % BST;
+          if (!tc::mbar_wait(&full[s], (it / BST) & 1, g.err, 2)) { ok = false; break; }
+          tc::tc_fence_after();
+          const uint32_t a_addr = tc::smem_u32(sA + s * BA_BYTES), b_addr = tc::smem_u32(sB + s * BB_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            tc::mma_f16_ss(tmem + buf * BN, tc::smem_desc_k_sw128(a_addr + kk * 32),
+                           tc::smem_desc_k_sw128(b_addr + kk * 32), idesc, (kt | kk) != 0);
+          tc::mma_commit(&empty[s]);
+        }
+        tc::mma_commit(&accf[buf]);
+        if (!ok) break;
+      }
+      tc::mma_commit(drain);
+      tc::mbar_wait_quiet(drain, 0);
+    }
+  } else {
+    // ---------------- epilogue warps 2..5
+    const int lg = warp & 3;
+    griddep_wait();  // residual / positions / slots come from earlier kernels
+    int i = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
+      int mt, nt;
+      big_tile(t, num_m, num_n, mt, nt);
+      const int buf = i & 1;
+      bool ok = tc::mbar_wait(&accf[buf], (i >> 1) & 1, g.err, 3);
+      ok = __all_sync(0xffffffffu, ok) && __shfl_sync(0xffffffffu, *g.err, 0) == 0;
+      tc::tc_fence_after();
+      if (!ok) break;
+      const int m = mt * BM + lg * 32 + lane;
+      big_epilogue<EPI>(g, tmem + buf * BN + (static_cast<uint32_t>(lg * 32) << 16), m, mt, nt);
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&acce[buf]);
+    }
+  }
+  if (threadIdx.x == 0) griddep_launch();
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 2) tc::tmem_dealloc(tmem, 512);
+}
+
+// =====================================================================================
+// host
+// =====================================================================================
+namespace {
+
+bool make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
+  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  return cuTensorMapEncodeTiled(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box,
+                                estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int sm_count(int dev) {
+  static int cached[64] = {0};
+  if (dev >= 0 && dev < 64 && cached[dev]) return cached[dev];
+  int sms = 0;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (dev >= 0 && dev < 64) cached[dev] = sms;
+  return sms;
+}
+
+template <typename Kernel>
+cudaError_t launch_pdl(Kernel kernel, dim3 grid, dim3 block, int smem, cudaStream_t st, const CUtensorMap& m0,
+                       const CUtensorMap& m1, const Args& g) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, m0, m1, g);
+}
+
+template <int NT, int EPI>
+cudaError_t launch_stream(const CUtensorMap& tw, const CUtensorMap& tx, const Args& g, cudaStream_t st) {
+  using C = StreamCfg<NT>;
+  auto kernel = gemm_stream_kernel<NT, EPI>;
+  static bool attr = false;
+  if (!attr) {
+    const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  return launch_pdl(kernel, dim3((g.N + 127) / 128, g.splits), dim3(128), C::SMEM, st, tw, tx, g);
+}
+
+template <int EPI>
+cudaError_t launch_stream_nt(int nt, const CUtensorMap& tw, const CUtensorMap& tx, const Args& g, cudaStream_t st) {
+  switch (nt) {
+    case 16: return launch_stream<16, EPI>(tw, tx, g, st);
+    case 32: return launch_stream<32, EPI>(tw, tx, g, st);
+    case 64: return launch_stream<64, EPI>(tw, tx, g, st);
+    case 128: return launch_stream<128, EPI>(tw, tx, g, st);
+    default: return launch_stream<256, EPI>(tw, tx, g, st);
+  }
+}
+
+template <int EPI>
+cudaError_t launch_big(const CUtensorMap& tx, const CUtensorMap& tw, const Args& g, int dev, cudaStream_t st) {
+  auto kernel = gemm_big_kernel<EPI>;
+  static bool attr = false;
+  if (!attr) {
+    const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BSMEM);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  const int tiles = ((g.M + BM - 1) / BM) * ((g.N + BN - 1) / BN);
+  const int grid = std::max(1, std::min(tiles, sm_count(dev)));
+  return launch_pdl(kernel, dim3(grid), dim3(BTHREADS), BSMEM, st, tx, tw, g);
+}
+
+}  // namespace
+
+int stream_nt(int64_t M) {
+  if (M <= 16) return 16;
+  if (M <= 32) return 32;
+  if (M <= 64) return 64;
+  if (M <= 128) return 128;
+  if (M <= 256) return 256;
+  return 0;
+}
+
+// Enough CTAs to give every SM its resident share of weight tiles, each CTA keeping at
+// least 4 k-blocks (256 of K).
+int stream_splits(int64_t M, int64_t N, int64_t K, int sms) {
+  const int nt = stream_nt(M);
+  const int64_t tiles = (N + 127) / 128, nk = (K + 63) / 64;
+  const int64_t slots = static_cast<int64_t>(sms) * (nt <= 128 ? 2 : 1);
+  if (tiles >= slots) return 1;
+  int64_t s = slots / tiles;
+  s = std::min<int64_t>(s, std::max<int64_t>(1, nk / 4));
+  return static_cast<int>(std::max<int64_t>(1, s));
+}
+
+void stream_workspace(int64_t M, int64_t N, int64_t K, int sms, int64_t* ws_floats, int64_t* counters) {
+  const int nt = stream_nt(M);
+  *ws_floats = 0;
+  *counters = 0;
+  if (nt == 0) return;
+  const int64_t s = stream_splits(M, N, K, sms);
+  const int64_t tiles = (N + 127) / 128;
+  *ws_floats = s > 1 ? tiles * s * nt * 128 : 0;
+  *counters = tiles;
+}
+
+std::string dense_gemm_launch(const DenseCall& c, cudaStream_t st) {
+  if (c.M == 0 || c.N == 0) return "";
+  if (c.K <= 0 || c.K % 8 != 0) return "K must be a positive multiple of 8";
+  if ((reinterpret_cast<uintptr_t>(c.x) | reinterpret_cast<uintptr_t>(c.w)) % 16 != 0 || (c.ldx * 2) % 16 != 0 ||
+      (c.ldw * 2) % 16 != 0)
+    return "x / w must be 16-byte aligned with row strides of a multiple of 16 bytes";
+  Args g{};
+  g.M = c.M;
+  g.N = c.N;
+  g.K = c.K;
+  g.err = c.err;
+  g.e.out = reinterpret_cast<__nv_bfloat16*>(c.out);
+  g.e.ldo = c.ldo;
+  if (c.epi == kSwiGLU && c.N % 128 != 0) return "SwiGLU: N must be a multiple of 128";
+  if (c.epi == kRope) {
+    if (c.N != (c.Hq + 2 * c.Hkv) * 128) return "RoPE: N must be (Hq + 2 Hkv) * 128";
+    if (!c.pos || !c.slots || !c.cos_sin || !c.kc || !c.vc || c.n_pos <= 0) return "RoPE: missing inputs";
+    g.e.pos = c.pos;
+    g.e.slots = c.slots;
+    g.e.cos_sin = c.cos_sin;
+    g.e.n_pos = c.n_pos;
+    g.e.kc = reinterpret_cast<char*>(c.kc);
+    g.e.vc = reinterpret_cast<char*>(c.vc);
+    g.e.blk_stride = c.blk_stride;
+    g.e.head_stride = c.head_stride;
+    g.e.Hq = c.Hq;
+    g.e.Hkv = c.Hkv;
+  }
+  if (c.epi == kResid) {
+    if (!c.res) return "RESID: missing residual";
+    g.e.res = reinterpret_cast<const __nv_bfloat16*>(c.res);
+    g.e.ldr = c.ldr;
+  }
+  if (c.epi < kStore || c.epi > kRope) return "unknown epilogue";
+  const int nt = stream_nt(c.M);
+  cudaError_t e;
+  if (nt != 0 && !c.force_big) {
+    const int nk = (c.K + 63) / 64;
+    g.splits = c.splits > 0 ? c.splits : stream_splits(c.M, c.N, c.K, sm_count(c.device));
+    g.splits = std::max(1, std::min(g.splits, nk));
+    if (g.splits > 1) {
+      if (!c.ws || !c.cnt) return "split-K scratch missing";
+      g.ws = c.ws;
+      g.cnt = c.cnt;
+    }
+    CUtensorMap tw, tx;
+    if (!make_map(&tw, c.w, c.N, c.K, c.ldw, 128) || !make_map(&tx, c.x, c.M, c.K, c.ldx, nt))
+      return "cuTensorMapEncodeTiled failed";
+    switch (c.epi) {
+      case kStore: e = launch_stream_nt<kStore>(nt, tw, tx, g, st); break;
+      case kResid: e = launch_stream_nt<kResid>(nt, tw, tx, g, st); break;
+      case kSwiGLU: e = launch_stream_nt<kSwiGLU>(nt, tw, tx, g, st); break;
+      default: e = launch_stream_nt<kRope>(nt, tw, tx, g, st); break;
+    }
+  } else {
+    CUtensorMap tx, tw;
+    if (!make_map(&tx, c.x, c.M, c.K, c.ldx, BM) || !make_map(&tw, c.w, c.N, c.K, c.ldw, BN))
+      return "cuTensorMapEncodeTiled failed";
+    switch (c.epi) {
+      case kStore: e = launch_big<kStore>(tx, tw, g, c.device, st); break;
+      case kResid: e = launch_big<kResid>(tx, tw, g, c.device, st); break;
+      case kSwiGLU: e = launch_big<kSwiGLU>(tx, tw, g, c.device, st); break;
+      default: e = launch_big<kRope>(tx, tw, g, c.device, st); break;
+    }
+  }
+  if (e != cudaSuccess) return std::string("launch failed: ") + cudaGetErrorString(e);
+  return "";
+}
+
+}  // namespace dense
+}  // namespace axr

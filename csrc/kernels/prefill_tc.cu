@@ -60,8 +60,13 @@ struct Params {
   volatile int* err;
   int num_splits;   // KV slices per (query tile, head, sequence); 1 = no split
   int gpack;        // 1: grid.y = query heads; G = Hq/Hkv: grid.y = KV heads, rows = (token, head of the group)
-  float* part_o;    // [T*Hq, S, 128] normalised partial outputs (S > 1)
-  float* part_lse;  // [T*Hq, S] log2-domain log-sum-exps (S > 1)
+  float* part_o;    // [T*Hq, S, 128] normalised partial outputs (S > 1 or partial_only)
+  float* part_lse;  // [T*Hq, S] log2-domain log-sum-exps (S > 1 or partial_only)
+  // Shared-prefix decode: every row sees all seq_lens[b] keys (no causal mask), row i's q
+  // is row q_index[i] of q, and the result stays as partials for a later merge.
+  int noncausal;
+  const int* q_index;  // nullable: token i reads q row i
+  int partial_only;
 };
 
 // byte offset of 16-byte unit u (0..15) of row r in a [128 x 128] bf16 K-major SW128 tile
@@ -100,7 +105,7 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
   if (row0 >= nrow) return;
   const bool has_b = row0 + BM < nrow;
   const int kv_len = p.seq_lens[b];
-  const int pos0 = kv_len - nq;  // absolute position of token 0
+  const int pos0 = p.noncausal ? kv_len : kv_len - nq;  // absolute position of token 0
   const int kvh = G > 1 ? hy : hy / (p.Hq / p.Hkv);
   const int m_last = (min(nrow, row0 + 2 * BM) - 1) / G;  // last token of the tile
   const int kv_end = min(kv_len, pos0 + m_last + 1);
@@ -110,7 +115,7 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
   const int t_begin = split * per;
   const int n_tiles = max(0, min(n_all, t_begin + per) - t_begin);
   if (n_tiles == 0) {  // no keys for this slice: mark its partials empty
-    for (int r = threadIdx.x; r < 2 * BM; r += blockDim.x) {
+    for (int r = threadIdx.x; p.part_lse != nullptr && r < 2 * BM; r += blockDim.x) {
       const int rr = row0 + r;
       if (rr < nrow) {
         const int head = G > 1 ? kvh * G + rr % G : hy;
@@ -234,7 +239,8 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
     const int hq = G > 1 ? kvh * G + qr % G : hy;
     const bool active = x == 0 || has_b;
     {
-      const char* src = reinterpret_cast<const char*>(p.q + ((long long)(q0 + qt) * p.Hq + hq) * HD);
+      const int src_tok = p.q_index != nullptr ? p.q_index[q0 + qt] : q0 + qt;
+      const char* src = reinterpret_cast<const char*>(p.q + ((long long)src_tok * p.Hq + hq) * HD);
 #pragma unroll
       for (int u = 0; u < 16; ++u) cp_async16_zfill(sQ + x * TILE + swz_off(row, u), src + u * 16, row_valid);
       cp_async_commit();
@@ -322,7 +328,7 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
     }
     // ---------------- epilogue: O / l -> out
     if (ok) ok = warp_ok(tc::mbar_wait(o_done, 0, p.err, 21), p.err);
-    if (ok && S > 1) {  // normalised partial output + log-sum-exp of this KV slice
+    if (ok && (S > 1 || p.partial_only)) {  // normalised partial output + log-sum-exp of this KV slice
       tc::tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       const long long pr = ((long long)(q0 + qt) * p.Hq + hq) * S + split;
@@ -389,7 +395,8 @@ void prefill_attention_tc(torch::Tensor q, int64_t k, int64_t v, int64_t blk_str
                           int64_t num_blocks, torch::Tensor block_table, torch::Tensor cu_q, torch::Tensor seq_lens,
                           int64_t Hkv, double scale, int64_t max_q, torch::Tensor out, torch::Tensor err,
                           int64_t num_splits, c10::optional<torch::Tensor> part_o,
-                          c10::optional<torch::Tensor> part_lse, int64_t gqa_pack) {
+                          c10::optional<torch::Tensor> part_lse, int64_t gqa_pack, int64_t noncausal,
+                          c10::optional<torch::Tensor> q_index, int64_t partial_only) {
   using namespace fa;
   TORCH_CHECK(q.is_cuda() && q.scalar_type() == torch::kBFloat16 && q.is_contiguous() && q.dim() == 3 &&
                   q.size(2) == HD,
@@ -424,10 +431,19 @@ void prefill_attention_tc(torch::Tensor q, int64_t k, int64_t v, int64_t blk_str
   p.gpack = gqa_pack > 1 ? G : 1;
   p.part_o = nullptr;
   p.part_lse = nullptr;
-  if (S > 1) {
+  p.noncausal = noncausal != 0;
+  p.partial_only = partial_only != 0;
+  p.q_index = nullptr;
+  // rows of the partials: q rows, or the q_index rows (shared-prefix decode)
+  const int64_t R = q_index.has_value() ? q_index->numel() : T;
+  if (q_index.has_value()) {
+    TORCH_CHECK(q_index->is_cuda() && q_index->scalar_type() == torch::kInt32, "prefill_tc: q_index int32");
+    p.q_index = q_index->data_ptr<int>();
+  }
+  if (S > 1 || p.partial_only) {
     TORCH_CHECK(part_o.has_value() && part_lse.has_value() && part_o->scalar_type() == torch::kFloat32 &&
                     part_lse->scalar_type() == torch::kFloat32 &&
-                    part_o->numel() >= (int64_t)T * Hq * S * HD && part_lse->numel() >= (int64_t)T * Hq * S,
+                    part_o->numel() >= R * Hq * S * HD && part_lse->numel() >= R * Hq * S,
                 "prefill_tc: split-KV scratch too small");
     p.part_o = part_o->data_ptr<float>();
     p.part_lse = part_lse->data_ptr<float>();
@@ -444,7 +460,7 @@ void prefill_attention_tc(torch::Tensor q, int64_t k, int64_t v, int64_t blk_str
   auto st = at::cuda::getCurrentCUDAStream();
   prefill_tc_kernel<<<grid, THREADS, SMEM, st>>>(tk, tv, p);
   AXR_CHECK_CUDA(cudaGetLastError());
-  if (S > 1 && T > 0) {
+  if (S > 1 && T > 0 && !p.partial_only) {
     decode_combine_kernel<128><<<T * Hq, 128, 0, st>>>(p.part_o, p.part_lse, p.out, S);
     AXR_CHECK_CUDA(cudaGetLastError());
   }
