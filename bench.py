@@ -9,11 +9,12 @@ NVLink by the fused pull + scatter kernel. Random-init weights of the real
 architecture; synthetic token data.
 
 Phases (every rank runs its own engine, one process per GPU):
-  1. populate: each rank prefills its share of the 64 prefixes cold and captures them
-     into their owner shards (untimed);
+  1. populate: each rank prefills the prefixes its pool shard owns, cold, and captures
+     them locally (untimed);
   2. latency probe: one request at a time, TTFT of AMF hits vs cold prefills and the
      restore bandwidth, timed with CUDA events;
-  3. throughput: W warm-up waves then exactly K timed waves of B requests per rank
+  3. throughput: W warm-up waves then exactly K timed waves of B requests per rank, drawn
+     from one global stream and routed by owner affinity (parallel/dp_router.py)
      (admission + restore/prefill + 128 decode steps each), bracketed by barrier +
      synchronize, CUDA-event timed, max over ranks. ``value`` = output tokens/s of
      the whole job;
@@ -128,24 +129,35 @@ class ClockSampler:
 
 # ----------------------------------------------------------------------------- workload
 class Workload:
-    def __init__(self, args, vocab: int, rank: int):
+    """Request streams of the bench. Waves come from one global stream that every rank
+    draws identically (N x B requests per wave), routed over the GPUs by owner affinity
+    (``parallel/dp_router.py``): a pooled prefix goes to the GPU whose shard owns it while
+    that GPU has room, cold prefixes are spread evenly. At N = 1 the global stream is the
+    single GPU's stream. The latency probes use per-rank streams."""
+
+    def __init__(self, args, vocab: int, rank: int, world: int = 1, owner=None):
         self.args = args
         self.vocab = vocab
+        self.rank, self.world = rank, world
+        self.owner = owner or (lambda toks: 0)
         g = np.random.default_rng(args.seed)
         self.prefixes = [g.integers(0, vocab, args.prefix_len, dtype=np.int64).tolist() for _ in range(args.prefixes)]
+        self.prefix_owner = [self.owner(p) for p in self.prefixes]
         ranks = np.arange(1, args.prefixes + 1, dtype=np.float64)
         p = ranks ** (-args.zipf)
         self.zipf_p = p / p.sum()
         # Reuse-or-fresh is decided by an exact schedule, not a coin: request k of the
         # stream brings a fresh prefix when floor((k+1) q) > floor(k q), q = 1 - reuse, so
         # every wave holds the configured share of cold 8 K prefills (3 or 4 of 32 at
-        # q = 0.1) on every GPU -- weak scaling with equal per-GPU work, and no sampling
-        # noise in a run of a few waves. The Zipf picks of reused prefixes and the random
-        # tokens are per-rank random streams. Replaying the schedule position and the pick
-        # stream gives a wave of the same mix with new tokens.
+        # q = 0.1 per GPU) -- weak scaling with equal per-GPU work, and no sampling noise in
+        # a run of a few waves. Replaying the schedule position and the pick stream gives a
+        # wave of the same mix with new tokens.
         self.k = 0
-        self.pick_rng = np.random.default_rng(args.seed * 1000 + 23 + rank)
-        self.tok_rng = np.random.default_rng(args.seed * 1000 + 29 + rank)
+        self.pick_rng = np.random.default_rng(args.seed * 1000 + 23)
+        self.tok_rng = np.random.default_rng(args.seed * 1000 + 29)
+        self.probe_pick = np.random.default_rng(args.seed * 1000 + 31 + rank)
+        self.probe_tok = np.random.default_rng(args.seed * 1000 + 37 + rank)
+        self.route_stats = {"pooled": 0, "routing_misses": 0}
 
     def _fresh_next(self) -> bool:
         q = 1.0 - self.args.reuse
@@ -154,15 +166,38 @@ class Workload:
         return fresh
 
     def request(self, force: str = ""):
+        """One latency-probe request of this rank: (prompt, reused)."""
         a = self.args
-        reuse = force == "hit" or (force != "cold" and not self._fresh_next())
+        reuse = force == "hit" or (force != "cold" and self.probe_pick.random() < a.reuse)
         if reuse:
-            i = int(self.pick_rng.choice(a.prefixes, p=self.zipf_p))
-            prefix = self.prefixes[i]
+            prefix = self.prefixes[int(self.probe_pick.choice(a.prefixes, p=self.zipf_p))]
         else:
-            prefix = self.tok_rng.integers(0, self.vocab, a.prefix_len, dtype=np.int64).tolist()
-        suffix = self.tok_rng.integers(0, self.vocab, a.suffix_len, dtype=np.int64).tolist()
+            prefix = self.probe_tok.integers(0, self.vocab, a.prefix_len, dtype=np.int64).tolist()
+        suffix = self.probe_tok.integers(0, self.vocab, a.suffix_len, dtype=np.int64).tolist()
         return prefix + suffix, reuse
+
+    def wave(self, per_rank: int):
+        """This rank's share of the next global wave of world x per_rank requests."""
+        from axropus_deploy_b200.parallel.dp_router import route_wave, routing_stats
+
+        a = self.args
+        prompts, owners, cold = [], [], []
+        for _ in range(per_rank * self.world):
+            if self._fresh_next():
+                prefix = self.tok_rng.integers(0, self.vocab, a.prefix_len, dtype=np.int64).tolist()
+                owners.append(self.owner(prefix) if self.world > 1 else 0)
+                cold.append(True)
+            else:
+                i = int(self.pick_rng.choice(a.prefixes, p=self.zipf_p))
+                prefix = self.prefixes[i]
+                owners.append(self.prefix_owner[i])
+                cold.append(False)
+            prompts.append(prefix + self.tok_rng.integers(0, self.vocab, a.suffix_len, dtype=np.int64).tolist())
+        assigned = route_wave(owners, cold, self.world, per_rank)
+        st = routing_stats(owners, cold, assigned)
+        self.route_stats["pooled"] += st["pooled"]
+        self.route_stats["routing_misses"] += st["routing_misses"]
+        return [p for p, r in zip(prompts, assigned) if r == self.rank]
 
     def choice_state(self):
         return self.k, self.pick_rng.bit_generator.state
@@ -223,7 +258,9 @@ def run_ours(args) -> None:
     amf = AmfManager(raw_pool=pool if args.pool == "raw" else None, comp_pool=pool if args.pool != "raw" else None,
                      min_tokens=64)
     eng.amf = amf
-    wl = Workload(args, cfg.vocab, info.rank)
+    from axropus_deploy_b200.amf.keys import pool_key
+
+    wl = Workload(args, cfg.vocab, info.rank, info.world, lambda toks: pool.owner(pool_key(toks[:args.prefix_len])))
     sp = SamplingParams(max_tokens=args.out_tokens)
 
     def run_requests(prompts):
@@ -233,7 +270,7 @@ def run_ours(args) -> None:
         return reqs
 
     # ---- 1. populate the pool (each rank its share), untimed
-    mine = [i for i in range(args.prefixes) if i % info.world == info.rank]
+    mine = [i for i in range(args.prefixes) if wl.prefix_owner[i] % info.world == info.rank]  # local captures
     for j in range(0, len(mine), 4):
         prompts = [wl.prefixes[i] + [1] * 16 for i in mine[j:j + 4]]
         reqs = [eng.add_request(p, SamplingParams(max_tokens=1), amf_prefix_len=args.prefix_len) for p in prompts]
@@ -272,7 +309,6 @@ def run_ours(args) -> None:
         ttft_cold.append(ms)
     # restore bandwidth with device timing: restore one prefix owned by this GPU's shard
     # and (N > 1) one owned by another GPU's shard (pulled over NVLink), 6 times each
-    from axropus_deploy_b200.amf.keys import pool_key
 
     def restore_gbps(owner_local: bool):
         for idx, pf in enumerate(wl.prefixes):
@@ -303,9 +339,11 @@ def run_ours(args) -> None:
 
     # ---- 3. throughput waves
     for _ in range(args.warmup):
-        run_requests([wl.request()[0] for _ in range(args.batch)])
+        run_requests(wl.wave(args.batch))
     choice_state = wl.choice_state()
-    waves = [[wl.request()[0] for _ in range(args.batch)] for _ in range(args.steps)]
+    route0 = dict(wl.route_stats)
+    waves = [wl.wave(args.batch) for _ in range(args.steps)]
+    route = {k: wl.route_stats[k] - route0[k] for k in route0}
     sampler = ClockSampler(dev.index)
     torch.cuda.synchronize()
     barrier(info)
@@ -346,7 +384,7 @@ def run_ours(args) -> None:
     # suffixes and fresh cold prefixes
     wl.set_choice_state(choice_state)
     n_e2e = args.e2e_waves or args.steps
-    e2e_waves = [[wl.request()[0] for _ in range(args.batch)] for _ in range(n_e2e)]
+    e2e_waves = [wl.wave(args.batch) for _ in range(n_e2e)]
     torch.cuda.synchronize()
     barrier(info)
     h0 = time.perf_counter()
@@ -398,6 +436,10 @@ def run_ours(args) -> None:
                                  "restore_gbps = prefix owned by this GPU's shard, restore_gbps_nvlink = owned by "
                                  "another GPU's shard (fused pull over NVLink + scatter)",
             "pool_slots_per_shard": slots_per_shard,
+            "routing": {"policy": "owner affinity, per-GPU cap = batch, cold prefixes spread evenly",
+                        "pooled_requests": route["pooled"], "routing_misses": route["routing_misses"],
+                        "nvlink_restore_share": round(route["routing_misses"] / max(1, route["pooled"]), 4)},
+            "cascade_decode": {k: eng.stat[k] - st0.get(k, 0) for k in ("cascade_steps", "cascade_grouped_seqs")},
             "wave_mix": gathered[0]["waves"], "amf_hits_rank0": gathered[0]["hits"],
             "ms_per_step_by_rank": [round(g["ms"] / args.steps, 1) for g in gathered],
             "graph_captures_in_timed_region_rank0": {"decode": graphs1[0] - graphs0[0],
