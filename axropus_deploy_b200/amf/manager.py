@@ -190,8 +190,12 @@ class AmfManager:
             if mirror_lm and promote_from != "lmcache":
                 self.lmcache.store(key, dense.t)
             if want_disk and promote_from != "disk":
-                if self.disk.save(t, dense.t, saved_ms=savings_ms):
-                    self.stat["disk_saves"] += 1
+                try:
+                    if self.disk.save(t, dense.t, saved_ms=savings_ms):
+                        self.stat["disk_saves"] += 1
+                except OSError as exc:  # a full or failing disk loses the mirror copy, never the step
+                    self.stat["disk_save_failures"] = self.stat.get("disk_save_failures", 0) + 1
+                    log.warning("AMF disk save failed: %s", exc)
         return ok
 
     # ------------------------------------------------------------------ telemetry

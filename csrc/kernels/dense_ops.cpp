@@ -73,7 +73,8 @@ void dense_gemm(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t epi
   if (nt != 0 && !force_big) {
     int64_t need_ws = 0, need_cnt = 0;
     const int sms = at::cuda::getDeviceProperties(c.device)->multiProcessorCount;
-    const int s = splits > 0 ? static_cast<int>(splits) : stream_splits(M, N, K, sms);
+    int s = splits > 0 ? static_cast<int>(splits) : stream_splits(M, N, K, sms);
+    s = std::max(1, std::min(std::min(s, static_cast<int>((K + 63) / 64)), stream_max_splits(nt)));
     if (s > 1) {
       need_ws = ((N + 127) / 128) * static_cast<int64_t>(s) * nt * 128;
       need_cnt = (N + 127) / 128;

@@ -189,7 +189,8 @@ __global__ void __launch_bounds__(128) gemm_stream_kernel(const __grid_constant_
   uint64_t* full = reinterpret_cast<uint64_t*>(base + C::ST * C::STAGE);
   uint64_t* empty = full + C::ST;
   uint64_t* accb = empty + C::ST;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accb + 1);
+  uint64_t* fixb = accb + 1;  // split-K partials staged into shared memory
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fixb + 1);
   int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -206,6 +207,7 @@ __global__ void __launch_bounds__(128) gemm_stream_kernel(const __grid_constant_
       tc::mbar_init(&empty[s], 1);
     }
     tc::mbar_init(accb, 1);
+    tc::mbar_init(fixb, 1);
     tc::fence_barrier_init();
     tc::prefetch_tmap(&tmW);
     tc::prefetch_tmap(&tmX);
@@ -298,23 +300,35 @@ __global__ void __launch_bounds__(128) gemm_stream_kernel(const __grid_constant_
     if (write) __threadfence();
   }
   if (write) {
+    // split-K: each chunk of CH tokens of every split's partial is staged into the idle
+    // TMA ring with one bulk copy per split (one round trip per chunk), then summed in
+    // split order -- the result does not depend on which CTA finished last
+    float* stage = reinterpret_cast<float*>(base);
+    if (g.splits > 1 && threadIdx.x == 0) tc::fence_proxy_async_global_mem();
 #pragma unroll 1
-    for (int c0 = 0; c0 < NT; c0 += C::CH) {
+    for (int c0 = 0, ci = 0; c0 < NT; c0 += C::CH, ++ci) {
       float v[C::CH];
       if (g.splits > 1) {
-        // every split's partial, own included, summed in split order: the result does not
-        // depend on which CTA finished last
+        if (threadIdx.x == 0) {
+          constexpr uint32_t chunk_bytes = C::CH * 128 * 4;
+          tc::mbar_arrive_expect_tx(fixb, chunk_bytes * g.splits);
+          for (int s2 = 0; s2 < g.splits; ++s2)
+            tc::bulk_load(stage + s2 * C::CH * 128, g.ws + ((long long)(tile * g.splits + s2) * NT + c0) * 128,
+                          chunk_bytes, fixb);
+        }
+        const bool ok = tc::mbar_wait(fixb, ci & 1, g.err, 4);
 #pragma unroll
         for (int j = 0; j < C::CH; ++j) v[j] = 0.f;
-        for (int s2 = 0; s2 < g.splits; ++s2) {
-          const float* p = g.ws + (long long)(tile * g.splits + s2) * NT * 128 + c0 * 128 + r;
+        for (int s2 = 0; ok && s2 < g.splits; ++s2) {
 #pragma unroll
-          for (int j = 0; j < C::CH; ++j) v[j] += __ldcg(p + j * 128);
+          for (int j = 0; j < C::CH; ++j) v[j] += stage[(s2 * C::CH + j) * 128 + r];
         }
+        __syncthreads();  // the stage is free for the epilogue's exchange / the next chunk
       } else {
         tmem_ld_chunk<C::CH>(trow + c0, v);
       }
       stream_epilogue<EPI, C::CH>(g, tile, c0, v, sx);
+      if (g.splits > 1) __syncthreads();
     }
   }
   tc::tc_fence_before();
@@ -650,6 +664,17 @@ cudaError_t launch_big(const CUtensorMap& tx, const CUtensorMap& tw, const Args&
 
 }  // namespace
 
+// Largest split count whose partials of one chunk (CH tokens) fit the TMA ring.
+int stream_max_splits(int nt) {
+  switch (nt) {
+    case 16: return (StreamCfg<16>::ST * StreamCfg<16>::STAGE) / (StreamCfg<16>::CH * 512);
+    case 32: return (StreamCfg<32>::ST * StreamCfg<32>::STAGE) / (StreamCfg<32>::CH * 512);
+    case 64: return (StreamCfg<64>::ST * StreamCfg<64>::STAGE) / (StreamCfg<64>::CH * 512);
+    case 128: return (StreamCfg<128>::ST * StreamCfg<128>::STAGE) / (StreamCfg<128>::CH * 512);
+    default: return (StreamCfg<256>::ST * StreamCfg<256>::STAGE) / (StreamCfg<256>::CH * 512);
+  }
+}
+
 int stream_nt(int64_t M) {
   if (M <= 16) return 16;
   if (M <= 32) return 32;
@@ -667,7 +692,8 @@ int stream_splits(int64_t M, int64_t N, int64_t K, int sms) {
   const int64_t slots = static_cast<int64_t>(sms) * (nt <= 128 ? 2 : 1);
   if (tiles >= slots) return 1;
   int64_t s = slots / tiles;
-  s = std::min<int64_t>(s, std::max<int64_t>(1, nk / 4));
+  s = std::min<int64_t>(s, std::max<int64_t>(1, nk / 8));  // >= 8 k-blocks (512 of K) per CTA
+  s = std::min<int64_t>(s, stream_max_splits(nt));          // every split's chunk fits the stage
   return static_cast<int>(std::max<int64_t>(1, s));
 }
 
@@ -721,7 +747,7 @@ std::string dense_gemm_launch(const DenseCall& c, cudaStream_t st) {
   if (nt != 0 && !c.force_big) {
     const int nk = (c.K + 63) / 64;
     g.splits = c.splits > 0 ? c.splits : stream_splits(c.M, c.N, c.K, sm_count(c.device));
-    g.splits = std::max(1, std::min(g.splits, nk));
+    g.splits = std::max(1, std::min(std::min(g.splits, nk), stream_max_splits(nt)));
     if (g.splits > 1) {
       if (!c.ws || !c.cnt) return "split-K scratch missing";
       g.ws = c.ws;

@@ -45,6 +45,8 @@ struct DenseCall {
 
 // Token-column padding of the stream kernel for M rows (0 = M > 256, big kernel).
 int stream_nt(int64_t M);
+// Largest split count of the stream kernel at token padding nt (its shared-memory stage).
+int stream_max_splits(int nt);
 // CTAs per 128-row weight tile of the stream kernel.
 int stream_splits(int64_t M, int64_t N, int64_t K, int sms);
 // {fp32 partial floats, counters} the stream kernel needs.

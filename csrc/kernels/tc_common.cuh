@@ -91,6 +91,18 @@ __device__ __forceinline__ void tma_load_2d(void* smem, const CUtensorMap* map, 
       : "memory");
 }
 
+// Untiled bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned) from this
+// GPU's global memory into shared memory, completion signalled on `bar` (no multicast).
+__device__ __forceinline__ void bulk_load(void* smem, const void* gmem, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(smem)),
+               "l"(gmem), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+// generic-proxy global writes (made visible at gpu scope) -> async-proxy reads
+__device__ __forceinline__ void fence_proxy_async_global_mem() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }
