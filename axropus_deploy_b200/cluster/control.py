@@ -22,10 +22,13 @@ billing and debug endpoints).
 from __future__ import annotations
 
 import json
+import os
 import statistics
 import uuid
 from pathlib import Path
 from typing import Any, Dict, List, Optional
+
+from . import jobspec as jobspec_v1
 
 from ..amf.keys import pool_key
 from ..amf.prompt_policy import amf_prefix_tokens, amf_tenant
@@ -51,7 +54,7 @@ def render_messages(messages: List[Dict[str, Any]]) -> str:
 class ControlPlane:
     def __init__(self, ledger, workers: Dict[str, Any], *, node_id: str = "node-0", node_registry=None,
                  snapshot_index=None, coordinator=None, metrics=GLOBAL_METRICS, max_tokens_limit: int = 32768,
-                 default_backend: str = "axr_engine"):
+                 default_backend: str = "axr_engine", strict_jobspec: Optional[bool] = None):
         self.ledger = ledger
         self.workers = workers  # worker_id -> ClusterWorker (this node's)
         self.node_id = node_id
@@ -61,6 +64,10 @@ class ControlPlane:
         self.metrics = metrics
         self.max_tokens_limit = max_tokens_limit
         self.default_backend = default_backend
+        # korith.jobspec.v1 only (KORITH_JOBSPEC_STRICT=1); otherwise v1 specs are checked
+        # against the contract and the short form ({"prompt": ..., "max_tokens": ...}) is accepted
+        self.strict_jobspec = (os.environ.get("KORITH_JOBSPEC_STRICT", "0") == "1" if strict_jobspec is None
+                               else bool(strict_jobspec))
         infos = []
         for wid, w in workers.items():
             eng = getattr(getattr(w, "adapters", None), "engine", None)
@@ -72,6 +79,11 @@ class ControlPlane:
     def _validate(self, job: Dict[str, Any]) -> Dict[str, Any]:
         if not isinstance(job, dict):
             raise JobError("jobspec must be a JSON object", "INVALID_JOBSPEC")
+        if "schema_version" in job or self.strict_jobspec:
+            errs = jobspec_v1.validate(job)
+            if errs:
+                raise JobError("invalid korith.jobspec.v1: " + "; ".join(errs), "INVALID_JOBSPEC")
+            job = jobspec_v1.to_job(job)
         if "messages" in job and "prompt" not in job:
             if not isinstance(job["messages"], list):
                 raise JobError("messages must be a list", "INVALID_JOBSPEC")
@@ -114,6 +126,8 @@ class ControlPlane:
     def submit(self, job: Dict[str, Any], org_id: str = "default", request_id: str = "",
                tenant_id: str = "default") -> str:
         job = self._validate(dict(job))
+        if org_id == "default" and job.get("org_id"):  # korith.jobspec.v1 owner.org_id
+            org_id = str(job["org_id"])
         job.setdefault("tenant_id", tenant_id)
         idem = job.get("idempotency_key")
         if idem:

@@ -14,9 +14,11 @@ Two step layouts:
   (o | down)``, both collectives fused into the tcgen05 GEMM kernels
   (``csrc/kernels/gemm_tp.cu``). Rows are padded to a multiple of ``128 * W``.
 * **Replicated** (decode and short prefills): every GPU holds all rows; the row-parallel
-  GEMMs are followed by an NCCL all-reduce. At a handful of rows the GEMMs read weights
-  at HBM speed and the all-reduce moves a few hundred KB, so a 1024-row padded fused
-  step would cost more than it saves.
+  GEMMs are followed by a one-shot peer all-reduce (``PeerAllReduce``, csrc/kernels/
+  allreduce.cu: each GPU stores its slice into every peer's receive slot over NVLink and
+  sums the world's slots; NCCL beyond its capacity). At a handful of rows the GEMMs read
+  weights at HBM speed and the all-reduce moves a few hundred KB, so a 1024-row padded
+  fused step would cost more than it saves.
 
 The reference has no tensor parallelism of its own (it passes ``tensor_parallel_size=1``
 to vLLM, axropus/server.py:110); this module is the B200 TP=8 path for Llama-3-70B.

@@ -54,16 +54,19 @@ class _Scratch:
         self.device = device
         self.ws = torch.zeros(0, dtype=torch.float32, device=device)
         self.cnt = torch.zeros(0, dtype=torch.int32, device=device)
+        self._retired = []  # outgrown buffers stay allocated: a captured CUDA graph may still use them
 
     def ensure(self, n_ws: int, n_cnt: int) -> None:
         capturing = torch.cuda.is_current_stream_capturing()
         if n_ws > self.ws.numel():
             if capturing:
                 raise RuntimeError("dense GEMM scratch must be reserved before CUDA-graph capture")
+            self._retired.append(self.ws)
             self.ws = torch.zeros(n_ws, dtype=torch.float32, device=self.device)
         if n_cnt > self.cnt.numel():
             if capturing:
                 raise RuntimeError("dense GEMM scratch must be reserved before CUDA-graph capture")
+            self._retired.append(self.cnt)
             self.cnt = torch.zeros(n_cnt, dtype=torch.int32, device=self.device)
 
     def reset_counters(self) -> None:
@@ -158,6 +161,8 @@ def linear(x: torch.Tensor, w: torch.Tensor, epi: str = "store", out: Optional[t
     nt = C.dense_stream_nt(M)
     if nt and not force_big:
         n_ws, n_cnt = C.dense_stream_workspace(M, N, x.shape[1], sm_count(dev))
+        if splits > 0:  # a forced split count needs its own partials
+            n_ws = max(n_ws, -(-N // 128) * splits * nt * 128)
         sc.ensure(n_ws, n_cnt)
     pos = slots = cos_sin = None
     kc = vc = bs = hs = 0

@@ -459,7 +459,7 @@ def run_ours(args) -> None:
 
 # ----------------------------------------------------------------------------- reference
 def run_reference(args) -> None:
-    from baseline_reference import run as ref_run  # noqa: E402
+    from reference_arm import run as ref_run  # noqa: E402
 
     ref_run(args)
 

@@ -12,6 +12,7 @@ attention of one layer alone.
 from __future__ import annotations
 
 import argparse
+import faulthandler
 import json
 import os
 import statistics
@@ -55,6 +56,7 @@ def build_tables(args, rng):
 
 
 def main():
+    faulthandler.enable()  # a host crash prints where it happened
     ap = argparse.ArgumentParser()
     ap.add_argument("--batch", type=int, default=32)
     ap.add_argument("--context", type=int, default=8448)
@@ -62,6 +64,9 @@ def main():
     ap.add_argument("--prefixes", type=int, default=64)
     ap.add_argument("--reps", type=int, default=20)
     ap.add_argument("--model", default="llama3-8b")
+    ap.add_argument("--prof", action="store_true",
+                    help="run one eager decode forward inside the NVTX range 'decode_step' and stop "
+                         "(for a per-kernel launch list under ncu --nvtx --nvtx-include decode_step/)")
     args = ap.parse_args()
     dev = torch.device("cuda", 0)
     cfg = get_config(args.model)
@@ -99,6 +104,19 @@ def main():
     flush = torch.empty(256 << 20, dtype=torch.int16, device=dev)
     out = {"batch": B, "context": args.context, "groups": [len(r) for r, _ in groups],
            "grouped_seqs": len(q_index), "decode_splits": S, "shared_splits": casc.num_splits}
+
+    if args.prof:
+        meta = AttnMeta(mode="decode", positions=pos, slots=slots, block_table=bt, seq_lens=lens,
+                        max_seq_len=args.context, num_splits=S)
+        for _ in range(2):
+            model.forward(toks, meta, cache)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("decode_step")
+        model.forward(toks, meta, cache)
+        torch.cuda.nvtx.range_pop()
+        torch.cuda.synchronize()
+        print(json.dumps(out), flush=True)
+        return
 
     def timed(fn, reps):
         ts = []

@@ -10,6 +10,7 @@ fraction of the measured copy bandwidth and cuBLAS bf16 peak in MEASURED_PEAKS.j
 from __future__ import annotations
 
 import argparse
+import faulthandler
 import json
 import os
 import statistics
@@ -56,11 +57,18 @@ def timed(fn, flush, reps):
 
 
 def main():
+    faulthandler.enable()  # a host crash prints where it happened
     ap = argparse.ArgumentParser()
     ap.add_argument("--rows", default="1,32,128,256,1024,8320")
     ap.add_argument("--reps", type=int, default=20)
     ap.add_argument("--shapes", default=",".join(SHAPES))
+    ap.add_argument("--chain", action="store_true",
+                    help="time back-to-back launches over rotating weight copies (> 512 MB in all, so every "
+                         "launch reads its weights from HBM), as in a decode step; per-launch average")
+    ap.add_argument("--splits", default="0", help="comma list of forced split counts (0 = automatic)")
     args = ap.parse_args()
+    if args.chain:
+        return chain(args)
     dev = torch.device("cuda", 0)
     hbm, tflops = peaks()
     flush = torch.empty(256 << 20, dtype=torch.int16, device=dev)
@@ -96,6 +104,44 @@ def main():
     from axropus_deploy_b200.ops.gemm import check_errors
 
     assert check_errors(dev) == 0
+
+
+def chain(args):
+    dev = torch.device("cuda", 0)
+    hbm, _ = peaks()
+    g = torch.Generator(device=dev).manual_seed(0)
+    for name in args.shapes.split(","):
+        N, K, epi = SHAPES[name]
+        copies = max(2, -(-(512 << 20) // (N * K * 2)))
+        ws = [torch.empty(N, K, dtype=torch.bfloat16, device=dev).normal_(0, 0.02, generator=g) for _ in range(copies)]
+        dense.reserve(dev, [(N, K)])
+        for M in [int(r) for r in args.rows.split(",")]:
+            x = torch.empty(M, K, dtype=torch.bfloat16, device=dev).normal_(0, 1, generator=g)
+            res = torch.empty(M, N, dtype=torch.bfloat16, device=dev).normal_(0, 1, generator=g)
+            variants = [("cublas", None)] + [(f"ours_s{s}", int(s)) for s in args.splits.split(",")]
+            row = {"shape": name, "M": M, "N": N, "K": K, "copies": copies}
+            for label, sp in variants:
+                def run():
+                    for w in ws:
+                        if sp is None:
+                            torch.matmul(x, w.t())
+                        elif epi == "resid":
+                            dense.linear(x, w, "resid", out=res, res=res, splits=sp)
+                        else:
+                            dense.linear(x, w, epi, splits=sp)
+                for _ in range(2):
+                    run()
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(3):
+                    run()
+                e1.record()
+                e1.synchronize()
+                us = e0.elapsed_time(e1) * 1e3 / (3 * copies)
+                row[label + "_us"] = round(us, 2)
+                row[label + "_frac_hbm"] = round(N * K * 2 / (us * 1e-6) / 1e9 / hbm, 3)
+            print(json.dumps(row), flush=True)
 
 
 if __name__ == "__main__":

@@ -35,6 +35,7 @@
 // Reference counterpart: the dense projections the reference leaves to vLLM / llama.cpp
 // library GEMMs (axropus/server.py:110, core/engine.cpp llama_decode).
 #include <algorithm>
+#include <cstdlib>
 #include <string>
 
 #include "common.cuh"
@@ -119,6 +120,9 @@ __device__ __forceinline__ void tmem_ld_chunk(uint32_t taddr, float (&v)[CH]) {
 
 // Epilogue of one chunk of CH token columns. Thread t holds weight row r = t of the tile
 // (feature n0 + r) for tokens c0 .. c0 + CH - 1. sx: [128][CH + 1] fp32 exchange space.
+// Every global input of a chunk is loaded before the chunk's first store: `out` may be
+// `res` (the residual stream updated in place), so a load after a store could not be
+// issued early and each token would cost a full memory round trip.
 template <int EPI, int CH>
 __device__ __forceinline__ void stream_epilogue(const Args& g, int tile, int c0, const float (&v)[CH], float* sx) {
   const int r = threadIdx.x;
@@ -126,25 +130,28 @@ __device__ __forceinline__ void stream_epilogue(const Args& g, int tile, int c0,
   if constexpr (EPI == kStore || EPI == kResid) {
     const int n = tile * 128 + r;
     if (n >= g.N) return;
+    float rv[CH];
 #pragma unroll
     for (int j = 0; j < CH; ++j) {
-      const int m = c0 + j;
-      if (m < g.M) {
-        float x = v[j];
-        if constexpr (EPI == kResid) x += __bfloat162float(e.res[(long long)m * e.ldr + n]);
-        e.out[(long long)m * e.ldo + n] = __float2bfloat16(x);
+      rv[j] = 0.f;
+      if constexpr (EPI == kResid) {
+        if (c0 + j < g.M) rv[j] = __bfloat162float(e.res[(long long)(c0 + j) * e.ldr + n]);
       }
     }
+#pragma unroll
+    for (int j = 0; j < CH; ++j)
+      if (c0 + j < g.M) e.out[(long long)(c0 + j) * e.ldo + n] = __float2bfloat16(v[j] + rv[j]);
   } else {
 #pragma unroll
     for (int j = 0; j < CH; ++j) sx[r * (CH + 1) + j] = v[j];
     __syncthreads();
     const int d = r & 63, jj = r >> 6;
+    constexpr int JN = CH / 2;  // tokens of this thread: jj, jj + 2, ...
     if constexpr (EPI == kSwiGLU) {
       const int f = tile * 64 + d;
-#pragma unroll 4
-      for (int j = jj; j < CH; j += 2) {
-        const int m = c0 + j;
+#pragma unroll
+      for (int t = 0; t < JN; ++t) {
+        const int j = jj + 2 * t, m = c0 + j;
         if (m < g.M) {
           const float gt = sx[d * (CH + 1) + j], up = sx[(d + 64) * (CH + 1) + j];
           e.out[(long long)m * e.ldo + f] = __float2bfloat16(silu(gt) * up);
@@ -153,27 +160,31 @@ __device__ __forceinline__ void stream_epilogue(const Args& g, int tile, int c0,
     } else {  // ROPE: tile = head row hr of [q | k | v]
       const int hr = tile;
       const bool rot = hr < e.Hq + e.Hkv, is_q = hr < e.Hq, is_v = !rot;
-#pragma unroll 4
-      for (int j = jj; j < CH; j += 2) {
-        const int m = c0 + j;
-        if (m >= g.M) continue;
+      float co[JN], si[JN];
+      __nv_bfloat16* dst[JN];
+#pragma unroll
+      for (int t = 0; t < JN; ++t) {  // positions, slots, cos / sin first
+        const int m = c0 + jj + 2 * t;
+        co[t] = 1.f;
+        si[t] = 0.f;
+        dst[t] = nullptr;
+        if (m < g.M) {
+          if (rot) {
+            const int ps = min(max(e.pos[m], 0), e.n_pos - 1);
+            co[t] = e.cos_sin[(long long)ps * 128 + d];
+            si[t] = e.cos_sin[(long long)ps * 128 + 64 + d];
+          }
+          dst[t] = is_q ? e.out + (long long)m * e.ldo + hr * 128
+                        : cache_row(e, is_v, is_v ? hr - e.Hq - e.Hkv : hr - e.Hq, m);
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < JN; ++t) {
+        if (dst[t] == nullptr) continue;
+        const int j = jj + 2 * t;
         const float x1 = sx[d * (CH + 1) + j], x2 = sx[(d + 64) * (CH + 1) + j];
-        float o1 = x1, o2 = x2;
-        if (rot) {
-          const int ps = min(max(e.pos[m], 0), e.n_pos - 1);
-          const float co = e.cos_sin[(long long)ps * 128 + d], si = e.cos_sin[(long long)ps * 128 + 64 + d];
-          o1 = x1 * co - x2 * si;
-          o2 = x2 * co + x1 * si;
-        }
-        __nv_bfloat16* dst;
-        if (is_q) {
-          dst = e.out + (long long)m * e.ldo + hr * 128;
-        } else {
-          dst = cache_row(e, is_v, is_v ? hr - e.Hq - e.Hkv : hr - e.Hq, m);
-          if (dst == nullptr) continue;
-        }
-        dst[d] = __float2bfloat16(o1);
-        dst[d + 64] = __float2bfloat16(o2);
+        dst[t][d] = __float2bfloat16(x1 * co[t] - x2 * si[t]);
+        dst[t][d + 64] = __float2bfloat16(x2 * co[t] + x1 * si[t]);
       }
     }
     __syncthreads();
@@ -608,6 +619,15 @@ int sm_count(int dev) {
   return sms;
 }
 
+// Programmatic dependent launch (AXR_DENSE_PDL=0 turns it off, for measurements).
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("AXR_DENSE_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 template <typename Kernel>
 cudaError_t launch_pdl(Kernel kernel, dim3 grid, dim3 block, int smem, cudaStream_t st, const CUtensorMap& m0,
                        const CUtensorMap& m1, const Args& g) {
@@ -620,7 +640,7 @@ cudaError_t launch_pdl(Kernel kernel, dim3 grid, dim3 block, int smem, cudaStrea
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kernel, m0, m1, g);
 }
 
