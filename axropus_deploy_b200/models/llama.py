@@ -57,10 +57,13 @@ class AttnMeta:
 
 class LlamaModel:
     def __init__(self, cfg: ModelConfig, device="cpu", dtype=torch.bfloat16, seed: int = 0,
-                 init_std: float = 0.02, layers: Optional[int] = None, ep_info=None, ep_max_tokens: int = 16384):
+                 init_std: float = 0.02, layers: Optional[int] = None, ep_info=None, ep_max_tokens: int = 16384,
+                 init: str = "random"):
         """``ep_info`` (a ``DistInfo``) splits the experts of an MoE model over the GPUs of
         an expert-parallel group: this process keeps ``E / world`` of them and every MoE
-        layer runs the fused dispatch / grouped GEMM / combine kernels."""
+        layer runs the fused dispatch / grouped GEMM / combine kernels. ``init="empty"``
+        allocates the weights without initialising them (a checkpoint loader fills them,
+        ``models/loader.py``)."""
         self.cfg = cfg
         self.device = torch.device(device)
         self.dtype = dtype
@@ -72,9 +75,12 @@ class LlamaModel:
         H, F = cfg.hidden, cfg.ffn
         n_layers = layers if layers is not None else cfg.num_layers
 
+        fill = init != "empty"
+
         def rnd(*shape, std=init_std):
             t = torch.empty(*shape, dtype=dtype, device=self.device)
-            t.normal_(0.0, std, generator=g)
+            if fill:
+                t.normal_(0.0, std, generator=g)
             return t
 
         def ones(n):
@@ -82,7 +88,8 @@ class LlamaModel:
 
         def rnd_g(gen, *shape, std=init_std):
             t = torch.empty(*shape, dtype=dtype, device=self.device)
-            t.normal_(0.0, std, generator=gen)
+            if fill:
+                t.normal_(0.0, std, generator=gen)
             return t
 
         self.embed = rnd(cfg.vocab, H, std=1.0)

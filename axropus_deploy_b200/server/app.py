@@ -6,7 +6,10 @@ bearer key. Unlike the reference -- which runs a plain ``LLM.generate`` and stor
 zero-filled stub KV on a miss (server.py:217-242) -- requests here run through the
 engine: a hit restores the prefix KV into the live cache and prefills only the
 suffix, a miss prefills and captures. Token ids can be sent directly
-(``prompt_token_ids``); text falls back to byte-level tokens like the reference.
+(``prompt_token_ids``). When ``AXROPUS_MODEL`` names a Hugging Face model directory the
+engine serves its weights (``models/loader.py``) and text goes through its
+``tokenizer.json`` (``models/tokenizer.py``), with the Llama-3 chat template for chat
+requests; without one, text falls back to byte-level tokens like the reference.
 """
 from __future__ import annotations
 
@@ -27,7 +30,13 @@ from .service import EngineService
 log = logging.getLogger(__name__)
 
 
-def render_messages(messages: List[Dict[str, Any]]) -> str:
+def render_messages(messages: List[Dict[str, Any]], tokenizer=None) -> str:
+    if tokenizer is not None and "<|start_header_id|>" in tokenizer.added:
+        # Llama-3 chat format: header per turn, end-of-turn marks, assistant header last
+        out = "<|begin_of_text|>"
+        for m in messages:
+            out += f"<|start_header_id|>{m.get('role', 'user')}<|end_header_id|>\n\n{m.get('content', '')}<|eot_id|>"
+        return out + "<|start_header_id|>assistant<|end_header_id|>\n\n"
     return "".join(f"<|{m.get('role', 'user')}|>{m.get('content', '')}<|/{m.get('role', 'user')}|>" for m in messages)
 
 
@@ -37,6 +46,22 @@ def byte_tokens(text: str) -> List[int]:
 
 def detok(tokens: List[int]) -> str:
     return bytes(t % 256 for t in tokens).decode("utf-8", "replace")
+
+
+def load_tokenizer(model_dir: str):
+    """The model directory's tokenizer.json, or None."""
+    import os
+
+    from ..models.tokenizer import Tokenizer
+
+    p = os.path.join(model_dir, "tokenizer.json")
+    return Tokenizer.from_file(p) if os.path.isfile(p) else None
+
+
+def is_model_dir(path: str) -> bool:
+    import os
+
+    return bool(path) and os.path.isfile(os.path.join(path, "config.json"))
 
 
 def build_engine(cfg: AxropusConfig, kcfg: Optional[KorithConfig] = None, *, num_blocks: Optional[int] = None):
@@ -51,10 +76,16 @@ def build_engine(cfg: AxropusConfig, kcfg: Optional[KorithConfig] = None, *, num
     from ..amf.pool import PoolSlab
 
     kcfg = kcfg or KorithConfig.from_env()
-    name = cfg.model if cfg.model in PRESETS else "tiny128"
-    mc = get_config(name)
     dev = torch.device(cfg.device if (cfg.device == "cpu" or torch.cuda.is_available()) else "cpu")
-    model = LlamaModel(mc, dev, seed=0)
+    if is_model_dir(cfg.model):  # a Hugging Face checkpoint directory
+        from ..models.loader import load_pretrained
+
+        model = load_pretrained(cfg.model, dev)
+        mc = model.cfg
+    else:
+        name = cfg.model if cfg.model in PRESETS else "tiny128"
+        mc = get_config(name)
+        model = LlamaModel(mc, dev, seed=0)
     amf = None
     if kcfg.enable_amf or kcfg.vram_cache_gb or kcfg.vram_pool_gb:
         raw = comp = None
@@ -86,8 +117,11 @@ def build_engine(cfg: AxropusConfig, kcfg: Optional[KorithConfig] = None, *, num
     return LLMEngine(model, ecfg, amf)
 
 
-def create_app(cfg: AxropusConfig, engine=None):
+def create_app(cfg: AxropusConfig, engine=None, tokenizer=None):
     eng = engine or build_engine(cfg)
+    tok = tokenizer if tokenizer is not None else (load_tokenizer(cfg.model) if is_model_dir(cfg.model) else None)
+    encode = (lambda text: tok.encode(text)) if tok is not None else byte_tokens
+    decode = tok.decode if tok is not None else detok
     svc = EngineService(eng)
     metrics = MetricRegistry(cfg.enable_prometheus)
     from contextlib import asynccontextmanager
@@ -108,7 +142,8 @@ def create_app(cfg: AxropusConfig, engine=None):
 
     @app.get("/healthz")
     def healthz():
-        return {"ok": True, "model": eng.model.cfg.name, "device": str(eng.device), "amf": eng.amf is not None}
+        return {"ok": True, "model": eng.model.cfg.name, "device": str(eng.device), "amf": eng.amf is not None,
+                "tokenizer": "tokenizer.json" if tok is not None else "bytes"}
 
     @app.get("/metrics")
     def prom():
@@ -134,7 +169,7 @@ def create_app(cfg: AxropusConfig, engine=None):
             "id": f"cmpl-{r.req_id}", "created": int(time.time()), "model": eng.model.cfg.name,
             "usage": {"prompt_tokens": len(prompt_ids), "completion_tokens": len(r.output),
                       "total_tokens": len(prompt_ids) + len(r.output)},
-            "token_ids": r.output, "text": detok(r.output),
+            "token_ids": r.output, "text": decode(r.output),
             "axropus": {"tier": r.amf_tier, "hit": r.amf_tier != "cold", "latency_ms": round(lat, 3),
                         "ttft_ms": round(r.ttft_ms, 3), "restored_tokens": r.restored_tokens,
                         "prefix_hash": pool_key(prompt_ids[: (len(prompt_ids) - 1) // 16 * 16])},
@@ -150,7 +185,7 @@ def create_app(cfg: AxropusConfig, engine=None):
             if isinstance(p, list):
                 ids = p
             else:  # canonical text, and the AMF prefix it keys on (KORITH_AMF_* prompt policy)
-                prep = prepare_prompt(str(p), byte_tokens)
+                prep = prepare_prompt(str(p), encode)
                 ids = prep["tokens"]
                 if body.get("amf_prefix_len") is None and prep["amf_prefix_len"] is not None:
                     body["amf_prefix_len"] = prep["amf_prefix_len"]
@@ -166,7 +201,7 @@ def create_app(cfg: AxropusConfig, engine=None):
         body = await request.json()
         ids = body.get("prompt_token_ids")
         if not ids:
-            prep = prepare_prompt(render_messages(body.get("messages") or []), byte_tokens)
+            prep = prepare_prompt(render_messages(body.get("messages") or [], tok), encode)
             ids = prep["tokens"]
             if body.get("amf_prefix_len") is None and prep["amf_prefix_len"] is not None:
                 body["amf_prefix_len"] = prep["amf_prefix_len"]
