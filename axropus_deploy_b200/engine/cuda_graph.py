@@ -7,11 +7,19 @@ copy (tokens, positions, slots, lengths) and one device gather of the block-tabl
 rows. Padding rows get length 0 and slot -1, which every kernel treats as "no work".
 The split-KV decode kernel is captured with the engine's maximum context, so its
 grid is fixed; splits past a sequence's last page exit immediately.
+
+The greedy token of every row (argmax) is part of the graph and lands in ``tok_out``;
+:meth:`DecodeGraphRunner.run` then starts one asynchronous copy of the tokens and the
+kernels' error flag into pinned memory. The next step may take its input tokens from
+``tok_out`` on the device (``dev_tokens``), so the engine can launch step t + 1 before
+it reads step t's tokens (decode pipelining). Host staging is double-buffered: a
+buffer is written again only two launches later, after the engine has waited for the
+earlier one.
 """
 from __future__ import annotations
 
 import bisect
-from typing import Dict, List
+from typing import Dict, List, Optional
 
 import torch
 
@@ -29,10 +37,16 @@ class DecodeGraphRunner:
         self.buckets = [b for b in BUCKETS if b < self.max_b] + [self.max_b]
         mb = engine.max_blocks_per_seq
         self.ints = torch.zeros(4, self.max_b, dtype=torch.int32, device=dev)  # tok, pos, slot, len
-        self.host = torch.zeros(4, self.max_b, dtype=torch.int32).pin_memory()
+        self.hosts = [torch.zeros(4, self.max_b, dtype=torch.int32).pin_memory() for _ in range(2)]
         self.bt = torch.zeros(self.max_b, mb, dtype=torch.int32, device=dev)
         self.rows = torch.zeros(self.max_b, dtype=torch.long, device=dev)
-        self.rows_host = torch.zeros(self.max_b, dtype=torch.long).pin_memory()
+        self.rows_hosts = [torch.zeros(self.max_b, dtype=torch.long).pin_memory() for _ in range(2)]
+        self.tok_out = torch.zeros(self.max_b, dtype=torch.int32, device=dev)  # greedy tokens of the last replay
+        self.tok_host = torch.zeros(2, self.max_b + 1, dtype=torch.int32).pin_memory()  # tokens + error flag
+        self.gather = torch.zeros(self.max_b, dtype=torch.long, device=dev)
+        self.gather_host = [torch.zeros(self.max_b, dtype=torch.long).pin_memory() for _ in range(2)]
+        self.events = [torch.cuda.Event(), torch.cuda.Event()]
+        self.flip = 0
         self.graphs: Dict[int, torch.cuda.CUDAGraph] = {}
         self.outs: Dict[int, torch.Tensor] = {}
         self.ws = DecodeWorkspace()
@@ -118,6 +132,9 @@ class DecodeGraphRunner:
             n0 = LAUNCHES[0]
             with torch.cuda.graph(g, pool=self.pool):
                 out = eng.model.forward(self.ints[0, :b], self._meta(b), cache)
+                from ..ops.layers import argmax
+
+                argmax(out, out=self.tok_out[:b])
             self.kernels[b] = LAUNCHES[0] - n0
             LAUNCHES[0] = n0
             if self.pool is None:
@@ -127,16 +144,22 @@ class DecodeGraphRunner:
         self.graphs[b] = g
         self.outs[b] = out
 
-    def run(self, reqs, toks: List[int], pos: List[int], slots: List[int], lens: List[int],
-            plan=None) -> torch.Tensor:
+    def run(self, reqs, toks: Optional[List[int]], pos: List[int], slots: List[int], lens: List[int],
+            plan=None, dev_tokens: Optional[List[int]] = None):
+        """Replays the bucket's graph for ``reqs``. Input tokens come from ``toks`` (host)
+        or, with ``dev_tokens``, from rows of the previous replay's ``tok_out``. Returns
+        (logits [n, vocab], pinned slot of the tokens + error flag, event after their copy)."""
         n = len(reqs)
         b = self.buckets[bisect.bisect_left(self.buckets, n)]
         if b not in self.graphs:
             self._capture(b)
         if self.cascade:
             self._load_plan(plan, n)
-        h = self.host
-        h[0, :n] = torch.tensor(toks, dtype=torch.int32)
+        slot = self.flip
+        self.flip ^= 1
+        h = self.hosts[slot]
+        if toks is not None:
+            h[0, :n] = torch.tensor(toks, dtype=torch.int32)
         h[1, :n] = torch.tensor(pos, dtype=torch.int32)
         h[2, :n] = torch.tensor(slots, dtype=torch.int32)
         h[3, :n] = torch.tensor(lens, dtype=torch.int32)
@@ -145,15 +168,34 @@ class DecodeGraphRunner:
             h[1, n:b] = 0
             h[2, n:b] = -1
             h[3, n:b] = 0
-        self.ints[:, :b].copy_(h[:, :b], non_blocking=True)
-        self.rows_host[:n] = torch.tensor([r.row for r in reqs], dtype=torch.long)
-        self.rows[:n].copy_(self.rows_host[:n], non_blocking=True)
+        if dev_tokens is None:
+            self.ints[:, :b].copy_(h[:, :b], non_blocking=True)
+        else:
+            self.ints[1:, :b].copy_(h[1:, :b], non_blocking=True)
+            if dev_tokens == list(range(n)):
+                self.ints[0, :n].copy_(self.tok_out[:n])
+            else:
+                gh = self.gather_host[slot]
+                gh[:n] = torch.tensor(dev_tokens, dtype=torch.long)
+                self.gather[:n].copy_(gh[:n], non_blocking=True)
+                self.ints[0, :n].copy_(self.tok_out.index_select(0, self.gather[:n]))
+            if b > n:
+                self.ints[0, n:b].zero_()
+        rh = self.rows_hosts[slot]
+        rh[:n] = torch.tensor([r.row for r in reqs], dtype=torch.long)
+        self.rows[:n].copy_(rh[:n], non_blocking=True)
         self.bt[:n] = self.eng.block_table.index_select(0, self.rows[:n])
         self.graphs[b].replay()
         from ..ops._ext import LAUNCHES
+        from ..ops.gemm import error_flag
 
         LAUNCHES[0] += self.kernels[b]
-        return self.outs[b][:n]
+        th = self.tok_host[slot]
+        th[:n].copy_(self.tok_out[:n], non_blocking=True)
+        th[n:n + 1].copy_(error_flag(self.eng.device)[:1], non_blocking=True)
+        ev = self.events[slot]
+        ev.record()
+        return self.outs[b][:n], slot, ev
 
     def close(self) -> None:
         self.graphs.clear()

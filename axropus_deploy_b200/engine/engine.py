@@ -109,6 +109,8 @@ class EngineConfig:
     # shared pages about once, because the CTAs of sequences that share them run together
     # and hit in L2 (0.127 ms per layer plain against 0.237 ms grouped, measured on B200)
     cascade_min_pages: int = 0
+    # greedy CUDA-graph decode launches step t + 1 before it reads step t's tokens
+    pipeline_decode: bool = True
 
 
 _NVTX = os.environ.get("AXR_NVTX", "0") == "1"
@@ -186,7 +188,9 @@ class LLMEngine:
             self.spec = SpecDecoder(self, cfg.spec_max_depth, drafter)
         self.stat = {"steps": 0, "prefill_tokens": 0, "decode_tokens": 0, "restored_tokens": 0,
                      "local_cached_tokens": 0, "cold_prefill_tokens": 0, "cascade_steps": 0,
-                     "cascade_grouped_seqs": 0}
+                     "cascade_grouped_seqs": 0, "pipelined_decode_steps": 0, "sync_wait_ms": 0.0}
+        # decode pipelining: a greedy graph decode launched but whose tokens are not read yet
+        self._pipe: Optional[dict] = None
         from ..ops.attention import cascade_supported
 
         self._cascade_on = (cfg.cascade_min_pages > 0 and self.device.type == "cuda" and
@@ -209,7 +213,7 @@ class LLMEngine:
         return r
 
     def has_unfinished(self) -> bool:
-        return bool(self.waiting or self.running)
+        return bool(self.waiting or self.running or self._pipe is not None)
 
     def generate(self, prompts: Sequence[Sequence[int]], params: Optional[SamplingParams] = None) -> List[List[int]]:
         reqs = [self.add_request(p, params) for p in prompts]
@@ -263,6 +267,9 @@ class LLMEngine:
     def close(self) -> None:
         """Release CUDA graphs (they hold device memory and must go before the
         process group is destroyed)."""
+        if self._pipe is not None:  # let the step in flight end before its buffers go
+            self._pipe["event"].synchronize()
+            self._pipe = None
         if self._graphs is not None:
             self._graphs.close()
             self._graphs = None
@@ -278,6 +285,18 @@ class LLMEngine:
     def step(self) -> List[Request]:
         self.stat["steps"] += 1
         done: List[Request] = []
+        if self._pipe is not None:
+            if not self.waiting:
+                # nothing to admit: launch the next decode on the device tokens of the one
+                # in flight, then read the in-flight step's tokens while the GPU runs it
+                pipe = self._pipe
+                cont = [r for r in pipe["reqs"] if r.state == "running" and len(r.output) + 1 < r.params.max_tokens]
+                nxt = self._decode_launch(cont, pipe) if cont else None
+                done += self._pipe_finish()
+                self._pipe = nxt
+                return done
+            done += self._pipe_finish()
+            self._pipe = None
         with _nvtx("admit"):
             admitted = self._admit()
         decoding = [r for r in self.running if r.state == "running" and r not in admitted]
@@ -292,11 +311,64 @@ class LLMEngine:
             self._idle_forward()
         if decoding:
             with _nvtx("decode"):
-                done += self._decode(decoding)
+                if self._pipelinable(decoding):
+                    self._pipe = self._decode_launch(decoding, None)
+                else:
+                    done += self._decode(decoding)
         elif self.cfg.lockstep and any_decode:
             self._idle_forward()
-        if self.device.type == "cuda":
+        if self.device.type == "cuda" and self._pipe is None:
             self._check_kernel_errors()
+        return done
+
+    # ------------------------------------------------------------------ decode pipelining
+    def _pipelinable(self, reqs: List[Request]) -> bool:
+        """Greedy CUDA-graph decode of the single-GPU model: the next step's input tokens can
+        stay on the device."""
+        return (self.cfg.pipeline_decode and self._graphs is not None and self.spec is None and not self.cfg.lockstep and
+                type(self.model) is LlamaModel and all(r.params.temperature <= 0 for r in reqs))
+
+    def _decode_launch(self, reqs: List[Request], prev: Optional[dict]) -> dict:
+        """Launches one decode step of ``reqs``. With ``prev`` (the step in flight) each
+        request's input token is the one ``prev`` is computing: it stays on the device."""
+        toks, pos, slots, lens = [], [], [], []
+        for r in reqs:
+            p = r.seq_len if prev is not None else r.seq_len - 1  # position of the input token
+            pos.append(p)
+            slots.append(r.blocks[p // PAGE] * PAGE + p % PAGE)
+            lens.append(p + 1)
+            if prev is None:
+                toks.append(r.output[-1])
+        plan = self.cascade_plan(reqs)
+        if plan is not None:
+            self.stat["cascade_steps"] += 1
+            self.stat["cascade_grouped_seqs"] += plan["grouped"]
+        dev_tokens = None
+        if prev is not None:
+            where = {id(r): i for i, r in enumerate(prev["reqs"])}
+            dev_tokens = [where[id(r)] for r in reqs]
+            self.stat["pipelined_decode_steps"] += 1
+        self.stat["decode_tokens"] += len(reqs)
+        _, slot, ev = self._graphs.run(reqs, None if prev is not None else toks, pos, slots, lens, plan, dev_tokens)
+        return {"reqs": reqs, "slot": slot, "event": ev}
+
+    def _pipe_finish(self) -> List[Request]:
+        """Waits for the step in flight, checks the kernels' error flag and appends its tokens
+        (requests that finished meanwhile on a stop token drop theirs)."""
+        pipe = self._pipe
+        t0 = time.perf_counter()
+        pipe["event"].synchronize()
+        self.stat["sync_wait_ms"] += (time.perf_counter() - t0) * 1e3
+        n = len(pipe["reqs"])
+        vals = self._graphs.tok_host[pipe["slot"], :n + 1].tolist()
+        if vals[n]:
+            self._pipe = None
+            raise RuntimeError(f"a fused kernel gave up waiting (error code {vals[n]}); outputs of this step are "
+                               "invalid (a peer GPU stopped or fell behind by more than the wait bound)")
+        done: List[Request] = []
+        for r, t in zip(pipe["reqs"], vals[:n]):
+            if r.state == "running":
+                self._append(r, t, done)
         return done
 
     def _check_kernel_errors(self) -> None:
@@ -631,7 +703,7 @@ class LLMEngine:
             self.stat["cascade_steps"] += 1
             self.stat["cascade_grouped_seqs"] += plan["grouped"]
         if self._graphs is not None:
-            logits = self._graphs.run(reqs, toks, pos, slots, lens, plan)
+            logits = self._graphs.run(reqs, toks, pos, slots, lens, plan)[0]
         else:
             casc = self._cascade_meta_eager(plan, max(lens))
             d_toks, d_pos, d_slots, d_lens, d_rows = self._stage_int32(toks, pos, slots, lens, [r.row for r in reqs])

@@ -49,3 +49,41 @@ def test_restore_overlapped_with_prefill(fmt, graphs):
     if graphs:
         assert eng._prefill_graphs.stat["replays"] >= 2
     eng.close()
+
+
+def test_pipelined_decode_matches_serial():
+    """Decode pipelining (step t + 1 launched on device tokens before step t is read) gives
+    the tokens of the serial loop: different lengths, a stop token, a request joining."""
+    import torch
+
+    from axropus_deploy_b200.engine import EngineConfig, LLMEngine, SamplingParams
+    from axropus_deploy_b200.models.config import get_config
+    from axropus_deploy_b200.models.llama import LlamaModel
+
+    dev = torch.device("cuda", 0)
+    model = LlamaModel(get_config("tiny128"), dev, seed=1)
+    g = torch.Generator().manual_seed(4)
+    prompts = [torch.randint(0, 32000, (n,), generator=g).tolist() for n in (40, 75, 130, 20)]
+
+    def run(pipe, stop=()):
+        eng = LLMEngine(model, EngineConfig(num_blocks=256, max_model_len=1024, max_batch=8, cuda_graphs=True,
+                                            pipeline_decode=pipe))
+        reqs = [eng.add_request(p, SamplingParams(max_tokens=m, stop_token_ids=stop))
+                for p, m in zip(prompts[:3], (12, 5, 20))]
+        for _ in range(3):
+            eng.step()
+        late = eng.add_request(prompts[3], SamplingParams(max_tokens=7, stop_token_ids=stop))
+        while eng.has_unfinished():
+            eng.step()
+        out = [r.output for r in reqs + [late]]
+        st = dict(eng.stat)
+        eng.close()
+        return out, st
+
+    serial, _ = run(False)
+    piped, st = run(True)
+    assert piped == serial and st["pipelined_decode_steps"] > 0
+    stop = serial[2][4]  # a stop token in the middle of the longest request
+    s2, _ = run(False, (stop,))
+    p2, _ = run(True, (stop,))
+    assert p2 == s2 and len(p2[2]) <= 5
