@@ -51,6 +51,7 @@ def test_restore_overlapped_with_prefill(fmt, graphs):
     eng.close()
 
 
+@pytest.mark.gpu
 def test_pipelined_decode_matches_serial():
     """Decode pipelining (step t + 1 launched on device tokens before step t is read) gives
     the tokens of the serial loop: different lengths, a stop token, a request joining."""
