@@ -44,7 +44,9 @@ C.gemm_tp(staging[:rows], w, out, 1, 0, W, rows, 1, peer_a, staging, flags, read
 torch.cuda.synchronize()
 dt = time.perf_counter() - t0
 code = int(err[0].item())
-assert code in (5, 7), f"expected a ready/flag wait code, got {code}"
+# whichever bounded wait runs out first records its code: the peer-flag waits (5, 7) or the
+# waits of the roles that depend on them (stage 2, accumulator 3)
+assert code in (2, 3, 5, 7), f"expected a wait code, got {code}"
 assert dt < 10.0, f"the kernel took {dt:.1f} s to give up"
 
 from axropus_deploy_b200.engine import EngineConfig, LLMEngine, SamplingParams
