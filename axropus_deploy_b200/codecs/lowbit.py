@@ -23,6 +23,7 @@ from typing import Dict, Tuple
 
 import torch
 
+from . import gpu
 from .base import FMT_NVFP4, FMT_TURBOQUANT, FP8_E4M3_MAX, Codec, CompressedKV, check_float_input, register_codec
 
 NVFP4_GROUP = 16
@@ -78,9 +79,14 @@ class NVFP4Codec(Codec):
 
     def compress(self, raw_kv: torch.Tensor) -> CompressedKV:
         check_float_input(raw_kv, type(self).__name__)
-        x = raw_kv.float()
-        last = x.shape[-1]
+        last = raw_kv.shape[-1]
         pad = (-last) % NVFP4_GROUP
+        meta = {"block_size": NVFP4_GROUP, "original_last": last, "padded_last": last + pad}
+        if raw_kv.is_cuda:
+            data, sbytes, amax, _ = gpu.encode(raw_kv, self.FORMAT)
+            return CompressedKV(self.FORMAT, data, sbytes, max(float(amax.item()), 1e-8), tuple(raw_kv.shape),
+                                raw_kv.dtype, meta)
+        x = raw_kv.float()
         xp = torch.nn.functional.pad(x, (0, pad))
         g = xp.unflatten(-1, (-1, NVFP4_GROUP))
         tensor_scale = float(g.abs().amax().clamp_min(1e-8))
@@ -88,10 +94,11 @@ class NVFP4Codec(Codec):
         sbytes = encode_scale_byte(gs).squeeze(-1)
         nib = encode_e2m1(g / gs).flatten(-2)
         return CompressedKV(self.FORMAT, _pack_nibbles(nib), sbytes, tensor_scale, tuple(raw_kv.shape),
-                            raw_kv.dtype, {"block_size": NVFP4_GROUP, "original_last": last,
-                                           "padded_last": last + pad})
+                            raw_kv.dtype, meta)
 
     def decompress_to(self, c: CompressedKV, target_dtype: torch.dtype = torch.float16) -> torch.Tensor:
+        if c.data.is_cuda:
+            return gpu.decode(c.data, c.scales, self.FORMAT, c.shape, target_dtype)
         padded, last = int(c.meta["padded_last"]), int(c.meta["original_last"])
         vals = decode_e2m1(_unpack_nibbles(c.data, padded)).unflatten(-1, (-1, NVFP4_GROUP))
         vals = vals * decode_scale_byte(c.scales).unsqueeze(-1).to(vals.device)

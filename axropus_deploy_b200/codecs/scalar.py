@@ -14,8 +14,8 @@ Packing (:502-538): INT4 stores ``q + 8`` as nibbles, even index in the low
 nibble; INT2 stores ``q + 2`` four to a byte, first value in the low bits. Odd
 trailing lengths are zero padded and trimmed on unpack.
 
-These are the CPU/PyTorch implementations; they run on any device the input lives
-on. The G1 pool's hot formats (``fp8_e4m3_block``, ``int4_g64_asym``) live in
+These are the PyTorch implementations; CUDA tensors of the INT4 / INT2 formats go
+to the kernels of :mod:`.gpu`, which write the same bytes. The G1 pool's hot formats (``fp8_e4m3_block``, ``int4_g64_asym``) live in
 :mod:`.paged` and have hand-written CUDA kernels.
 """
 from __future__ import annotations
@@ -27,6 +27,7 @@ from typing import Any
 
 import torch
 
+from . import gpu
 from .base import (FMT_FP8_E4M3, FMT_FP8_E5M2, FMT_INT2_SYM, FMT_INT4_BLOCK, FMT_INT4_SYM,
                    FP8_E4M3_MAX, FP8_E5M2_MAX, Codec, CompressedKV, check_float_input,
                    register_codec)
@@ -165,6 +166,9 @@ class INT4PerChannelCodec(Codec):
 
     def compress(self, raw_kv: torch.Tensor) -> CompressedKV:
         check_float_input(raw_kv, type(self).__name__)
+        if raw_kv.is_cuda:
+            data, s16, _, _ = gpu.encode(raw_kv, self.FORMAT)
+            return CompressedKV(self.FORMAT, data, s16, 1.0, tuple(raw_kv.shape), raw_kv.dtype, {"zero_point": 0})
         x = raw_kv.float()
         scale = x.abs().amax(dim=tuple(range(x.dim() - 1))).clamp_min(1e-8) / 7.0
         q = torch.round(x / scale).clamp(-8, 7).to(torch.int8)
@@ -172,6 +176,8 @@ class INT4PerChannelCodec(Codec):
                             raw_kv.dtype, {"zero_point": 0})
 
     def decompress_to(self, c: CompressedKV, target_dtype: torch.dtype = torch.float16) -> torch.Tensor:
+        if c.data.is_cuda:
+            return gpu.decode(c.data, c.scales, self.FORMAT, c.shape, target_dtype)
         q = unpack_int4(c.data, c.shape[-1]).float()
         return (q * c.scales.float()).view(c.shape).to(target_dtype)
 
@@ -187,18 +193,24 @@ class INT4PerBlockCodec(Codec):
         check_float_input(raw_kv, type(self).__name__)
         if raw_kv.dim() < 3:
             raise ValueError(f"{type(self).__name__} needs [..., tokens, heads, head_dim], got {tuple(raw_kv.shape)}")
-        x = raw_kv.float()
-        t = x.shape[-3]
+        t = raw_kv.shape[-3]
         nb = math.ceil(t / self.BLOCK)
+        meta = {"block_size": self.BLOCK, "n_tokens": t, "n_blocks": nb}
+        if raw_kv.is_cuda:
+            data, s16, _, _ = gpu.encode(raw_kv, self.FORMAT, self.BLOCK)
+            return CompressedKV(self.FORMAT, data, s16, 1.0, tuple(raw_kv.shape), raw_kv.dtype, meta)
+        x = raw_kv.float()
         xp = torch.nn.functional.pad(x, (0, 0, 0, 0, 0, nb * self.BLOCK - t))
         blocks = xp.unflatten(-3, (nb, self.BLOCK))  # [..., nb, BLOCK, H, D]
         scale = blocks.abs().amax(dim=(-3, -2, -1)).clamp_min(1e-8) / 7.0  # [..., nb]
         q = torch.round(blocks / scale[..., None, None, None]).clamp(-8, 7).to(torch.int8)
         q = q.flatten(-4, -3)[..., :t, :, :]
         return CompressedKV(self.FORMAT, pack_int4(q), scale.to(torch.float16), 1.0, tuple(raw_kv.shape),
-                            raw_kv.dtype, {"block_size": self.BLOCK, "n_tokens": t, "n_blocks": nb})
+                            raw_kv.dtype, meta)
 
     def decompress_to(self, c: CompressedKV, target_dtype: torch.dtype = torch.float16) -> torch.Tensor:
+        if c.data.is_cuda:
+            return gpu.decode(c.data, c.scales, self.FORMAT, c.shape, target_dtype, c.meta)
         q = unpack_int4(c.data, c.shape[-1]).float()
         t, nb, bs = c.meta["n_tokens"], c.meta["n_blocks"], c.meta["block_size"]
         qp = torch.nn.functional.pad(q, (0, 0, 0, 0, 0, nb * bs - t)).unflatten(-3, (nb, bs))
@@ -214,6 +226,9 @@ class INT2PerChannelCodec(Codec):
 
     def compress(self, raw_kv: torch.Tensor) -> CompressedKV:
         check_float_input(raw_kv, type(self).__name__)
+        if raw_kv.is_cuda:
+            data, s16, _, _ = gpu.encode(raw_kv, self.FORMAT)
+            return CompressedKV(self.FORMAT, data, s16, 1.0, tuple(raw_kv.shape), raw_kv.dtype, {})
         x = raw_kv.float()
         scale = x.abs().amax(dim=tuple(range(x.dim() - 1))).clamp_min(1e-8) / 2.0
         q = torch.round(x / scale).clamp(-2, 1)
@@ -221,6 +236,8 @@ class INT2PerChannelCodec(Codec):
                             tuple(raw_kv.shape), raw_kv.dtype, {})
 
     def decompress_to(self, c: CompressedKV, target_dtype: torch.dtype = torch.float16) -> torch.Tensor:
+        if c.data.is_cuda:
+            return gpu.decode(c.data, c.scales, self.FORMAT, c.shape, target_dtype)
         q = unpack_int2(c.data, c.shape[-1]).float() - 2.0
         return (q * c.scales.float()).view(c.shape).to(target_dtype)
 

@@ -20,6 +20,8 @@ _KERNELS_PER_CALL = {
     # attention kernel + combine unless the partials are kept for a later merge
     "prefill_attention_tc": lambda a: 2 if (a[14] > 1 and not (len(a) > 20 and a[20])) else 1,
     "prefill_attention": lambda a: 2 if a[17] > 1 else 1,
+    # amax (+ scales) + encode; NVFP4 is one kernel
+    "codec_encode": lambda a: 1 if a[1] == 3 else 3,
 }
 
 

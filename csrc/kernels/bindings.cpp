@@ -66,6 +66,13 @@ int64_t dense_stream_nt(int64_t M);
 int64_t dense_stream_splits(int64_t M, int64_t N, int64_t K, int64_t sms);
 std::vector<int64_t> dense_stream_workspace(int64_t M, int64_t N, int64_t K, int64_t sms);
 }  // namespace dense
+namespace codec {
+void codec_encode(torch::Tensor x, int64_t fmt, std::vector<int64_t> geom, torch::Tensor out, torch::Tensor amax,
+                  c10::optional<torch::Tensor> scale32, c10::optional<torch::Tensor> scale16,
+                  c10::optional<torch::Tensor> sbytes);
+void codec_decode(torch::Tensor in, int64_t fmt, std::vector<int64_t> geom, torch::Tensor out,
+                  c10::optional<torch::Tensor> scale16, c10::optional<torch::Tensor> sbytes);
+}  // namespace codec
 }  // namespace axr
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -91,4 +98,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dense_stream_nt", &axr::dense::dense_stream_nt);
   m.def("dense_stream_splits", &axr::dense::dense_stream_splits);
   m.def("dense_stream_workspace", &axr::dense::dense_stream_workspace);
+  m.def("codec_encode", &axr::codec::codec_encode);
+  m.def("codec_decode", &axr::codec::codec_decode);
 }
