@@ -286,15 +286,20 @@ class LLMEngine:
         self.stat["steps"] += 1
         done: List[Request] = []
         if self._pipe is not None:
-            if not self.waiting:
-                # nothing to admit: launch the next decode on the device tokens of the one
-                # in flight, then read the in-flight step's tokens while the GPU runs it
-                pipe = self._pipe
+            pipe = self._pipe
+            in_pipe = {id(r) for r in pipe["reqs"]}
+            joined = any(r.state == "running" and id(r) not in in_pipe for r in self.running)
+            if not self.waiting and not joined:
+                # nothing to admit and nobody new to decode: launch the next decode on the
+                # device tokens of the one in flight, then read the in-flight step's tokens
+                # while the GPU runs it
                 cont = [r for r in pipe["reqs"] if r.state == "running" and len(r.output) + 1 < r.params.max_tokens]
                 nxt = self._decode_launch(cont, pipe) if cont else None
                 done += self._pipe_finish()
                 self._pipe = nxt
                 return done
+            # requests to admit, or admitted last step (their first decode input is on the
+            # host): end the pipeline for one step so the next launch batches everyone
             done += self._pipe_finish()
             self._pipe = None
         with _nvtx("admit"):

@@ -81,9 +81,11 @@ def test_pipelined_decode_matches_serial():
         eng.close()
         return out, st
 
-    serial, _ = run(False)
+    serial, st0 = run(False)
     piped, st = run(True)
     assert piped == serial and st["pipelined_decode_steps"] > 0
+    # the late request joins the pipelined batch instead of decoding alone afterwards
+    assert st["steps"] <= st0["steps"] + 1, (st["steps"], st0["steps"])
     stop = serial[2][4]  # a stop token in the middle of the longest request
     s2, _ = run(False, (stop,))
     p2, _ = run(True, (stop,))
