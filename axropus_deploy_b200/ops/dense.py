@@ -161,8 +161,6 @@ def linear(x: torch.Tensor, w: torch.Tensor, epi: str = "store", out: Optional[t
     nt = C.dense_stream_nt(M)
     if nt and not force_big:
         n_ws, n_cnt = C.dense_stream_workspace(M, N, x.shape[1], sm_count(dev))
-        if splits > 0:  # a forced split count needs its own partials
-            n_ws = max(n_ws, -(-N // 128) * splits * nt * 128)
         sc.ensure(n_ws, n_cnt)
     pos = slots = cos_sin = None
     kc = vc = bs = hs = 0

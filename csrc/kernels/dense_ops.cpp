@@ -10,8 +10,9 @@ namespace dense {
 
 // x [M, K] bf16, w [N, K] bf16 -> epilogue(x w^T). epi: 0 store, 1 residual (res [M, N],
 // may be out), 2 SwiGLU (out [M, N/2]), 3 RoPE + bf16 paged KV write (out = q [M, Hq*128]).
-// ws fp32 / cnt int32: split-K scratch of the stream kernel (see dense_stream_workspace;
-// cnt zero-initialised once, left at zero by every call). splits <= 0: automatic.
+// ws fp32 / cnt int32: scratch (the split-K partials of the stream kernel stay in its
+// clusters' shared memory; see dense_stream_workspace). splits <= 0: automatic, else the
+// stream kernel's CTAs per weight tile (at most 8, one cluster).
 void dense_gemm(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t epi, c10::optional<torch::Tensor> res,
                 c10::optional<torch::Tensor> pos, c10::optional<torch::Tensor> slots,
                 c10::optional<torch::Tensor> cos_sin, int64_t kc, int64_t vc, int64_t blk_stride, int64_t head_stride,
@@ -71,18 +72,9 @@ void dense_gemm(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t epi
   c.device = x.device().index();
   const int nt = stream_nt(M);
   if (nt != 0 && !force_big) {
-    int64_t need_ws = 0, need_cnt = 0;
     const int sms = at::cuda::getDeviceProperties(c.device)->multiProcessorCount;
     int s = splits > 0 ? static_cast<int>(splits) : stream_splits(M, N, K, sms);
     s = std::max(1, std::min(std::min(s, static_cast<int>((K + 63) / 64)), stream_max_splits(nt)));
-    if (s > 1) {
-      need_ws = ((N + 127) / 128) * static_cast<int64_t>(s) * nt * 128;
-      need_cnt = (N + 127) / 128;
-      TORCH_CHECK(ws.numel() >= need_ws && cnt.numel() >= need_cnt, "dense_gemm: split-K scratch too small (",
-                  ws.numel(), " < ", need_ws, " floats or ", cnt.numel(), " < ", need_cnt, " counters)");
-      c.ws = ws.data_ptr<float>();
-      c.cnt = cnt.data_ptr<int>();
-    }
     c.splits = s;
   }
   c.err = err.data_ptr<int>();

@@ -9,10 +9,12 @@
 // * gemm_stream_kernel (M <= 256: decode steps, AMF-hit suffix prefills). The weights
 //   are the only large operand, so the kernel is a weight stream: the MMA's M side is
 //   128 weight rows (swap-AB), its N side the M token rows padded to NT (16..256).
-//   The reduction is split over `splits` CTAs per 128-row tile so that every SM keeps
-//   TMA loads of weights in flight; the last CTA of a tile to finish (a per-tile
-//   arrival counter) sums all CTAs' fp32 partials in split order and runs the epilogue, then
-//   puts the counter back to zero for the next call. The kernel is launched with
+//   The reduction is split over `splits` (<= 8) CTAs per 128-row tile so that every SM
+//   keeps TMA loads of weights in flight. The CTAs of a tile form a thread-block cluster:
+//   each parks its fp32 partial in its own shared memory and each sums a share of the
+//   tile's token columns over all of them through distributed shared memory (in split
+//   order, so the result does not depend on timing) and runs that share's epilogue; no
+//   partial goes through global memory. The kernel is launched with
 //   programmatic dependent launch: it fills its TMA ring with weight tiles before it
 //   waits for the previous kernel (griddepcontrol.wait), so the stream starts while
 //   the previous kernel drains; activations and every epilogue input are read after
@@ -63,8 +65,6 @@ struct EpiArgs {
 struct Args {
   int M, N, K;
   int splits;   // stream kernel: CTAs per 128-row weight tile
-  float* ws;    // stream kernel split-K partials [tiles * splits][NT][128]
-  int* cnt;     // stream kernel per-tile arrival counters (zero between calls)
   volatile int* err;
   EpiArgs e;
 };
@@ -100,6 +100,21 @@ struct StreamCfg {
   static constexpr int CH = NT < 32 ? NT : 32;  // epilogue columns (tokens) per TMEM load
   static constexpr int CTAS_PER_SM = NT <= 128 ? 2 : 1;
 };
+
+// Every thread of every CTA of the cluster (release / acquire: shared-memory writes before
+// it are visible to the cluster after it).
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// The float at this CTA's shared address `p`, read from cluster CTA `rank`'s shared memory.
+__device__ __forceinline__ float ld_dsmem(const float* p, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(tc::smem_u32(p)), "r"(rank));
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+  return v;
+}
 
 template <int CH>
 __device__ __forceinline__ void tmem_ld_chunk(uint32_t taddr, float (&v)[CH]) {
@@ -200,9 +215,7 @@ __global__ void __launch_bounds__(128) gemm_stream_kernel(const __grid_constant_
   uint64_t* full = reinterpret_cast<uint64_t*>(base + C::ST * C::STAGE);
   uint64_t* empty = full + C::ST;
   uint64_t* accb = empty + C::ST;
-  uint64_t* fixb = accb + 1;  // split-K partials staged into shared memory
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fixb + 1);
-  int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accb + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x, split = blockIdx.y;
@@ -218,7 +231,6 @@ __global__ void __launch_bounds__(128) gemm_stream_kernel(const __grid_constant_
       tc::mbar_init(&empty[s], 1);
     }
     tc::mbar_init(accb, 1);
-    tc::mbar_init(fixb, 1);
     tc::fence_barrier_init();
     tc::prefetch_tmap(&tmW);
     tc::prefetch_tmap(&tmX);
@@ -283,64 +295,54 @@ __global__ void __launch_bounds__(128) gemm_stream_kernel(const __grid_constant_
   ready = __syncthreads_and(ready && *g.err == 0) != 0;
   const uint32_t trow = tmem + (static_cast<uint32_t>(warp * 32) << 16);
   const int r = threadIdx.x;
-  float* sx = reinterpret_cast<float*>(base);  // the TMA ring is idle once the accumulator is complete
-  bool write = ready;
-  if (g.splits > 1) {
+  const int mt = min(g.M, NT);  // token columns that hold rows
+  if (g.splits == 1) {
+    float* sx = reinterpret_cast<float*>(base);  // the TMA ring is idle once the accumulator is complete
     if (ready) {
-      float* mine = g.ws + (long long)(tile * g.splits + split) * NT * 128;
 #pragma unroll 1
-      for (int c0 = 0; c0 < NT; c0 += C::CH) {
+      for (int c0 = 0; c0 < mt; c0 += C::CH) {
+        float v[C::CH];
+        tmem_ld_chunk<C::CH>(trow + c0, v);
+        stream_epilogue<EPI, C::CH>(g, tile, c0, v, sx);
+      }
+    }
+  } else {
+    // split-K inside the cluster: each CTA parks its fp32 partial [NT][128] in its idle
+    // ring, and after a cluster barrier CTA `split` sums the 16-token chunks c with
+    // c % splits == split over every CTA's shared memory (distributed shared memory, in
+    // split order: deterministic) and runs their epilogue; a second barrier keeps every
+    // partial alive until all CTAs have read it. Both barriers are reached by every
+    // thread of every CTA, failed or not.
+    float* part = reinterpret_cast<float*>(base);
+    float* sx = part + NT * 128;
+    if (ready) {
+#pragma unroll 1
+      for (int c0 = 0; c0 < mt; c0 += C::CH) {
         float v[C::CH];
         tmem_ld_chunk<C::CH>(trow + c0, v);
 #pragma unroll
-        for (int j = 0; j < C::CH; ++j) __stcg(mine + (c0 + j) * 128 + r, v[j]);
+        for (int j = 0; j < C::CH; ++j) part[(c0 + j) * 128 + r] = v[j];
       }
-      __threadfence();
     }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      int last = 0;
-      if (ready) {
-        last = atomicAdd(g.cnt + tile, 1) == g.splits - 1;
-        if (last) g.cnt[tile] = 0;  // every split has arrived: ready for the next call
-      }
-      *last_flag = last;
-    }
-    __syncthreads();
-    write = *last_flag != 0;
-    if (write) __threadfence();
-  }
-  if (write) {
-    // split-K: each chunk of CH tokens of every split's partial is staged into the idle
-    // TMA ring with one bulk copy per split (one round trip per chunk), then summed in
-    // split order -- the result does not depend on which CTA finished last
-    float* stage = reinterpret_cast<float*>(base);
-    if (g.splits > 1 && threadIdx.x == 0) tc::fence_proxy_async_global_mem();
+    cluster_sync();
+    if (ready) {
 #pragma unroll 1
-    for (int c0 = 0, ci = 0; c0 < NT; c0 += C::CH, ++ci) {
-      float v[C::CH];
-      if (g.splits > 1) {
-        if (threadIdx.x == 0) {
-          constexpr uint32_t chunk_bytes = C::CH * 128 * 4;
-          tc::mbar_arrive_expect_tx(fixb, chunk_bytes * g.splits);
-          for (int s2 = 0; s2 < g.splits; ++s2)
-            tc::bulk_load(stage + s2 * C::CH * 128, g.ws + ((long long)(tile * g.splits + s2) * NT + c0) * 128,
-                          chunk_bytes, fixb);
-        }
-        const bool ok = tc::mbar_wait(fixb, ci & 1, g.err, 4);
+      for (int c0 = split * 16; c0 < mt; c0 += g.splits * 16) {
+        float v[16];
 #pragma unroll
-        for (int j = 0; j < C::CH; ++j) v[j] = 0.f;
-        for (int s2 = 0; ok && s2 < g.splits; ++s2) {
+        for (int j = 0; j < 16; ++j) v[j] = 0.f;
+#pragma unroll 1
+        for (int q = 0; q < g.splits; ++q) {
+          float pv[16];
 #pragma unroll
-          for (int j = 0; j < C::CH; ++j) v[j] += stage[(s2 * C::CH + j) * 128 + r];
+          for (int j = 0; j < 16; ++j) pv[j] = ld_dsmem(part + (c0 + j) * 128 + r, q);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] += pv[j];
         }
-        __syncthreads();  // the stage is free for the epilogue's exchange / the next chunk
-      } else {
-        tmem_ld_chunk<C::CH>(trow + c0, v);
+        stream_epilogue<EPI, 16>(g, tile, c0, v, sx);
       }
-      stream_epilogue<EPI, C::CH>(g, tile, c0, v, sx);
-      if (g.splits > 1) __syncthreads();
     }
+    cluster_sync();
   }
   tc::tc_fence_before();
   __syncthreads();
@@ -628,19 +630,31 @@ bool pdl_enabled() {
   return on;
 }
 
+// cluster_y > 1: clusters of (1, cluster_y, 1) CTAs (the split-K CTAs of one weight tile).
 template <typename Kernel>
 cudaError_t launch_pdl(Kernel kernel, dim3 grid, dim3 block, int smem, cudaStream_t st, const CUtensorMap& m0,
-                       const CUtensorMap& m1, const Args& g) {
+                       const CUtensorMap& m1, const Args& g, int cluster_y = 1) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster_y > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = 1;
+    attr[n].val.clusterDim.y = cluster_y;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cfg.numAttrs = n;
   return cudaLaunchKernelEx(&cfg, kernel, m0, m1, g);
 }
 
@@ -654,7 +668,7 @@ cudaError_t launch_stream(const CUtensorMap& tw, const CUtensorMap& tx, const Ar
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  return launch_pdl(kernel, dim3((g.N + 127) / 128, g.splits), dim3(128), C::SMEM, st, tw, tx, g);
+  return launch_pdl(kernel, dim3((g.N + 127) / 128, g.splits), dim3(128), C::SMEM, st, tw, tx, g, g.splits);
 }
 
 template <int EPI>
@@ -685,14 +699,10 @@ cudaError_t launch_big(const CUtensorMap& tx, const CUtensorMap& tw, const Args&
 }  // namespace
 
 // Largest split count whose partials of one chunk (CH tokens) fit the TMA ring.
+// Split-K CTAs of one weight tile form a cluster: at most the portable cluster size.
 int stream_max_splits(int nt) {
-  switch (nt) {
-    case 16: return (StreamCfg<16>::ST * StreamCfg<16>::STAGE) / (StreamCfg<16>::CH * 512);
-    case 32: return (StreamCfg<32>::ST * StreamCfg<32>::STAGE) / (StreamCfg<32>::CH * 512);
-    case 64: return (StreamCfg<64>::ST * StreamCfg<64>::STAGE) / (StreamCfg<64>::CH * 512);
-    case 128: return (StreamCfg<128>::ST * StreamCfg<128>::STAGE) / (StreamCfg<128>::CH * 512);
-    default: return (StreamCfg<256>::ST * StreamCfg<256>::STAGE) / (StreamCfg<256>::CH * 512);
-  }
+  (void)nt;
+  return 8;
 }
 
 int stream_nt(int64_t M) {
@@ -706,26 +716,27 @@ int stream_nt(int64_t M) {
 
 // Enough CTAs to give every SM its resident share of weight tiles, each CTA keeping at
 // least 4 k-blocks (256 of K).
+// CTAs per weight tile: as many as fit (<= 8, the portable cluster size; >= 8 k-blocks
+// each) while all tiles' clusters stay within ~7/8 of the resident CTA slots. Clusters
+// are placed whole inside a GPC, so a grid that asks for every slot does not become
+// resident at once, and its last clusters run as a second wave (measured: 288 CTAs of
+// 6-CTA clusters took 1.6x the time of 240 CTAs of 5).
 int stream_splits(int64_t M, int64_t N, int64_t K, int sms) {
   const int nt = stream_nt(M);
   const int64_t tiles = (N + 127) / 128, nk = (K + 63) / 64;
   const int64_t slots = static_cast<int64_t>(sms) * (nt <= 128 ? 2 : 1);
-  if (tiles >= slots) return 1;
-  int64_t s = slots / tiles;
-  s = std::min<int64_t>(s, std::max<int64_t>(1, nk / 8));  // >= 8 k-blocks (512 of K) per CTA
-  s = std::min<int64_t>(s, stream_max_splits(nt));          // every split's chunk fits the stage
+  if (nt == 0 || tiles >= slots) return 1;
+  int64_t s = (slots * 7 / 8) / tiles;
+  s = std::min<int64_t>(s, std::max<int64_t>(1, nk / 8));
+  s = std::min<int64_t>(s, stream_max_splits(nt));
   return static_cast<int>(std::max<int64_t>(1, s));
 }
 
+// The split-K partials stay in the cluster's shared memory: no global scratch.
 void stream_workspace(int64_t M, int64_t N, int64_t K, int sms, int64_t* ws_floats, int64_t* counters) {
-  const int nt = stream_nt(M);
+  (void)M, (void)N, (void)K, (void)sms;
   *ws_floats = 0;
   *counters = 0;
-  if (nt == 0) return;
-  const int64_t s = stream_splits(M, N, K, sms);
-  const int64_t tiles = (N + 127) / 128;
-  *ws_floats = s > 1 ? tiles * s * nt * 128 : 0;
-  *counters = tiles;
 }
 
 std::string dense_gemm_launch(const DenseCall& c, cudaStream_t st) {
@@ -768,11 +779,6 @@ std::string dense_gemm_launch(const DenseCall& c, cudaStream_t st) {
     const int nk = (c.K + 63) / 64;
     g.splits = c.splits > 0 ? c.splits : stream_splits(c.M, c.N, c.K, sm_count(c.device));
     g.splits = std::max(1, std::min(std::min(g.splits, nk), stream_max_splits(nt)));
-    if (g.splits > 1) {
-      if (!c.ws || !c.cnt) return "split-K scratch missing";
-      g.ws = c.ws;
-      g.cnt = c.cnt;
-    }
     CUtensorMap tw, tx;
     if (!make_map(&tw, c.w, c.N, c.K, c.ldw, 128) || !make_map(&tx, c.x, c.M, c.K, c.ldx, nt))
       return "cuTensorMapEncodeTiled failed";
