@@ -28,13 +28,12 @@
 //
 // Reference counterpart: the prefill attention the reference delegates to llama.cpp /
 // vLLM library kernels; the reference has no prefill attention kernel of its own.
-#include <torch/extension.h>
-#include <ATen/cuda/CUDAContext.h>
-
 #include <cfloat>
+#include <string>
 
 #include "attn_combine.cuh"
 #include "common.cuh"
+#include "prefill_tc.h"
 #include "tc_common.cuh"
 
 namespace axr {
@@ -95,10 +94,13 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tile_m = gridDim.x - 1 - blockIdx.x;  // longest (most KV tiles) first
+  // blocks start in x-fastest order: every head of the longest query tile (most KV tiles)
+  // first, then the next tile, so the last CTAs to start are the short ones (measured
+  // 0.84 against 0.98 ms for 8192 tokens x 32 heads with the tiles of one head first)
+  const int tile_m = gridDim.y - 1 - blockIdx.y;
   const int S = p.num_splits;
   const int G = p.gpack;
-  const int hy = blockIdx.y, b = blockIdx.z / S, split = blockIdx.z % S;
+  const int hy = blockIdx.x, b = blockIdx.z / S, split = blockIdx.z % S;
   const int q0 = p.cu_q[b], nq = p.cu_q[b + 1] - q0;
   const int nrow = nq * G;           // rows of this sequence: tokens x packed heads
   const int row0 = tile_m * 2 * BM;  // first row of sub-tile A
@@ -374,96 +376,65 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
   if (warp == 9) tc::tmem_dealloc(tmem, 512);
 }
 
-void make_page_map(CUtensorMap* map, const void* ptr, int64_t rows) {
-  TORCH_CHECK(reinterpret_cast<uintptr_t>(ptr) % 16 == 0, "prefill_tc: page base must be 16-byte aligned");
+bool make_page_map(CUtensorMap* map, const void* ptr, int64_t rows) {
+  if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0) return false;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(HD), static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(HD * 2)};
   cuuint32_t box[2] = {64, 16};
   cuuint32_t estr[2] = {1, 1};
-  const CUresult rc = cuTensorMapEncodeTiled(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims,
-                                             strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                                             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  TORCH_CHECK(rc == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", static_cast<int>(rc));
+  return cuTensorMapEncodeTiled(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box,
+                                estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+std::string prefill_launch(const PrefillCall& c, cudaStream_t st) {
+  if (c.B == 0 || c.max_q == 0) return "";
+  if (c.Hq % c.Hkv != 0) return "Hq must be a multiple of Hkv";
+  CUtensorMap tk, tv;
+  if (!make_page_map(&tk, c.k, c.num_blocks * c.Hkv * 16) || !make_page_map(&tv, c.v, c.num_blocks * c.Hkv * 16))
+    return "page regions must be 16-byte aligned (cuTensorMapEncodeTiled failed)";
+  Params p;
+  p.q = reinterpret_cast<const __nv_bfloat16*>(c.q);
+  p.out = reinterpret_cast<__nv_bfloat16*>(c.out);
+  p.Hq = c.Hq;
+  p.Hkv = c.Hkv;
+  p.block_table = c.block_table;
+  p.bt_stride = c.bt_stride;
+  p.cu_q = c.cu_q;
+  p.seq_lens = c.seq_lens;
+  p.scale_log2 = c.scale * 1.4426950408889634f;
+  p.err = c.err;
+  const int S = c.num_splits > 1 ? c.num_splits : 1;
+  p.num_splits = S;
+  p.gpack = c.gqa_pack > 1 ? c.Hq / c.Hkv : 1;
+  p.part_o = c.part_o;
+  p.part_lse = c.part_lse;
+  p.noncausal = c.noncausal != 0;
+  p.partial_only = c.partial_only != 0;
+  p.q_index = c.q_index;
+  if ((S > 1 || p.partial_only) && (p.part_o == nullptr || p.part_lse == nullptr)) return "split-KV scratch missing";
+  if ((int64_t)c.B * S >= 65536) return "too many sequences x splits";
+  static bool attr = false;
+  if (!attr) {
+    const cudaError_t e = cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+    if (e != cudaSuccess) return std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e);
+    attr = true;
+  }
+  const int64_t rows = (int64_t)c.max_q * p.gpack;
+  const int64_t tiles = (rows + 2 * BM - 1) / (2 * BM);
+  const unsigned heads = p.gpack > 1 ? static_cast<unsigned>(c.Hkv) : static_cast<unsigned>(c.Hq);
+  if (tiles >= 65536) return "too many query tiles";
+  const dim3 grid(heads, static_cast<unsigned>(tiles), c.B * S);
+  prefill_tc_kernel<<<grid, THREADS, SMEM, st>>>(tk, tv, p);
+  cudaError_t e = cudaPeekAtLastError();
+  if (e != cudaSuccess) return std::string("launch failed: ") + cudaGetErrorString(e);
+  if (S > 1 && c.T > 0 && !p.partial_only) {
+    decode_combine_kernel<128><<<c.T * c.Hq, 128, 0, st>>>(p.part_o, p.part_lse, p.out, S);
+    e = cudaPeekAtLastError();
+    if (e != cudaSuccess) return std::string("combine launch failed: ") + cudaGetErrorString(e);
+  }
+  return "";
 }
 
 }  // namespace fa
-
-// q [T, Hq, 128] bf16; k/v: the layer's bf16 K and V page regions ([num_blocks, Hkv, 16, 128]
-// each, contiguous); block_table [B, max_blocks] int32; cu_q [B+1]; seq_lens [B]; err int32.
-void prefill_attention_tc(torch::Tensor q, int64_t k, int64_t v, int64_t blk_stride, int64_t head_stride,
-                          int64_t num_blocks, torch::Tensor block_table, torch::Tensor cu_q, torch::Tensor seq_lens,
-                          int64_t Hkv, double scale, int64_t max_q, torch::Tensor out, torch::Tensor err,
-                          int64_t num_splits, c10::optional<torch::Tensor> part_o,
-                          c10::optional<torch::Tensor> part_lse, int64_t gqa_pack, int64_t noncausal,
-                          c10::optional<torch::Tensor> q_index, int64_t partial_only) {
-  using namespace fa;
-  TORCH_CHECK(q.is_cuda() && q.scalar_type() == torch::kBFloat16 && q.is_contiguous() && q.dim() == 3 &&
-                  q.size(2) == HD,
-              "prefill_tc: q must be contiguous bf16 [T, Hq, 128]");
-  TORCH_CHECK(out.is_contiguous() && out.scalar_type() == torch::kBFloat16, "prefill_tc: out must be contiguous bf16");
-  TORCH_CHECK(blk_stride == Hkv * 16 * HD * 2 && head_stride == 16 * HD * 2,
-              "prefill_tc: expects contiguous bf16 pages [blocks, Hkv, 16, 128]");
-  TORCH_CHECK(block_table.scalar_type() == torch::kInt32 && cu_q.scalar_type() == torch::kInt32 &&
-                  seq_lens.scalar_type() == torch::kInt32 && err.scalar_type() == torch::kInt32,
-              "prefill_tc: index tensors must be int32");
-  const int B = seq_lens.size(0), Hq = q.size(1);
-  TORCH_CHECK(Hq % Hkv == 0, "Hq must be a multiple of Hkv");
-  if (B == 0 || max_q == 0) return;
-  CUtensorMap tk, tv;
-  make_page_map(&tk, reinterpret_cast<const void*>(k), num_blocks * Hkv * 16);
-  make_page_map(&tv, reinterpret_cast<const void*>(v), num_blocks * Hkv * 16);
-  Params p;
-  p.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
-  p.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
-  p.Hq = Hq;
-  p.Hkv = static_cast<int>(Hkv);
-  p.block_table = block_table.data_ptr<int>();
-  p.bt_stride = block_table.stride(0);
-  p.cu_q = cu_q.data_ptr<int>();
-  p.seq_lens = seq_lens.data_ptr<int>();
-  p.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
-  p.err = err.data_ptr<int>();
-  const int S = static_cast<int>(std::max<int64_t>(1, num_splits));
-  const int T = q.size(0);
-  p.num_splits = S;
-  const int G = Hq / static_cast<int>(Hkv);
-  p.gpack = gqa_pack > 1 ? G : 1;
-  p.part_o = nullptr;
-  p.part_lse = nullptr;
-  p.noncausal = noncausal != 0;
-  p.partial_only = partial_only != 0;
-  p.q_index = nullptr;
-  // rows of the partials: q rows, or the q_index rows (shared-prefix decode)
-  const int64_t R = q_index.has_value() ? q_index->numel() : T;
-  if (q_index.has_value()) {
-    TORCH_CHECK(q_index->is_cuda() && q_index->scalar_type() == torch::kInt32, "prefill_tc: q_index int32");
-    p.q_index = q_index->data_ptr<int>();
-  }
-  if (S > 1 || p.partial_only) {
-    TORCH_CHECK(part_o.has_value() && part_lse.has_value() && part_o->scalar_type() == torch::kFloat32 &&
-                    part_lse->scalar_type() == torch::kFloat32 &&
-                    part_o->numel() >= R * Hq * S * HD && part_lse->numel() >= R * Hq * S,
-                "prefill_tc: split-KV scratch too small");
-    p.part_o = part_o->data_ptr<float>();
-    p.part_lse = part_lse->data_ptr<float>();
-  }
-  TORCH_CHECK((int64_t)B * S < 65536, "prefill_tc: too many sequences x splits");
-  static bool attr = false;
-  if (!attr) {
-    AXR_CHECK_CUDA(cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
-    attr = true;
-  }
-  const int64_t rows = max_q * p.gpack;
-  dim3 grid(static_cast<unsigned>((rows + 2 * BM - 1) / (2 * BM)), p.gpack > 1 ? static_cast<unsigned>(Hkv) : Hq,
-            B * S);
-  auto st = at::cuda::getCurrentCUDAStream();
-  prefill_tc_kernel<<<grid, THREADS, SMEM, st>>>(tk, tv, p);
-  AXR_CHECK_CUDA(cudaGetLastError());
-  if (S > 1 && T > 0 && !p.partial_only) {
-    decode_combine_kernel<128><<<T * Hq, 128, 0, st>>>(p.part_o, p.part_lse, p.out, S);
-    AXR_CHECK_CUDA(cudaGetLastError());
-  }
-}
-
 }  // namespace axr

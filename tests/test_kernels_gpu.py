@@ -249,3 +249,4 @@ def test_silu_mul_argmax_verify():
     drb[0, 5] = (drb[0, 5] + 1) % 1001
     gb = spec_verify(lgb.to(DEV), drb.to(DEV)).cpu()
     assert gb[:, 0].tolist() == [5, 8, 8] and torch.equal(gb, spec_verify(lgb.float(), drb))
+
