@@ -19,6 +19,7 @@
 #include <ATen/cuda/CUDAContext.h>
 
 #include <cfloat>
+#include <cstdlib>
 
 #include "attn_combine.cuh"
 #include "common.cuh"
@@ -61,8 +62,8 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(DecodeParams p) {
   __shared__ float wm[4][G], wl[4][G];
   __shared__ float wacc[4][G][D];
 
-  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
-  const int S = gridDim.x;
+  const int kvh = blockIdx.x, b = blockIdx.y, split = blockIdx.z;
+  const int S = gridDim.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int seq_len = p.seq_lens[b];
   const int n_pages = (seq_len + kPage - 1) / kPage;
@@ -416,7 +417,7 @@ __global__ void __launch_bounds__(128) decode_tc_kernel(DecodeParams p) {
   using C = TcCfg<FMT>;
   constexpr bool F16 = FMT != kBF16;
   extern __shared__ __align__(128) char smem[];
-  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z, S = gridDim.x;
+  const int kvh = blockIdx.x, b = blockIdx.y, split = blockIdx.z, S = gridDim.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   char* wbase = smem + warp * C::WARP;
@@ -800,13 +801,21 @@ static void launch_g(int G, dim3 grid, const DecodeParams& p, cudaStream_t st) {
 // that fit one SM (shared memory bound); the split count in [fill/2, 2*fill] with the
 // best last-wave occupancy wins (fewest splits on ties), keeping >= 4 pages per split.
 int64_t decode_num_splits(int64_t batch, int64_t kv_heads, int64_t max_pages, int64_t sms, int64_t fmt) {
+  // AXR_DECODE_SPLITS=n fixes the count (for measurements)
+  static const int64_t forced = [] {
+    const char* e = getenv("AXR_DECODE_SPLITS");
+    return e ? static_cast<int64_t>(atoi(e)) : 0;
+  }();
+  const int64_t s_max = std::max<int64_t>(1, std::min<int64_t>(64, max_pages / 4));
+  if (forced > 0) return std::min(forced, s_max);
   const int64_t base = std::max<int64_t>(1, batch * kv_heads);
   int64_t per_sm = 4;
   if (fmt == kBF16) per_sm = (227 * 1024) / TcCfg<kBF16>::SMEM;
   else if (fmt == kFP8Token) per_sm = (227 * 1024) / TcCfg<kFP8Token>::SMEM;
   else if (fmt == kINT4G64) per_sm = (227 * 1024) / TcCfg<kINT4G64>::SMEM;
-  const int64_t cap = sms * std::max<int64_t>(1, std::min<int64_t>(per_sm, 16));
-  const int64_t s_max = std::max<int64_t>(1, std::min<int64_t>(64, max_pages / 4));
+  const int64_t cap = sms * std::max<int64_t>(1, std::min<int64_t>(per_sm, 16));  // resident CTAs
+  // the fewest slices with the best wave fill: every extra slice costs partials and a
+  // combine (B = 32 x 8448 tokens, bf16: 1 slice 0.127 ms per layer, 2: 0.137, 5: 0.149)
   const int64_t fill = (cap + base - 1) / base;
   int64_t best = 1;
   double best_eff = -1.0;
@@ -873,7 +882,10 @@ void decode_attention(torch::Tensor q, int64_t k, int64_t v, int64_t km, int64_t
   p.part_lse = S > 1 || cascade ? part_lse.data_ptr<float>() : nullptr;
   p.page_start = cascade ? page_start->data_ptr<int>() : nullptr;
   const int G = Hq / static_cast<int>(Hkv);
-  dim3 grid(S, Hkv, B);
+  // KV-slice major: the first slice of every (sequence, KV head) starts together, so
+  // sequences that share prefix pages read them at the same time (once from DRAM, the
+  // rest from L2), and the later slices backfill SMs as earlier CTAs finish
+  dim3 grid(Hkv, B, S);
   auto st = at::cuda::getCurrentCUDAStream();
   if (D == 128) {
     if (fmt == kBF16) launch_tc<kBF16>(G, grid, p, st);
