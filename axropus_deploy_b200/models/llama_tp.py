@@ -13,8 +13,9 @@ Two step layouts:
   block is ``rmsnorm -> all-gather->GEMM (QKV | gate-up) -> ... -> GEMM->reduce-scatter
   (o | down)``, both collectives fused into the tcgen05 GEMM kernels
   (``csrc/kernels/gemm_tp.cu``). Rows are padded to a multiple of ``128 * W``.
-* **Replicated** (decode and short prefills): every GPU holds all rows; the row-parallel
-  GEMMs are followed by a one-shot peer all-reduce (``PeerAllReduce``, csrc/kernels/
+* **Replicated** (decode and short prefills): every GPU holds all rows; the projections run
+  on the dense tcgen05 kernels of ``ops.dense`` (weight streaming up to 256 rows), and the
+  row-parallel ones are followed by a one-shot peer all-reduce (``PeerAllReduce``, csrc/kernels/
   allreduce.cu: each GPU stores its slice into every peer's receive slot over NVLink and
   sums the world's slots; NCCL beyond its capacity). At a handful of rows the GEMMs read
   weights at HBM speed and the all-reduce moves a few hundred KB, so a 1024-row padded
@@ -30,9 +31,9 @@ from typing import List, Optional
 
 import torch
 import torch.distributed as dist
-import torch.nn.functional as F
 
 from .. import ops
+from ..ops import dense as dgemm
 from ..ops.kvcache import KVCache
 from ..parallel.dist import DistInfo
 from ..parallel.tp import TILE_M, PeerAllReduce, TpGemm, ag_gemm_nccl, gemm_rs_nccl
@@ -164,7 +165,7 @@ class TpLlamaModel:
         return x
 
     def _logits(self, x: torch.Tensor) -> torch.Tensor:
-        local = F.linear(x, self.lm_head).float()
+        local = dgemm.linear(x, self.lm_head).float()
         if self.world == 1:
             return local
         parts = [torch.empty_like(local) for _ in range(self.world)]
@@ -202,10 +203,10 @@ class TpLlamaModel:
         for li, lw in enumerate(self.layers):
             if li > 0:
                 x = ops.rmsnorm(h, lw.attn_norm, cfg.rms_eps, residual=residual)
-            self._attend(li, F.linear(x, lw.wqkv), meta, cache, attn)
-            h = self._all_reduce(F.linear(attn.view(T, self.hq * D), lw.wo))
+            self._attend(li, dgemm.linear(x, lw.wqkv), meta, cache, attn)
+            h = self._all_reduce(dgemm.linear(attn.view(T, self.hq * D), lw.wo))
             x = ops.rmsnorm(h, lw.mlp_norm, cfg.rms_eps, residual=residual)
-            h = self._all_reduce(F.linear(ops.silu_mul(F.linear(x, lw.w_gate_up)), lw.w_down))
+            h = self._all_reduce(dgemm.linear(ops.silu_mul(dgemm.linear(x, lw.w_gate_up)), lw.w_down))
         idx = (meta.logits_idx if meta.logits_idx is not None else torch.arange(T, device=tokens.device)).long()
         x = ops.rmsnorm(h[idx], self.final_norm, cfg.rms_eps, residual=residual[idx].clone())
         return self._logits(x)
