@@ -253,7 +253,10 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
     }
     const int qpos = pos0 + qt;
     const int qpos_min = pos0 + (row0 + x * BM) / G;
-    float m_used = -FLT_MAX, l = 0.f;
+    // scores stay raw: the softmax scale (log2 units, > 0) enters the row maximum once and
+    // every exponential through one FMA, 2^(c s - m)
+    const float csc = p.scale_log2;
+    float m_used = -INFINITY, l = 0.f;
     bool ok = active;
     for (int j = 0; ok && j < n_tiles; ++j) {
       ok = warp_ok(tc::mbar_wait(&s_full[x], j & 1, p.err, 18), p.err);
@@ -268,13 +271,14 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
 #pragma unroll
         for (int c = 0; c < 4; ++c)
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[c * 32 + i] = __uint_as_float(r[c][i]) * p.scale_log2;
+          for (int i = 0; i < 32; ++i) v[c * 32 + i] = __uint_as_float(r[c][i]);  // raw q.k
+
       }
       const int n0 = (t_begin + j) * BN;
       if (n0 + BN - 1 > qpos_min || n0 + BN > kv_len) {
 #pragma unroll
         for (int i = 0; i < BN; ++i)
-          if (n0 + i > qpos || n0 + i >= kv_len) v[i] = -FLT_MAX;
+          if (n0 + i > qpos || n0 + i >= kv_len) v[i] = -INFINITY;
       }
       // row maximum as 8 independent chains (a single 128-long fmax chain is latency-bound)
       float mx8[8];
@@ -284,8 +288,8 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
       for (int i = 8; i < BN; i += 8)
 #pragma unroll
         for (int c = 0; c < 8; ++c) mx8[c] = fmaxf(mx8[c], v[i + c]);
-      const float mt = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      const float mt = csc * fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                                   fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       if (j == 0) {
         m_used = mt;
       } else {
@@ -310,14 +314,14 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
         }
       }
       char* pbuf = sP + x * TILE;
-      // masked scores are -FLT_MAX: exp2 of (-FLT_MAX - m) is 0 for any finite m, and
-      // while every score so far was masked (m = -FLT_MAX) subtracting 0 gives 0 as well
-      const float msub = m_used == -FLT_MAX ? 0.f : m_used;
+      // masked scores are -inf: 2^(c (-inf) - m) is 0 for any finite m, and while every
+      // score so far was masked (m = -inf) subtracting 0 gives 0 as well
+      const float msub = m_used == -INFINITY ? 0.f : m_used;
 #pragma unroll
       for (int u = 0; u < 16; ++u) {
         float e[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) e[i] = exp2f(v[u * 8 + i] - msub);
+        for (int i = 0; i < 8; ++i) e[i] = exp2f(fmaf(v[u * 8 + i], csc, -msub));
         l += ((e[0] + e[1]) + (e[2] + e[3])) + ((e[4] + e[5]) + (e[6] + e[7]));
         *reinterpret_cast<uint4*>(pbuf + swz_off(row, u)) =
             make_uint4(pack_bf16x2(e[0], e[1]), pack_bf16x2(e[2], e[3]), pack_bf16x2(e[4], e[5]),
