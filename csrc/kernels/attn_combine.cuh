@@ -10,12 +10,16 @@
 
 #include <cfloat>
 
+#include "common.cuh"
+
 namespace axr {
 
 template <int D>
 __global__ void decode_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_lse,
                                       __nv_bfloat16* __restrict__ out, int S) {
   const long long bh = blockIdx.x;
+  pdl_trigger();
+  pdl_wait();  // the partials come from the attention kernel before
   const float* lse = part_lse + bh * S;
   float M = -FLT_MAX;
   for (int s = 0; s < S; ++s) M = fmaxf(M, lse[s]);
@@ -39,6 +43,8 @@ __global__ void cascade_combine_kernel(const float* __restrict__ part_o, const f
                                        const float* __restrict__ part_o2, const float* __restrict__ part_lse2, int S2,
                                        const int* __restrict__ row_of, int Hq, __nv_bfloat16* __restrict__ out) {
   const long long bh = blockIdx.x;
+  pdl_trigger();
+  pdl_wait();
   const int b = static_cast<int>(bh / Hq), h = static_cast<int>(bh % Hq);
   const float* lse = part_lse + bh * S;
   const int r = row_of[b];

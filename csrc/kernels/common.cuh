@@ -8,6 +8,8 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <cstdlib>
+#include <utility>
 
 namespace axr {
 
@@ -111,6 +113,43 @@ __device__ __forceinline__ void cp_async16_zfill(void* smem, const void* gmem, b
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N)); }
+
+// ---- programmatic dependent launch ----------------------------------------------------
+// A kernel started with launch_pdl() may begin while the kernel before it in the stream is
+// still running (once every CTA of that kernel has called pdl_trigger(), or it has ended).
+// Before reading anything an earlier kernel wrote, such a kernel calls pdl_wait(), which
+// returns once the kernels before it have completed and their writes are visible; it calls
+// pdl_wait() on every path before it ends, so completions stay in stream order (a kernel
+// that ended early would otherwise release its own successor's wait while its predecessor
+// still runs). pdl_trigger() right after a kernel's set-up lets the next kernel's CTAs come
+// up on free SM space and start their independent loads (weights, old KV pages).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// AXR_PDL=0 launches every kernel with plain stream order (for measurements).
+inline bool pdl_enabled_env() {
+  static const bool on = [] {
+    const char* e = std::getenv("AXR_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled_env() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 }  // namespace axr
 

@@ -431,6 +431,24 @@ __global__ void __launch_bounds__(128) decode_tc_kernel(DecodeParams p) {
   const int my_n = pg1 > pg0 + warp ? (pg1 - pg0 - warp + 3) / 4 : 0;
   const int* bt = p.block_table + (long long)b * p.bt_stride;
 
+  // Programmatic dependent launch: seq_lens, the block table and every page but the
+  // sequence's last two were written before this forward began, so the first pages of
+  // the ring are fetched before waiting for the kernel before (the projection that
+  // writes q and the newest KV row); q and the newest pages are read after the wait.
+  pdl_trigger();
+  const int stable_pages = max(0, (seq_len - 1) / kPage - 1);
+  const bool early = pg0 + warp + 4 * (C::STAGES - 2) < stable_pages;
+  auto prologue = [&]() {
+#pragma unroll
+    for (int s = 0; s < C::STAGES - 1; ++s) {
+      if (s < my_n) tc_issue_page<FMT>(p, bt[pg0 + warp + 4 * s], kvh, wbase + s * C::STAGE, lane);
+      cp_async_commit();
+    }
+  };
+  if (early) prologue();
+  pdl_wait();
+  if (!early) prologue();
+
   // Q^T fragments (B operand), dims permuted: k-step kk, lane t -> dims base..base+3
   uint32_t qb[8][2];
   float qsum[2] = {0.f, 0.f};  // INT4: sum of this lane's q dims per group, head g
@@ -481,12 +499,6 @@ __global__ void __launch_bounds__(128) decode_tc_kernel(DecodeParams p) {
   float zacc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
   float m[2] = {-FLT_MAX, -FLT_MAX}, l[2] = {0.f, 0.f};
 
-  // prologue
-#pragma unroll
-  for (int s = 0; s < C::STAGES - 1; ++s) {
-    if (s < my_n) tc_issue_page<FMT>(p, bt[pg0 + warp + 4 * s], kvh, wbase + s * C::STAGE, lane);
-    cp_async_commit();
-  }
   for (int i = 0; i < my_n; ++i) {
     {
       const int ni = i + C::STAGES - 1;
@@ -772,8 +784,8 @@ template <int FMT>
 static void launch_tc(int G, dim3 grid, const DecodeParams& p, cudaStream_t st) {
   constexpr int smem = TcCfg<FMT>::SMEM;
   auto go = [&](auto kern) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    kern<<<grid, 128, smem, st>>>(p);
+    AXR_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    AXR_CHECK_CUDA(launch_pdl(kern, grid, dim3(128), smem, st, p));
   };
   switch (G) {
     case 1: go(decode_tc_kernel<FMT, 1>); break;
@@ -903,14 +915,16 @@ void decode_attention(torch::Tensor q, int64_t k, int64_t v, int64_t km, int64_t
   AXR_CHECK_CUDA(cudaGetLastError());
   if (cascade) {
     TORCH_CHECK(D == 128, "shared-prefix decode: head_dim 128");
-    cascade_combine_kernel<128><<<B * Hq, 128, 0, st>>>(p.part_o, p.part_lse, S, part_o2->data_ptr<float>(),
-                                                        part_lse2->data_ptr<float>(), static_cast<int>(S2),
-                                                        row_of->data_ptr<int>(), Hq, p.out);
-    AXR_CHECK_CUDA(cudaGetLastError());
+    AXR_CHECK_CUDA(launch_pdl(cascade_combine_kernel<128>, dim3(B * Hq), dim3(128), 0, st,
+                              static_cast<const float*>(p.part_o), static_cast<const float*>(p.part_lse),
+                              static_cast<int>(S), static_cast<const float*>(part_o2->data_ptr<float>()),
+                              static_cast<const float*>(part_lse2->data_ptr<float>()), static_cast<int>(S2),
+                              static_cast<const int*>(row_of->data_ptr<int>()), Hq, p.out));
   } else if (S > 1) {
-    if (D == 128) decode_combine_kernel<128><<<B * Hq, 128, 0, st>>>(p.part_o, p.part_lse, p.out, S);
-    else decode_combine_kernel<64><<<B * Hq, 64, 0, st>>>(p.part_o, p.part_lse, p.out, S);
-    AXR_CHECK_CUDA(cudaGetLastError());
+    const float* po = p.part_o;
+    const float* pl = p.part_lse;
+    if (D == 128) AXR_CHECK_CUDA(launch_pdl(decode_combine_kernel<128>, dim3(B * Hq), dim3(128), 0, st, po, pl, p.out, S));
+    else AXR_CHECK_CUDA(launch_pdl(decode_combine_kernel<64>, dim3(B * Hq), dim3(64), 0, st, po, pl, p.out, S));
   }
 }
 

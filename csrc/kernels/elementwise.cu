@@ -18,10 +18,15 @@ template <int VPT>  // bf16 values per thread (8 per 16-byte vector)
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const __nv_bfloat16* __restrict__ x,
                                                       __nv_bfloat16* __restrict__ residual,
                                                       const __nv_bfloat16* __restrict__ w,
-                                                      __nv_bfloat16* __restrict__ out, int H, float eps) {
+                                                      __nv_bfloat16* __restrict__ out, int H, float eps,
+                                                      int early) {
   const long long row = blockIdx.x;
   const __nv_bfloat16* xr = x + row * H;
   __nv_bfloat16* rr = residual ? residual + row * H : nullptr;
+  // A decode-sized norm releases the next projection at once, so its weight stream starts
+  // during the norm; a prefill-sized one does not (see the launch).
+  if (early) pdl_trigger();
+  pdl_wait();  // x / residual come from the kernels before
   float v[VPT];
   float ss = 0.f;
 #pragma unroll
@@ -92,11 +97,18 @@ void rmsnorm(torch::Tensor x, c10::optional<torch::Tensor> residual, torch::Tens
   const auto* wp = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
   auto* op = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   const int per = (H + 256 * 8 - 1) / (256 * 8);
-  if (per <= 1) rmsnorm_kernel<8><<<rows, 256, 0, st>>>(xp, r, wp, op, H, (float)eps);
-  else if (per <= 2) rmsnorm_kernel<16><<<rows, 256, 0, st>>>(xp, r, wp, op, H, (float)eps);
-  else if (per <= 4) rmsnorm_kernel<32><<<rows, 256, 0, st>>>(xp, r, wp, op, H, (float)eps);
-  else rmsnorm_kernel<64><<<rows, 256, 0, st>>>(xp, r, wp, op, H, (float)eps);
-  AXR_CHECK_CUDA(cudaGetLastError());
+  const dim3 grid(static_cast<unsigned>(rows));
+  const float fe = static_cast<float>(eps);
+  // Early release only for decode-sized batches (<= 256 rows, the weight-streaming GEMMs):
+  // a prefill GEMM launched early parks its CTAs beside thousands of norm CTAs, which cost
+  // clock under the power cap.
+  const int early = rows <= 256 ? 1 : 0;
+  cudaError_t e;
+  if (per <= 1) e = launch_pdl(rmsnorm_kernel<8>, grid, dim3(256), 0, st, xp, r, wp, op, H, fe, early);
+  else if (per <= 2) e = launch_pdl(rmsnorm_kernel<16>, grid, dim3(256), 0, st, xp, r, wp, op, H, fe, early);
+  else if (per <= 4) e = launch_pdl(rmsnorm_kernel<32>, grid, dim3(256), 0, st, xp, r, wp, op, H, fe, early);
+  else e = launch_pdl(rmsnorm_kernel<64>, grid, dim3(256), 0, st, xp, r, wp, op, H, fe, early);
+  AXR_CHECK_CUDA(e);
 }
 
 // ------------------------------------------------------------------------ RoPE + KV
@@ -120,6 +132,8 @@ struct RopeKvParams {
 template <int FMT>
 __global__ void __launch_bounds__(256) rope_kv_kernel(RopeKvParams p) {
   constexpr int D = 128;
+  pdl_trigger();
+  pdl_wait();  // qkv comes from the projection before (and every path waits)
   const int lane = threadIdx.x & 31;
   const long long wid = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
   const int rows_per_tok = p.Hq + 2 * p.Hkv;
@@ -211,11 +225,12 @@ void rope_kv_write(torch::Tensor qkv, torch::Tensor pos, torch::Tensor slots, to
   const long long warps = (long long)T * (Hq + 2 * Hkv);
   const int grid = static_cast<int>((warps + 7) / 8);
   auto st = at::cuda::getCurrentCUDAStream();
-  if (fmt == kBF16) rope_kv_kernel<kBF16><<<grid, 256, 0, st>>>(p);
-  else if (fmt == kFP8Token) rope_kv_kernel<kFP8Token><<<grid, 256, 0, st>>>(p);
-  else if (fmt == kINT4G64) rope_kv_kernel<kINT4G64><<<grid, 256, 0, st>>>(p);
+  cudaError_t e;
+  if (fmt == kBF16) e = launch_pdl(rope_kv_kernel<kBF16>, dim3(grid), dim3(256), 0, st, p);
+  else if (fmt == kFP8Token) e = launch_pdl(rope_kv_kernel<kFP8Token>, dim3(grid), dim3(256), 0, st, p);
+  else if (fmt == kINT4G64) e = launch_pdl(rope_kv_kernel<kINT4G64>, dim3(grid), dim3(256), 0, st, p);
   else TORCH_CHECK(false, "rope_kv_write: unsupported cache format ", fmt);
-  AXR_CHECK_CUDA(cudaGetLastError());
+  AXR_CHECK_CUDA(e);
 }
 
 // --------------------------------------------------------------------------- SiLU*mul
