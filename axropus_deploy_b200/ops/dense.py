@@ -144,9 +144,12 @@ def _reference(x, w, epi, out, res, rope):
 
 
 def linear(x: torch.Tensor, w: torch.Tensor, epi: str = "store", out: Optional[torch.Tensor] = None,
-           res: Optional[torch.Tensor] = None, rope=None, splits: int = 0, force_big: bool = False) -> torch.Tensor:
+           res: Optional[torch.Tensor] = None, rope=None, splits: int = 0, force_big: bool = False,
+           one_cta: bool = False) -> torch.Tensor:
     """``epilogue(x @ w.T)``; ``rope`` = (pos, slots, cos_sin, cache, layer, Hq, Hkv) for
-    ``epi="rope"`` (bf16 cache)."""
+    ``epi="rope"`` (bf16 cache). ``force_big`` runs the prefill-sized (persistent) path at
+    any M; ``one_cta`` runs that path on the 1-CTA kernel instead of the CTA-pair one."""
+    force_big = force_big or one_cta
     M, N = x.shape[0], w.shape[0]
     if out is None:
         width = N // 2 if epi == "swiglu" else (rope[5] * 128 if epi == "rope" else N)
@@ -171,5 +174,5 @@ def linear(x: torch.Tensor, w: torch.Tensor, epi: str = "store", out: Optional[t
             raise ValueError("linear(epi='rope') writes a bf16 cache; other formats use ops.rope_kv_write")
         kc, vc, _, _, bs, hs, _, _ = cache.layer_args(layer)
     C.dense_gemm(x, w, out, EPI[epi], res, pos, slots, cos_sin, kc, vc, bs, hs, Hq, Hkv, sc.ws, sc.cnt,
-                 error_flag(dev), splits, 1 if force_big else 0)
+                 error_flag(dev), splits, (2 if one_cta else 1) if force_big else 0)
     return out

@@ -95,6 +95,7 @@ def main():
             from axropus_deploy_b200.ops._ext import cuda_ext
             row = {"shape": name, "M": M, "N": N, "K": K, "epilogue": epi,
                    "splits": cuda_ext().dense_stream_splits(M, N, K, dense.sm_count(dev)) if M <= 256 else 0,
+                   "pair_clusters": cuda_ext().dense_pair_clusters(dev.index) if M > 256 else 0,
                    "ours_ms": round(t_ours, 4),
                    "cublas_ms": round(t_ref, 4), "speedup": round(t_ref / t_ours, 3),
                    "ours_weight_gbs": round(wbytes / t_ours / 1e6, 1),

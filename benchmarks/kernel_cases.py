@@ -2,7 +2,7 @@
 (e.g. under ncu with -k/-c). Sizes are chosen so inputs exceed the 126 MB L2 while the
 whole run stays within a few GB of device memory.
 
-    python benchmarks/kernel_cases.py decode|decode_int4|decode_fp8|restore|restore_fp8|capture_int4|
+    python benchmarks/kernel_cases.py decode|decode_int4|decode_fp8|decode_shared|restore|restore_fp8|capture_int4|
                                       prefill|prefill_split|gemm|gemm_tp|moe|rmsnorm|rope|
                                       silu_mul|argmax|spec_verify
 """
@@ -12,6 +12,7 @@ import sys
 import torch
 
 sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
 
 from axropus_deploy_b200 import ops  # noqa: E402
 from axropus_deploy_b200.amf.pool import PoolSlab  # noqa: E402
@@ -34,6 +35,30 @@ def decode(fmt="bf16"):
     q = torch.randn(B, 32, 128, device="cuda").to(torch.bfloat16)
     for _ in range(3):
         ops.decode_attention(q, cache, 0, bt, sl, max_seq_len=T)
+
+
+def decode_shared():
+    # the headline bench's decode batch: 32 sequences of 8448 tokens whose 8192-token
+    # prefixes follow its Zipf(1.1) reuse over 64 prefixes (10 % fresh), one layer
+    import numpy as np
+
+    from decode_step import build_tables
+
+    class A:
+        batch, context, prefix_len, prefixes = 32, 8448, 8192, 64
+
+    lists, nblocks = build_tables(A, np.random.default_rng(0))
+    cache = KVCache(1, nblocks + 8, 8, 128, "bf16", "cuda")
+    cache.data.normal_()
+    width = max(len(x) for x in lists)
+    bt = torch.zeros(A.batch, width, dtype=torch.int32)
+    for i, x in enumerate(lists):
+        bt[i, :len(x)] = torch.tensor(x, dtype=torch.int32)
+    bt = bt.cuda()
+    sl = torch.full((A.batch,), A.context, dtype=torch.int32, device="cuda")
+    q = torch.randn(A.batch, 32, 128, device="cuda").to(torch.bfloat16)
+    for _ in range(3):
+        ops.decode_attention(q, cache, 0, bt, sl, max_seq_len=A.context)
 
 
 def restore(pool_fmt="raw", cache_fmt="bf16"):
@@ -161,7 +186,8 @@ def spec_verify():
 
 
 CASES = {"decode": lambda: decode("bf16"), "decode_int4": lambda: decode("int4"),
-         "decode_fp8": lambda: decode("fp8"), "restore": lambda: restore("raw", "bf16"),
+         "decode_fp8": lambda: decode("fp8"), "decode_shared": decode_shared,
+         "restore": lambda: restore("raw", "bf16"),
          "restore_fp8": lambda: restore("fp8", "bf16"), "capture_int4": lambda: capture("int4"),
          "prefill": prefill, "gemm": gemm_case, "rmsnorm": rmsnorm, "rope": rope,
          "prefill_split": prefill_split, "gemm_tp": gemm_tp_plain, "moe": moe, "silu_mul": silu_mul,

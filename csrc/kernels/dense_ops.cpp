@@ -12,7 +12,8 @@ namespace dense {
 // may be out), 2 SwiGLU (out [M, N/2]), 3 RoPE + bf16 paged KV write (out = q [M, Hq*128]).
 // ws fp32 / cnt int32: scratch (the split-K partials of the stream kernel stay in its
 // clusters' shared memory; see dense_stream_workspace). splits <= 0: automatic, else the
-// stream kernel's CTAs per weight tile (at most 8, one cluster).
+// stream kernel's CTAs per weight tile (at most 8, one cluster). force_big: 0 automatic,
+// 1 the big-M path at any M, 2 the big-M path on the 1-CTA kernel (not the CTA-pair one).
 void dense_gemm(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t epi, c10::optional<torch::Tensor> res,
                 c10::optional<torch::Tensor> pos, c10::optional<torch::Tensor> slots,
                 c10::optional<torch::Tensor> cos_sin, int64_t kc, int64_t vc, int64_t blk_stride, int64_t head_stride,
@@ -79,11 +80,14 @@ void dense_gemm(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t epi
   }
   c.err = err.data_ptr<int>();
   c.force_big = force_big != 0;
+  c.force_one_cta = force_big == 2;
   const std::string msg = dense_gemm_launch(c, at::cuda::getCurrentCUDAStream());
   TORCH_CHECK(msg.empty(), "dense_gemm: ", msg);
 }
 
 int64_t dense_stream_nt(int64_t M) { return stream_nt(M); }
+
+int64_t dense_pair_clusters(int64_t device) { return pair_grid_clusters(static_cast<int>(device)); }
 
 int64_t dense_stream_splits(int64_t M, int64_t N, int64_t K, int64_t sms) {
   return stream_splits(M, N, K, static_cast<int>(sms));

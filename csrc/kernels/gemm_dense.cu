@@ -604,6 +604,244 @@ __global__ void __launch_bounds__(BTHREADS, 1) gemm_big_kernel(const __grid_cons
 }
 
 // =====================================================================================
+// persistent CTA-pair kernel (tcgen05 cta_group::2): one 256 x 256 output tile per pair
+// =====================================================================================
+// The two CTAs of a cluster run the tensor cores of two SMs as one 256-row MMA: CTA r
+// loads rows [128 r, 128 r + 128) of the tile's X rows and of its W rows (half of B
+// each) into its own shared memory; the leader (r = 0) issues tcgen05.mma.cta_group::2
+// with M = N = 256, which reads A and B from both CTAs' shared memory and accumulates
+// each CTA's 128 rows x 256 columns in that CTA's TMEM. Per SM that is 32 KB of operands
+// per 64-deep k step instead of 48 KB for a 1-CTA 128 x 256 tile at the same MMA rate:
+// a third less L2 -> SM and shared-memory traffic (and energy under the power cap) per
+// FLOP (8320 x 28672 x 4096 + SwiGLU: 1.261 ms against 1.333 ms for the 1-CTA kernel).
+//
+// Synchronisation: both CTAs' TMA loads (plain per-CTA loads of this GPU's memory, no
+// multicast; the .cta_group::2 form lets a load complete on the peer's barrier) count
+// their bytes on the leader's full[s], for which the leader's producer expects both
+// halves. The leader's commits are multicast to both CTAs (stage free: empty[s];
+// accumulator ready: accf[b]); both CTAs' epilogue warps arrive on the leader's acce[b]
+// (count 8) when their half of a TMEM buffer is drained. A cluster barrier at the end
+// keeps either CTA from leaving while the other may still read its shared memory or
+// arrive on its barriers. (Measured and dropped: each CTA's loads completing on its own
+// barrier and a peer thread relaying the completion to the leader -- the extra hop
+// starved the 6-stage ring and halved the rate.)
+constexpr int PST = 6;
+constexpr int PA_BYTES = 128 * BK * 2;   // this CTA's 128 X rows
+constexpr int PB_BYTES = 128 * BK * 2;   // this CTA's 128 W rows (half of the tile's 256)
+constexpr int PSTAGE = PA_BYTES + PB_BYTES;
+constexpr int PSMEM = 1024 + PST * PSTAGE + 256;
+constexpr int PBM = 256, PBN = 256;
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t mapa_rank(const void* p, uint32_t rank) {
+  uint32_t a;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(tc::smem_u32(p)), "r"(rank));
+  return a;
+}
+// Arrive on the barrier at shared::cluster address `a` (possibly another CTA's), release
+// at cluster scope: the arriving thread's earlier writes (and fenced tcgen05 reads) are
+// ordered before the waiter's acquire.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t a) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(a) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t phase) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(tc::smem_u32(bar)), "r"(phase)
+      : "memory");
+  return ok != 0;
+}
+// Bounded cluster-scope wait (barriers that a thread of the other CTA arrives on).
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t phase, volatile int* err, int code) {
+  if (mbar_try_wait_cluster(bar, phase)) return true;
+  const unsigned long long t0 = tc::globaltimer();
+  while (true) {
+    if (mbar_try_wait_cluster(bar, phase)) return true;
+    if (*err != 0) return false;
+    if (tc::globaltimer() - t0 > tc::kWaitLimitNs) {
+      atomicCAS(const_cast<int*>(err), 0, code);
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tc::smem_u32(dst)),
+               "r"(ncols));
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::);
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols));
+}
+__device__ __forceinline__ void mma_pair(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+// Arrive on the barrier at this shared offset in both CTAs of the pair once every earlier
+// MMA of this thread has completed.
+__device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          tc::smem_u32(bar)),
+      "h"(static_cast<uint16_t>(3))
+      : "memory");
+}
+
+// 2D tiled TMA load into this CTA's shared memory whose completion is counted on the
+// barrier at shared::cluster address `bar_cluster` (the pair leader's); no multicast.
+__device__ __forceinline__ void tma_load_2d_pair(void* smem, const CUtensorMap* map, int x, int y,
+                                                 uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+      "%3}], [%4];" ::"r"(tc::smem_u32(smem)),
+      "l"(map), "r"(x), "r"(y), "r"(bar_cluster)
+      : "memory");
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(BTHREADS, 1) gemm_pair_kernel(const __grid_constant__ CUtensorMap tmX,
+                                                                const __grid_constant__ CUtensorMap tmW, Args g) {
+  extern __shared__ __align__(1024) char smem_raw[];
+  char* base = align1024(smem_raw);  // same offset in both CTAs (same kernel, same layout)
+  char* sA = base;
+  char* sB = base + PST * PA_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + PST * PB_BYTES);
+  uint64_t* empty = full + PST;
+  uint64_t* accf = empty + PST;  // [2]
+  uint64_t* acce = accf + 2;     // [2] (used in the leader)
+  uint64_t* drain = acce + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const int pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
+  const int num_m = (g.M + PBM - 1) / PBM, num_n = (g.N + PBN - 1) / PBN;
+  const int tiles = num_m * num_n;
+  const int nk = (g.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < PST; ++s) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      tc::mbar_init(&accf[b], 1);
+      tc::mbar_init(&acce[b], 8);
+    }
+    tc::mbar_init(drain, 1);
+    tc::fence_barrier_init();
+    tc::prefetch_tmap(&tmX);
+    tc::prefetch_tmap(&tmW);
+  }
+  if (warp == 2) {
+    tmem_alloc_pair(tmem_slot, 512);
+    tmem_relinquish_pair();
+  }
+  tc::tc_fence_before();
+  cluster_sync();  // both CTAs' barriers exist before any remote arrive or multicast commit
+  tc::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {  // ---------------- TMA producer (both CTAs): this CTA's halves
+      int it = 0;
+      bool ok = true, waited = false;
+      for (int t = pair; ok && t < tiles; t += pairs) {
+        int mt, nt;
+        big_tile(t, num_m, num_n, mt, nt);
+        for (int kt = 0; kt < nk; ++kt, ++it) {
+          const int s = it % PST;
+          if (it >= PST && !tc::mbar_wait(&empty[s], ((it / PST) + 1) & 1, g.err, 1)) { ok = false; break; }
+          const int wy = nt * PBN + static_cast<int>(rank) * 128, xy = mt * PBM + static_cast<int>(rank) * 128;
+          // both CTAs' bytes complete on the leader's full[s]; the leader expects them all
+          if (rank == 0) tc::mbar_arrive_expect_tx(&full[s], 2 * PSTAGE);
+          const uint32_t bar = mapa_rank(&full[s], 0);
+          tma_load_2d_pair(sB + s * PB_BYTES, &tmW, kt * BK, wy, bar);
+          if (!waited) {
+            griddep_wait();
+            waited = true;
+          }
+          tma_load_2d_pair(sA + s * PA_BYTES, &tmX, kt * BK, xy, bar);
+        }
+      }
+      if (!waited) griddep_wait();
+      if (!ok && rank == 0) {
+        // let the pair's loads land before shared memory can be released: the leader's
+        // barriers count both CTAs' bytes (the peer's in-flight loads land long before the
+        // bounded waits of the failed roles run out and both CTAs reach the final barrier)
+        for (int j = max(0, it - PST); j < it; ++j) tc::mbar_wait_quiet(&full[j % PST], (j / PST) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      if (rank == 0) {  // ---------------- MMA issuer for the pair
+        constexpr uint32_t idesc = tc::idesc_bf16_f32(PBM, PBN);
+        int it = 0, i = 0;
+        for (int t = pair; t < tiles; t += pairs, ++i) {
+          const int buf = i & 1;
+          if (i >= 2 && !mbar_wait_cluster(&acce[buf], ((i >> 1) + 1) & 1, g.err, 6)) break;
+          tc::tc_fence_after();
+          bool ok = true;
+          for (int kt = 0; kt < nk; ++kt, ++it) {
+            const int s = it % PST;
+            if (!mbar_wait_cluster(&full[s], (it / PST) & 1, g.err, 2)) { ok = false; break; }
+            tc::tc_fence_after();
+            const uint32_t a_addr = tc::smem_u32(sA + s * PA_BYTES), b_addr = tc::smem_u32(sB + s * PB_BYTES);
+#pragma unroll
+            for (int kk = 0; kk < BK / 16; ++kk)
+              mma_pair(tmem + buf * PBN, tc::smem_desc_k_sw128(a_addr + kk * 32),
+                       tc::smem_desc_k_sw128(b_addr + kk * 32), idesc, (kt | kk) != 0);
+            mma_commit_pair(&empty[s]);
+          }
+          mma_commit_pair(&accf[buf]);
+          if (!ok) break;
+        }
+        mma_commit_pair(drain);  // fires in both CTAs once every MMA of the pair is done
+      }
+      tc::mbar_wait_quiet(drain, 0);  // no MMA still reads this CTA's shared memory / writes its TMEM
+    }
+  } else {
+    // ---------------- epilogue warps 2..5 (both CTAs): this CTA's 128 rows of each tile
+    const int lg = warp & 3;
+    griddep_wait();  // residual / positions / slots come from earlier kernels
+    const uint32_t acce_leader = mapa_rank(&acce[0], 0);
+    int i = 0;
+    for (int t = pair; t < tiles; t += pairs, ++i) {
+      int mt, nt;
+      big_tile(t, num_m, num_n, mt, nt);
+      const int buf = i & 1;
+      bool ok = tc::mbar_wait(&accf[buf], (i >> 1) & 1, g.err, 3);
+      ok = __all_sync(0xffffffffu, ok) && __shfl_sync(0xffffffffu, *g.err, 0) == 0;
+      tc::tc_fence_after();
+      if (!ok) break;
+      const int m = mt * PBM + static_cast<int>(rank) * 128 + lg * 32 + lane;
+      big_epilogue<EPI>(g, tmem + buf * PBN + (static_cast<uint32_t>(lg * 32) << 16), m, mt, nt);
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acce_leader + buf * 8);
+    }
+  }
+  __syncwarp();
+  if (threadIdx.x == 0) griddep_launch();
+  tc::tc_fence_before();
+  cluster_sync();  // neither CTA leaves while the other may read its shared memory or arrive on its barriers
+  tc::tc_fence_after();
+  if (warp == 2) tmem_dealloc_pair(tmem, 512);
+}
+
+// =====================================================================================
 // host
 // =====================================================================================
 namespace {
@@ -639,7 +877,7 @@ bool pdl_enabled() {
 // cluster_y > 1: clusters of (1, cluster_y, 1) CTAs (the split-K CTAs of one weight tile).
 template <typename Kernel>
 cudaError_t launch_dense(Kernel kernel, dim3 grid, dim3 block, int smem, cudaStream_t st, const CUtensorMap& m0,
-                       const CUtensorMap& m1, const Args& g, int cluster_y = 1) {
+                       const CUtensorMap& m1, const Args& g, int cluster_y = 1, int cluster_x = 1) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
@@ -652,9 +890,9 @@ cudaError_t launch_dense(Kernel kernel, dim3 grid, dim3 block, int smem, cudaStr
     attr[n].val.programmaticStreamSerializationAllowed = 1;
     ++n;
   }
-  if (cluster_y > 1) {
+  if (cluster_y > 1 || cluster_x > 1) {
     attr[n].id = cudaLaunchAttributeClusterDimension;
-    attr[n].val.clusterDim.x = 1;
+    attr[n].val.clusterDim.x = cluster_x;
     attr[n].val.clusterDim.y = cluster_y;
     attr[n].val.clusterDim.z = 1;
     ++n;
@@ -702,7 +940,67 @@ cudaError_t launch_big(const CUtensorMap& tx, const CUtensorMap& tw, const Args&
   return launch_dense(kernel, dim3(grid), dim3(BTHREADS), BSMEM, st, tx, tw, g);
 }
 
+// AXR_DENSE_PAIR=0 runs prefill-sized GEMMs on the 1-CTA kernel (for measurements).
+bool pair_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("AXR_DENSE_PAIR");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+// Clusters of the pair kernel that fit the GPU at once (per device, cached): the
+// persistent grid must be resident in one wave, and GPCs with an odd number of free SMs
+// hold fewer pairs than SMs / 2.
+template <int EPI>
+int pair_clusters(int dev) {
+  static const int forced = [] {
+    const char* e = getenv("AXR_DENSE_PAIR_CLUSTERS");
+    return e ? atoi(e) : 0;
+  }();
+  if (forced > 0) return forced;
+  static int cached[64] = {0};
+  if (dev >= 0 && dev < 64 && cached[dev]) return cached[dev];
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * 74);
+  cfg.blockDim = dim3(BTHREADS);
+  cfg.dynamicSmemBytes = PSMEM;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, gemm_pair_kernel<EPI>, &cfg) != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    n = sm_count(dev) / 2;
+  }
+  if (dev >= 0 && dev < 64) cached[dev] = n;
+  return n;
+}
+
+template <int EPI>
+cudaError_t launch_pair(const CUtensorMap& tx, const CUtensorMap& tw, const Args& g, int dev, cudaStream_t st) {
+  auto kernel = gemm_pair_kernel<EPI>;
+  static bool attr = false;
+  if (!attr) {
+    const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PSMEM);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  const int tiles = ((g.M + PBM - 1) / PBM) * ((g.N + PBN - 1) / PBN);
+  const int clusters = std::max(1, std::min(tiles, pair_clusters<EPI>(dev)));
+  return launch_dense(kernel, dim3(2 * clusters), dim3(BTHREADS), PSMEM, st, tx, tw, g, 1, 2);
+}
+
 }  // namespace
+
+int pair_grid_clusters(int dev) {
+  cudaFuncSetAttribute(gemm_pair_kernel<kStore>, cudaFuncAttributeMaxDynamicSharedMemorySize, PSMEM);
+  return pair_clusters<kStore>(dev);
+}
 
 // Largest split count whose partials of one chunk (CH tokens) fit the TMA ring.
 // Split-K CTAs of one weight tile form a cluster: at most the portable cluster size.
@@ -793,6 +1091,16 @@ std::string dense_gemm_launch(const DenseCall& c, cudaStream_t st) {
       case kResid: e = launch_stream_nt<kResid>(nt, tw, tx, g, st); break;
       case kSwiGLU: e = launch_stream_nt<kSwiGLU>(nt, tw, tx, g, st); break;
       default: e = launch_stream_nt<kRope>(nt, tw, tx, g, st); break;
+    }
+  } else if (pair_enabled() && !c.force_one_cta) {
+    CUtensorMap tx, tw;  // 128-row boxes: each CTA of a pair loads its half of the 256-row tile
+    if (!make_map(&tx, c.x, c.M, c.K, c.ldx, 128) || !make_map(&tw, c.w, c.N, c.K, c.ldw, 128))
+      return "cuTensorMapEncodeTiled failed";
+    switch (c.epi) {
+      case kStore: e = launch_pair<kStore>(tx, tw, g, c.device, st); break;
+      case kResid: e = launch_pair<kResid>(tx, tw, g, c.device, st); break;
+      case kSwiGLU: e = launch_pair<kSwiGLU>(tx, tw, g, c.device, st); break;
+      default: e = launch_pair<kRope>(tx, tw, g, c.device, st); break;
     }
   } else {
     CUtensorMap tx, tw;

@@ -40,6 +40,7 @@ struct DenseCall {
   int* err;    // error flag (bounded waits)
   int splits;  // <= 0: stream_splits
   bool force_big;
+  bool force_one_cta;  // big-M path on the 1-CTA kernel instead of the CTA-pair kernel
   int device;
 };
 
@@ -51,6 +52,8 @@ int stream_max_splits(int nt);
 int stream_splits(int64_t M, int64_t N, int64_t K, int sms);
 // {fp32 partial floats, counters} the stream kernel needs.
 void stream_workspace(int64_t M, int64_t N, int64_t K, int sms, int64_t* ws_floats, int64_t* counters);
+// Thread-block clusters (CTA pairs) the prefill-sized kernel keeps resident on device `dev`.
+int pair_grid_clusters(int dev);
 // Checks the call and launches; returns an empty string or the reason it refused.
 std::string dense_gemm_launch(const DenseCall& c, cudaStream_t st);
 

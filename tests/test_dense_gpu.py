@@ -113,3 +113,58 @@ def test_error_flag_clear_after_calls():
     dense.linear(x, w)
     torch.cuda.synchronize()
     assert check_errors(x.device) == 0
+
+
+# ---- prefill-sized path: CTA-pair kernel (tcgen05 cta_group::2) against the 1-CTA kernel
+# and the fp32 oracle: ragged M and N, several tiles per pair (persistent loop, both TMEM
+# accumulator buffers), every epilogue.
+@pytest.mark.parametrize("M", [257, 384, 1000, 4100])
+@pytest.mark.parametrize("NK", [(384, 512), (1536, 4096), (520, 1024), (4096, 640)])
+def test_pair_kernel_store(M, NK):
+    N, K = NK
+    x = _rand(M, K, seed=21)
+    w = _rand(N, K, std=0.05, seed=22)
+    pair = dense.linear(x, w)
+    one = dense.linear(x, w, one_cta=True)
+    _close(pair.cpu(), dense.linear(x.cpu(), w.cpu()))
+    _close(pair, one, tol=1e-2)
+
+
+@pytest.mark.parametrize("M", [300, 2049])
+def test_pair_kernel_epilogues(M):
+    K, Fd, N = 1024, 768, 1024
+    x = _rand(M, K, seed=23)
+    gate, up = _rand(Fd, K, std=0.05, seed=24), _rand(Fd, K, std=0.05, seed=25)
+    w = dense.interleave_gate_up(gate, up)
+    out = dense.linear(x, w, "swiglu")
+    ref = torch.nn.functional.silu(x.float() @ gate.float().t()) * (x.float() @ up.float().t())
+    _close(out.cpu(), ref.cpu())
+    w2 = _rand(N, K, std=0.05, seed=26)
+    res = _rand(M, N, seed=27)
+    want = dense.linear(x.cpu(), w2.cpu(), "resid", res=res.cpu())
+    dense.linear(x, w2, "resid", out=res, res=res)
+    _close(res.cpu(), want)
+
+
+def test_pair_kernel_rope():
+    M, Hq, Hkv, D, H = 777, 8, 2, 128, 512
+    x = _rand(M, H, seed=28)
+    w = _rand((Hq + 2 * Hkv) * D, H, std=0.05, seed=29)
+    cos_sin = rope_cos_sin(4096, D, 500000.0, None, DEV)
+    pos = torch.randint(0, 4000, (M,), device=DEV, dtype=torch.int32)
+    nb = (M + 15) // 16 + 4
+    slots = torch.randperm(nb * 16, device=DEV)[:M].to(torch.int32)
+    cache = KVCache(1, nb, Hkv, D, "bf16", DEV)
+    q = dense.linear(x, w, "rope", rope=(pos, slots, cos_sin, cache, 0, Hq, Hkv))
+    cache1 = KVCache(1, nb, Hkv, D, "bf16", DEV)
+    q1 = dense.linear(x, w, "rope", rope=(pos, slots, cos_sin, cache1, 0, Hq, Hkv), one_cta=True)
+    cache_ref = KVCache(1, nb, Hkv, D, "bf16", "cpu")
+    q_ref = dense.linear(x.cpu(), w.cpu(), "rope", rope=(pos.cpu(), slots.cpu(), cos_sin.cpu(), cache_ref, 0, Hq, Hkv))
+    _close(q.cpu(), q_ref)
+    _close(cache.data.cpu(), cache_ref.data)
+    _close(q, q1, tol=1e-2)
+    _close(cache.data, cache1.data, tol=1e-2)
+    from axropus_deploy_b200.ops.gemm import check_errors
+
+    torch.cuda.synchronize()
+    assert check_errors(x.device) == 0
