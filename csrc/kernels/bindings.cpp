@@ -64,6 +64,7 @@ void dense_gemm(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t epi
                 int64_t force_big);
 int64_t dense_stream_nt(int64_t M);
 int64_t dense_pair_clusters(int64_t device);
+std::vector<int64_t> dense_trace_read();
 int64_t dense_stream_splits(int64_t M, int64_t N, int64_t K, int64_t sms);
 std::vector<int64_t> dense_stream_workspace(int64_t M, int64_t N, int64_t K, int64_t sms);
 }  // namespace dense
@@ -98,6 +99,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dense_gemm", &axr::dense::dense_gemm);
   m.def("dense_stream_nt", &axr::dense::dense_stream_nt);
   m.def("dense_pair_clusters", &axr::dense::dense_pair_clusters);
+  m.def("dense_trace_read", &axr::dense::dense_trace_read);
   m.def("dense_stream_splits", &axr::dense::dense_stream_splits);
   m.def("dense_stream_workspace", &axr::dense::dense_stream_workspace);
   m.def("codec_encode", &axr::codec::codec_encode);

@@ -89,6 +89,12 @@ int64_t dense_stream_nt(int64_t M) { return stream_nt(M); }
 
 int64_t dense_pair_clusters(int64_t device) { return pair_grid_clusters(static_cast<int>(device)); }
 
+std::vector<int64_t> dense_trace_read() {
+  std::vector<unsigned long long> v;
+  dense_trace(&v);
+  return std::vector<int64_t>(v.begin(), v.end());
+}
+
 int64_t dense_stream_splits(int64_t M, int64_t N, int64_t K, int64_t sms) {
   return stream_splits(M, N, K, static_cast<int>(sms));
 }

@@ -39,6 +39,7 @@
 #include <algorithm>
 #include <cstdlib>
 #include <string>
+#include <vector>
 
 #include "common.cuh"
 #include "gemm_dense.h"
@@ -65,6 +66,7 @@ struct EpiArgs {
 struct Args {
   int M, N, K;
   int splits;   // stream kernel: CTAs per 128-row weight tile
+  unsigned long long* trace;  // stream kernel timeline (AXR_DENSE_TRACE=1): 8 %globaltimer stamps per CTA
   volatile int* err;
   EpiArgs e;
 };
@@ -224,6 +226,8 @@ __global__ void __launch_bounds__(128) gemm_stream_kernel(const __grid_constant_
   const int kb0 = static_cast<int>((long long)split * nk / g.splits);
   const int kb1 = static_cast<int>((long long)(split + 1) * nk / g.splits);
   const int nkb = kb1 - kb0;
+  unsigned long long* tr = g.trace ? g.trace + 8ull * (blockIdx.y * gridDim.x + blockIdx.x) : nullptr;
+  if (tr && threadIdx.x == 0) tr[0] = tc::globaltimer();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::ST; ++s) {
@@ -243,6 +247,7 @@ __global__ void __launch_bounds__(128) gemm_stream_kernel(const __grid_constant_
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (tr && threadIdx.x == 0) tr[1] = tc::globaltimer();
   // Set-up done (tensor memory held): the next kernel may come up on free SM space and
   // start its own independent loads while this one streams.
   if (threadIdx.x == 0) griddep_launch();
@@ -276,6 +281,7 @@ __global__ void __launch_bounds__(128) gemm_stream_kernel(const __grid_constant_
     for (int i = 0; i < nkb; ++i) {
       const int s = i % C::ST;
       if (!tc::mbar_wait(&full[s], (i / C::ST) & 1, g.err, 2)) { ok = false; break; }
+      if (tr && (i == 0 || i == nkb - 1)) tr[i == 0 ? 2 : 3] = tc::globaltimer();
       tc::tc_fence_after();
       const uint32_t a_addr = tc::smem_u32(base + s * C::STAGE);
       const uint32_t b_addr = a_addr + C::A_BYTES;
@@ -292,6 +298,7 @@ __global__ void __launch_bounds__(128) gemm_stream_kernel(const __grid_constant_
 
   // ---------------- epilogue (all 4 warps; warp w reads TMEM lanes 32w..32w+31)
   bool ready = tc::mbar_wait(accb, 0, g.err, 3);
+  if (tr && threadIdx.x == 0) tr[4] = tc::globaltimer();
   tc::tc_fence_after();
   griddep_wait();  // residual, positions and slots come from earlier kernels
   ready = __syncthreads_and(ready && *g.err == 0) != 0;
@@ -310,11 +317,17 @@ __global__ void __launch_bounds__(128) gemm_stream_kernel(const __grid_constant_
     }
   } else {
     // split-K inside the cluster: each CTA parks its fp32 partial [NT][128] in its idle
-    // ring, and after a cluster barrier CTA `split` sums the 16-token chunks c with
+    // ring, and after a cluster barrier CTA `split` sums the CHR-token chunks c with
     // c % splits == split over every CTA's shared memory (distributed shared memory, in
     // split order: deterministic) and runs their epilogue; a second barrier keeps every
     // partial alive until all CTAs have read it. Both barriers are reached by every
-    // thread of every CTA, failed or not.
+    // thread of every CTA, failed or not. Chunks are small enough that every CTA of the
+    // cluster takes a share (32 tokens over 8 CTAs: 4 each), and each thread issues its
+    // loads from all splits before the first add (one remote round trip, not one per
+    // split): the reduction tail was 4-5 us of a 13-16 us projection with 16-token chunks
+    // summed split by split.
+    constexpr int CHR = NT <= 32 ? 4 : (NT <= 64 ? 8 : 16);
+    constexpr int QB = CHR <= 4 ? 8 : (CHR <= 8 ? 4 : 2);  // splits per batch of loads
     float* part = reinterpret_cast<float*>(base);
     float* sx = part + NT * 128;
     if (ready) {
@@ -327,28 +340,51 @@ __global__ void __launch_bounds__(128) gemm_stream_kernel(const __grid_constant_
       }
     }
     cluster_sync();
+    if (tr && threadIdx.x == 0) tr[5] = tc::globaltimer();
     if (ready) {
+      const int n = tile * 128 + r;
 #pragma unroll 1
-      for (int c0 = split * 16; c0 < mt; c0 += g.splits * 16) {
-        float v[16];
+      for (int c0 = split * CHR; c0 < mt; c0 += g.splits * CHR) {
+        float v[CHR], rv[CHR];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] = 0.f;
-#pragma unroll 1
-        for (int q = 0; q < g.splits; ++q) {
-          float pv[16];
-#pragma unroll
-          for (int j = 0; j < 16; ++j) pv[j] = ld_dsmem(part + (c0 + j) * 128 + r, q);
-#pragma unroll
-          for (int j = 0; j < 16; ++j) v[j] += pv[j];
+        for (int j = 0; j < CHR; ++j) {
+          v[j] = 0.f;
+          rv[j] = 0.f;
+          if constexpr (EPI == kResid) {  // epilogue input loaded with the partials
+            if (n < g.N && c0 + j < g.M) rv[j] = __bfloat162float(g.e.res[(long long)(c0 + j) * g.e.ldr + n]);
+          }
         }
-        stream_epilogue<EPI, 16>(g, tile, c0, v, sx);
+#pragma unroll 1
+        for (int q0 = 0; q0 < g.splits; q0 += QB) {
+          float pv[QB][CHR];
+#pragma unroll
+          for (int qq = 0; qq < QB; ++qq)
+#pragma unroll
+            for (int j = 0; j < CHR; ++j)
+              pv[qq][j] = q0 + qq < g.splits ? ld_dsmem(part + (c0 + j) * 128 + r, q0 + qq) : 0.f;
+#pragma unroll
+          for (int qq = 0; qq < QB; ++qq)
+#pragma unroll
+            for (int j = 0; j < CHR; ++j) v[j] += pv[qq][j];
+        }
+        if constexpr (EPI == kStore || EPI == kResid) {
+          if (n < g.N) {
+#pragma unroll
+            for (int j = 0; j < CHR; ++j)
+              if (c0 + j < g.M) g.e.out[(long long)(c0 + j) * g.e.ldo + n] = __float2bfloat16(v[j] + rv[j]);
+          }
+        } else {
+          stream_epilogue<EPI, CHR>(g, tile, c0, v, sx);
+        }
       }
     }
+    if (tr && threadIdx.x == 0) tr[6] = tc::globaltimer();
     cluster_sync();
   }
   tc::tc_fence_before();
   __syncthreads();
   if (warp == 2) tc::tmem_dealloc(tmem, C::TMEM_COLS);
+  if (tr && threadIdx.x == 0) tr[7] = tc::globaltimer();
 }
 
 // =====================================================================================
@@ -1043,6 +1079,29 @@ void stream_workspace(int64_t M, int64_t N, int64_t K, int sms, int64_t* ws_floa
   *counters = 0;
 }
 
+// AXR_DENSE_TRACE=1: the stream kernel records 8 %globaltimer stamps per CTA into one
+// device buffer (a measurement aid: entry, set-up done, first / last stage landed,
+// accumulator ready, partials parked, epilogue done, exit); dense_trace() reads it back.
+namespace {
+unsigned long long* g_trace = nullptr;
+int g_trace_ctas = 0;
+bool trace_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("AXR_DENSE_TRACE");
+    return e && e[0] == '1';
+  }();
+  return on;
+}
+}  // namespace
+
+int dense_trace(std::vector<unsigned long long>* out) {
+  out->clear();
+  if (!g_trace || g_trace_ctas == 0) return 0;
+  out->resize(8ull * g_trace_ctas);
+  if (cudaMemcpy(out->data(), g_trace, out->size() * 8, cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+  return g_trace_ctas;
+}
+
 std::string dense_gemm_launch(const DenseCall& c, cudaStream_t st) {
   if (c.M == 0 || c.N == 0) return "";
   if (c.K <= 0 || c.K % 8 != 0) return "K must be a positive multiple of 8";
@@ -1086,6 +1145,12 @@ std::string dense_gemm_launch(const DenseCall& c, cudaStream_t st) {
     CUtensorMap tw, tx;
     if (!make_map(&tw, c.w, c.N, c.K, c.ldw, 128) || !make_map(&tx, c.x, c.M, c.K, c.ldx, nt))
       return "cuTensorMapEncodeTiled failed";
+    if (trace_enabled()) {
+      const int ctas = ((c.N + 127) / 128) * g.splits;
+      if (!g_trace) cudaMalloc(&g_trace, 8ull * 8 * 4096);
+      g_trace_ctas = std::min(ctas, 4096);
+      g.trace = ctas <= 4096 ? g_trace : nullptr;
+    }
     switch (c.epi) {
       case kStore: e = launch_stream_nt<kStore>(nt, tw, tx, g, st); break;
       case kResid: e = launch_stream_nt<kResid>(nt, tw, tx, g, st); break;

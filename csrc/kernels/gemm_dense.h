@@ -6,6 +6,7 @@
 
 #include <cstdint>
 #include <string>
+#include <vector>
 
 namespace axr {
 namespace dense {
@@ -52,6 +53,8 @@ int stream_max_splits(int nt);
 int stream_splits(int64_t M, int64_t N, int64_t K, int sms);
 // {fp32 partial floats, counters} the stream kernel needs.
 void stream_workspace(int64_t M, int64_t N, int64_t K, int sms, int64_t* ws_floats, int64_t* counters);
+// Timeline of the last traced stream-kernel launch (AXR_DENSE_TRACE=1): 8 stamps per CTA.
+int dense_trace(std::vector<unsigned long long>* out);
 // Thread-block clusters (CTA pairs) the prefill-sized kernel keeps resident on device `dev`.
 int pair_grid_clusters(int dev);
 // Checks the call and launches; returns an empty string or the reason it refused.
