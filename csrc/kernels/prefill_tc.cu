@@ -73,6 +73,32 @@ __device__ __forceinline__ uint32_t swz_off(int r, int u) {
   return (u >> 3) * CHUNK + r * 128 + (((u & 7) ^ (r & 7)) << 4);
 }
 
+// Packed fp32 pairs (sm_100 f32x2 arithmetic: one instruction for two values) and the
+// three-input maximum: they halve the FMA-pipe instructions of the softmax.
+__device__ __forceinline__ unsigned long long f2(float a, float b) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_split(unsigned long long x, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(x));
+}
+__device__ __forceinline__ unsigned long long f2_fma(unsigned long long a, unsigned long long b, unsigned long long c) {
+  unsigned long long r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ unsigned long long f2_add(unsigned long long a, unsigned long long b) {
+  unsigned long long r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 __device__ __forceinline__ bool warp_ok(bool ok, volatile int* err) {
   return __all_sync(0xffffffffu, ok) && __shfl_sync(0xffffffffu, *err, 0) == 0;
 }
@@ -280,16 +306,18 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
         for (int i = 0; i < BN; ++i)
           if (n0 + i > qpos || n0 + i >= kv_len) v[i] = -INFINITY;
       }
-      // row maximum as 8 independent chains (a single 128-long fmax chain is latency-bound)
+      // row maximum as 8 independent chains of three-input maxima (a single 128-long
+      // chain is latency-bound)
       float mx8[8];
 #pragma unroll
-      for (int c = 0; c < 8; ++c) mx8[c] = v[c];
+      for (int c = 0; c < 8; ++c) mx8[c] = max3(v[c], v[8 + c], v[16 + c]);
 #pragma unroll
-      for (int i = 8; i < BN; i += 8)
+      for (int i = 24; i + 16 <= BN; i += 16)
 #pragma unroll
-        for (int c = 0; c < 8; ++c) mx8[c] = fmaxf(mx8[c], v[i + c]);
-      const float mt = csc * fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                                   fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+        for (int c = 0; c < 8; ++c) mx8[c] = max3(mx8[c], v[i + c], v[i + 8 + c]);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) mx8[c] = fmaxf(mx8[c], v[BN - 8 + c]);
+      const float mt = csc * max3(max3(mx8[0], mx8[1], mx8[2]), max3(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]));
       if (j == 0) {
         m_used = mt;
       } else {
@@ -317,15 +345,31 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
       // masked scores are -inf: 2^(c (-inf) - m) is 0 for any finite m, and while every
       // score so far was masked (m = -inf) subtracting 0 gives 0 as well
       const float msub = m_used == -INFINITY ? 0.f : m_used;
+      // exponent arguments c s - m and the row sum on packed pairs
+      const unsigned long long sc2 = f2(csc, csc), ms2 = f2(-msub, -msub);
+      unsigned long long l2[4] = {0ull, 0ull, 0ull, 0ull};  // +0.0f pairs
 #pragma unroll
       for (int u = 0; u < 16; ++u) {
         float e[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) e[i] = exp2f(fmaf(v[u * 8 + i], csc, -msub));
-        l += ((e[0] + e[1]) + (e[2] + e[3])) + ((e[4] + e[5]) + (e[6] + e[7]));
+        for (int q = 0; q < 4; ++q) {
+          float a, b;
+          f2_split(f2_fma(f2(v[u * 8 + 2 * q], v[u * 8 + 2 * q + 1]), sc2, ms2), a, b);
+          e[2 * q] = exp2f(a);
+          e[2 * q + 1] = exp2f(b);
+          l2[q] = f2_add(l2[q], f2(e[2 * q], e[2 * q + 1]));
+        }
         *reinterpret_cast<uint4*>(pbuf + swz_off(row, u)) =
             make_uint4(pack_bf16x2(e[0], e[1]), pack_bf16x2(e[2], e[3]), pack_bf16x2(e[4], e[5]),
                        pack_bf16x2(e[6], e[7]));
+      }
+      {
+        float a0, b0, a1, b1, a2, b2, a3, b3;
+        f2_split(l2[0], a0, b0);
+        f2_split(l2[1], a1, b1);
+        f2_split(l2[2], a2, b2);
+        f2_split(l2[3], a3, b3);
+        l += ((a0 + b0) + (a1 + b1)) + ((a2 + b2) + (a3 + b3));
       }
       tc::fence_proxy_async_smem();
       tc::tc_fence_before();
