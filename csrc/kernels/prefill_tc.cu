@@ -7,21 +7,27 @@
 //
 //   warp 8     TMA producer: K_j and V_j (128 tokens each) are gathered through the
 //              block table as 8 pages x 2 halves of [16 tokens x 64 dims] boxes into a
-//              ring of three 128-byte-swizzled [128 x 128] slots (K_0 V_0 K_1 V_1 ...).
+//              ring of five 128-byte-swizzled [128 x 128] slots (K_0 V_0 K_1 V_1 ...).
 //   warp 9     MMA issuer (one thread), per KV tile j:
 //                PV_A(j), S_A(j+1), PV_B(j), S_B(j+1)
-//              S_x = Q_x K^T goes to sub-tile x's TMEM S columns, O_x += P_x V (V read
-//              MN-major from shared memory) to its TMEM O columns.
+//              S_x = Q_x K^T goes to sub-tile x's TMEM S columns, O_x += P_x V (P_x read
+//              from TMEM, V MN-major from shared memory) to its TMEM O columns.
 //   warps 0-3 / 4-7   softmax of sub-tile A / B, one thread per query row (= TMEM
-//              lane): S from TMEM, causal mask, running max, exp2, row sum, P (bf16)
-//              into a swizzled shared tile. The running max only moves when a tile's
+//              lane): S from TMEM, causal mask, running max, exp2, row sum, P (bf16
+//              pairs) back into the first half of S's TMEM columns, where the PV MMA
+//              reads it (P never touches shared memory, which leaves room for a
+//              five-slot ring; with P in shared memory the ring had three slots and
+//              K_{j+1} could only load once PV(j-1) was done, so the tensor pipe waited
+//              on the load every tile). The running max only moves when a tile's
 //              max exceeds it by more than 2^8 (O is then rescaled in TMEM), so the
 //              exponentials stay below 256 and the rescale is rare.
 //   epilogue   O / l from TMEM straight to the output rows.
 //
 // Ordering comes from tcgen05.commit, which fires only when every earlier MMA of the
 // issuing thread has completed: when S_x(j+1) is ready, PV_x(j) is done, so the softmax
-// may overwrite P_x and rescale O_x without further waits. While one sub-tile's
+// may overwrite P_x and rescale O_x without further waits. S_x(j+1), which overwrites the
+// TMEM columns holding P_x(j), is issued after PV_x(j) by the same thread, and one
+// thread's MMAs execute in issue order. While one sub-tile's
 // softmax runs, the tensor core works on the other's MMAs. Every mbarrier wait is
 // bounded; on timeout the kernel records an error code, drains its own TMA loads and
 // MMAs, frees TMEM and returns.
@@ -42,8 +48,8 @@ namespace fa {
 constexpr int BM = 128, BN = 128, HD = 128;
 constexpr int CHUNK = 128 * 128;  // one [128 rows x 64 bf16] swizzled chunk (16 KB)
 constexpr int TILE = 2 * CHUNK;   // [128 x 128] bf16 tile (32 KB)
-constexpr int RING = 3;           // K/V slots
-constexpr int SMEM = 1024 + 2 * TILE /*Q_A,Q_B*/ + 2 * TILE /*P_A,P_B*/ + RING * TILE + 256;
+constexpr int RING = 5;           // K/V slots
+constexpr int SMEM = 1024 + 2 * TILE /*Q_A,Q_B*/ + RING * TILE + 256;
 constexpr int THREADS = 320;
 constexpr float RESCALE_T = 8.f;  // log2 units
 
@@ -108,8 +114,7 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
   extern __shared__ __align__(1024) char fa_raw[];
   char* base = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(fa_raw) + 1023) & ~uintptr_t(1023));
   char* sQ = base;             // [2][TILE]
-  char* sP = sQ + 2 * TILE;    // [2][TILE]
-  char* sR = sP + 2 * TILE;    // [RING][TILE]
+  char* sR = sQ + 2 * TILE;    // [RING][TILE]
   uint64_t* slot_full = reinterpret_cast<uint64_t*>(sR + RING * TILE);
   uint64_t* slot_free = slot_full + RING;
   uint64_t* s_full = slot_free + RING;  // [2] (A, B)
@@ -219,13 +224,12 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
         }
         tc::mma_commit(&s_full[x]);
       };
-      auto issue_pv = [&](int x, int j) {  // O_x += P_x V_j
-        const uint32_t p_addr = tc::smem_u32(sP + x * TILE);
+      auto issue_pv = [&](int x, int j) {  // O_x += P_x V_j, P_x (bf16) in TMEM over S_x's first 64 columns
         const uint32_t v_addr = tc::smem_u32(sR + ((2 * j + 1) % RING) * TILE);
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
-          tc::mma_f16_ss(tmem + 256 + x * 128, tc::smem_desc_k_sw128(p_addr + (kk >> 2) * CHUNK + (kk & 3) * 32),
-                         tc::smem_desc_mn_sw128(v_addr + kk * 2048, CHUNK), idesc_pv, (j | kk) != 0);
+          tc::mma_f16_ts(tmem + 256 + x * 128, tmem + x * 128 + kk * 8, tc::smem_desc_mn_sw128(v_addr + kk * 2048, CHUNK),
+                         idesc_pv, (j | kk) != 0);
         }
       };
       bool ok = tc::mbar_wait(q_full, 0, p.err, 12) && tc::mbar_wait(&slot_full[0], 0, p.err, 13);
@@ -341,27 +345,32 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
           tc::tmem_st_wait();
         }
       }
-      char* pbuf = sP + x * TILE;
       // masked scores are -inf: 2^(c (-inf) - m) is 0 for any finite m, and while every
       // score so far was masked (m = -inf) subtracting 0 gives 0 as well
       const float msub = m_used == -INFINITY ? 0.f : m_used;
       // exponent arguments c s - m and the row sum on packed pairs
       const unsigned long long sc2 = f2(csc, csc), ms2 = f2(-msub, -msub);
       unsigned long long l2[4] = {0ull, 0ull, 0ull, 0ull};  // +0.0f pairs
+      // P as bf16 pairs into S_x's first 64 TMEM columns (S_x is already in registers), 16
+      // columns per store; the PV MMA reads it from there as its A operand
 #pragma unroll
-      for (int u = 0; u < 16; ++u) {
-        float e[8];
+      for (int u4 = 0; u4 < 4; ++u4) {
+        uint32_t pk[16];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          float a, b;
-          f2_split(f2_fma(f2(v[u * 8 + 2 * q], v[u * 8 + 2 * q + 1]), sc2, ms2), a, b);
-          e[2 * q] = exp2f(a);
-          e[2 * q + 1] = exp2f(b);
-          l2[q] = f2_add(l2[q], f2(e[2 * q], e[2 * q + 1]));
+        for (int uu = 0; uu < 4; ++uu) {
+          const int u = u4 * 4 + uu;
+          float e[8];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            float a, b;
+            f2_split(f2_fma(f2(v[u * 8 + 2 * q], v[u * 8 + 2 * q + 1]), sc2, ms2), a, b);
+            e[2 * q] = exp2f(a);
+            e[2 * q + 1] = exp2f(b);
+            l2[q] = f2_add(l2[q], f2(e[2 * q], e[2 * q + 1]));
+            pk[uu * 4 + q] = pack_bf16x2(e[2 * q], e[2 * q + 1]);
+          }
         }
-        *reinterpret_cast<uint4*>(pbuf + swz_off(row, u)) =
-            make_uint4(pack_bf16x2(e[0], e[1]), pack_bf16x2(e[2], e[3]), pack_bf16x2(e[4], e[5]),
-                       pack_bf16x2(e[6], e[7]));
+        tc::tmem_st16(tS + u4 * 16, pk);
       }
       {
         float a0, b0, a1, b1, a2, b2, a3, b3;
@@ -371,7 +380,7 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
         f2_split(l2[3], a3, b3);
         l += ((a0 + b0) + (a1 + b1)) + ((a2 + b2) + (a3 + b3));
       }
-      tc::fence_proxy_async_smem();
+      tc::tmem_st_wait();
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&p_full[x]);
