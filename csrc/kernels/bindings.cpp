@@ -56,6 +56,7 @@ void moe_combine(torch::Tensor comb, torch::Tensor out, torch::Tensor comb_flag,
 void peer_allreduce(torch::Tensor x, torch::Tensor out, int64_t rank, int64_t world, torch::Tensor peers,
                     torch::Tensor buf, torch::Tensor flag, torch::Tensor epoch, torch::Tensor bar, int64_t cap,
                     torch::Tensor err);
+std::vector<int64_t> prefill_trace_read();
 namespace dense {
 void dense_gemm(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t epi, c10::optional<torch::Tensor> res,
                 c10::optional<torch::Tensor> pos, c10::optional<torch::Tensor> slots,
@@ -85,6 +86,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_attention", &axr::decode_attention);
   m.def("prefill_attention", &axr::prefill_attention);
   m.def("prefill_attention_tc", &axr::prefill_attention_tc);
+  m.def("prefill_trace_read", &axr::prefill_trace_read);
   m.def("rmsnorm", &axr::rmsnorm);
   m.def("rope_kv_write", &axr::rope_kv_write);
   m.def("silu_mul", &axr::silu_mul);

@@ -35,6 +35,7 @@
 // Reference counterpart: the prefill attention the reference delegates to llama.cpp /
 // vLLM library kernels; the reference has no prefill attention kernel of its own.
 #include <cfloat>
+#include <cstdlib>
 #include <string>
 
 #include "attn_combine.cuh"
@@ -72,6 +73,7 @@ struct Params {
   int noncausal;
   const int* q_index;  // nullable: token i reads q row i
   int partial_only;
+  long long* trace;    // AXR_PREFILL_TRACE=1: clock64 stamps of the CTA (0, 0, 0), 8 per KV tile
 };
 
 // byte offset of 16-byte unit u (0..15) of row r in a [128 x 128] bf16 K-major SW128 tile
@@ -232,6 +234,7 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
                          idesc_pv, (j | kk) != 0);
         }
       };
+      long long* mtr = (p.trace != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) ? p.trace : nullptr;
       bool ok = tc::mbar_wait(q_full, 0, p.err, 12) && tc::mbar_wait(&slot_full[0], 0, p.err, 13);
       if (ok) {
         tc::tc_fence_after();
@@ -241,12 +244,15 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
       for (int j = 0; ok && j < n_tiles; ++j) {
         const int iv = 2 * j + 1, ik = 2 * j + 2;  // ring items V_j, K_{j+1}
         if (!tc::mbar_wait(&slot_full[iv % RING], (iv / RING) & 1, p.err, 14)) break;
+        if (mtr && j < 128) mtr[j * 8 + 3] = clock64();  // V_j landed
         for (int x = 0; x < nsub; ++x) {
           if (!tc::mbar_wait(&p_full[x], j & 1, p.err, 16)) { ok = false; break; }
+          if (mtr && j < 128) mtr[j * 8 + 4 * x + 2] = clock64();
           tc::tc_fence_after();
           issue_pv(x, j);
           if (j + 1 < n_tiles) {
             if (x == 0 && !tc::mbar_wait(&slot_full[ik % RING], (ik / RING) & 1, p.err, 15)) { ok = false; break; }
+            if (mtr && x == 0 && j < 128) mtr[j * 8 + 7] = clock64();  // K_{j+1} landed
             tc::tc_fence_after();
             issue_s(x, j + 1);
           }
@@ -288,9 +294,12 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
     const float csc = p.scale_log2;
     float m_used = -INFINITY, l = 0.f;
     bool ok = active;
+    long long* tr = (p.trace != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && row == 0)
+                        ? p.trace : nullptr;
     for (int j = 0; ok && j < n_tiles; ++j) {
       ok = warp_ok(tc::mbar_wait(&s_full[x], j & 1, p.err, 18), p.err);
       if (!ok) break;
+      if (tr && j < 128) tr[j * 8 + 4 * x] = clock64();
       tc::tc_fence_after();
       float v[BN];
       {
@@ -384,6 +393,7 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&p_full[x]);
+      if (tr && j < 128) tr[j * 8 + 4 * x + 1] = clock64();
     }
     // ---------------- epilogue: O / l -> out
     if (ok) ok = warp_ok(tc::mbar_wait(o_done, 0, p.err, 21), p.err);
@@ -444,6 +454,19 @@ bool make_page_map(CUtensorMap* map, const void* ptr, int64_t rows) {
                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+namespace {
+long long* g_prefill_trace = nullptr;
+}
+
+// Measurement aid (AXR_PREFILL_TRACE=1): clock64 stamps of the last launch's CTA (0, 0, 0),
+// 8 per KV tile j: [softmax A: S ready, P stored; MMA: P_A seen; V_j landed; softmax B: S
+// ready, P stored; MMA: P_B seen; K_{j+1} landed].
+int prefill_trace(long long* host, int n) {
+  if (!g_prefill_trace) return 0;
+  n = n < 8 * 128 ? n : 8 * 128;
+  return cudaMemcpy(host, g_prefill_trace, n * sizeof(long long), cudaMemcpyDeviceToHost) == cudaSuccess ? n : -1;
+}
+
 std::string prefill_launch(const PrefillCall& c, cudaStream_t st) {
   if (c.B == 0 || c.max_q == 0) return "";
   if (c.Hq % c.Hkv != 0) return "Hq must be a multiple of Hkv";
@@ -469,6 +492,17 @@ std::string prefill_launch(const PrefillCall& c, cudaStream_t st) {
   p.noncausal = c.noncausal != 0;
   p.partial_only = c.partial_only != 0;
   p.q_index = c.q_index;
+  p.trace = nullptr;
+  {
+    static const bool on = [] {
+      const char* e = getenv("AXR_PREFILL_TRACE");
+      return e && e[0] == '1';
+    }();
+    if (on) {
+      if (!g_prefill_trace) cudaMalloc(&g_prefill_trace, 8 * 128 * sizeof(long long));
+      p.trace = g_prefill_trace;
+    }
+  }
   if ((S > 1 || p.partial_only) && (p.part_o == nullptr || p.part_lse == nullptr)) return "split-KV scratch missing";
   if ((int64_t)c.B * S >= 65536) return "too many sequences x splits";
   static bool attr = false;

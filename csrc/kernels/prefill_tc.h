@@ -37,6 +37,8 @@ struct PrefillCall {
 // Launches the attention (and the split-KV combine when num_splits > 1 and the partials
 // are not kept); returns an empty string or the reason it refused.
 std::string prefill_launch(const PrefillCall& c, cudaStream_t st);
+// Measurement aid: per-KV-tile clock64 stamps of the last launch traced with AXR_PREFILL_TRACE=1.
+int prefill_trace(long long* host, int n);
 
 }  // namespace fa
 }  // namespace axr
