@@ -73,7 +73,7 @@ struct Params {
   int noncausal;
   const int* q_index;  // nullable: token i reads q row i
   int partial_only;
-  long long* trace;    // AXR_PREFILL_TRACE=1: clock64 stamps of the CTA (0, 0, 0), 8 per KV tile
+  long long* trace;    // AXR_PREFILL_TRACE=1: clock64 stamps of the CTA (0, 0, 0), 12 per KV tile
 };
 
 // byte offset of 16-byte unit u (0..15) of row r in a [128 x 128] bf16 K-major SW128 tile
@@ -191,16 +191,35 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
     if (lane == 0) {  // ---------------- TMA producer: items K_0, V_0, K_1, V_1, ...
       int issued = 0;
       bool ok = true;
+      long long* ptr = (p.trace != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) ? p.trace : nullptr;
+      // The 8 block-table entries of a KV tile are read one tile ahead, as independent
+      // loads: read next to the TMA issues (whose asm orders every memory access) they
+      // were 8 dependent round trips per item and the ring ran dry (measured: a K tile
+      // landed ~2600 cycles after issue, the MMA thread waited ~1200 of them every tile).
+      int cur[8], nxt[8];
+      auto page_ids = [&](int j, int (&o)[8]) {
+#pragma unroll
+        for (int pg = 0; pg < 8; ++pg) {
+          const int tok = (t_begin + j) * BN + pg * 16;
+          o[pg] = (j < n_tiles && tok < kv_len) ? bt[tok >> 4] : 0;
+        }
+      };
+      page_ids(0, nxt);
       for (int i = 0; i < 2 * n_tiles; ++i) {
         const int s = i % RING, j = i >> 1;
+        if ((i & 1) == 0) {  // K_j: its pages (shared with V_j) were read a tile ago
+#pragma unroll
+          for (int pg = 0; pg < 8; ++pg) cur[pg] = nxt[pg];
+          page_ids(j + 1, nxt);
+        }
+        if (ptr && j < 128) ptr[j * 12 + 10 + (i & 1)] = clock64();
         if (i >= RING && !tc::mbar_wait(&slot_free[s], ((i / RING) + 1) & 1, p.err, 11)) { ok = false; break; }
+        if (ptr && j < 128) ptr[j * 12 + 8 + (i & 1)] = clock64();
         const CUtensorMap* map = (i & 1) ? &tmV : &tmK;
         tc::mbar_arrive_expect_tx(&slot_full[s], TILE);
 #pragma unroll
         for (int pg = 0; pg < 8; ++pg) {
-          const int tok = (t_begin + j) * BN + pg * 16;
-          const int blk = tok < kv_len ? bt[tok >> 4] : 0;
-          const int y = (blk * p.Hkv + kvh) * 16;
+          const int y = (cur[pg] * p.Hkv + kvh) * 16;
           tc::tma_load_2d(sR + s * TILE + pg * 2048, map, 0, y, &slot_full[s]);
           tc::tma_load_2d(sR + s * TILE + CHUNK + pg * 2048, map, 64, y, &slot_full[s]);
         }
@@ -244,15 +263,15 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
       for (int j = 0; ok && j < n_tiles; ++j) {
         const int iv = 2 * j + 1, ik = 2 * j + 2;  // ring items V_j, K_{j+1}
         if (!tc::mbar_wait(&slot_full[iv % RING], (iv / RING) & 1, p.err, 14)) break;
-        if (mtr && j < 128) mtr[j * 8 + 3] = clock64();  // V_j landed
+        if (mtr && j < 128) mtr[j * 12 + 3] = clock64();  // V_j landed
         for (int x = 0; x < nsub; ++x) {
           if (!tc::mbar_wait(&p_full[x], j & 1, p.err, 16)) { ok = false; break; }
-          if (mtr && j < 128) mtr[j * 8 + 4 * x + 2] = clock64();
+          if (mtr && j < 128) mtr[j * 12 + 4 * x + 2] = clock64();
           tc::tc_fence_after();
           issue_pv(x, j);
           if (j + 1 < n_tiles) {
             if (x == 0 && !tc::mbar_wait(&slot_full[ik % RING], (ik / RING) & 1, p.err, 15)) { ok = false; break; }
-            if (mtr && x == 0 && j < 128) mtr[j * 8 + 7] = clock64();  // K_{j+1} landed
+            if (mtr && x == 0 && j < 128) mtr[j * 12 + 7] = clock64();  // K_{j+1} landed
             tc::tc_fence_after();
             issue_s(x, j + 1);
           }
@@ -299,7 +318,7 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
     for (int j = 0; ok && j < n_tiles; ++j) {
       ok = warp_ok(tc::mbar_wait(&s_full[x], j & 1, p.err, 18), p.err);
       if (!ok) break;
-      if (tr && j < 128) tr[j * 8 + 4 * x] = clock64();
+      if (tr && j < 128) tr[j * 12 + 4 * x] = clock64();
       tc::tc_fence_after();
       float v[BN];
       {
@@ -393,7 +412,7 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_tc_kernel(const __grid_con
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&p_full[x]);
-      if (tr && j < 128) tr[j * 8 + 4 * x + 1] = clock64();
+      if (tr && j < 128) tr[j * 12 + 4 * x + 1] = clock64();
     }
     // ---------------- epilogue: O / l -> out
     if (ok) ok = warp_ok(tc::mbar_wait(o_done, 0, p.err, 21), p.err);
@@ -459,11 +478,12 @@ long long* g_prefill_trace = nullptr;
 }
 
 // Measurement aid (AXR_PREFILL_TRACE=1): clock64 stamps of the last launch's CTA (0, 0, 0),
-// 8 per KV tile j: [softmax A: S ready, P stored; MMA: P_A seen; V_j landed; softmax B: S
-// ready, P stored; MMA: P_B seen; K_{j+1} landed].
+// 12 per KV tile j: [softmax A: S ready, P stored; MMA: P_A seen; V_j landed; softmax B: S
+// ready, P stored; MMA: P_B seen; K_{j+1} landed; producer: K_j issued, V_j issued, K_j slot
+// wait started, V_j slot wait started].
 int prefill_trace(long long* host, int n) {
   if (!g_prefill_trace) return 0;
-  n = n < 8 * 128 ? n : 8 * 128;
+  n = n < 12 * 128 ? n : 12 * 128;
   return cudaMemcpy(host, g_prefill_trace, n * sizeof(long long), cudaMemcpyDeviceToHost) == cudaSuccess ? n : -1;
 }
 
@@ -499,7 +519,7 @@ std::string prefill_launch(const PrefillCall& c, cudaStream_t st) {
       return e && e[0] == '1';
     }();
     if (on) {
-      if (!g_prefill_trace) cudaMalloc(&g_prefill_trace, 8 * 128 * sizeof(long long));
+      if (!g_prefill_trace) cudaMalloc(&g_prefill_trace, 12 * 128 * sizeof(long long));
       p.trace = g_prefill_trace;
     }
   }

@@ -68,7 +68,7 @@ void prefill_attention_tc(torch::Tensor q, int64_t k, int64_t v, int64_t blk_str
 }
 
 std::vector<int64_t> prefill_trace_read() {
-  std::vector<long long> v(8 * 128, 0);
+  std::vector<long long> v(12 * 128, 0);
   const int n = fa::prefill_trace(v.data(), static_cast<int>(v.size()));
   if (n <= 0) return {};
   return std::vector<int64_t>(v.begin(), v.begin() + n);
