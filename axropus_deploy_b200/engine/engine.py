@@ -111,6 +111,9 @@ class EngineConfig:
     cascade_min_pages: int = 0
     # greedy CUDA-graph decode launches step t + 1 before it reads step t's tokens
     pipeline_decode: bool = True
+    # a step that admits prompts while others decode runs both in one forward (the decode
+    # rows ride along the prefill's projections instead of streaming the weights again)
+    mixed_batch: bool = True
 
 
 _NVTX = os.environ.get("AXR_NVTX", "0") == "1"
@@ -188,7 +191,7 @@ class LLMEngine:
             self.spec = SpecDecoder(self, cfg.spec_max_depth, drafter)
         self.stat = {"steps": 0, "prefill_tokens": 0, "decode_tokens": 0, "restored_tokens": 0,
                      "local_cached_tokens": 0, "cold_prefill_tokens": 0, "cascade_steps": 0,
-                     "cascade_grouped_seqs": 0, "pipelined_decode_steps": 0, "sync_wait_ms": 0.0}
+                     "cascade_grouped_seqs": 0, "pipelined_decode_steps": 0, "sync_wait_ms": 0.0, "mixed_steps": 0}
         # decode pipelining: a greedy graph decode launched but whose tokens are not read yet
         self._pipe: Optional[dict] = None
         from ..ops.attention import cascade_supported
@@ -309,6 +312,9 @@ class LLMEngine:
         if self.cfg.lockstep and hasattr(self.model, "ep_any"):
             # a forward runs on every GPU when it runs on any (the MoE layers need all of them)
             any_prefill, any_decode = self.model.ep_any([any_prefill, any_decode])
+        if admitted and decoding and self._mixable(admitted, decoding):
+            with _nvtx("mixed"):
+                return done + self._mixed(admitted, decoding)
         if admitted:
             with _nvtx("prefill"):
                 done += self._prefill(admitted)
@@ -584,7 +590,9 @@ class LLMEngine:
             off += a.size
         return out
 
-    def _prefill(self, reqs: List[Request]) -> List[Request]:
+    def _prefill_inputs(self, reqs: List[Request]):
+        """Host arrays of a prefill of ``reqs``: tokens, positions, slots, cu_q, lengths and
+        each request's first prefilled position."""
         toks, pos, slots, cu, lens = [], [], [], [0], []
         prefilled_from = {}
         for r in reqs:
@@ -601,6 +609,10 @@ class LLMEngine:
             self.stat["prefill_tokens"] += n
             if r.amf_tier == "cold":
                 self.stat["cold_prefill_tokens"] += n
+        return toks, pos, slots, cu, lens, prefilled_from
+
+    def _prefill(self, reqs: List[Request]) -> List[Request]:
+        toks, pos, slots, cu, lens, prefilled_from = self._prefill_inputs(reqs)
         self._set_rows(reqs)
         t_pf = time.perf_counter()
         try:
@@ -620,8 +632,12 @@ class LLMEngine:
             self._settle_restores(reqs, ok=False)
             raise
         self._settle_restores(reqs)
-        pf_ms = (time.perf_counter() - t_pf) * 1e3
-        n_new = len(toks)
+        return self._finish_prefill(reqs, new, prefilled_from, len(toks), (time.perf_counter() - t_pf) * 1e3)
+
+    def _finish_prefill(self, reqs: List[Request], new: List[int], prefilled_from: dict, n_new: int,
+                        pf_ms: float) -> List[Request]:
+        """After a prefill's tokens are sampled: trace lines, prefix-cache registration, AMF
+        capture of what the step computed, first output tokens."""
         cold = [r for r in reqs if r.amf_tier == "cold"]
         if cold and len(cold) == len(reqs):
             self.trace.note_prefill(n_new, pf_ms)
@@ -643,6 +659,49 @@ class LLMEngine:
                                                                               dtype=torch.int32))
             r.num_computed = len(r.prompt)
             self._append(r, t, done)
+        return done
+
+    # ------------------------------------------------------------------ mixed steps
+    def _mixable(self, admitted: List[Request], decoding: List[Request]) -> bool:
+        """One forward for the step's prefills and decodes: the single-GPU dense model, no
+        lockstep (expert parallelism), no speculative decoding."""
+        return (self.cfg.mixed_batch and type(self.model) is LlamaModel and not self.cfg.lockstep and
+                self.spec is None and self.model.ep is None)
+
+    def _mixed(self, preqs: List[Request], dreqs: List[Request]) -> List[Request]:
+        """Prefill of ``preqs`` and one decode step of ``dreqs`` in one forward: rows
+        [0, Tp) are the prompts' new tokens, the rows after them one token per decoding
+        sequence; every projection runs once over all rows, attention in two kernels."""
+        toks, pos, slots, cu, lens, prefilled_from = self._prefill_inputs(preqs)
+        dtoks, dpos, dslots, dlens = self.decode_meta(dreqs)
+        self.stat["decode_tokens"] += len(dreqs)
+        self.stat["mixed_steps"] += 1
+        tp = len(toks)
+        self._set_rows(preqs)
+        idx = [c - 1 for c in cu[1:]] + list(range(tp, tp + len(dreqs)))
+        t_pf = time.perf_counter()
+        try:
+            d_toks, d_pos, d_slots, d_lens, d_cu, d_idx, d_rows, d_dlens, d_drows = self._stage_int32(
+                toks + dtoks, pos + dpos, slots + dslots, lens, cu, idx, [r.row for r in preqs], dlens,
+                [r.row for r in dreqs])
+            dmeta = AttnMeta(mode="decode", positions=d_pos[tp:], slots=d_slots[tp:],
+                             block_table=self.block_table.index_select(0, d_drows.long()), seq_lens=d_dlens,
+                             max_seq_len=max(dlens))
+            meta = AttnMeta(mode="mixed", positions=d_pos, slots=d_slots,
+                            block_table=self.block_table.index_select(0, d_rows.long()), seq_lens=d_lens, cu_q=d_cu,
+                            max_q=max(cu[i + 1] - cu[i] for i in range(len(preqs))), max_seq_len=max(lens),
+                            logits_idx=d_idx, decode=dmeta)
+            logits = self.model.forward(d_toks, meta, self.cache)
+            new = self._sample(logits, preqs + dreqs)
+        except BaseException:
+            self._settle_restores(preqs, ok=False)
+            raise
+        self._settle_restores(preqs)
+        done = self._finish_prefill(preqs, new[:len(preqs)], prefilled_from, tp, (time.perf_counter() - t_pf) * 1e3)
+        for r, t in zip(dreqs, new[len(preqs):]):
+            self._append(r, t, done)
+        if self.device.type == "cuda":
+            self._check_kernel_errors()
         return done
 
     def decode_meta(self, reqs: List[Request]) -> tuple:

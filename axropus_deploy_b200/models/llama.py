@@ -53,6 +53,10 @@ class AttnMeta:
     logits_idx: Optional[torch.Tensor] = None  # [B] rows of the hidden state to sample
     num_splits: Optional[int] = None
     cascade: Optional[object] = None  # ops.attention.CascadeMeta: shared-prefix decode
+    # mode "mixed": rows [0, cu_q[-1]) are prefill tokens described by the fields above,
+    # the rows after them one decode token per sequence described by ``decode`` (its
+    # block_table / seq_lens / max_seq_len); positions and slots cover every row
+    decode: Optional["AttnMeta"] = None
 
 
 class LlamaModel:
@@ -213,6 +217,14 @@ class LlamaModel:
                 a = ops.decode_attention(q, cache, li, meta.block_table, meta.seq_lens, self.scale,
                                          max_seq_len=meta.max_seq_len, num_splits=meta.num_splits,
                                          cascade=meta.cascade)
+            elif meta.mode == "mixed":
+                tp = T - meta.decode.seq_lens.shape[0]
+                a = torch.empty_like(q)
+                ops.prefill_attention(q[:tp], cache, li, meta.block_table, meta.cu_q, meta.seq_lens, meta.max_q,
+                                      self.scale, out=a[:tp], max_seq_len=meta.max_seq_len)
+                d = meta.decode
+                ops.decode_attention(q[tp:], cache, li, d.block_table, d.seq_lens, self.scale, out=a[tp:],
+                                     max_seq_len=d.max_seq_len, num_splits=d.num_splits)
             else:
                 a = ops.prefill_attention(q, cache, li, meta.block_table, meta.cu_q, meta.seq_lens, meta.max_q,
                                           self.scale, max_seq_len=meta.max_seq_len)

@@ -442,7 +442,7 @@ def run_ours(args) -> None:
                         "nvlink_restore_share": round(route["routing_misses"] / max(1, route["pooled"]), 4)},
             "cascade_decode": {k: eng.stat[k] - st0.get(k, 0) for k in ("cascade_steps", "cascade_grouped_seqs")},
             "decode_pipeline": {k: round(eng.stat[k] - st0.get(k, 0), 1)
-                                for k in ("pipelined_decode_steps", "sync_wait_ms", "decode_steps")
+                                for k in ("pipelined_decode_steps", "sync_wait_ms", "decode_steps", "mixed_steps")
                                 if k in eng.stat},
             "wave_mix": gathered[0]["waves"], "amf_hits_rank0": gathered[0]["hits"],
             "ms_per_step_by_rank": [round(g["ms"] / args.steps, 1) for g in gathered],

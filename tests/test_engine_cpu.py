@@ -165,3 +165,25 @@ def test_prefill_graph_runner_padding_matches_eager(model):
     assert eng._prefill_graphs.stat["eager"] >= 1
     # the second prompt reuses the first one's cached prefix: its prefill is the 100-token suffix
     assert eng.stat["local_cached_tokens"] == 256
+
+
+def test_mixed_steps_match_separate_forwards(model):
+    """Prompts admitted while others decode run in one forward with the decode rows
+    (mixed step); the generated tokens equal those of separate prefill and decode forwards."""
+    g = torch.Generator().manual_seed(5)
+    prompts = [torch.randint(0, model.cfg.vocab, (n,), generator=g).tolist() for n in (40, 70, 33, 90, 51)]
+    sp = SamplingParams(max_tokens=6)
+
+    def run(mixed: bool):
+        # a small prefill budget admits one prompt per step, so later prompts join running decodes
+        eng = LLMEngine(model, EngineConfig(num_blocks=128, max_model_len=512, max_prefill_tokens=64,
+                                            mixed_batch=mixed))
+        reqs = [eng.add_request(p, sp) for p in prompts]
+        while eng.has_unfinished():
+            eng.step()
+        return [r.output for r in reqs], eng.stat["mixed_steps"]
+
+    ref, n_ref = run(False)
+    out, n_mixed = run(True)
+    assert n_ref == 0 and n_mixed > 0
+    assert out == ref
