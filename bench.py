@@ -67,6 +67,9 @@ def parse_args(argv=None):
     p.add_argument("--graphs", type=int, default=1)
     p.add_argument("--prefill-graphs", type=int, default=1, help="CUDA-graph one-sequence prefills (with --graphs)")
     p.add_argument("--pipeline", type=int, default=1, help="launch decode step t+1 before reading step t's tokens")
+    p.add_argument("--mixed", type=int, default=1, help="prefill admitted prompts and decode running ones in one forward")
+    p.add_argument("--prefill-chunk", type=int, default=0,
+                   help="new prompt tokens per step while others decode (0: whole prompts)")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--layers", type=int, default=None, help="debug only: fewer layers (invalidates the number)")
     return p.parse_args(argv)
@@ -243,7 +246,8 @@ def run_ours(args) -> None:
     ecfg = EngineConfig(num_blocks=num_blocks, kv_fmt=args.kv_fmt, max_batch=args.batch,
                         max_prefill_tokens=2 * (args.prefix_len + args.suffix_len),
                         max_model_len=tok_per_req + PAGE, cuda_graphs=bool(args.graphs),
-                        prefill_graphs=bool(args.prefill_graphs), pipeline_decode=bool(args.pipeline))
+                        prefill_graphs=bool(args.prefill_graphs), pipeline_decode=bool(args.pipeline),
+                        mixed_batch=bool(args.mixed), prefill_chunk=args.prefill_chunk)
     eng = LLMEngine(model, ecfg, None)
     # G1 pool: at least 1.25x the prefix set over the node, grown into the HBM left after
     # weights and the live cache (keeping 12 GB of headroom for activations and graphs)
@@ -442,7 +446,8 @@ def run_ours(args) -> None:
                         "nvlink_restore_share": round(route["routing_misses"] / max(1, route["pooled"]), 4)},
             "cascade_decode": {k: eng.stat[k] - st0.get(k, 0) for k in ("cascade_steps", "cascade_grouped_seqs")},
             "decode_pipeline": {k: round(eng.stat[k] - st0.get(k, 0), 1)
-                                for k in ("pipelined_decode_steps", "sync_wait_ms", "decode_steps", "mixed_steps")
+                                for k in ("pipelined_decode_steps", "sync_wait_ms", "decode_steps", "mixed_steps",
+                                          "chunked_prefills")
                                 if k in eng.stat},
             "wave_mix": gathered[0]["waves"], "amf_hits_rank0": gathered[0]["hits"],
             "ms_per_step_by_rank": [round(g["ms"] / args.steps, 1) for g in gathered],

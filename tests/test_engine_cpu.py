@@ -187,3 +187,33 @@ def test_mixed_steps_match_separate_forwards(model):
     out, n_mixed = run(True)
     assert n_ref == 0 and n_mixed > 0
     assert out == ref
+
+
+def test_chunked_prefill_matches_whole_prompts(model):
+    """While others decode, long prompts are prefilled in chunks over several mixed steps;
+    the generated tokens equal those of whole-prompt prefills, and a prompt restored
+    from the AMF pool after a chunked cold run gives the cold run's tokens."""
+    g = torch.Generator().manual_seed(9)
+    prompts = [torch.randint(0, model.cfg.vocab, (n,), generator=g).tolist() for n in (30, 200, 170, 260)]
+    sp = SamplingParams(max_tokens=5)
+
+    def run(chunk: int, amf=None):
+        eng = LLMEngine(model, EngineConfig(num_blocks=160, max_model_len=512, max_prefill_tokens=64,
+                                            prefill_chunk=chunk), amf)
+        reqs = [eng.add_request(p, sp, amf_prefix_len=len(p) // 16 * 16) for p in prompts]
+        while eng.has_unfinished():
+            eng.step()
+        return [r.output for r in reqs], eng
+
+    ref, e0 = run(0)
+    pool = G1Pool(model.num_layers, model.cfg.num_kv_heads, model.cfg.head_dim, "raw", slots_per_shard=128,
+                  device="cpu")
+    out, e1 = run(48, AmfManager(raw_pool=pool, min_tokens=32))
+    assert e0.stat["chunked_prefills"] == 0 and e1.stat["chunked_prefills"] > 0
+    assert out == ref
+    # the chunked cold prefills were captured whole: a fresh engine restores them
+    eng = LLMEngine(model, EngineConfig(num_blocks=160, max_model_len=512), AmfManager(raw_pool=pool, min_tokens=32))
+    r = eng.add_request(prompts[3], sp, amf_prefix_len=len(prompts[3]) // 16 * 16)
+    while eng.has_unfinished():
+        eng.step()
+    assert r.amf_tier.startswith("g1") and r.output == ref[3]
