@@ -23,13 +23,17 @@ here for the GPUs of one node.
 """
 from __future__ import annotations
 
-from typing import List, Sequence
+from typing import List, Optional, Sequence
 
 
-def route_wave(owners: Sequence[int], cold: Sequence[bool], world: int, per_rank: int) -> List[int]:
+def route_wave(owners: Sequence[int], cold: Sequence[bool], world: int, per_rank: int,
+               cold_carry: Optional[List[int]] = None) -> List[int]:
     """owners[i]: shard owner of request i's prefix; cold[i]: no pooled prefix expected.
     Returns the GPU of each request; every GPU gets at most ``per_rank`` (callers pass
-    len(owners) / world for an even wave)."""
+    len(owners) / world for an even wave). ``cold_carry`` (one count per GPU, updated in
+    place) carries the cold prefills of earlier waves: when a wave's cold requests do not
+    divide evenly, the extra ones go to the GPUs with the fewest so far, so over a run of
+    waves no GPU collects every remainder (the slowest GPU sets a data-parallel step)."""
     n = len(owners)
     if world <= 1:
         return [0] * n
@@ -37,6 +41,7 @@ def route_wave(owners: Sequence[int], cold: Sequence[bool], world: int, per_rank
         raise ValueError("route_wave: per_rank * world must cover the wave")
     load = [0] * world
     cold_load = [0] * world
+    carry = cold_carry if cold_carry is not None else [0] * world
     out = [-1] * n
 
     def least(keys) -> int:
@@ -46,13 +51,16 @@ def route_wave(owners: Sequence[int], cold: Sequence[bool], world: int, per_rank
         if not cold[i]:
             continue
         o = owners[i] % world
-        if cold_load[o] == min(cold_load) and load[o] < per_rank:
+        best = min((cold_load[q], carry[q]) for q in range(world) if load[q] < per_rank)
+        if (cold_load[o], carry[o]) == best and load[o] < per_rank:
             r = o
         else:
-            r = least(lambda q: (load[q] >= per_rank, cold_load[q], load[q]))
+            r = least(lambda q: (load[q] >= per_rank, cold_load[q], carry[q], load[q]))
         out[i] = r
         load[r] += 1
         cold_load[r] += 1
+    for q in range(world):
+        carry[q] += cold_load[q]
     for i in range(n):
         if cold[i]:
             continue

@@ -162,6 +162,7 @@ class Workload:
         self.probe_pick = np.random.default_rng(args.seed * 1000 + 31 + rank)
         self.probe_tok = np.random.default_rng(args.seed * 1000 + 37 + rank)
         self.route_stats = {"pooled": 0, "routing_misses": 0}
+        self.cold_carry = [0] * world  # cold prefills routed to each GPU so far (balanced over waves)
 
     def _fresh_next(self) -> bool:
         q = 1.0 - self.args.reuse
@@ -197,17 +198,18 @@ class Workload:
                 owners.append(self.prefix_owner[i])
                 cold.append(False)
             prompts.append(prefix + self.tok_rng.integers(0, self.vocab, a.suffix_len, dtype=np.int64).tolist())
-        assigned = route_wave(owners, cold, self.world, per_rank)
+        assigned = route_wave(owners, cold, self.world, per_rank, self.cold_carry)
         st = routing_stats(owners, cold, assigned)
         self.route_stats["pooled"] += st["pooled"]
         self.route_stats["routing_misses"] += st["routing_misses"]
         return [p for p, r in zip(prompts, assigned) if r == self.rank]
 
     def choice_state(self):
-        return self.k, self.pick_rng.bit_generator.state
+        return self.k, self.pick_rng.bit_generator.state, list(self.cold_carry)
 
     def set_choice_state(self, state) -> None:
-        self.k, self.pick_rng.bit_generator.state = state
+        self.k, self.pick_rng.bit_generator.state, carry = state
+        self.cold_carry = list(carry)
 
 
 def pct(xs, q):

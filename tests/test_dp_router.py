@@ -31,3 +31,20 @@ def test_single_gpu_and_capacity_check():
         pass
     else:
         raise AssertionError("capacity below the wave size must be refused")
+
+
+def test_cold_remainders_balanced_over_waves():
+    """Waves whose cold requests do not divide evenly: with the carried counts, no GPU
+    collects every remainder, the cumulative cold prefills stay within one of each other."""
+    import random
+
+    rng = random.Random(3)
+    world, per = 4, 8
+    carry = [0] * world
+    for _ in range(25):
+        n_cold = rng.choice([2, 3, 5])
+        cold = [True] * n_cold + [False] * (world * per - n_cold)
+        owners = [rng.randrange(world) for _ in cold]
+        a = route_wave(owners, cold, world, per, carry)
+        assert all(sum(1 for r in a if r == q) <= per for q in range(world))
+        assert max(carry) - min(carry) <= 1
