@@ -67,6 +67,8 @@ def parse_args(argv=None):
     p.add_argument("--graphs", type=int, default=1)
     p.add_argument("--prefill-graphs", type=int, default=1, help="CUDA-graph one-sequence prefills (with --graphs)")
     p.add_argument("--pipeline", type=int, default=1, help="launch decode step t+1 before reading step t's tokens")
+    p.add_argument("--max-prefill-tokens", type=int, default=0,
+                   help="engine prefill budget per step (0: two prompts' worth)")
     p.add_argument("--mixed", type=int, default=1, help="prefill admitted prompts and decode running ones in one forward")
     p.add_argument("--prefill-chunk", type=int, default=0,
                    help="new prompt tokens per step while others decode (0: whole prompts)")
@@ -246,7 +248,7 @@ def run_ours(args) -> None:
     num_blocks = int(args.batch * blocks_per_req * 1.15) + 64
     pages_per_prefix = args.prefix_len // PAGE
     ecfg = EngineConfig(num_blocks=num_blocks, kv_fmt=args.kv_fmt, max_batch=args.batch,
-                        max_prefill_tokens=2 * (args.prefix_len + args.suffix_len),
+                        max_prefill_tokens=args.max_prefill_tokens or 2 * (args.prefix_len + args.suffix_len),
                         max_model_len=tok_per_req + PAGE, cuda_graphs=bool(args.graphs),
                         prefill_graphs=bool(args.prefill_graphs), pipeline_decode=bool(args.pipeline),
                         mixed_batch=bool(args.mixed), prefill_chunk=args.prefill_chunk)
