@@ -98,8 +98,10 @@ class EngineConfig:
     # expert parallelism: every GPU runs exactly one prefill and one decode forward per
     # step (empty when it has nothing to do) so the MoE collectives of all GPUs line up
     lockstep: bool = False
-    # speculative decoding of greedy requests: "" (off), "ngram" (prompt lookup) or
-    # "model" (needs a draft model); depth adapts between 1 and spec_max_depth
+    # speculative decoding of greedy requests: "" (off), "ngram" (prompt lookup), "model"
+    # (needs a draft model) or "pool" (several drafters, each sequence's distinct drafts
+    # verified together on copy-on-write KV branches); depth adapts between 1 and
+    # spec_max_depth
     spec: str = ""
     spec_max_depth: int = 8
     # [AMF_*] trace lines (None: KORITH_AMF_TRACE decides)
@@ -192,11 +194,25 @@ class LLMEngine:
                 if hasattr(draft_model, "ensure_positions"):
                     draft_model.ensure_positions(cfg.max_model_len + PAGE)
                 drafter = ModelDrafter(draft_model, cfg.num_blocks)
-            elif cfg.spec == "ngram":
+            elif cfg.spec in ("ngram", "pool"):
                 drafter = None
             else:
                 raise ValueError(f"unknown spec mode {cfg.spec!r}")
-            self.spec = SpecDecoder(self, cfg.spec_max_depth, drafter)
+            if cfg.spec == "pool":
+                # a pool of draft engines (n-gram lookups of several lengths, plus the draft
+                # model when one is given); each sequence's distinct proposals are verified
+                # together on copy-on-write KV branches
+                from .pool import DraftPool, PoolSpecDecoder
+                from .spec import NgramDrafter
+
+                drafters = [NgramDrafter(3, 1), NgramDrafter(3, 1, skip=1), NgramDrafter(6, 4)]
+                if draft_model is not None:
+                    if hasattr(draft_model, "ensure_positions"):
+                        draft_model.ensure_positions(cfg.max_model_len + PAGE)
+                    drafters.insert(0, ModelDrafter(draft_model, cfg.num_blocks))
+                self.spec = PoolSpecDecoder(self, cfg.spec_max_depth, DraftPool(drafters))
+            else:
+                self.spec = SpecDecoder(self, cfg.spec_max_depth, drafter)
         self.stat = {"steps": 0, "prefill_tokens": 0, "decode_tokens": 0, "restored_tokens": 0,
                      "local_cached_tokens": 0, "cold_prefill_tokens": 0, "cascade_steps": 0,
                      "cascade_grouped_seqs": 0, "pipelined_decode_steps": 0, "sync_wait_ms": 0.0, "mixed_steps": 0,
@@ -288,6 +304,9 @@ class LLMEngine:
         if self._prefill_graphs is not None:
             self._prefill_graphs.close()
             self._prefill_graphs = None
+        pool = getattr(self.spec, "pool", None)
+        if pool is not None:
+            pool.close()
 
     def evict_live_cache(self, fraction: float = 1.0) -> int:
         """Drop cached (unreferenced) KV blocks -- forces later requests to restore from AMF."""

@@ -36,10 +36,12 @@ from ..ops.kvcache import PAGE
 
 
 class NgramDrafter:
-    """Prompt-lookup drafting over the last ``window`` tokens of a sequence."""
+    """Prompt-lookup drafting over the last ``window`` tokens of a sequence. ``skip`` > 0
+    proposes what followed an earlier occurrence of the tail instead of the most recent
+    one (a second candidate for multi-draft verification)."""
 
-    def __init__(self, max_n: int = 3, min_n: int = 1, window: int = 4096):
-        self.max_n, self.min_n, self.window = max_n, min_n, window
+    def __init__(self, max_n: int = 3, min_n: int = 1, window: int = 4096, skip: int = 0):
+        self.max_n, self.min_n, self.window, self.skip = max_n, min_n, window, skip
 
     def propose(self, tokens: Sequence[int], k: int) -> List[int]:
         toks = np.asarray(tokens[-self.window:], dtype=np.int64)
@@ -50,8 +52,12 @@ class NgramDrafter:
             tail = toks[L - n:]
             # candidate starts: positions i with toks[i:i+n] == tail and i + n < L
             cand = np.flatnonzero(toks[: L - n] == tail[0])
+            skip = self.skip
             for i in cand[::-1]:
                 if i + n < L and np.array_equal(toks[i:i + n], tail):
+                    if skip > 0:
+                        skip -= 1
+                        continue
                     nxt = toks[i + n:i + n + k].tolist()
                     if nxt:
                         return (nxt + [nxt[-1]] * k)[:k]
@@ -111,6 +117,12 @@ class ModelDrafter:
 
     def forget(self, req_id: str) -> None:
         self.synced.pop(req_id, None)
+
+    def rewind(self, req_id: str, pos: int) -> None:
+        """The sequence's pages from ``pos`` on were replaced (a speculative branch won):
+        the draft K/V written there is recomputed on the next proposal."""
+        if req_id in self.synced:
+            self.synced[req_id] = min(self.synced[req_id], pos)
 
 
 class SpecDecoder:

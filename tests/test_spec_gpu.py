@@ -48,3 +48,32 @@ def test_spec_gpu_ngram_and_model():
         assert st["steps"] > 0
         if mode == "model":
             assert st["acceptance"] > 0.8
+
+
+@pytest.mark.gpu
+def test_spec_gpu_pool_branches():
+    """Pool of drafters on the GPU: an always-wrong drafter and the target as its own draft
+    model; the second proposal is verified on a copy-on-write branch and wins, its pages
+    are swapped in, and every emitted token is a greedy choice of the target."""
+    from axropus_deploy_b200.engine.engine import EngineConfig, LLMEngine, SamplingParams
+    from axropus_deploy_b200.engine.pool import DraftPool, PoolSpecDecoder
+    from axropus_deploy_b200.engine.spec import ModelDrafter
+    from axropus_deploy_b200.models.config import get_config
+    from axropus_deploy_b200.models.llama import LlamaModel
+
+    class Wrong:
+        def propose(self, tokens, k):
+            return [(int(tokens[-1]) + 1) % 32000] * k
+
+    m = LlamaModel(get_config("tiny128"), "cuda", seed=7, init_std=0.05)
+    g = torch.Generator().manual_seed(3)
+    prompts = [torch.randint(0, 32000, (n,), generator=g).tolist() for n in (61, 100)]
+    eng = LLMEngine(m, EngineConfig(num_blocks=128, max_batch=4, max_model_len=512))
+    eng.spec = PoolSpecDecoder(eng, 6, DraftPool([Wrong(), ModelDrafter(m, 128)]))
+    got = eng.generate(prompts, SamplingParams(max_tokens=32))
+    for p, o in zip(prompts, got):
+        assert len(o) == 32
+        assert _check_greedy(m, p, o)
+    st = eng.spec.stats()
+    assert st["branch_wins"] > 0 and st["acceptance"] > 0.5
+    eng.close()
