@@ -106,6 +106,21 @@ class RewardLedger:
         s = np.stack([np.frombuffer(r[1], np.float32) for r in rows])
         return s, np.array([r[2] for r in rows], np.int64), np.array([r[3] for r in rows], np.float32)
 
+    def scored(self, limit: int = 4096, consume: bool = True) -> List[Dict[str, Any]]:
+        """Decisions with at least one outcome and not yet consumed, oldest first, as
+        ``{decision_id, state, decision, reward}`` rows (``decision`` a :class:`Decision`);
+        marked consumed unless ``consume`` is False."""
+        with self._mu:
+            rows = self._db.execute(
+                "SELECT d.decision_id, d.state, d.decision_json, SUM(o.reward) FROM decisions d JOIN outcomes o "
+                "ON o.decision_id = d.decision_id WHERE d.consumed = 0 GROUP BY d.decision_id ORDER BY d.ts LIMIT ?",
+                (int(limit),)).fetchall()
+            if consume:
+                self._db.executemany("UPDATE decisions SET consumed=1 WHERE decision_id=?", [(r[0],) for r in rows])
+                self._db.commit()
+        return [{"decision_id": r[0], "state": np.frombuffer(r[1], np.float32).copy(),
+                 "decision": Decision.from_dict(json.loads(r[2])), "reward": float(r[3])} for r in rows]
+
     def summary(self) -> Dict[str, Any]:
         with self._mu:
             rows = self._db.execute("SELECT outcome, COUNT(*), SUM(reward) FROM outcomes GROUP BY outcome").fetchall()

@@ -1,0 +1,370 @@
+"""Local reasoning model with LoRA adapters, and its DPO learning loop.
+
+:class:`LocalReasoningModel` makes the policy decision with a language model held by this
+process (any :class:`~..models.llama.LlamaModel`: a Hugging Face checkpoint through
+``models/loader.py``, or random-init weights in tests). The state vector becomes a prompt
+(slot name = value), and instead of parsing free text the model *ranks* a fixed set of
+candidate decisions, each rendered as a compact JSON object: the candidate with the highest
+log-likelihood given the prompt wins. Every answer is therefore a valid decision, and the
+same score is what the learning loop trains.
+
+:class:`LoRA` adds rank-``r`` adapters ``scale * B A`` to the attention and MLP projections
+of every layer. :func:`lm_forward` is a differentiable PyTorch forward of the same model
+(the serving kernels have no backward) that applies the adapters; :func:`dpo_step` trains
+only the adapter parameters with Direct Preference Optimisation (Rafailov et al. 2023)
+against the frozen base model as the reference policy, on pairs (state, preferred decision,
+rejected decision) -- e.g. from the reward ledger. :meth:`LoRA.merge` folds the adapters
+into the weights so the fused GPU kernels serve the fine-tuned model; :meth:`LoRA.unmerge`
+restores them.
+
+Reference counterparts: the local 8B NF4 reasoning model emitting decision vectors
+(platform/reasoning/reasoning_model.py:183-326) and its LoRA PPO/DPO learning loop
+(platform/reasoning/learning_loop.py:159).
+"""
+from __future__ import annotations
+
+import json
+import math
+import os
+import threading
+import time
+from dataclasses import dataclass
+from itertools import product
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+from ..ops.dense import SWIGLU_GROUP
+from .decide import DEPTHS, Decision
+from .state import Slot
+
+TARGETS = ("wqkv", "wo", "w_gate_up", "w_down")
+
+
+class LoRA(torch.nn.Module):
+    """Rank-``r`` adapters on the projections ``TARGETS`` of every layer of ``model``."""
+
+    def __init__(self, model, r: int = 8, alpha: float = 16.0, seed: int = 0):
+        super().__init__()
+        self.model, self.r, self.scale = model, r, alpha / r
+        g = torch.Generator().manual_seed(seed)
+        self.A = torch.nn.ParameterDict()
+        self.B = torch.nn.ParameterDict()
+        for li, lw in enumerate(model.layers):
+            for name in TARGETS:
+                w = getattr(lw, name, None)
+                if w is None:
+                    continue
+                out_f, in_f = w.shape
+                key = f"{li}_{name}"
+                # A random, B zero: the adapted model starts equal to the base model
+                self.A[key] = torch.nn.Parameter(torch.randn(r, in_f, generator=g) / math.sqrt(in_f))
+                self.B[key] = torch.nn.Parameter(torch.zeros(out_f, r))
+        self.to(model.embed.device)
+        self.merged = False
+
+    def delta(self, li: int, name: str) -> Optional[torch.Tensor]:
+        key = f"{li}_{name}"
+        if key not in self.A:
+            return None
+        return self.scale * (self.B[key] @ self.A[key])
+
+    def merge(self) -> None:
+        """W += scale B A for every adapted projection (serving with the fused kernels)."""
+        if self.merged:
+            return
+        with torch.no_grad():
+            for li, lw in enumerate(self.model.layers):
+                for name in TARGETS:
+                    d = self.delta(li, name)
+                    if d is not None:
+                        w = getattr(lw, name)
+                        w.copy_((w.float() + d.to(w.device)).to(w.dtype))
+        self.merged = True
+
+    def unmerge(self) -> None:
+        if not self.merged:
+            return
+        with torch.no_grad():
+            for li, lw in enumerate(self.model.layers):
+                for name in TARGETS:
+                    d = self.delta(li, name)
+                    if d is not None:
+                        w = getattr(lw, name)
+                        w.copy_((w.float() - d.to(w.device)).to(w.dtype))
+        self.merged = False
+
+
+def _rms(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * w.float()
+
+
+def lm_forward(model, tokens: torch.Tensor, lora: Optional[LoRA] = None) -> torch.Tensor:
+    """Differentiable causal forward of a dense ``LlamaModel`` over ``tokens`` [B, T] (or
+    [T]) -> logits [B, T, vocab] (or [T, vocab]) in fp32, with ``lora``'s adapters applied
+    unless they are merged. Rows are independent; right padding does not change the logits
+    of the positions before it. Matmuls run in fp32 on the CPU and in the weights' dtype on
+    the GPU (fp32 accumulation)."""
+    cfg = model.cfg
+    squeeze = tokens.dim() == 1
+    if squeeze:
+        tokens = tokens[None]
+    B, T = tokens.shape
+    Hq, Hkv, D = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
+    cd = torch.float32 if tokens.device.type == "cpu" else model.dtype
+    pos = torch.arange(T, device=tokens.device)
+    cs = model.cos_sin.to(tokens.device)[pos].float()
+    half = D // 2
+    cos, sin = cs[None, :, None, :half], cs[None, :, None, half:]
+    use = lora is not None and not lora.merged
+
+    def proj(x, li, name, w):
+        y = (x.to(cd) @ w.to(cd).t()).float()
+        if use:
+            d = lora.delta(li, name)
+            if d is not None:
+                y = y + x @ d.to(x.device).t()
+        return y
+
+    def rope(x):
+        x1, x2 = x[..., :half], x[..., half:]
+        return torch.cat((x1 * cos - x2 * sin, x2 * cos + x1 * sin), dim=-1)
+
+    h = model.embed[tokens.long()].float()
+    rep = Hq // Hkv
+    for li, lw in enumerate(model.layers):
+        if lw.w_gate_up is None:
+            raise ValueError("lm_forward: dense (non-MoE) models only")
+        x = _rms(h, lw.attn_norm, cfg.rms_eps)
+        qkv = proj(x, li, "wqkv", lw.wqkv).view(B, T, Hq + 2 * Hkv, D)
+        q = rope(qkv[:, :, :Hq])
+        k = rope(qkv[:, :, Hq:Hq + Hkv]).repeat_interleave(rep, dim=2)
+        v = qkv[:, :, Hq + Hkv:].repeat_interleave(rep, dim=2)
+        a = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
+                                           is_causal=True).transpose(1, 2)
+        h = h + proj(a.reshape(B, T, Hq * D), li, "wo", lw.wo)
+        x = _rms(h, lw.mlp_norm, cfg.rms_eps)
+        gu = proj(x, li, "w_gate_up", lw.w_gate_up)
+        n = gu.shape[-1]
+        g4 = gu.view(B, T, n // (2 * SWIGLU_GROUP), 2, SWIGLU_GROUP)  # gate/up interleaved by 64 rows
+        act = (F.silu(g4[..., 0, :]) * g4[..., 1, :]).reshape(B, T, n // 2)
+        h = h + proj(act, li, "w_down", lw.w_down)
+    logits = (_rms(h, model.final_norm, cfg.rms_eps).to(cd) @ model.lm_head.to(cd).t()).float()
+    return logits[0] if squeeze else logits
+
+
+def candidate_decisions() -> List[Decision]:
+    """The discrete decision set the model ranks: admission x speculative depth x back-pressure."""
+    out = []
+    for admit, depth, thr in product((True, False), DEPTHS, (0.0, 0.25, 0.5)):
+        out.append(Decision(cache_admission=admit, spec_decode_depth=depth, spec_decode_enable=depth > 2,
+                            throttle_back_pressure=thr))
+    return out
+
+
+def render(d: Decision) -> str:
+    return json.dumps({"cache_admission": d.cache_admission, "spec_decode_depth": d.spec_decode_depth,
+                       "throttle_back_pressure": d.throttle_back_pressure}, separators=(",", ":"))
+
+
+class LocalReasoningModel:
+    """Policy decisions from a local language model by ranking candidate decisions."""
+
+    def __init__(self, model, tokenizer=None, lora: Optional[LoRA] = None,
+                 candidates: Optional[Sequence[Decision]] = None, max_prompt_tokens: int = 256):
+        self.model, self.tok, self.lora = model, tokenizer, lora
+        self.candidates = list(candidates or candidate_decisions())
+        self.max_prompt_tokens = max_prompt_tokens
+
+    def encode(self, text: str) -> List[int]:
+        if self.tok is not None:
+            return list(self.tok.encode(text))
+        return [b % self.model.cfg.vocab for b in text.encode()]  # bytes as token ids
+
+    def prompt(self, v: np.ndarray) -> List[int]:
+        named = {k: round(float(v[i]), 3) for k, i in vars(Slot).items() if k.isupper() and i < len(v)}
+        text = "state " + json.dumps(named, separators=(",", ":")) + " decision "
+        return self.encode(text)[-self.max_prompt_tokens:]
+
+    def scores(self, v: np.ndarray, lora: Optional[LoRA] = None,
+               candidates: Optional[Sequence[Decision]] = None) -> torch.Tensor:
+        """Log-likelihood of every candidate given the state prompt [len(candidates)]: one
+        batched forward, one right-padded row per candidate."""
+        p = self.prompt(v)
+        cands = [self.encode(render(d)) for d in (candidates if candidates is not None else self.candidates)]
+        T = len(p) + max(len(c) for c in cands)
+        rows = [p + c + [0] * (T - len(p) - len(c)) for c in cands]
+        dev = self.model.embed.device
+        toks = torch.tensor(rows, dtype=torch.long, device=dev)
+        mask = torch.zeros(len(cands), T - 1, device=dev)
+        for i, c in enumerate(cands):
+            mask[i, len(p) - 1:len(p) - 1 + len(c)] = 1.0
+        lp = F.log_softmax(lm_forward(self.model, toks, lora)[:, :-1], dim=-1)
+        tok_lp = lp.gather(2, toks[:, 1:, None])[..., 0]
+        return (tok_lp * mask).sum(1)
+
+    def decide(self, v: np.ndarray) -> Decision:
+        """The highest-scoring candidate; any failure returns a fallback decision (fail closed,
+        like the endpoint model)."""
+        t0 = time.perf_counter()
+        try:
+            with torch.no_grad():
+                s = self.scores(v, self.lora)
+            d = Decision(**self.candidates[int(torch.argmax(s))].to_dict())
+        except Exception:
+            d = Decision(is_fallback=True)
+        d.inference_ms = (time.perf_counter() - t0) * 1e3
+        return d
+
+
+def dpo_step(lm: LocalReasoningModel, lora: LoRA, opt: torch.optim.Optimizer,
+             pairs: Sequence[Tuple[np.ndarray, Decision, Decision]], beta: float = 0.1) -> float:
+    """One DPO update of the adapters on (state, preferred, rejected) pairs; the reference
+    policy is the base model (adapters off). Returns the mean loss."""
+    losses = []
+    for v, good, bad in pairs:
+        with torch.no_grad():
+            ref = lm.scores(v, None, [good, bad])
+        cur = lm.scores(v, lora, [good, bad])
+        margin = beta * ((cur[0] - ref[0]) - (cur[1] - ref[1]))
+        losses.append(-F.logsigmoid(margin))
+    loss = torch.stack(losses).mean()
+    opt.zero_grad()
+    loss.backward()
+    opt.step()
+    return float(loss.detach())
+
+
+def preference_pairs(ledger_rows: Sequence[Dict]) -> List[Tuple]:
+    """Pairs for :func:`dpo_step` from rows {state, decision, reward}: within groups of rows
+    with the same rounded state, the highest-reward decision is preferred over the lowest."""
+    groups: Dict[bytes, List[Dict]] = {}
+    for r in ledger_rows:
+        key = np.round(np.asarray(r["state"], dtype=np.float32), 2).tobytes()
+        groups.setdefault(key, []).append(r)
+    pairs = []
+    for rows in groups.values():
+        if len(rows) < 2:
+            continue
+        rows = sorted(rows, key=lambda r: r["reward"])
+        lo, hi = rows[0], rows[-1]
+        if hi["reward"] > lo["reward"]:
+            pairs.append((np.asarray(hi["state"], dtype=np.float32), hi["decision"], lo["decision"]))
+    return pairs
+
+
+def sft_step(lm: LocalReasoningModel, lora: LoRA, opt: torch.optim.Optimizer,
+             rows: Sequence[Tuple[np.ndarray, Decision, float]]) -> float:
+    """One update raising the log-likelihood of each (state, decision) weighted by its
+    ``weight``: weights 1 on positive-reward rows is supervised fine-tuning on good
+    decisions; centred rewards as weights is REINFORCE with a mean baseline."""
+    losses = [-w * lm.scores(v, lora, [d])[0] for v, d, w in rows]
+    loss = torch.stack(losses).mean()
+    opt.zero_grad()
+    loss.backward()
+    opt.step()
+    return float(loss.detach())
+
+
+@dataclass
+class TrainingResult:
+    examples_used: int
+    mean_reward: float
+    loss: float
+    adapter_path: Optional[str]
+    elapsed_s: float
+    skipped: bool
+    skip_reason: str = ""
+
+
+class LoraLearningLoop:
+    """Periodic LoRA fine-tuning of a :class:`LocalReasoningModel` from its own scored
+    decisions in a :class:`~.learn.RewardLedger`. ``level`` picks the objective: 1 SFT on
+    positive-reward decisions, 2 reward-weighted policy gradient (REINFORCE with a mean
+    baseline), 4 DPO on best-versus-worst pairs of the same state (level 3, PPO over the
+    speculative depth, is :func:`~.learn.ppo_update` on the small :class:`~.learn.DepthPolicy`).
+    Each cycle trains a copy of the live adapters and swaps it in under a lock, so
+    ``decide`` never sees half-updated weights; the adapters are saved to ``adapter_dir``.
+    """
+
+    def __init__(self, lm: LocalReasoningModel, ledger, level: int = 4, interval_s: float = 3600.0,
+                 batch_size: int = 64, min_examples: int = 8, epochs: int = 2, lr: float = 1e-3, beta: float = 0.1,
+                 r: int = 8, alpha: float = 16.0, adapter_dir: Optional[str] = None):
+        self.lm, self.ledger, self.level = lm, ledger, int(level)
+        self.interval_s, self.batch_size, self.min_examples = max(1.0, float(interval_s)), batch_size, min_examples
+        self.epochs, self.lr, self.beta, self.r, self.alpha = epochs, lr, beta, r, alpha
+        self.adapter_dir = adapter_dir
+        self.cycles = 0
+        self._swap = threading.Lock()
+        self._stop = threading.Event()
+        self._thread: Optional[threading.Thread] = None
+
+    def _examples(self, rows) -> Tuple[str, list]:
+        if self.level >= 4:
+            return "dpo", preference_pairs(rows)
+        if self.level >= 2:
+            mean = float(np.mean([r["reward"] for r in rows])) if rows else 0.0
+            return "pg", [(r["state"], r["decision"], r["reward"] - mean) for r in rows if r["reward"] != mean]
+        return "sft", [(r["state"], r["decision"], 1.0) for r in rows if r["reward"] > 0]
+
+    def run_once(self) -> TrainingResult:
+        t0 = time.perf_counter()
+        rows = self.ledger.scored(self.batch_size, consume=False)
+        if not rows:
+            return TrainingResult(0, 0.0, 0.0, None, time.perf_counter() - t0, True, "no scored decisions")
+        kind, ex = self._examples(rows)
+        if len(ex) < self.min_examples:
+            return TrainingResult(len(ex), 0.0, 0.0, None, time.perf_counter() - t0, True,
+                                  f"only {len(ex)} {kind} examples < {self.min_examples}")
+        live = self.lm.lora
+        lora = LoRA(self.lm.model, self.r, self.alpha)
+        if live is not None:
+            lora.load_state_dict(live.state_dict())
+        opt = torch.optim.AdamW(lora.parameters(), lr=self.lr)
+        loss = 0.0
+        for _ in range(self.epochs):
+            loss = dpo_step(self.lm, lora, opt, ex, self.beta) if kind == "dpo" else sft_step(self.lm, lora, opt, ex)
+        with self._swap:
+            self.lm.lora = lora
+        self.ledger.scored(len(rows), consume=True)
+        path = self.save(lora) if self.adapter_dir else None
+        self.cycles += 1
+        return TrainingResult(len(ex), float(np.mean([r["reward"] for r in rows])), loss, path,
+                              time.perf_counter() - t0, False)
+
+    def decide(self, v: np.ndarray) -> Decision:
+        with self._swap:
+            return self.lm.decide(v)
+
+    def save(self, lora: LoRA) -> str:
+        os.makedirs(self.adapter_dir, exist_ok=True)
+        path = os.path.join(self.adapter_dir, f"adapter_{self.cycles:05d}.pt")
+        torch.save({"r": lora.r, "scale": lora.scale, "state": lora.state_dict()}, path)
+        return path
+
+    def start(self) -> None:
+        if self._thread is not None and self._thread.is_alive():
+            return
+        self._stop.clear()
+        self._thread = threading.Thread(target=self._run, daemon=True, name="lora-learning-loop")
+        self._thread.start()
+
+    def _run(self) -> None:
+        while not self._stop.wait(self.interval_s):
+            self.run_once()
+
+    def stop(self, timeout: float = 10.0) -> None:
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join(timeout)
+            self._thread = None
+
+
+def load_adapter(model, path: str) -> LoRA:
+    """A :class:`LoRA` for ``model`` with the weights saved by :meth:`LoraLearningLoop.save`."""
+    blob = torch.load(path, map_location="cpu")
+    lora = LoRA(model, blob["r"], blob["scale"] * blob["r"])
+    lora.load_state_dict(blob["state"])
+    return lora

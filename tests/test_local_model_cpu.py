@@ -1,0 +1,183 @@
+"""Local reasoning model with LoRA adapters: differentiable forward, candidate ranking,
+merge/unmerge, DPO / SFT / policy-gradient updates and the learning loop (CPU, fp32)."""
+import numpy as np
+import pytest
+import torch
+
+from axropus_deploy_b200.models.config import ModelConfig
+from axropus_deploy_b200.models.llama import LlamaModel
+from axropus_deploy_b200.policy.decide import Decision
+from axropus_deploy_b200.policy.learn import RewardLedger
+from axropus_deploy_b200.policy.local_model import (LoRA, LocalReasoningModel, LoraLearningLoop, dpo_step,
+                                                    load_adapter, lm_forward, preference_pairs, sft_step)
+from axropus_deploy_b200.policy.state import WIDTH
+
+MICRO = ModelConfig("micro", 2, 64, 4, 2, 16, 128, 320, 10000.0, None, max_position=1024)
+
+
+def _model(seed=0):
+    return LlamaModel(MICRO, "cpu", dtype=torch.float32, seed=seed, init_std=0.1)
+
+
+def _sdpa_free_forward(model, toks):
+    """Token-by-token fp32 forward with explicit softmax attention (no SDPA, no batching)."""
+    cfg = model.cfg
+    T = toks.shape[0]
+    Hq, Hkv, D = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
+
+    def rms(x, w):
+        return x / torch.sqrt((x * x).mean(-1, keepdim=True) + cfg.rms_eps) * w
+
+    def rope(x, p):
+        c, s = model.cos_sin[p, :D // 2], model.cos_sin[p, D // 2:]
+        a, b = x[..., :D // 2], x[..., D // 2:]
+        return torch.cat((a * c - b * s, b * c + a * s), -1)
+
+    h = model.embed[toks]
+    for lw in model.layers:
+        x = rms(h, lw.attn_norm)
+        qkv = (x @ lw.wqkv.t()).view(T, Hq + 2 * Hkv, D)
+        out = torch.zeros(T, Hq, D)
+        for t in range(T):
+            for hq in range(Hq):
+                hk = hq // (Hq // Hkv)
+                q = rope(qkv[t, hq], t)
+                ks = torch.stack([rope(qkv[j, Hq + hk], j) for j in range(t + 1)])
+                vs = qkv[: t + 1, Hq + Hkv + hk]
+                w = torch.softmax(ks @ q / D ** 0.5, 0)
+                out[t, hq] = w @ vs
+        h = h + out.reshape(T, -1) @ lw.wo.t()
+        x = rms(h, lw.mlp_norm)
+        gu = x @ lw.w_gate_up.t()
+        g = gu.view(T, -1, 2, 64)
+        h = h + (torch.nn.functional.silu(g[:, :, 0]) * g[:, :, 1]).reshape(T, -1) @ lw.w_down.t()
+    return rms(h, model.final_norm) @ model.lm_head.t()
+
+
+def test_lm_forward_matches_explicit_attention():
+    m = _model()
+    toks = torch.randint(0, MICRO.vocab, (9,), generator=torch.Generator().manual_seed(1))
+    ref = _sdpa_free_forward(m, toks)
+    out = lm_forward(m, toks)
+    torch.testing.assert_close(out, ref, rtol=1e-4, atol=1e-4)
+    # batched with right padding: rows unchanged before the padding
+    b = torch.stack([toks, torch.cat([toks[:5], torch.zeros(4, dtype=torch.long)])])
+    outb = lm_forward(m, b)
+    torch.testing.assert_close(outb[0], ref, rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(outb[1, :5], ref[:5], rtol=1e-4, atol=1e-4)
+
+
+def test_lora_zero_init_merge_unmerge():
+    m = _model()
+    lora = LoRA(m, r=4)
+    toks = torch.arange(12) % MICRO.vocab
+    base = lm_forward(m, toks)
+    torch.testing.assert_close(lm_forward(m, toks, lora), base)  # B = 0: adapted == base
+    with torch.no_grad():
+        for p in lora.B.values():
+            p.normal_(0, 0.05)
+    adapted = lm_forward(m, toks, lora)
+    assert (adapted - base).abs().max() > 1e-3
+    w0 = m.layers[0].wqkv.clone()
+    lora.merge()
+    torch.testing.assert_close(lm_forward(m, toks), adapted, rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(lm_forward(m, toks, lora), adapted, rtol=1e-4, atol=1e-4)  # merged: not applied twice
+    lora.unmerge()
+    torch.testing.assert_close(m.layers[0].wqkv, w0, rtol=0, atol=1e-6)
+    torch.testing.assert_close(lm_forward(m, toks), base, rtol=1e-4, atol=1e-4)
+
+
+def test_scores_are_candidate_log_likelihoods():
+    m = _model()
+    lm = LocalReasoningModel(m, max_prompt_tokens=48)
+    v = np.random.default_rng(0).random(WIDTH).astype(np.float32)
+    s = lm.scores(v)
+    assert s.shape == (len(lm.candidates),) and torch.isfinite(s).all() and (s < 0).all()
+    # one candidate alone scores the same as inside the padded batch
+    d = lm.candidates[5]
+    torch.testing.assert_close(lm.scores(v, candidates=[d])[0], s[5], rtol=1e-4, atol=1e-3)
+    dec = lm.decide(v)
+    assert dec.to_dict()["spec_decode_depth"] == lm.candidates[int(torch.argmax(s))].spec_decode_depth
+    assert dec.inference_ms > 0 and not dec.validate()
+
+
+def _pair(lm):
+    v = np.linspace(0, 1, WIDTH, dtype=np.float32)
+    s = lm.scores(v).detach()
+    good = lm.candidates[int(torch.argmin(s))]  # the base model's least likely decision
+    bad = lm.candidates[int(torch.argmax(s))]
+    return v, good, bad
+
+
+def test_dpo_moves_decision_to_preferred():
+    torch.manual_seed(0)
+    m = _model()
+    lm = LocalReasoningModel(m, max_prompt_tokens=32)
+    v, good, bad = _pair(lm)
+    lora = LoRA(m, r=4, alpha=8)
+    lm.lora = lora
+    opt = torch.optim.Adam(lora.parameters(), lr=2e-2)
+    losses = [dpo_step(lm, lora, opt, [(v, good, bad)], beta=0.5) for _ in range(25)]
+    assert losses[-1] < losses[0] * 0.5
+    with torch.no_grad():
+        s = lm.scores(v, lora, [good, bad])
+    assert s[0] > s[1]
+
+
+def test_sft_raises_likelihood():
+    m = _model()
+    lm = LocalReasoningModel(m, max_prompt_tokens=32)
+    v, good, _ = _pair(lm)
+    lora = LoRA(m, r=4)
+    opt = torch.optim.Adam(lora.parameters(), lr=1e-2)
+    before = float(lm.scores(v, lora, [good])[0].detach())
+    for _ in range(10):
+        sft_step(lm, lora, opt, [(v, good, 1.0)])
+    assert float(lm.scores(v, lora, [good])[0].detach()) > before + 1.0
+
+
+def test_preference_pairs_group_by_state():
+    a = np.zeros(WIDTH, np.float32)
+    b = np.ones(WIDTH, np.float32)
+    d1, d2, d3 = Decision(spec_decode_depth=2), Decision(spec_decode_depth=8), Decision(spec_decode_depth=16)
+    rows = [{"state": a, "decision": d1, "reward": -1.0}, {"state": a + 1e-4, "decision": d2, "reward": 2.0},
+            {"state": a, "decision": d3, "reward": 0.5}, {"state": b, "decision": d1, "reward": 1.0}]
+    pairs = preference_pairs(rows)
+    assert len(pairs) == 1
+    _, good, bad = pairs[0]
+    assert good.spec_decode_depth == 8 and bad.spec_decode_depth == 2
+
+
+@pytest.mark.parametrize("level", [1, 2, 4])
+def test_learning_loop_cycle(tmp_path, level):
+    m = _model()
+    lm = LocalReasoningModel(m, max_prompt_tokens=24)
+    led = RewardLedger()
+    rng = np.random.default_rng(0)
+    states = [rng.random(WIDTH).astype(np.float32) for _ in range(3)]
+    for v in states:
+        for d, outcome in ((Decision(spec_decode_depth=8), "spec_high_acceptance"),
+                           (Decision(spec_decode_depth=2, cache_admission=False), "spec_low_acceptance")):
+            led.record_outcome(led.record_decision(d, v), outcome)
+    loop = LoraLearningLoop(lm, led, level=level, min_examples=3, epochs=2, lr=1e-2, r=4,
+                            adapter_dir=str(tmp_path))
+    res = loop.run_once()
+    assert not res.skipped, res.skip_reason
+    assert res.examples_used >= 3 and res.adapter_path and lm.lora is not None
+    assert led.scored(100) == []  # consumed
+    again = loop.run_once()
+    assert again.skipped
+    back = load_adapter(m, res.adapter_path)
+    for k in back.A:
+        torch.testing.assert_close(back.A[k], lm.lora.A[k])
+        torch.testing.assert_close(back.B[k], lm.lora.B[k])
+    assert isinstance(loop.decide(states[0]), Decision)
+
+
+def test_learning_loop_skips_without_data():
+    m = _model()
+    loop = LoraLearningLoop(LocalReasoningModel(m), RewardLedger(), interval_s=1)
+    r = loop.run_once()
+    assert r.skipped and "no scored" in r.skip_reason
+    loop.start()
+    loop.stop()
