@@ -1,0 +1,201 @@
+"""Hosted backend: accounts and tokens, keys, metering, dashboard, billing, benchmark data,
+the inference proxy (fake upstream) and SSH deployment (fake SSH client)."""
+import json
+import time
+from datetime import timedelta
+
+import httpx
+import pytest
+from fastapi.testclient import TestClient
+
+from axropus_deploy_b200.saas import Store, create_app, make_token, read_token
+from axropus_deploy_b200.saas.store import iso, utcnow
+
+
+def _upstream():
+    seen = []
+
+    def handler(req: httpx.Request):
+        seen.append((req.method, str(req.url), req.content))
+        if req.url.path == "/v1/models":
+            return httpx.Response(200, json={"data": [{"id": "llama3-8b"}]})
+        body = json.loads(req.content)
+        if body.get("stream"):
+            return httpx.Response(200, content=b"data: {\"x\":1}\n\ndata: [DONE]\n\n",
+                                  headers={"content-type": "text/event-stream"})
+        return httpx.Response(200, json={"choices": [{"text": "hi"}], "echo": body})
+    return httpx.MockTransport(handler), seen
+
+
+@pytest.fixture
+def env(tmp_path):
+    transport, seen = _upstream()
+    bench = tmp_path / "bench"
+    bench.mkdir()
+    (bench / "BENCH_a.json").write_text(json.dumps({"metric": "output_tok_s", "value": 2900.0, "n_gpus": 1,
+                                                    "config": {"model": "llama3-8b"}}) + "\n")
+    (bench / "BENCH_b.json").write_text(json.dumps({"metric": "output_tok_s", "value": 2343.1, "n_gpus": 1,
+                                                    "impl": "reference", "config": {"model": "llama3-8b"}}) + "\n")
+    app = create_app(Store(str(tmp_path / "db.sqlite")), "s3cret", default_upstream="http://node:8000",
+                     upstream=transport, bench_dir=str(bench), rate_limit=5, rate_window_s=60,
+                     ssh_connect=lambda *a: FakeSSH(), http_get=lambda url: 200, register_wait_s=10)
+    return TestClient(app), seen
+
+
+def _signup(c, email="a@x.io"):
+    r = c.post("/api/auth/signup", json={"email": email, "password": "hunter22!", "company_name": "acme"})
+    assert r.status_code == 200, r.text
+    d = r.json()
+    return {"Authorization": "Bearer " + d["access_token"]}, d["api_key"]
+
+
+def test_tokens_roundtrip_and_reject():
+    t = make_token("k", 7, ttl_s=60, now=1000)
+    assert read_token("k", t, now=1010) == 7
+    with pytest.raises(ValueError):
+        read_token("other", t, now=1010)
+    with pytest.raises(ValueError):
+        read_token("k", t, now=2000)  # expired
+    h, b, s = t.split(".")
+    with pytest.raises(ValueError):
+        read_token("k", h + "." + b[:-2] + "xx." + s, now=1010)
+
+
+def test_health_auth_keys(env):
+    c, _ = env
+    assert c.get("/health").json() == {"status": "ok"}
+    assert c.get("/health/ready").json() == {"status": "ready"}
+    assert c.get("/health").headers["x-frame-options"] == "DENY"
+    h, key = _signup(c)
+    assert key.startswith("ax-") and len(key) == 35
+    assert c.post("/api/auth/signup", json={"email": "a@x.io", "password": "hunter22!"}).status_code == 409
+    assert c.post("/api/auth/login", json={"email": "a@x.io", "password": "wrong-pass"}).status_code == 401
+    tok = c.post("/api/auth/login", json={"email": "A@x.io", "password": "hunter22!"}).json()["access_token"]
+    assert c.get("/api/auth/me", headers={"Authorization": "Bearer " + tok}).json()["email"] == "a@x.io"
+    assert c.get("/api/auth/me").status_code == 401
+    assert c.get("/api/keys/validate/" + key).json()["tier"] == "trial"
+    k2 = c.post("/api/keys/generate", json={"tier": "standard"}, headers=h).json()
+    assert k2["status"] == "active" and k2["expires_at"] is None
+    assert c.post("/api/keys/generate", json={"tier": "gold"}, headers=h).status_code == 400
+    assert len(c.get("/api/keys", headers=h).json()) == 2
+    assert c.delete(f"/api/keys/{k2['id']}", headers=h).status_code == 200
+    assert c.get("/api/keys/validate/" + k2["key"]).json()["valid"] is False
+    h2, _ = _signup(c, "b@x.io")
+    assert c.delete(f"/api/keys/{k2['id']}", headers=h2).status_code == 404  # not theirs
+
+
+def _metric(key, **kw):
+    d = {"api_key": key, "timestamp": iso(utcnow()), "tokens_processed": 1000, "amf_hit_rate": 0.5,
+         "compute_saved_pct": 0.8, "effective_tps": 2900.0, "baseline_tps": 2343.1, "model_family": "llama3"}
+    d.update(kw)
+    return d
+
+
+def test_metrics_dashboard_billing(env):
+    c, _ = env
+    h, trial = _signup(c)
+    std = c.post("/api/keys/generate", json={"tier": "standard"}, headers=h).json()["key"]
+    assert c.post("/api/metrics", json=_metric(trial)).status_code == 200
+    assert c.post("/api/metrics", json=_metric(std, tokens_processed=3_000_000)).status_code == 200
+    assert c.post("/api/metrics", json=_metric(trial, prompt="secret text")).status_code == 400  # not whitelisted
+    assert c.post("/api/metrics", json=_metric(trial, model_family="/models/llama.gguf")).status_code == 400
+    assert c.post("/api/metrics", json=_metric(trial, adapter_type="10.0.0.1")).status_code == 400
+    assert c.post("/api/metrics", json=_metric(trial, amf_hit_rate=1.5)).status_code == 400
+    assert c.post("/api/metrics", json=_metric("ax-nope")).status_code == 401
+    assert c.post("/api/metrics", json={"api_key": trial}).status_code == 400
+    d = c.get("/api/dashboard", headers=h).json()
+    assert d["total_tokens_processed"] == 3_001_000 and d["tokens_today"] == 3_001_000
+    assert d["status"] == "active" and d["current_effective_tps"] == 2900.0
+    assert d["estimated_monthly_savings_usd"] == pytest.approx(3_001_000 * 0.8 * 2.5 / 250_000.0)
+    b = c.get("/api/billing/summary", headers=h).json()["current_period"]
+    assert b["trial_tokens"] == 1000 and b["standard_tokens"] == 3_000_000
+    assert b["billable_tokens"] == 3_000_000 and b["amount_cents"] == 30  # trial tokens within the free allowance
+    # a closed month becomes an invoice
+    old = iso(utcnow().replace(day=1) - timedelta(days=20))
+    assert c.post("/api/metrics", json=_metric(std, timestamp=old, tokens_processed=50_000_000)).status_code == 200
+    inv = c.get("/api/billing/invoices", headers=h).json()
+    assert len(inv) == 1 and inv[0]["amount_cents"] == 500 and inv[0]["total_tokens"] == 50_000_000
+    assert len(c.get("/api/billing/invoices", headers=h).json()) == 1  # not duplicated
+
+
+def test_benchmarks(env):
+    c, _ = env
+    runs = c.get("/api/benchmarks/runs", params={"model": "llama3-8b"}).json()
+    assert len(runs) == 2
+    s = c.get("/api/benchmarks/summary").json()
+    assert s[0]["best"] == 2900.0
+    m = c.get("/api/benchmarks/mixed").json()["output_tok_s"]
+    assert m["reference"] == [2343.1] and m["axropus-b200"] == [2900.0]
+    assert "axropus-deploy-b200" in c.get("/").text
+
+
+def test_inference_proxy_and_rate_limit(env):
+    c, seen = env
+    _, key = _signup(c)
+    bad = c.post("/v1/completions", json={"prompt": "x"}, headers={"Authorization": "Bearer ax-0000"})
+    assert bad.status_code == 401
+    r = c.post("/v1/completions", json={"prompt": "hello", "max_tokens": 4},
+               headers={"Authorization": "Bearer " + key})
+    assert r.status_code == 200 and r.json()["echo"]["prompt"] == "hello"
+    assert seen[-1][1] == "http://node:8000/v1/completions"
+    s = c.post("/v1/chat/completions", json={"messages": [], "stream": True}, headers={"x-api-key": key})
+    assert s.headers["content-type"].startswith("text/event-stream") and b"[DONE]" in s.content
+    assert c.get("/v1/models", headers={"x-api-key": key}).json()["data"][0]["id"] == "llama3-8b"
+    codes = [c.get("/v1/models", headers={"x-api-key": key}).status_code for _ in range(4)]
+    assert codes[-1] == 429  # 5 requests per window
+
+
+class _Out:
+    def __init__(self, code, text):
+        self.code, self.text = code, text
+        self.channel = self
+
+    def recv_exit_status(self):
+        return self.code
+
+    def read(self):
+        return self.text.encode()
+
+
+class FakeSSH:
+    commands = []
+
+    def exec_command(self, cmd, timeout=None):
+        FakeSSH.commands.append(cmd)
+        if "--version" in cmd:
+            return None, _Out(0, "Python 3.12.3"), _Out(0, "")
+        if "nvidia-smi" in cmd:
+            return None, _Out(0, "NVIDIA B200, 183359 MiB\nNVIDIA B200, 183359 MiB"), _Out(0, "")
+        return None, _Out(0, ""), _Out(0, "")
+
+    def close(self):
+        pass
+
+
+def test_deploy_over_ssh(env):
+    c, seen = env
+    h, key = _signup(c)
+    assert c.post("/api/deploy", json={"host": "gpu1", "username": "ops", "password": "pw"}, headers=h).status_code == 200
+    dep = c.get("/api/deploy/status/1", headers=h).json()
+    assert dep["deployment"]["runtime"] == "axropus-b200"
+    deadline = time.time() + 10
+    while time.time() < deadline:
+        log = c.get("/api/deploy/status/1", headers=h).json()["log"]
+        if any("waiting for the node" in e["message"] for e in log):
+            break
+        time.sleep(0.02)
+    assert c.post("/api/deploy/1/register", json={"api_key": "ax-" + "0" * 32,
+                                                   "inference_url": "http://gpu1:8000"}).status_code == 403
+    assert c.post("/api/deploy/1/register", json={"api_key": key, "inference_url": "http://gpu1:8000"}).status_code == 200
+    while time.time() < deadline:
+        st = c.get("/api/deploy/status/1", headers=h).json()
+        if st["deployment"]["status"] in ("active", "failed"):
+            break
+        time.sleep(0.02)
+    assert st["deployment"]["status"] == "active", st["log"]
+    assert all("pw" != e["message"] and key not in e["message"] for e in st["log"])
+    assert any("B200" in e["message"] for e in st["log"])
+    assert any("-m axropus_deploy_b200 serve --model llama3-8b" in cmd for cmd in FakeSSH.commands)
+    # the key's traffic now goes to the deployed node
+    c.post("/v1/completions", json={"prompt": "x"}, headers={"x-api-key": key})
+    assert seen[-1][1] == "http://gpu1:8000/v1/completions"
