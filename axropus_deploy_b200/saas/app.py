@@ -23,13 +23,15 @@ Routes (the reference backend's paths, backend/main.py:50-76 and the routers it 
 * ``/api/benchmarks/summary|runs|mixed`` -- benchmark JSON lines from ``bench_dir``
 * ``/v1/completions``, ``/v1/chat/completions``, ``/v1/models`` -- proxied to the key owner's
   active deployment (else ``default_upstream``), rate limited per key
-* ``POST /api/deploy``, ``/api/deploy/status/{id}``, ``/api/deploy/{id}/register`` -- install
+* ``POST /api/deploy``, ``/api/deploy/status/{id}``, ``/api/deploy/{id}/register``, the websocket
+  ``/api/deploy/stream/{id}?token=`` (progress messages as they happen) -- install
   and start this framework's server on a customer GPU host over SSH, wait for the node to
   register its URL, probe its health (backend/deploy.py:129-455)
 * ``/`` -- a single-page dashboard (static HTML + fetch calls to the routes above)
 """
 from __future__ import annotations
 
+import asyncio
 import glob
 import json
 import os
@@ -43,7 +45,7 @@ from datetime import datetime, timedelta
 from typing import Any, Callable, Deque, Dict, List, Optional
 
 import httpx
-from fastapi import Depends, FastAPI, HTTPException, Request
+from fastapi import Depends, FastAPI, HTTPException, Request, WebSocket, WebSocketDisconnect
 from fastapi.responses import HTMLResponse, JSONResponse, Response, StreamingResponse
 from pydantic import BaseModel, Field
 
@@ -568,6 +570,35 @@ def create_app(store: Optional[Store] = None, secret: Optional[str] = None, *, d
         with progress_mu:
             log = progress[dep_id][since:]
         return {"deployment": row, "log": log, "next": since + len(log)}
+
+    @app.websocket("/api/deploy/stream/{dep_id}")
+    async def deploy_stream(ws: WebSocket, dep_id: int):
+        """Progress messages of a deployment as they are logged, until it is active or failed
+        (browsers cannot set headers on a websocket: the access token comes as ``?token=``)."""
+        try:
+            cid = read_token(secret, ws.query_params.get("token", ""))
+        except ValueError:
+            await ws.close(code=4401)
+            return
+        if store.one("SELECT id FROM deployments WHERE id=? AND customer_id=?", (dep_id, cid)) is None:
+            await ws.close(code=4404)
+            return
+        await ws.accept()
+        cursor = 0
+        try:
+            while True:
+                with progress_mu:
+                    msgs = progress[dep_id][cursor:]
+                for m in msgs:
+                    await ws.send_json(m)
+                cursor += len(msgs)
+                row = store.one("SELECT status FROM deployments WHERE id=?", (dep_id,))
+                if not msgs and row["status"] in ("active", "failed"):
+                    break
+                await asyncio.sleep(0.05)
+        except WebSocketDisconnect:
+            return
+        await ws.close()
 
     @app.post("/api/deploy/{dep_id}/register")
     def register(dep_id: int, body: RegisterIn):

@@ -196,6 +196,18 @@ def test_deploy_over_ssh(env):
     assert all("pw" != e["message"] and key not in e["message"] for e in st["log"])
     assert any("B200" in e["message"] for e in st["log"])
     assert any("-m axropus_deploy_b200 serve --model llama3-8b" in cmd for cmd in FakeSSH.commands)
+    # the websocket replays the whole progress log and closes once the deployment is active
+    with c.websocket_connect("/api/deploy/stream/1?token=" + h["Authorization"][7:]) as ws:
+        msgs = []
+        try:
+            while True:
+                msgs.append(ws.receive_json())
+        except Exception:
+            pass
+    assert [m["step"] for m in msgs] == [e["step"] for e in st["log"]]
+    with pytest.raises(Exception):
+        with c.websocket_connect("/api/deploy/stream/1?token=bad") as ws:
+            ws.receive_json()
     # the key's traffic now goes to the deployed node
     c.post("/v1/completions", json={"prompt": "x"}, headers={"x-api-key": key})
     assert seen[-1][1] == "http://gpu1:8000/v1/completions"
