@@ -324,8 +324,12 @@ class LoraLearningLoop:
             lora.load_state_dict(live.state_dict())
         opt = torch.optim.AdamW(lora.parameters(), lr=self.lr)
         loss = 0.0
-        for _ in range(self.epochs):
-            loss = dpo_step(self.lm, lora, opt, ex, self.beta) if kind == "dpo" else sft_step(self.lm, lora, opt, ex)
+        try:
+            for _ in range(self.epochs):
+                loss = (dpo_step(self.lm, lora, opt, ex, self.beta) if kind == "dpo"
+                        else sft_step(self.lm, lora, opt, ex))
+        except Exception as e:  # the live adapters stay; the rows stay unconsumed for the next cycle
+            return TrainingResult(len(ex), 0.0, 0.0, None, time.perf_counter() - t0, True, f"fine-tune error: {e}")
         with self._swap:
             self.lm.lora = lora
         self.ledger.scored(len(rows), consume=True)

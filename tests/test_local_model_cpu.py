@@ -181,3 +181,22 @@ def test_learning_loop_skips_without_data():
     assert r.skipped and "no scored" in r.skip_reason
     loop.start()
     loop.stop()
+
+
+def test_learning_loop_survives_training_error(monkeypatch):
+    import axropus_deploy_b200.policy.local_model as lm_mod
+
+    m = _model()
+    lm = LocalReasoningModel(m, max_prompt_tokens=24)
+    led = RewardLedger()
+    v = np.zeros(WIDTH, np.float32)
+    for d, o in ((Decision(spec_decode_depth=8), "spec_high_acceptance"), (Decision(spec_decode_depth=2), "spec_low_acceptance")):
+        led.record_outcome(led.record_decision(d, v), o)
+    loop = LoraLearningLoop(lm, led, level=4, min_examples=1)
+
+    def boom(*a, **k):
+        raise RuntimeError("out of memory")
+    monkeypatch.setattr(lm_mod, "dpo_step", boom)
+    r = loop.run_once()
+    assert r.skipped and "fine-tune error" in r.skip_reason and lm.lora is None
+    assert len(led.scored(10, consume=False)) == 2  # still there for the next cycle
