@@ -440,8 +440,10 @@ def create_app(store: Optional[Store] = None, secret: Optional[str] = None, *, d
         url = _upstream_url(key) + path
         body = await request.body()
         client = httpx.AsyncClient(transport=upstream, timeout=600.0)
+        # the node was started with the owner's key (``axropus serve --api-key``): present it
         req = client.build_request(request.method, url, content=body,
-                                   headers={"content-type": request.headers.get("content-type", "application/json")})
+                                   headers={"content-type": request.headers.get("content-type", "application/json"),
+                                            "authorization": "Bearer " + key["key"]})
         resp = await client.send(req, stream=True)
         ctype = resp.headers.get("content-type", "application/json")
         if ctype.startswith("text/event-stream"):

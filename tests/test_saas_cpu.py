@@ -16,7 +16,7 @@ def _upstream():
     seen = []
 
     def handler(req: httpx.Request):
-        seen.append((req.method, str(req.url), req.content))
+        seen.append((req.method, str(req.url), req.content, req.headers.get("authorization")))
         if req.url.path == "/v1/models":
             return httpx.Response(200, json={"data": [{"id": "llama3-8b"}]})
         body = json.loads(req.content)
@@ -137,7 +137,7 @@ def test_inference_proxy_and_rate_limit(env):
     r = c.post("/v1/completions", json={"prompt": "hello", "max_tokens": 4},
                headers={"Authorization": "Bearer " + key})
     assert r.status_code == 200 and r.json()["echo"]["prompt"] == "hello"
-    assert seen[-1][1] == "http://node:8000/v1/completions"
+    assert seen[-1][1] == "http://node:8000/v1/completions" and seen[-1][3] == "Bearer " + key
     s = c.post("/v1/chat/completions", json={"messages": [], "stream": True}, headers={"x-api-key": key})
     assert s.headers["content-type"].startswith("text/event-stream") and b"[DONE]" in s.content
     assert c.get("/v1/models", headers={"x-api-key": key}).json()["data"][0]["id"] == "llama3-8b"
