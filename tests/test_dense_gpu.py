@@ -130,6 +130,27 @@ def test_pair_kernel_store(M, NK):
     _close(pair, one, tol=1e-2)
 
 
+@pytest.mark.parametrize("epi", ["store", "resid"])
+def test_pair_kernel_many_waves(epi):
+    """8320 x 4096 output (the o / down projections of an 8320-token prefill): 528 tiles of
+    256 x 256, seven full waves of 74 pairs and a partial eighth, every column block checked."""
+    M, N, K = 8320, 4096, 640
+    x = _rand(M, K, seed=31)
+    w = _rand(N, K, std=0.05, seed=32)
+    ref = x.float() @ w.float().t()
+    if epi == "store":
+        out = dense.linear(x, w)
+    else:
+        res = _rand(M, N, seed=33)
+        ref = ref + res.float()
+        out = dense.linear(x, w, "resid", out=res, res=res)
+    _close(out, ref)
+    # every 128-column block is right (not only the largest element)
+    err = (out.float() - ref).abs().amax(dim=0).view(-1, 128).amax(dim=1)
+    scale = ref.abs().amax(dim=0).view(-1, 128).amax(dim=1)
+    assert bool((err / scale < 2e-2).all())
+
+
 @pytest.mark.parametrize("M", [300, 2049])
 def test_pair_kernel_epilogues(M):
     K, Fd, N = 1024, 768, 1024
