@@ -184,9 +184,13 @@ class LocalReasoningModel:
         return [b % self.model.cfg.vocab for b in text.encode()]  # bytes as token ids
 
     def prompt(self, v: np.ndarray) -> List[int]:
-        named = {k: round(float(v[i]), 3) for k, i in vars(Slot).items() if k.isupper() and i < len(v)}
-        text = "state " + json.dumps(named, separators=(",", ":")) + " decision "
-        return self.encode(text)[-self.max_prompt_tokens:]
+        """``state {slot: value, ...} decision `` over the non-zero named slots (in slot
+        order), cut to ``max_prompt_tokens`` from the front so the early slots stay."""
+        named = {k: round(float(v[i]), 3) for k, i in sorted(((k, i) for k, i in vars(Slot).items()
+                                                              if k.isupper() and isinstance(i, int)), key=lambda x: x[1])
+                 if i < len(v) and abs(float(v[i])) >= 5e-4}
+        body = self.encode("state " + json.dumps(named, separators=(",", ":")))
+        return body[:self.max_prompt_tokens] + self.encode(" decision ")
 
     def scores(self, v: np.ndarray, lora: Optional[LoRA] = None,
                candidates: Optional[Sequence[Decision]] = None) -> torch.Tensor:

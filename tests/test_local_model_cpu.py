@@ -200,3 +200,22 @@ def test_learning_loop_survives_training_error(monkeypatch):
     r = loop.run_once()
     assert r.skipped and "fine-tune error" in r.skip_reason and lm.lora is None
     assert len(led.scored(10, consume=False)) == 2  # still there for the next cycle
+
+
+def test_dpo_learns_a_state_conditional_choice():
+    """Two states that differ in one slot want opposite decisions; DPO on both pairs makes
+    the model's choice follow the slot (the prompt keeps that slot)."""
+    from axropus_deploy_b200.policy.state import Slot
+
+    m = _model()
+    shallow, deep = Decision(spec_decode_depth=2), Decision(spec_decode_depth=8)
+    lm = LocalReasoningModel(m, candidates=[shallow, deep], max_prompt_tokens=48)
+    lo, hi = np.zeros(WIDTH, np.float32), np.zeros(WIDTH, np.float32)
+    lo[Slot.HIT_RATE], hi[Slot.HIT_RATE] = 0.1, 0.9
+    assert lm.prompt(lo) != lm.prompt(hi)
+    lora = LoRA(m, r=4, alpha=8)
+    lm.lora = lora
+    opt = torch.optim.Adam(lora.parameters(), lr=2e-2)
+    for _ in range(30):
+        dpo_step(lm, lora, opt, [(hi, deep, shallow), (lo, shallow, deep)], beta=0.5)
+    assert lm.decide(hi).spec_decode_depth == 8 and lm.decide(lo).spec_decode_depth == 2
