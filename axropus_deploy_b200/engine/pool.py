@@ -106,6 +106,8 @@ class DraftPool:
             t0 = time.perf_counter_ns()
             if isinstance(d, ModelDrafter):
                 out = d.propose_batch(eng, reqs, k)
+            elif isinstance(d, NgramDrafter):
+                out = [d.propose_req(r, k) for r in reqs]
             else:
                 out = [d.propose(r.prompt + r.output, k) for r in reqs]
             return out, time.perf_counter_ns() - t0
@@ -128,7 +130,7 @@ class DraftPool:
 
     def forget(self, req_id: str) -> None:
         for d in self.drafters:
-            if isinstance(d, ModelDrafter):
+            if hasattr(d, "forget"):
                 d.forget(req_id)
 
     def rewind(self, req_id: str, pos: int) -> None:

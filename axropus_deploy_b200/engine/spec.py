@@ -38,10 +38,40 @@ from ..ops.kvcache import PAGE
 class NgramDrafter:
     """Prompt-lookup drafting over the last ``window`` tokens of a sequence. ``skip`` > 0
     proposes what followed an earlier occurrence of the tail instead of the most recent
-    one (a second candidate for multi-draft verification)."""
+    one (a second candidate for multi-draft verification).
+
+    :meth:`propose_req` keeps one native incremental index per request
+    (``csrc/native/ngram.cpp``: every appended token adds the n-grams ending at it, a
+    proposal is a hash lookup) and feeds it only the tokens generated since the last call,
+    so a step costs O(new tokens) instead of a scan of the window; it releases the GIL, so
+    the drafters of a pool run in parallel threads. :meth:`propose` is the stateless scan
+    (any token list) and the oracle of the index."""
 
     def __init__(self, max_n: int = 3, min_n: int = 1, window: int = 4096, skip: int = 0):
         self.max_n, self.min_n, self.window, self.skip = max_n, min_n, window, skip
+        self._tables: Dict[str, object] = {}
+
+    def propose_req(self, r, k: int) -> List[int]:
+        """``propose(r.prompt + r.output, k)`` through the request's native index."""
+        ent = self._tables.get(r.req_id)
+        n_prompt, total = len(r.prompt), len(r.prompt) + len(r.output)
+        if ent is None or ent[1] > total:
+            from .._native_loader import native
+
+            # only the tokens a proposal can still reach are indexed: the last window + max_n
+            start = max(0, total - self.window - self.max_n)
+            ent = self._tables[r.req_id] = [native().NgramTable(self.max_n, self.min_n, self.window), start]
+        t, have = ent
+        if have < n_prompt:
+            t.extend(np.asarray(r.prompt[have:], dtype=np.int32))
+            t.extend(np.asarray(r.output, dtype=np.int32))
+        elif have < total:
+            t.extend(np.asarray(r.output[have - n_prompt:], dtype=np.int32))
+        ent[1] = total
+        return t.propose(k, self.skip)
+
+    def forget(self, req_id: str) -> None:
+        self._tables.pop(req_id, None)
 
     def propose(self, tokens: Sequence[int], k: int) -> List[int]:
         toks = np.asarray(tokens[-self.window:], dtype=np.int64)
@@ -147,6 +177,8 @@ class SpecDecoder:
         k = max(1, min(k, 64))
         if isinstance(self.drafter, ModelDrafter):
             drafts = self.drafter.propose_batch(eng, reqs, k)
+        elif isinstance(self.drafter, NgramDrafter):
+            drafts = [self.drafter.propose_req(r, k) for r in reqs]
         else:
             drafts = [self.drafter.propose(r.prompt + r.output, k) for r in reqs]
         toks, pos, slots, cu, lens = [], [], [], [0], []
@@ -177,7 +209,7 @@ class SpecDecoder:
                 if r.state != "running":
                     break
                 eng._append(r, int(t), done)
-            if r.state != "running" and isinstance(self.drafter, ModelDrafter):
+            if r.state != "running" and hasattr(self.drafter, "forget"):
                 self.drafter.forget(r.req_id)
         n = len(reqs)
         self.stat["steps"] += 1

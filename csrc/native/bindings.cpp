@@ -6,6 +6,7 @@
 
 #include "amf_store.h"
 #include "fnv.h"
+#include "ngram.h"
 #include "runtime.h"
 #include "shard_dir.h"
 
@@ -443,4 +444,5 @@ PYBIND11_MODULE(_native, m) {
       });
 
   bind_runtime(m);
+  bind_ngram(m);
 }
