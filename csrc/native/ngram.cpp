@@ -4,13 +4,14 @@
 // are skipped by the walk (the window only moves forward).
 #include "ngram.h"
 
+#ifndef AXR_NO_PYBIND
 #include <pybind11/numpy.h>
 #include <pybind11/stl.h>
+namespace py = pybind11;
+#endif
 
 #include <algorithm>
 #include <stdexcept>
-
-namespace py = pybind11;
 
 namespace axr {
 
@@ -74,6 +75,7 @@ std::vector<std::int32_t> NgramTable::propose(int k, int skip) const {
   return out;
 }
 
+#ifndef AXR_NO_PYBIND
 void bind_ngram(py::module_& m) {
   py::class_<NgramTable>(m, "NgramTable")
       .def(py::init<int, int, int>(), py::arg("max_n"), py::arg("min_n"), py::arg("window"))
@@ -96,5 +98,7 @@ void bind_ngram(py::module_& m) {
            py::arg("k"), py::arg("skip") = 0)
       .def("__len__", &NgramTable::size);
 }
+
+#endif
 
 }  // namespace axr

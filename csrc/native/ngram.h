@@ -2,7 +2,9 @@
 // tokens that followed the most recent earlier occurrence of the sequence's tail.
 #pragma once
 
+#ifndef AXR_NO_PYBIND
 #include <pybind11/pybind11.h>
+#endif
 
 #include <cstdint>
 #include <unordered_map>
@@ -29,6 +31,8 @@ class NgramTable {
   std::vector<std::unordered_map<std::uint64_t, std::vector<std::int32_t>>> ends_;
 };
 
+#ifndef AXR_NO_PYBIND
 void bind_ngram(pybind11::module_& m);
+#endif
 
 }  // namespace axr

@@ -5,12 +5,15 @@
 //   * ShardDirectory (process-private): 6 threads insert / commit / abort / look up
 //     (pinned) / unpin / remove / reclaim on 2 shards; afterwards every READY entry's
 //     slots are distinct across the shard and the free-slot count adds up.
+//   * NgramTable: 4 threads each grow their own tables token by token and check every
+//     proposal against a plain scan of the window.
 //   * AmfStore (temporary directory): 4 threads store entries and look up prefixes of
 //     shared and private token streams while a fifth thread flushes the index and
 //     evicts expired entries; the index then reloads with the same entry count.
 //
 // Exit code 0 = every check held; the sanitizers abort the process on a data race,
 // leak, overflow or undefined behaviour.
+#include <algorithm>
 #include <atomic>
 #include <chrono>
 #include <cstdio>
@@ -22,6 +25,7 @@
 #include <vector>
 
 #include "../amf_store.h"
+#include "../ngram.h"
 #include "../shard_dir.h"
 
 using namespace axr;
@@ -171,12 +175,58 @@ static void amf_store_stress(const std::string& root) {
   std::printf("amf_store entries=%llu\n", static_cast<unsigned long long>(n_entries));
 }
 
+// Proposal by scanning the window (the definition the index must reproduce).
+static std::vector<std::int32_t> scan_propose(const std::vector<std::int32_t>& all, int max_n, int min_n, int window,
+                                              int k, int skip) {
+  const long long L = static_cast<long long>(all.size()), lo = std::max(0LL, L - window);
+  for (int n = max_n; n >= min_n; --n) {
+    if (L - lo <= n) continue;
+    int left = skip;
+    for (long long i = L - n - 1; i >= lo; --i) {
+      bool eq = true;
+      for (int j = 0; j < n && eq; ++j) eq = all[i + j] == all[L - n + j];
+      if (!eq) continue;
+      if (left > 0) { --left; continue; }
+      std::vector<std::int32_t> out(all.begin() + i + n, all.begin() + std::min(L, i + n + k));
+      while (static_cast<int>(out.size()) < k) out.push_back(out.back());
+      return out;
+    }
+  }
+  return std::vector<std::int32_t>(k, L ? all.back() : 0);
+}
+
+static void ngram_stress() {
+  std::vector<std::thread> ts;
+  for (int t = 0; t < 4; ++t) {
+    ts.emplace_back([t] {
+      std::mt19937 rng(1234 + t);
+      for (int trial = 0; trial < 20; ++trial) {
+        const int vocab = 2 + static_cast<int>(rng() % 40), max_n = 1 + static_cast<int>(rng() % 5);
+        const int min_n = 1 + static_cast<int>(rng() % max_n), window = 8 + static_cast<int>(rng() % 300);
+        NgramTable tab(max_n, min_n, window);
+        std::vector<std::int32_t> all;
+        for (int step = 0; step < 300; ++step) {
+          const int add = 1 + static_cast<int>(rng() % 4);
+          std::vector<std::int32_t> fresh;
+          for (int a = 0; a < add; ++a) fresh.push_back(static_cast<std::int32_t>(rng() % vocab));
+          tab.extend(fresh.data(), fresh.size());
+          all.insert(all.end(), fresh.begin(), fresh.end());
+          const int k = 1 + static_cast<int>(rng() % 8), skip = static_cast<int>(rng() % 3);
+          CHECK(tab.propose(k, skip) == scan_propose(all, max_n, min_n, window, k, skip));
+        }
+      }
+    });
+  }
+  for (auto& th : ts) th.join();
+}
+
 int main(int argc, char** argv) {
   if (argc < 2) {
     std::fprintf(stderr, "usage: %s <empty temp dir>\n", argv[0]);
     return 2;
   }
   shard_dir_stress();
+  ngram_stress();
   amf_store_stress(argv[1]);
   if (g_fail.load() != 0) {
     std::fprintf(stderr, "%d check(s) failed\n", g_fail.load());

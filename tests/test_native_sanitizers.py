@@ -1,4 +1,4 @@
-"""Host runtime under sanitizers: the shard directory and the AMF disk store are built
+"""Host runtime under sanitizers: the shard directory, the AMF disk store and the n-gram index are built
 from source with AddressSanitizer + UndefinedBehaviorSanitizer and with ThreadSanitizer,
 and a multi-threaded stress program (csrc/native/tests/native_stress.cpp) runs against
 each build. A data race, leak, overflow or undefined behaviour aborts the program."""
@@ -9,7 +9,7 @@ import subprocess
 import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-SRC = [os.path.join(ROOT, "csrc", "native", f) for f in ("tests/native_stress.cpp", "amf_store.cpp", "shard_dir.cpp")]
+SRC = [os.path.join(ROOT, "csrc", "native", f) for f in ("tests/native_stress.cpp", "amf_store.cpp", "shard_dir.cpp", "ngram.cpp")]
 
 
 @pytest.mark.skipif(shutil.which("g++") is None, reason="needs g++")
@@ -17,7 +17,7 @@ SRC = [os.path.join(ROOT, "csrc", "native", f) for f in ("tests/native_stress.cp
 def test_native_store_under_sanitizer(san, tmp_path):
     exe = tmp_path / "native_stress"
     build = subprocess.run(["g++", "-std=c++17", "-O1", "-g", f"-fsanitize={san}", "-fno-omit-frame-pointer",
-                            "-I", os.path.join(ROOT, "csrc", "native"), *SRC, "-o", str(exe), "-lpthread", "-lrt"],
+                            "-DAXR_NO_PYBIND", "-I", os.path.join(ROOT, "csrc", "native"), *SRC, "-o", str(exe), "-lpthread", "-lrt"],
                            capture_output=True, text=True, timeout=600)
     assert build.returncode == 0, build.stderr[-3000:]
     data = tmp_path / "amf"
