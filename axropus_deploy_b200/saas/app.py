@@ -143,8 +143,13 @@ def create_app(store: Optional[Store] = None, secret: Optional[str] = None, *, d
                upstream: Optional[httpx.AsyncBaseTransport] = None, ssh_connect: Callable = _paramiko_connect,
                http_get: Callable[[str], int] = _http_get, bench_dir: Optional[str] = None,
                rate_limit: int = 600, rate_window_s: float = 60.0, register_wait_s: float = 600.0,
-               install_cmd: str = "{py} -m pip install --upgrade axropus-deploy-b200") -> FastAPI:
+               install_cmd: str = "{py} -m pip install --upgrade axropus-deploy-b200",
+               backend_url: Optional[str] = None) -> FastAPI:
+    """``backend_url``: this backend's address as the deployed nodes reach it; when set, a
+    deployment also starts the node agent (``saas/agent.py``), which registers the node and
+    reports its usage."""
     store = store or Store(os.environ.get("AXROPUS_SAAS_DB", ":memory:"))
+    backend_url = backend_url if backend_url is not None else os.environ.get("AXROPUS_SAAS_PUBLIC_URL", "")
     secret = secret or os.environ.get("AXROPUS_SAAS_SECRET") or os.urandom(32).hex()
     limiter = RateLimiter()
     progress: Dict[int, List[Dict[str, Any]]] = defaultdict(list)
@@ -514,6 +519,13 @@ def create_app(store: Optional[Store] = None, secret: Optional[str] = None, *, d
             code, out, err = _run(ssh, start)
             if code != 0:
                 raise RuntimeError("server start failed: " + (err or out)[-400:])
+            if backend_url:
+                agent = (f"nohup {py} -m axropus_deploy_b200.saas.agent --backend {shlex.quote(backend_url)} "
+                         f"--deployment-id {dep_id} --api-key {shlex.quote(key_value)} --port {int(body.serve_port)} "
+                         f"--model-family {shlex.quote(body.model_family)} > axropus_agent.log 2>&1 &")
+                code, out, err = _run(ssh, agent)
+                if code != 0:
+                    raise RuntimeError("agent start failed: " + (err or out)[-400:])
             _log(dep_id, 5, "success", "server started; waiting for the node to register", 0.70, mask)
             url = None
             t_end = time.monotonic() + register_wait_s

@@ -211,3 +211,73 @@ def test_deploy_over_ssh(env):
     # the key's traffic now goes to the deployed node
     c.post("/v1/completions", json={"prompt": "x"}, headers={"x-api-key": key})
     assert seen[-1][1] == "http://gpu1:8000/v1/completions"
+
+
+def test_usage_report_increments():
+    from axropus_deploy_b200.saas.agent import usage_report
+
+    prev = {"prefill_tokens": 100, "decode_tokens": 50, "restored_tokens": 0, "local_cached_tokens": 0,
+            "cold_prefill_tokens": 100, "amf": {"lookups": 1, "misses": 1}, "spec": {"drafted": 10, "accepted": 5}}
+    cur = {"prefill_tokens": 8500, "decode_tokens": 1050, "restored_tokens": 8192, "local_cached_tokens": 8192,
+           "cold_prefill_tokens": 8292, "amf": {"lookups": 5, "misses": 2}, "spec": {"drafted": 110, "accepted": 85}}
+    r = usage_report(prev, cur, 10.0, 2)
+    assert r["tokens_processed"] == 8400 + 1000 and r["prefix_skipped"] == 16384
+    assert r["amf_hit_rate"] == pytest.approx(3 / 4) and r["spec_acceptance_rate"] == pytest.approx(0.8)
+    assert r["compute_saved_pct"] == pytest.approx(16384 / (16384 + 8192))
+    assert r["effective_tps"] == pytest.approx(940.0) and r["gpu_count"] == 2 and r["decode_accelerated"] == 80
+
+
+def test_agent_registers_and_reports(env):
+    from axropus_deploy_b200.saas.agent import Agent
+
+    c, seen = env
+    h, key = _signup(c)
+    c.post("/api/deploy", json={"host": "gpu2", "username": "ops", "password": "pw"}, headers=h)
+
+    def post_json(url, payload):
+        r = c.post("/" + url.split("://", 1)[1].split("/", 1)[1], json=payload)
+        if r.status_code >= 400:
+            raise RuntimeError(r.text)
+        return r.json()
+
+    snaps = iter([{"prefill_tokens": 0, "decode_tokens": 0},
+                  {"prefill_tokens": 8320, "decode_tokens": 128, "restored_tokens": 8192, "cold_prefill_tokens": 128}])
+
+    def get_json(url, headers=None):
+        if url.endswith("/healthz"):
+            return {"ok": True}
+        return next(snaps)
+
+    t = iter([0.0, 0.0, 60.0])
+    a = Agent("http://backend", key, 1, 8000, "http://gpu2:8000", interval_s=60, post_json=post_json,
+              get_json=get_json, clock=lambda: next(t, 60.0))
+    assert a.wait_healthy(5) and a.register()
+    deadline = time.time() + 10
+    while time.time() < deadline:  # the deployment thread sees the registration and goes active
+        if c.get("/api/deploy/status/1", headers=h).json()["deployment"]["status"] == "active":
+            break
+        time.sleep(0.02)
+    assert c.get("/api/deploy/status/1", headers=h).json()["deployment"]["inference_url"] == "http://gpu2:8000"
+    assert a.report_once() is None  # baseline
+    body = a.report_once()
+    assert body["tokens_processed"] == 8448 and body["prefix_skipped"] == 8192
+    d = c.get("/api/dashboard", headers=h).json()
+    assert d["total_tokens_processed"] == 8448 and d["total_prefix_skipped"] == 8192
+
+
+def test_deploy_starts_the_agent_when_the_backend_url_is_known(tmp_path):
+    FakeSSH.commands = []
+    app = create_app(Store(str(tmp_path / "db2.sqlite")), "k", ssh_connect=lambda *a: FakeSSH(),
+                     http_get=lambda url: 200, register_wait_s=0.2, backend_url="https://backend.example")
+    c = TestClient(app)
+    h, key = _signup(c, "agent@x.io")
+    assert c.post("/api/deploy", json={"host": "gpu3", "username": "ops", "password": "pw"}, headers=h).status_code == 200
+    deadline = time.time() + 10
+    while time.time() < deadline:
+        st = c.get("/api/deploy/status/1", headers=h).json()
+        if st["deployment"]["status"] in ("active", "failed"):
+            break
+        time.sleep(0.02)
+    agent = [cmd for cmd in FakeSSH.commands if "axropus_deploy_b200.saas.agent" in cmd]
+    assert len(agent) == 1 and "--backend https://backend.example" in agent[0] and "--deployment-id 1" in agent[0]
+    assert st["deployment"]["status"] == "failed"  # nobody registered within the 0.2 s given here
