@@ -219,3 +219,21 @@ def test_dpo_learns_a_state_conditional_choice():
     for _ in range(30):
         dpo_step(lm, lora, opt, [(hi, deep, shallow), (lo, shallow, deep)], beta=0.5)
     assert lm.decide(hi).spec_decode_depth == 8 and lm.decide(lo).spec_decode_depth == 2
+
+
+def test_adaptive_policy_consults_the_local_model():
+    from axropus_deploy_b200.policy import AdaptivePolicy
+
+    m = _model()
+    lm = LocalReasoningModel(m, candidates=[Decision(spec_decode_depth=12, cache_admission=False)], max_prompt_tokens=32)
+    pol = AdaptivePolicy(model=lm, model_primary=True)
+    d = pol.decide(np.zeros(WIDTH, np.float32), "t1", "abc")
+    assert d.spec_decode_depth == 12 and d.cache_admission is False and pol.stat["model"] == 1
+
+    class Broken(LocalReasoningModel):
+        def scores(self, *a, **k):
+            raise RuntimeError("device lost")
+
+    pol2 = AdaptivePolicy(model=Broken(m), model_primary=True)
+    d2 = pol2.decide(np.zeros(WIDTH, np.float32), "t1", "abc")  # falls back to the local rules
+    assert pol2.stat["model_failures"] == 1 and pol2.stat["local"] == 1 and not d2.validate()
