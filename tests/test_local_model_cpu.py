@@ -237,3 +237,31 @@ def test_adaptive_policy_consults_the_local_model():
     pol2 = AdaptivePolicy(model=Broken(m), model_primary=True)
     d2 = pol2.decide(np.zeros(WIDTH, np.float32), "t1", "abc")  # falls back to the local rules
     assert pol2.stat["model_failures"] == 1 and pol2.stat["local"] == 1 and not d2.validate()
+
+
+def test_fedavg_of_lora_deltas():
+    """Two nodes tune copies of the same adapters on different pairs; the sample-weighted
+    FedAvg of their deltas (the federated loop's payload) loads back into an adapter."""
+    from axropus_deploy_b200.policy.learn import fedavg, state_delta
+
+    m = _model()
+    lm = LocalReasoningModel(m, candidates=[Decision(spec_decode_depth=2), Decision(spec_decode_depth=8)],
+                             max_prompt_tokens=32)
+    base = LoRA(m, r=4)
+    base_state = {k: v.clone() for k, v in base.state_dict().items()}
+    v = np.linspace(0, 1, WIDTH, dtype=np.float32)
+    deltas = []
+    for node, (good, bad), n in ((0, (1, 0), 3), (1, (0, 1), 1)):
+        lora = LoRA(m, r=4)
+        lora.load_state_dict(base_state)
+        opt = torch.optim.Adam(lora.parameters(), lr=1e-2)
+        for _ in range(3):
+            dpo_step(lm, lora, opt, [(v, lm.candidates[good], lm.candidates[bad])])
+        deltas.append((state_delta(lora, base_state), n))
+    avg = fedavg(deltas)
+    merged = LoRA(m, r=4)
+    merged.load_state_dict({k: base_state[k] + torch.as_tensor(avg[k]) for k in base_state})
+    for k, t in merged.state_dict().items():
+        want = base_state[k] + (3 * torch.as_tensor(deltas[0][0][k]) + torch.as_tensor(deltas[1][0][k])) / 4
+        torch.testing.assert_close(t, want, rtol=1e-5, atol=1e-6)
+    assert any(float(np.abs(a).max()) > 0 for a in avg.values())
