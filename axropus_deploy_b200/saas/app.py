@@ -449,7 +449,11 @@ def create_app(store: Optional[Store] = None, secret: Optional[str] = None, *, d
         req = client.build_request(request.method, url, content=body,
                                    headers={"content-type": request.headers.get("content-type", "application/json"),
                                             "authorization": "Bearer " + key["key"]})
-        resp = await client.send(req, stream=True)
+        try:
+            resp = await client.send(req, stream=True)
+        except httpx.HTTPError as e:
+            await client.aclose()
+            raise HTTPException(502, f"serving node unavailable: {type(e).__name__}") from None
         ctype = resp.headers.get("content-type", "application/json")
         if ctype.startswith("text/event-stream"):
             async def gen():

@@ -281,3 +281,24 @@ def test_deploy_starts_the_agent_when_the_backend_url_is_known(tmp_path):
     agent = [cmd for cmd in FakeSSH.commands if "axropus_deploy_b200.saas.agent" in cmd]
     assert len(agent) == 1 and "--backend https://backend.example" in agent[0] and "--deployment-id 1" in agent[0]
     assert st["deployment"]["status"] == "failed"  # nobody registered within the 0.2 s given here
+
+
+def test_proxy_reports_an_unreachable_node(tmp_path):
+    def down(req):
+        raise httpx.ConnectError("connection refused", request=req)
+
+    app = create_app(Store(str(tmp_path / "db3.sqlite")), "k", default_upstream="http://node:8000",
+                     upstream=httpx.MockTransport(down))
+    c = TestClient(app)
+    _, key = _signup(c, "down@x.io")
+    r = c.post("/v1/completions", json={"prompt": "x"}, headers={"x-api-key": key})
+    assert r.status_code == 502 and "unavailable" in r.json()["detail"]
+
+
+def test_enterprise_usage_is_not_billed_per_token(env):
+    c, _ = env
+    h, _ = _signup(c, "ent@x.io")
+    ent = c.post("/api/keys/generate", json={"tier": "enterprise"}, headers=h).json()["key"]
+    assert c.post("/api/metrics", json=_metric(ent, tokens_processed=5_000_000)).status_code == 200
+    b = c.get("/api/billing/summary", headers=h).json()["current_period"]
+    assert b["enterprise_tokens"] == 5_000_000 and b["amount_cents"] == 0 and b["pricing"] == "custom annual pricing"
