@@ -101,12 +101,18 @@ def _rms(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
     return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * w.float()
 
 
-def lm_forward(model, tokens: torch.Tensor, lora: Optional[LoRA] = None) -> torch.Tensor:
+def lm_forward(model, tokens: torch.Tensor, lora: Optional[LoRA] = None, start: int = 0,
+               past: Optional[List[Tuple[torch.Tensor, torch.Tensor]]] = None, return_kv: bool = False):
     """Differentiable causal forward of a dense ``LlamaModel`` over ``tokens`` [B, T] (or
     [T]) -> logits [B, T, vocab] (or [T, vocab]) in fp32, with ``lora``'s adapters applied
     unless they are merged. Rows are independent; right padding does not change the logits
     of the positions before it. Matmuls run in fp32 on the CPU and in the weights' dtype on
-    the GPU (fp32 accumulation)."""
+    the GPU (fp32 accumulation).
+
+    ``past`` (per layer (K, V) [1, P, Hq, D] of a shared prefix, from a call with
+    ``return_kv=True``) continues every row after that prefix: positions start at ``start``
+    (= P) and each row attends to the whole prefix, then causally to itself. With
+    ``return_kv`` the result is (logits, per-layer (K, V) of this call's tokens)."""
     cfg = model.cfg
     squeeze = tokens.dim() == 1
     if squeeze:
@@ -114,11 +120,16 @@ def lm_forward(model, tokens: torch.Tensor, lora: Optional[LoRA] = None) -> torc
     B, T = tokens.shape
     Hq, Hkv, D = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
     cd = torch.float32 if tokens.device.type == "cpu" else model.dtype
-    pos = torch.arange(T, device=tokens.device)
+    pos = torch.arange(start, start + T, device=tokens.device)
     cs = model.cos_sin.to(tokens.device)[pos].float()
     half = D // 2
     cos, sin = cs[None, :, None, :half], cs[None, :, None, half:]
     use = lora is not None and not lora.merged
+    P = past[0][0].shape[1] if past else 0
+    mask = None
+    if P:  # prefix fully visible, own tokens causal
+        own = torch.ones(T, T, dtype=torch.bool, device=tokens.device).tril()
+        mask = torch.cat((torch.ones(T, P, dtype=torch.bool, device=tokens.device), own), dim=1)
 
     def proj(x, li, name, w):
         y = (x.to(cd) @ w.to(cd).t()).float()
@@ -134,6 +145,7 @@ def lm_forward(model, tokens: torch.Tensor, lora: Optional[LoRA] = None) -> torc
 
     h = model.embed[tokens.long()].float()
     rep = Hq // Hkv
+    kv_out = []
     for li, lw in enumerate(model.layers):
         if lw.w_gate_up is None:
             raise ValueError("lm_forward: dense (non-MoE) models only")
@@ -142,8 +154,16 @@ def lm_forward(model, tokens: torch.Tensor, lora: Optional[LoRA] = None) -> torc
         q = rope(qkv[:, :, :Hq])
         k = rope(qkv[:, :, Hq:Hq + Hkv]).repeat_interleave(rep, dim=2)
         v = qkv[:, :, Hq + Hkv:].repeat_interleave(rep, dim=2)
-        a = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
-                                           is_causal=True).transpose(1, 2)
+        if return_kv:
+            kv_out.append((k, v))
+        if P:
+            k = torch.cat((past[li][0].expand(B, -1, -1, -1), k), dim=1)
+            v = torch.cat((past[li][1].expand(B, -1, -1, -1), v), dim=1)
+            a = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
+                                               attn_mask=mask).transpose(1, 2)
+        else:
+            a = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
+                                               is_causal=True).transpose(1, 2)
         h = h + proj(a.reshape(B, T, Hq * D), li, "wo", lw.wo)
         x = _rms(h, lw.mlp_norm, cfg.rms_eps)
         gu = proj(x, li, "w_gate_up", lw.w_gate_up)
@@ -152,7 +172,8 @@ def lm_forward(model, tokens: torch.Tensor, lora: Optional[LoRA] = None) -> torc
         act = (F.silu(g4[..., 0, :]) * g4[..., 1, :]).reshape(B, T, n // 2)
         h = h + proj(act, li, "w_down", lw.w_down)
     logits = (_rms(h, model.final_norm, cfg.rms_eps).to(cd) @ model.lm_head.to(cd).t()).float()
-    return logits[0] if squeeze else logits
+    logits = logits[0] if squeeze else logits
+    return (logits, kv_out) if return_kv else logits
 
 
 def candidate_decisions() -> List[Decision]:
@@ -194,20 +215,24 @@ class LocalReasoningModel:
 
     def scores(self, v: np.ndarray, lora: Optional[LoRA] = None,
                candidates: Optional[Sequence[Decision]] = None) -> torch.Tensor:
-        """Log-likelihood of every candidate given the state prompt [len(candidates)]: one
-        batched forward, one right-padded row per candidate."""
+        """Log-likelihood of every candidate given the state prompt [len(candidates)]: the
+        prompt runs once, and all candidates (right-padded rows) continue from its K/V."""
         p = self.prompt(v)
         cands = [self.encode(render(d)) for d in (candidates if candidates is not None else self.candidates)]
-        T = len(p) + max(len(c) for c in cands)
-        rows = [p + c + [0] * (T - len(p) - len(c)) for c in cands]
         dev = self.model.embed.device
-        toks = torch.tensor(rows, dtype=torch.long, device=dev)
-        mask = torch.zeros(len(cands), T - 1, device=dev)
-        for i, c in enumerate(cands):
-            mask[i, len(p) - 1:len(p) - 1 + len(c)] = 1.0
-        lp = F.log_softmax(lm_forward(self.model, toks, lora)[:, :-1], dim=-1)
-        tok_lp = lp.gather(2, toks[:, 1:, None])[..., 0]
-        return (tok_lp * mask).sum(1)
+        plog, kv = lm_forward(self.model, torch.tensor([p], dtype=torch.long, device=dev), lora, return_kv=True)
+        first = F.log_softmax(plog[0, -1], dim=-1)  # the prompt's last position predicts token 0
+        T = max(len(c) for c in cands)
+        toks = torch.tensor([c + [0] * (T - len(c)) for c in cands], dtype=torch.long, device=dev)
+        out = first[toks[:, 0]]
+        if T > 1:
+            lp = F.log_softmax(lm_forward(self.model, toks[:, :-1], lora, start=len(p), past=kv), dim=-1)
+            tok_lp = lp.gather(2, toks[:, 1:, None])[..., 0]
+            mask = torch.zeros(len(cands), T - 1, device=dev)
+            for i, c in enumerate(cands):
+                mask[i, :len(c) - 1] = 1.0
+            out = out + (tok_lp * mask).sum(1)
+        return out
 
     def decide(self, v: np.ndarray) -> Decision:
         """The highest-scoring candidate; any failure returns a fallback decision (fail closed,

@@ -265,3 +265,28 @@ def test_fedavg_of_lora_deltas():
         want = base_state[k] + (3 * torch.as_tensor(deltas[0][0][k]) + torch.as_tensor(deltas[1][0][k])) / 4
         torch.testing.assert_close(t, want, rtol=1e-5, atol=1e-6)
     assert any(float(np.abs(a).max()) > 0 for a in avg.values())
+
+
+def test_shared_prompt_scores_match_full_sequences():
+    """Scores from one prompt pass + candidates continuing from its K/V equal the
+    log-likelihoods of the whole (prompt + candidate) sequences, adapters included."""
+    import torch.nn.functional as F
+
+    from axropus_deploy_b200.policy.local_model import render
+
+    m = _model()
+    lora = LoRA(m, r=4)
+    with torch.no_grad():
+        for p_ in lora.B.values():
+            p_.normal_(0, 0.05)
+    lm = LocalReasoningModel(m, max_prompt_tokens=40)
+    v = np.random.default_rng(3).random(WIDTH).astype(np.float32)
+    got = lm.scores(v, lora)
+    p = lm.prompt(v)
+    want = []
+    for d in lm.candidates:
+        c = lm.encode(render(d))
+        toks = torch.tensor(p + c)
+        lp = F.log_softmax(lm_forward(m, toks, lora)[len(p) - 1:-1], dim=-1)
+        want.append(lp.gather(1, toks[len(p):, None]).sum())
+    torch.testing.assert_close(got, torch.stack(want), rtol=1e-4, atol=2e-3)
