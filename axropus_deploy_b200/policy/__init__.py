@@ -5,7 +5,8 @@ controllers for batch size. Optional: a worker runs without it."""
 from .decide import AdaptivePolicy, Decision, DecisionExecutor, EndpointModel, read_decode_config
 from .learn import (REWARD_WEIGHTS, DepthPolicy, FederatedAverager, RewardLedger, RolloutBuffer, adversarial, curriculum,
                     dpo_update, fedavg, ppo_update, reinforce_update, replay_trace)
-from .local_model import LocalReasoningModel, LoRA, LoraLearningLoop, lm_forward, load_adapter
+from .local_model import (LocalReasoningModel, LoRA, LoraLearningLoop, lm_forward, load_adapter, load_peft_adapter,
+                          save_peft_adapter)
 from .orchestrator import BatchController, Pid, PolicyOrchestrator, power_fraction
 from .state import WIDTH, PowerSampler, Slot, StateCollector
 
@@ -13,4 +14,4 @@ __all__ = ["AdaptivePolicy", "Decision", "DecisionExecutor", "EndpointModel", "r
            "DepthPolicy", "FederatedAverager", "RewardLedger", "RolloutBuffer", "curriculum", "fedavg", "ppo_update",
            "reinforce_update", "dpo_update", "adversarial", "replay_trace", "BatchController", "Pid", "PolicyOrchestrator", "power_fraction", "WIDTH",
            "PowerSampler", "Slot", "StateCollector", "LocalReasoningModel", "LoRA", "LoraLearningLoop", "lm_forward",
-           "load_adapter"]
+           "load_adapter", "load_peft_adapter", "save_peft_adapter"]

@@ -401,3 +401,125 @@ def load_adapter(model, path: str) -> LoRA:
     lora = LoRA(model, blob["r"], blob["scale"] * blob["r"])
     lora.load_state_dict(blob["state"])
     return lora
+
+
+# ------------------------------------------------------------------ PEFT adapter format
+_PEFT_PREFIX = "base_model.model.model.layers.{}."
+_PEFT_MODULES = {"wqkv": ("self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj"), "wo": ("self_attn.o_proj",),
+                 "w_gate_up": ("mlp.gate_proj", "mlp.up_proj"), "w_down": ("mlp.down_proj",)}
+
+
+def _gate_up_rows(F2: int, part: int) -> torch.Tensor:
+    """Rows of the 64-row-interleaved gate/up matrix [2F, H] that belong to gate (part 0)
+    or up (part 1), in order."""
+    g = torch.arange(F2).view(F2 // (2 * SWIGLU_GROUP), 2, SWIGLU_GROUP)
+    return g[:, part].reshape(-1)
+
+
+def save_peft_adapter(lora: LoRA, path: str) -> None:
+    """Writes ``lora`` as a Hugging Face PEFT adapter directory (``adapter_config.json`` +
+    ``adapter_model.safetensors``; separate q/k/v and gate/up projections, which share the
+    fused adapter's A and take their rows of its B)."""
+    from ..models.loader import save_safetensors
+
+    os.makedirs(path, exist_ok=True)
+    cfg = lora.model.cfg
+    q, kv = cfg.q_size, cfg.kv_size
+    out: Dict[str, torch.Tensor] = {}
+    rank_pattern: Dict[str, int] = {}
+    alpha_pattern: Dict[str, float] = {}
+    for li in range(len(lora.model.layers)):
+        pre = _PEFT_PREFIX.format(li)
+        for name, mods in _PEFT_MODULES.items():
+            key = f"{li}_{name}"
+            if key not in lora.A:
+                continue
+            A, B = lora.A[key].detach().float().cpu(), lora.B[key].detach().float().cpu()
+            if A.shape[0] != lora.r:  # an imported fused adapter: its own rank, same scaling
+                for mod in mods:
+                    rank_pattern[f"model.layers.{li}.{mod}"] = int(A.shape[0])
+                    alpha_pattern[f"model.layers.{li}.{mod}"] = lora.scale * A.shape[0]
+            if name == "wqkv":
+                parts = [B[:q], B[q:q + kv], B[q + kv:]]
+            elif name == "w_gate_up":
+                parts = [B[_gate_up_rows(B.shape[0], 0)], B[_gate_up_rows(B.shape[0], 1)]]
+            else:
+                parts = [B]
+            for mod, b in zip(mods, parts):
+                out[pre + mod + ".lora_A.weight"] = A.contiguous()
+                out[pre + mod + ".lora_B.weight"] = b.contiguous()
+    save_safetensors(os.path.join(path, "adapter_model.safetensors"), out)
+    with open(os.path.join(path, "adapter_config.json"), "w") as f:
+        json.dump({"peft_type": "LORA", "r": lora.r, "lora_alpha": lora.scale * lora.r,
+                   "rank_pattern": rank_pattern, "alpha_pattern": alpha_pattern,
+                   "target_modules": ["q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj"],
+                   "bias": "none", "task_type": "CAUSAL_LM"}, f, indent=1)
+
+
+def load_peft_adapter(model, path: str) -> LoRA:
+    """A :class:`LoRA` for ``model`` from a Hugging Face PEFT adapter directory. Separate
+    q/k/v (gate/up) adapters become one adapter of the fused projection: A stacked, B block
+    diagonal (its gate/up rows interleaved by 64 like the weights), so its delta is exactly
+    the separate deltas stacked; projections the adapter does not cover get none."""
+    from ..models.loader import SafetensorsFile
+
+    with open(os.path.join(path, "adapter_config.json")) as f:
+        conf = json.load(f)
+    r, alpha = int(conf["r"]), float(conf.get("lora_alpha", conf["r"]))
+    rank_pat, alpha_pat = conf.get("rank_pattern") or {}, conf.get("alpha_pattern") or {}
+
+    def module_scale(module: str) -> float:
+        """PEFT's alpha / r of this module (patterns match by suffix) over the global one."""
+        r_m = next((int(v) for k, v in rank_pat.items() if module.endswith(k)), r)
+        a_m = next((float(v) for k, v in alpha_pat.items() if module.endswith(k)), alpha)
+        return (a_m / r_m) / (alpha / r)
+
+    st = SafetensorsFile(os.path.join(path, "adapter_model.safetensors"))
+    names = set(st.keys())
+    cfg = model.cfg
+    lora = LoRA(model, r, alpha)
+    dev = model.embed.device
+    for li, lw in enumerate(model.layers):
+        pre = _PEFT_PREFIX.format(li)
+        for name, mods in _PEFT_MODULES.items():
+            key = f"{li}_{name}"
+            w = getattr(lw, name, None)
+            if w is None or key not in lora.A:
+                continue
+            if name == "wqkv":
+                rows = [cfg.q_size, cfg.kv_size, cfg.kv_size]
+            elif name == "w_gate_up":
+                rows = [w.shape[0] // 2, w.shape[0] // 2]
+            else:
+                rows = [w.shape[0]]
+            As, blocks = [], []  # blocks: (row offset in the [part0; part1; ...] layout, B block)
+            off = 0
+            for mod, nrow in zip(mods, rows):
+                a_n, b_n = pre + mod + ".lora_A.weight", pre + mod + ".lora_B.weight"
+                if a_n in names and b_n in names:
+                    A_p, B_p = st.get(a_n).float(), st.get(b_n).float()
+                    if B_p.shape[0] != nrow or A_p.shape[1] != w.shape[1] or B_p.shape[1] != A_p.shape[0]:
+                        raise ValueError(f"{mod} of layer {li}: adapter shapes {tuple(A_p.shape)} / "
+                                         f"{tuple(B_p.shape)} do not fit the projection")
+                    As.append(A_p)
+                    blocks.append((off, B_p * module_scale(f"model.layers.{li}.{mod}")))
+                off += nrow
+            if not As:  # this projection has no adapter
+                del lora.A[key], lora.B[key]
+                continue
+            A = torch.cat(As, dim=0)
+            B = torch.zeros(w.shape[0], A.shape[0])
+            col = 0
+            for row0, B_p in blocks:
+                B[row0:row0 + B_p.shape[0], col:col + B_p.shape[1]] = B_p
+                col += B_p.shape[1]
+            if name == "w_gate_up":  # [gate; up] rows -> the weights' 64-row interleave
+                F2 = w.shape[0]
+                inter = torch.empty_like(B)
+                inter[_gate_up_rows(F2, 0)] = B[:F2 // 2]
+                inter[_gate_up_rows(F2, 1)] = B[F2 // 2:]
+                B = inter
+            lora.A[key] = torch.nn.Parameter(A.to(dev))
+            lora.B[key] = torch.nn.Parameter(B.to(dev))
+    st.close()
+    return lora

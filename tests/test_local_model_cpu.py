@@ -1,5 +1,7 @@
 """Local reasoning model with LoRA adapters: differentiable forward, candidate ranking,
 merge/unmerge, DPO / SFT / policy-gradient updates and the learning loop (CPU, fp32)."""
+import json
+
 import numpy as np
 import pytest
 import torch
@@ -290,3 +292,58 @@ def test_shared_prompt_scores_match_full_sequences():
         lp = F.log_softmax(lm_forward(m, toks, lora)[len(p) - 1:-1], dim=-1)
         want.append(lp.gather(1, toks[len(p):, None]).sum())
     torch.testing.assert_close(got, torch.stack(want), rtol=1e-4, atol=2e-3)
+
+
+def test_peft_adapter_import_export(tmp_path):
+    """A PEFT-format adapter (separate q/k/v/o/gate/up/down, random A and B) loaded onto the
+    fused projections gives the same forward as the base weights with each projection's
+    delta added the plain way; exporting it again and re-importing keeps the deltas."""
+    from axropus_deploy_b200.models.loader import save_safetensors
+    from axropus_deploy_b200.ops.dense import interleave_gate_up, split_gate_up
+    from axropus_deploy_b200.policy.local_model import load_peft_adapter, save_peft_adapter
+
+    m = _model()
+    cfg = m.cfg
+    H, q, kv, F_ = cfg.hidden, cfg.q_size, cfg.kv_size, cfg.ffn
+    g = torch.Generator().manual_seed(5)
+    shapes = {"self_attn.q_proj": (q, H), "self_attn.k_proj": (kv, H), "self_attn.v_proj": (kv, H),
+              "self_attn.o_proj": (H, q), "mlp.gate_proj": (F_, H), "mlp.up_proj": (F_, H), "mlp.down_proj": (H, F_)}
+    r, alpha = 4, 8.0
+    tensors, deltas = {}, {}
+    for li in range(len(m.layers)):
+        for mod, (o, i) in shapes.items():
+            if li == 1 and mod == "self_attn.k_proj":
+                continue  # an uncovered part
+            A = torch.randn(r, i, generator=g) * 0.1
+            B = torch.randn(o, r, generator=g) * 0.1
+            tensors[f"base_model.model.model.layers.{li}.{mod}.lora_A.weight"] = A
+            tensors[f"base_model.model.model.layers.{li}.{mod}.lora_B.weight"] = B
+            deltas[(li, mod)] = (alpha / r) * B @ A
+    d = tmp_path / "peft"
+    d.mkdir()
+    save_safetensors(str(d / "adapter_model.safetensors"), tensors)
+    (d / "adapter_config.json").write_text(json.dumps({"peft_type": "LORA", "r": r, "lora_alpha": alpha}))
+    lora = load_peft_adapter(m, str(d))
+    toks = torch.arange(20) * 7 % cfg.vocab
+    got = lm_forward(m, toks, lora)
+
+    ref = _model()  # same seed: same base weights
+    z = lambda o, i: torch.zeros(o, i)  # noqa: E731
+    for li, lw in enumerate(ref.layers):
+        dq = deltas[(li, "self_attn.q_proj")]
+        dk = deltas.get((li, "self_attn.k_proj"), z(kv, H))
+        dv = deltas[(li, "self_attn.v_proj")]
+        lw.wqkv += torch.cat([dq, dk, dv])
+        lw.wo += deltas[(li, "self_attn.o_proj")]
+        gate, up = split_gate_up(lw.w_gate_up)
+        lw.w_gate_up.copy_(interleave_gate_up(gate + deltas[(li, "mlp.gate_proj")], up + deltas[(li, "mlp.up_proj")]))
+        lw.w_down += deltas[(li, "mlp.down_proj")]
+    torch.testing.assert_close(got, lm_forward(ref, toks), rtol=1e-4, atol=1e-4)
+
+    save_peft_adapter(lora, str(tmp_path / "out"))
+    back = load_peft_adapter(m, str(tmp_path / "out"))
+    for key in lora.A:
+        li, name = key.split("_", 1)
+        torch.testing.assert_close(back.delta(int(li), name), lora.delta(int(li), name), rtol=1e-5, atol=1e-6)
+    conf = json.loads((tmp_path / "out" / "adapter_config.json").read_text())
+    assert conf["rank_pattern"]["model.layers.0.self_attn.q_proj"] == 3 * r  # fused q/k/v rank
