@@ -234,6 +234,16 @@ class LocalReasoningModel:
             out = out + (tok_lp * mask).sum(1)
         return out
 
+    def policy_logprob(self, v: np.ndarray, d: Decision, lora: Optional[LoRA] = None) -> torch.Tensor:
+        """log pi(d | state) of the policy that picks among the candidates with probabilities
+        softmax(scores); ``d`` joins the candidate set if it is not in it."""
+        cands = list(self.candidates)
+        idx = next((i for i, c in enumerate(cands) if render(c) == render(d)), None)
+        if idx is None:
+            cands.append(d)
+            idx = len(cands) - 1
+        return F.log_softmax(self.scores(v, lora, cands), dim=0)[idx]
+
     def decide(self, v: np.ndarray) -> Decision:
         """The highest-scoring candidate; any failure returns a fallback decision (fail closed,
         like the endpoint model)."""
@@ -297,6 +307,22 @@ def sft_step(lm: LocalReasoningModel, lora: LoRA, opt: torch.optim.Optimizer,
     return float(loss.detach())
 
 
+def ppo_step(lm: LocalReasoningModel, lora: LoRA, opt: torch.optim.Optimizer,
+             rows: Sequence[Tuple[np.ndarray, Decision, float, float]], clip: float = 0.2) -> float:
+    """One clipped-surrogate PPO update (Schulman et al. 2017) on (state, decision,
+    advantage, behaviour log-prob) rows; the policy is the softmax over the candidates'
+    scores."""
+    losses = []
+    for v, d, adv, old_lp in rows:
+        ratio = torch.exp(lm.policy_logprob(v, d, lora) - old_lp)
+        losses.append(-torch.min(ratio * adv, torch.clamp(ratio, 1 - clip, 1 + clip) * adv))
+    loss = torch.stack(losses).mean()
+    opt.zero_grad()
+    loss.backward()
+    opt.step()
+    return float(loss.detach())
+
+
 @dataclass
 class TrainingResult:
     examples_used: int
@@ -312,8 +338,8 @@ class LoraLearningLoop:
     """Periodic LoRA fine-tuning of a :class:`LocalReasoningModel` from its own scored
     decisions in a :class:`~.learn.RewardLedger`. ``level`` picks the objective: 1 SFT on
     positive-reward decisions, 2 reward-weighted policy gradient (REINFORCE with a mean
-    baseline), 4 DPO on best-versus-worst pairs of the same state (level 3, PPO over the
-    speculative depth, is :func:`~.learn.ppo_update` on the small :class:`~.learn.DepthPolicy`).
+    baseline), 3 PPO (clipped ratio, :func:`ppo_step`) over the model's distribution on the
+    candidate decisions, 4 DPO on best-versus-worst pairs of the same state.
     Each cycle trains a copy of the live adapters and swaps it in under a lock, so
     ``decide`` never sees half-updated weights; the adapters are saved to ``adapter_dir``.
     """
@@ -333,6 +359,11 @@ class LoraLearningLoop:
     def _examples(self, rows) -> Tuple[str, list]:
         if self.level >= 4:
             return "dpo", preference_pairs(rows)
+        if self.level == 3:
+            mean = float(np.mean([r["reward"] for r in rows])) if rows else 0.0
+            ex = [(r["state"], r["decision"], r["reward"] - mean) for r in rows if r["reward"] != mean]
+            with torch.no_grad():  # behaviour policy: the live adapters before this cycle
+                return "ppo", [(v, d, a, float(self.lm.policy_logprob(v, d, self.lm.lora))) for v, d, a in ex]
         if self.level >= 2:
             mean = float(np.mean([r["reward"] for r in rows])) if rows else 0.0
             return "pg", [(r["state"], r["decision"], r["reward"] - mean) for r in rows if r["reward"] != mean]
@@ -355,8 +386,12 @@ class LoraLearningLoop:
         loss = 0.0
         try:
             for _ in range(self.epochs):
-                loss = (dpo_step(self.lm, lora, opt, ex, self.beta) if kind == "dpo"
-                        else sft_step(self.lm, lora, opt, ex))
+                if kind == "dpo":
+                    loss = dpo_step(self.lm, lora, opt, ex, self.beta)
+                elif kind == "ppo":
+                    loss = ppo_step(self.lm, lora, opt, ex)
+                else:
+                    loss = sft_step(self.lm, lora, opt, ex)
         except Exception as e:  # the live adapters stay; the rows stay unconsumed for the next cycle
             return TrainingResult(len(ex), 0.0, 0.0, None, time.perf_counter() - t0, True, f"fine-tune error: {e}")
         with self._swap:

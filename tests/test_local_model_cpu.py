@@ -150,7 +150,7 @@ def test_preference_pairs_group_by_state():
     assert good.spec_decode_depth == 8 and bad.spec_decode_depth == 2
 
 
-@pytest.mark.parametrize("level", [1, 2, 4])
+@pytest.mark.parametrize("level", [1, 2, 3, 4])
 def test_learning_loop_cycle(tmp_path, level):
     m = _model()
     lm = LocalReasoningModel(m, max_prompt_tokens=24)
@@ -347,3 +347,23 @@ def test_peft_adapter_import_export(tmp_path):
         torch.testing.assert_close(back.delta(int(li), name), lora.delta(int(li), name), rtol=1e-5, atol=1e-6)
     conf = json.loads((tmp_path / "out" / "adapter_config.json").read_text())
     assert conf["rank_pattern"]["model.layers.0.self_attn.q_proj"] == 3 * r  # fused q/k/v rank
+
+
+def test_ppo_moves_probability_to_the_rewarded_decision():
+    from axropus_deploy_b200.policy.local_model import ppo_step
+
+    m = _model()
+    lo_d, hi_d = Decision(spec_decode_depth=2), Decision(spec_decode_depth=8)
+    lm = LocalReasoningModel(m, candidates=[lo_d, hi_d], max_prompt_tokens=32)
+    v = np.linspace(0, 1, WIDTH, dtype=np.float32)
+    lora = LoRA(m, r=4, alpha=8)
+    p0 = float(torch.exp(lm.policy_logprob(v, hi_d, lora)).detach())
+    opt = torch.optim.Adam(lora.parameters(), lr=1e-2)
+    for _ in range(4):  # a few cycles: behaviour log-probs refreshed each time, 3 epochs each
+        with torch.no_grad():
+            rows = [(v, hi_d, 1.0, float(lm.policy_logprob(v, hi_d, lora))),
+                    (v, lo_d, -1.0, float(lm.policy_logprob(v, lo_d, lora)))]
+        for _ in range(3):
+            ppo_step(lm, lora, opt, rows)
+    p1 = float(torch.exp(lm.policy_logprob(v, hi_d, lora)).detach())
+    assert p1 > p0 + 0.2 and p1 > 0.7
