@@ -346,11 +346,14 @@ class LoraLearningLoop:
 
     def __init__(self, lm: LocalReasoningModel, ledger, level: int = 4, interval_s: float = 3600.0,
                  batch_size: int = 64, min_examples: int = 8, epochs: int = 2, lr: float = 1e-3, beta: float = 0.1,
-                 r: int = 8, alpha: float = 16.0, adapter_dir: Optional[str] = None):
+                 r: int = 8, alpha: float = 16.0, adapter_dir: Optional[str] = None, adapter_format: str = "peft"):
         self.lm, self.ledger, self.level = lm, ledger, int(level)
         self.interval_s, self.batch_size, self.min_examples = max(1.0, float(interval_s)), batch_size, min_examples
         self.epochs, self.lr, self.beta, self.r, self.alpha = epochs, lr, beta, r, alpha
         self.adapter_dir = adapter_dir
+        if adapter_format not in ("peft", "pt"):
+            raise ValueError("adapter_format must be 'peft' or 'pt'")
+        self.adapter_format = adapter_format
         self.cycles = 0
         self._swap = threading.Lock()
         self._stop = threading.Event()
@@ -407,7 +410,14 @@ class LoraLearningLoop:
             return self.lm.decide(v)
 
     def save(self, lora: LoRA) -> str:
+        """This cycle's adapters under ``adapter_dir``: a PEFT adapter directory
+        (``adapter_format="peft"``, loads with :func:`load_peft_adapter` or Hugging Face PEFT)
+        or one ``.pt`` file (``"pt"``, :func:`load_adapter`)."""
         os.makedirs(self.adapter_dir, exist_ok=True)
+        if self.adapter_format == "peft":
+            path = os.path.join(self.adapter_dir, f"adapter_{self.cycles:05d}")
+            save_peft_adapter(lora, path)
+            return path
         path = os.path.join(self.adapter_dir, f"adapter_{self.cycles:05d}.pt")
         torch.save({"r": lora.r, "scale": lora.scale, "state": lora.state_dict()}, path)
         return path

@@ -169,7 +169,14 @@ def test_learning_loop_cycle(tmp_path, level):
     assert led.scored(100) == []  # consumed
     again = loop.run_once()
     assert again.skipped
-    back = load_adapter(m, res.adapter_path)
+    from axropus_deploy_b200.policy.local_model import load_peft_adapter
+
+    back = load_peft_adapter(m, res.adapter_path)  # PEFT directory by default
+    for k in lm.lora.A:
+        li, name = k.split("_", 1)
+        torch.testing.assert_close(back.delta(int(li), name), lm.lora.delta(int(li), name), rtol=1e-5, atol=1e-6)
+    pt = LoraLearningLoop(lm, led, adapter_dir=str(tmp_path / "pt"), adapter_format="pt").save(lm.lora)
+    back = load_adapter(m, pt)
     for k in back.A:
         torch.testing.assert_close(back.A[k], lm.lora.A[k])
         torch.testing.assert_close(back.B[k], lm.lora.B[k])
