@@ -374,3 +374,26 @@ def test_ppo_moves_probability_to_the_rewarded_decision():
             ppo_step(lm, lora, opt, rows)
     p1 = float(torch.exp(lm.policy_logprob(v, hi_d, lora)).detach())
     assert p1 > p0 + 0.2 and p1 > 0.7
+
+
+def test_orchestrator_with_local_model_and_lora_loop():
+    """The worker hooks with the local model as the policy's model and its LoRA loop
+    training on the orchestrator's own reward ledger."""
+    from axropus_deploy_b200.cluster.runtime import SpecKController
+    from axropus_deploy_b200.policy import AdaptivePolicy, DecisionExecutor, PolicyOrchestrator, StateCollector
+
+    m = _model()
+    lm = LocalReasoningModel(m, candidates=[Decision(spec_decode_depth=4), Decision(spec_decode_depth=8)],
+                             max_prompt_tokens=32)
+    led = RewardLedger()
+    loop = LoraLearningLoop(lm, led, level=2, min_examples=1, epochs=1, r=4)
+    orch = PolicyOrchestrator(StateCollector(), policy=AdaptivePolicy(model=loop, model_primary=True),
+                              executor=DecisionExecutor(SpecKController(4)), rewards=led)
+    for i, acc in enumerate((9, 1)):
+        tok = orch.before_job({"org_id": "acme", "fingerprint_hash": f"fp{i}"})
+        assert tok is not None and tok[1].spec_decode_depth in (4, 8)
+        orch.after_job(tok, {"amf": {"decision": "hit", "tier": "g1_raw", "saved_ms": 50.0},
+                             "spec": {"drafted": 10, "accepted": acc}, "perf": {}}, mode="speculative")
+    assert orch.policy.stat["model"] == 2
+    r = loop.run_once()
+    assert not r.skipped and lm.lora is not None
