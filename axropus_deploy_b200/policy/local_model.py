@@ -520,51 +520,53 @@ def load_peft_adapter(model, path: str) -> LoRA:
         return (a_m / r_m) / (alpha / r)
 
     st = SafetensorsFile(os.path.join(path, "adapter_model.safetensors"))
-    names = set(st.keys())
-    cfg = model.cfg
-    lora = LoRA(model, r, alpha)
-    dev = model.embed.device
-    for li, lw in enumerate(model.layers):
-        pre = _PEFT_PREFIX.format(li)
-        for name, mods in _PEFT_MODULES.items():
-            key = f"{li}_{name}"
-            w = getattr(lw, name, None)
-            if w is None or key not in lora.A:
-                continue
-            if name == "wqkv":
-                rows = [cfg.q_size, cfg.kv_size, cfg.kv_size]
-            elif name == "w_gate_up":
-                rows = [w.shape[0] // 2, w.shape[0] // 2]
-            else:
-                rows = [w.shape[0]]
-            As, blocks = [], []  # blocks: (row offset in the [part0; part1; ...] layout, B block)
-            off = 0
-            for mod, nrow in zip(mods, rows):
-                a_n, b_n = pre + mod + ".lora_A.weight", pre + mod + ".lora_B.weight"
-                if a_n in names and b_n in names:
-                    A_p, B_p = st.get(a_n).float(), st.get(b_n).float()
-                    if B_p.shape[0] != nrow or A_p.shape[1] != w.shape[1] or B_p.shape[1] != A_p.shape[0]:
-                        raise ValueError(f"{mod} of layer {li}: adapter shapes {tuple(A_p.shape)} / "
-                                         f"{tuple(B_p.shape)} do not fit the projection")
-                    As.append(A_p)
-                    blocks.append((off, B_p * module_scale(f"model.layers.{li}.{mod}")))
-                off += nrow
-            if not As:  # this projection has no adapter
-                del lora.A[key], lora.B[key]
-                continue
-            A = torch.cat(As, dim=0)
-            B = torch.zeros(w.shape[0], A.shape[0])
-            col = 0
-            for row0, B_p in blocks:
-                B[row0:row0 + B_p.shape[0], col:col + B_p.shape[1]] = B_p
-                col += B_p.shape[1]
-            if name == "w_gate_up":  # [gate; up] rows -> the weights' 64-row interleave
-                F2 = w.shape[0]
-                inter = torch.empty_like(B)
-                inter[_gate_up_rows(F2, 0)] = B[:F2 // 2]
-                inter[_gate_up_rows(F2, 1)] = B[F2 // 2:]
-                B = inter
-            lora.A[key] = torch.nn.Parameter(A.to(dev))
-            lora.B[key] = torch.nn.Parameter(B.to(dev))
-    st.close()
+    try:
+        names = set(st.keys())
+        cfg = model.cfg
+        lora = LoRA(model, r, alpha)
+        dev = model.embed.device
+        for li, lw in enumerate(model.layers):
+            pre = _PEFT_PREFIX.format(li)
+            for name, mods in _PEFT_MODULES.items():
+                key = f"{li}_{name}"
+                w = getattr(lw, name, None)
+                if w is None or key not in lora.A:
+                    continue
+                if name == "wqkv":
+                    rows = [cfg.q_size, cfg.kv_size, cfg.kv_size]
+                elif name == "w_gate_up":
+                    rows = [w.shape[0] // 2, w.shape[0] // 2]
+                else:
+                    rows = [w.shape[0]]
+                As, blocks = [], []  # blocks: (row offset in the [part0; part1; ...] layout, B block)
+                off = 0
+                for mod, nrow in zip(mods, rows):
+                    a_n, b_n = pre + mod + ".lora_A.weight", pre + mod + ".lora_B.weight"
+                    if a_n in names and b_n in names:
+                        A_p, B_p = st.get(a_n).float(), st.get(b_n).float()
+                        if B_p.shape[0] != nrow or A_p.shape[1] != w.shape[1] or B_p.shape[1] != A_p.shape[0]:
+                            raise ValueError(f"{mod} of layer {li}: adapter shapes {tuple(A_p.shape)} / "
+                                             f"{tuple(B_p.shape)} do not fit the projection")
+                        As.append(A_p)
+                        blocks.append((off, B_p * module_scale(f"model.layers.{li}.{mod}")))
+                    off += nrow
+                if not As:  # this projection has no adapter
+                    del lora.A[key], lora.B[key]
+                    continue
+                A = torch.cat(As, dim=0)
+                B = torch.zeros(w.shape[0], A.shape[0])
+                col = 0
+                for row0, B_p in blocks:
+                    B[row0:row0 + B_p.shape[0], col:col + B_p.shape[1]] = B_p
+                    col += B_p.shape[1]
+                if name == "w_gate_up":  # [gate; up] rows -> the weights' 64-row interleave
+                    F2 = w.shape[0]
+                    inter = torch.empty_like(B)
+                    inter[_gate_up_rows(F2, 0)] = B[:F2 // 2]
+                    inter[_gate_up_rows(F2, 1)] = B[F2 // 2:]
+                    B = inter
+                lora.A[key] = torch.nn.Parameter(A.to(dev))
+                lora.B[key] = torch.nn.Parameter(B.to(dev))
+    finally:
+        st.close()
     return lora
