@@ -244,6 +244,47 @@ class LocalReasoningModel:
             idx = len(cands) - 1
         return F.log_softmax(self.scores(v, lora, cands), dim=0)[idx]
 
+    def decode_text(self, ids: List[int]) -> str:
+        if self.tok is not None:
+            return self.tok.decode(ids)
+        return bytes(int(t) % 256 for t in ids).decode("utf-8", errors="replace")
+
+    def generate(self, v: np.ndarray, max_new: int = 192, lora: Optional[LoRA] = None) -> Tuple[str, List[int]]:
+        """Greedy free-form answer to the state prompt, one token at a time over the cached
+        K/V of the prompt and the tokens so far; stops when the JSON object it opened closes."""
+        dev = self.model.embed.device
+        ids = self.prompt(v) + self.encode("{")
+        logits, kv = lm_forward(self.model, torch.tensor([ids], dtype=torch.long, device=dev), lora, return_kv=True)
+        out = list(self.encode("{"))
+        depth, n = 1, len(ids)
+        for _ in range(max_new):
+            nxt = int(torch.argmax(logits[0, -1]))
+            out.append(nxt)
+            text = self.decode_text(out)
+            depth = text.count("{") - text.count("}")
+            if depth <= 0:
+                break
+            logits, new_kv = lm_forward(self.model, torch.tensor([[nxt]], dtype=torch.long, device=dev), lora,
+                                        start=n, past=kv, return_kv=True)
+            kv = [(torch.cat((pk, k), dim=1), torch.cat((pv, vv), dim=1)) for (pk, pv), (k, vv) in zip(kv, new_kv)]
+            n += 1
+        return self.decode_text(out), out
+
+    def decide_generated(self, v: np.ndarray, max_new: int = 192) -> Decision:
+        """The reference's way: the model writes the decision JSON itself (nested or flat
+        fields); anything that does not parse or validate returns a fallback decision."""
+        t0 = time.perf_counter()
+        try:
+            with torch.no_grad():
+                text, _ = self.generate(v, max_new, self.lora)
+            d = Decision.from_dict(json.loads(text[text.index("{"):text.rindex("}") + 1]))
+            if d.validate():
+                raise ValueError("; ".join(d.validate()))
+        except Exception:
+            d = Decision(is_fallback=True)
+        d.inference_ms = (time.perf_counter() - t0) * 1e3
+        return d
+
     def decide(self, v: np.ndarray) -> Decision:
         """The highest-scoring candidate; any failure returns a fallback decision (fail closed,
         like the endpoint model)."""

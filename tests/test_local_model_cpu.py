@@ -397,3 +397,33 @@ def test_orchestrator_with_local_model_and_lora_loop():
     assert orch.policy.stat["model"] == 2
     r = loop.run_once()
     assert not r.skipped and lm.lora is not None
+
+
+def test_generate_reuses_the_cache_and_parses_decisions(monkeypatch):
+    import axropus_deploy_b200.policy.local_model as lmm
+
+    m = _model()
+    lm = LocalReasoningModel(m, max_prompt_tokens=24)
+    v = np.zeros(WIDTH, np.float32)
+    text, ids = lm.generate(v, max_new=6)
+    # the incremental logits pick the same tokens as full-sequence forwards
+    full = lm.prompt(v) + ids
+    n0 = len(lm.prompt(v)) + 1
+    ref = lm_forward(m, torch.tensor(full[:-1]))
+    assert [int(t) for t in ref[n0 - 1:].argmax(-1)] == ids[1:]
+
+    want = '{"decode": {"spec_decode_depth": 12}, "cache_admission": false}'
+    real = lmm.lm_forward
+
+    def scripted(model, tokens, lora=None, start=0, past=None, return_kv=False):
+        logits, kv = real(model, tokens, lora, start, past, return_kv=True)
+        produced = start + tokens.shape[1] - len(lm.prompt(v))  # tokens of the answer so far
+        forced = torch.full_like(logits, -1e9)
+        forced[..., ord(want[produced]) if produced < len(want) else 0] = 0.0
+        return (forced, kv) if return_kv else forced
+
+    monkeypatch.setattr(lmm, "lm_forward", scripted)
+    d = lm.decide_generated(v)
+    assert not d.is_fallback and d.spec_decode_depth == 12 and d.cache_admission is False
+    monkeypatch.setattr(lmm, "lm_forward", real)
+    assert lm.decide_generated(v, max_new=4).is_fallback  # an unfinished answer falls back
