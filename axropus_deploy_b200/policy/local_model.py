@@ -65,6 +65,17 @@ class LoRA(torch.nn.Module):
         self.to(model.embed.device)
         self.merged = False
 
+    def clone(self) -> "LoRA":
+        """A trainable copy with the same keys, ranks and scaling (the model is shared)."""
+        c = LoRA(self.model, self.r, self.scale * self.r)
+        for key in list(c.A.keys()):
+            if key not in self.A:
+                del c.A[key], c.B[key]
+        for key in self.A.keys():
+            c.A[key] = torch.nn.Parameter(self.A[key].detach().clone())
+            c.B[key] = torch.nn.Parameter(self.B[key].detach().clone())
+        return c
+
     def delta(self, li: int, name: str) -> Optional[torch.Tensor]:
         key = f"{li}_{name}"
         if key not in self.A:
@@ -423,9 +434,10 @@ class LoraLearningLoop:
             return TrainingResult(len(ex), 0.0, 0.0, None, time.perf_counter() - t0, True,
                                   f"only {len(ex)} {kind} examples < {self.min_examples}")
         live = self.lm.lora
-        lora = LoRA(self.lm.model, self.r, self.alpha)
-        if live is not None:
-            lora.load_state_dict(live.state_dict())
+        if live is not None and live.merged:  # the weights carry its delta: training on them would count it twice
+            return TrainingResult(len(ex), 0.0, 0.0, None, time.perf_counter() - t0, True,
+                                  "live adapters are merged into the weights: unmerge before training")
+        lora = live.clone() if live is not None else LoRA(self.lm.model, self.r, self.alpha)
         opt = torch.optim.AdamW(lora.parameters(), lr=self.lr)
         loss = 0.0
         try:
@@ -611,3 +623,45 @@ def load_peft_adapter(model, path: str) -> LoRA:
     finally:
         st.close()
     return lora
+
+
+def main(argv: Optional[Sequence[str]] = None) -> int:
+    """One offline learning cycle over a reward ledger:
+
+        python -m axropus_deploy_b200.policy.local_model --ledger rewards.sqlite \\
+            --model-dir /models/llama-3.1-8b --level 4 --out adapters/ [--adapter adapters/adapter_00003]
+
+    trains (starting from ``--adapter`` when given) on the ledger's unconsumed scored
+    decisions, writes the new adapters under ``--out`` and prints one JSON line."""
+    import argparse
+
+    from .learn import RewardLedger
+
+    ap = argparse.ArgumentParser(description="one LoRA learning cycle of the local reasoning model")
+    ap.add_argument("--ledger", required=True)
+    ap.add_argument("--model-dir", required=True)
+    ap.add_argument("--out", required=True)
+    ap.add_argument("--level", type=int, default=4)
+    ap.add_argument("--adapter", default=None, help="PEFT adapter directory to continue from")
+    ap.add_argument("--epochs", type=int, default=2)
+    ap.add_argument("--lr", type=float, default=1e-3)
+    ap.add_argument("--min-examples", type=int, default=8)
+    ap.add_argument("--device", default="cuda" if torch.cuda.is_available() else "cpu")
+    a = ap.parse_args(argv)
+    from ..models.loader import load_pretrained
+    from ..server.app import load_tokenizer
+
+    model = load_pretrained(a.model_dir, a.device)
+    lm = LocalReasoningModel(model, load_tokenizer(a.model_dir))
+    if a.adapter:
+        lm.lora = load_peft_adapter(model, a.adapter)
+    loop = LoraLearningLoop(lm, RewardLedger(a.ledger), level=a.level, epochs=a.epochs, lr=a.lr,
+                            min_examples=a.min_examples, adapter_dir=a.out)
+    r = loop.run_once()
+    print(json.dumps({k: getattr(r, k) for k in ("examples_used", "mean_reward", "loss", "adapter_path", "elapsed_s",
+                                                 "skipped", "skip_reason")}))
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

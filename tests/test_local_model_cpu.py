@@ -427,3 +427,27 @@ def test_generate_reuses_the_cache_and_parses_decisions(monkeypatch):
     assert not d.is_fallback and d.spec_decode_depth == 12 and d.cache_admission is False
     monkeypatch.setattr(lmm, "lm_forward", real)
     assert lm.decide_generated(v, max_new=4).is_fallback  # an unfinished answer falls back
+
+
+def test_offline_learning_cycle_cli(tmp_path, capsys):
+    """``python -m axropus_deploy_b200.policy.local_model``: a saved checkpoint and a ledger
+    file in, a PEFT adapter directory out; a second cycle continues from it."""
+    from axropus_deploy_b200.models.loader import save_pretrained
+    from axropus_deploy_b200.policy.local_model import main
+
+    m = _model()
+    save_pretrained(m, str(tmp_path / "ckpt"))
+    led = RewardLedger(str(tmp_path / "rewards.sqlite"))
+    v = np.zeros(WIDTH, np.float32)
+    for d, o in ((Decision(spec_decode_depth=8), "spec_high_acceptance"), (Decision(spec_decode_depth=2), "spec_low_acceptance")):
+        led.record_outcome(led.record_decision(d, v), o)
+    args = ["--ledger", str(tmp_path / "rewards.sqlite"), "--model-dir", str(tmp_path / "ckpt"), "--out",
+            str(tmp_path / "ad"), "--level", "4", "--min-examples", "1", "--device", "cpu"]
+    assert main(args) == 0
+    out = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert not out["skipped"] and out["adapter_path"].endswith("adapter_00000")
+    led.record_outcome(led.record_decision(Decision(spec_decode_depth=8), v), "spec_high_acceptance")
+    led.record_outcome(led.record_decision(Decision(spec_decode_depth=2), v), "spec_low_acceptance")
+    assert main(args + ["--adapter", out["adapter_path"]]) == 0
+    out2 = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert not out2["skipped"]
