@@ -302,3 +302,24 @@ def test_enterprise_usage_is_not_billed_per_token(env):
     assert c.post("/api/metrics", json=_metric(ent, tokens_processed=5_000_000)).status_code == 200
     b = c.get("/api/billing/summary", headers=h).json()["current_period"]
     assert b["enterprise_tokens"] == 5_000_000 and b["amount_cents"] == 0 and b["pricing"] == "custom annual pricing"
+
+
+def test_security_boundaries(env):
+    """Cross-account access, forged tokens, injected strings and brute force are refused."""
+    c, _ = env
+    ha, key_a = _signup(c, "a1@x.io")
+    hb, key_b = _signup(c, "b1@x.io")
+    assert c.post("/api/deploy", json={"host": "h", "username": "u", "password": "p", "api_key": key_b},
+                  headers=ha).status_code == 400  # another account's key
+    assert c.post("/api/deploy", json={"host": "h", "username": "u", "password": "p"}, headers=ha).status_code == 200
+    assert c.get("/api/deploy/status/1", headers=hb).status_code == 404  # not B's deployment
+    forged = make_token("not-the-secret", 1)
+    assert c.get("/api/auth/me", headers={"Authorization": "Bearer " + forged}).status_code == 401
+    for bad in ("x'; DROP TABLE metrics;--", "../../etc/passwd", "llama<script>"):
+        assert c.post("/api/metrics", json=_metric(key_a, sdk_version=bad)).status_code == 400
+    assert c.get("/api/keys/validate/' OR 1=1 --").json()["valid"] is False
+    codes = [c.post("/api/auth/login", json={"email": "a1@x.io", "password": "wrong-pass"}).status_code
+             for _ in range(32)]
+    assert codes[0] == 401 and codes[-1] == 429
+    r = c.get("/api/keys", headers=ha)
+    assert r.headers["x-content-type-options"] == "nosniff" and r.headers["cache-control"] == "no-store"
